@@ -1,0 +1,232 @@
+/*
+ * ttn.h -- C ABI of the ThinTNPU-B200 op-pass library (libttn.so).
+ *
+ * This header is the drop-in boundary for the fp16 tensor-library hot path that
+ * runs between the YOLO convolutions: SiLU/sigmoid, broadcast arithmetic,
+ * concat/split, NC1HWC0<->NCHW layout, nearest-2x upsample, max-pool/SPPF,
+ * row/DFL softmax with anchor decode, and YOLO26 top-k detection selection.
+ *
+ * Every entry point
+ *   - takes raw device pointers, element sizes/strides as int64_t, and a
+ *     cudaStream_t (passed as ttn_stream, the same pointer type);
+ *   - enqueues its kernels on that stream and returns without synchronising;
+ *   - never throws, never aborts, and reports failures as a ttn_status, with a
+ *     human-readable message available from ttn_last_error() on the same
+ *     thread;
+ *   - allocates no device memory: scratch space is passed in by the caller
+ *     (sizes from the matching *_workspace_size function).
+ * Each declaration names the reference (maxesisnclaw/ThinTNPU) interface it
+ * replaces as file:line.
+ */
+#ifndef TTN_H
+#define TTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without including cuda_runtime.h. */
+typedef struct CUstream_st* ttn_stream;
+
+typedef enum ttn_status {
+  TTN_OK = 0,
+  TTN_INVALID_ARG = 1,       /* a shape, stride, pointer or flag is malformed */
+  TTN_UNSUPPORTED = 2,       /* well-formed but outside what the op supports */
+  TTN_CUDA_ERROR = 3,        /* a CUDA runtime call or a launch failed */
+  TTN_TIMEOUT = 4,           /* a bounded device wait ran out */
+  TTN_DEVICE_FAULT_FLAG = 5  /* a kernel raised its device status word */
+} ttn_status;
+
+typedef enum ttn_dtype { TTN_F16 = 0, TTN_F32 = 1 } ttn_dtype;
+
+typedef enum ttn_binary_op {
+  TTN_SUB = 0, /* x - alpha*y */
+  TTN_MUL = 1, /* x * y */
+  TTN_DIV = 2, /* x / y */
+  TTN_ADD = 3  /* x + alpha*y */
+} ttn_binary_op;
+
+typedef enum ttn_layout { TTN_NCHW = 0, TTN_NC1HWC0 = 1 } ttn_layout;
+
+#define TTN_MAX_DIMS 8
+#define TTN_C0 16
+
+/* A strided view: data points at element [0,...,0]; strides count elements. */
+typedef struct ttn_tensor {
+  void* data;
+  int32_t ndim;
+  int32_t dtype; /* ttn_dtype */
+  int64_t sizes[TTN_MAX_DIMS];
+  int64_t strides[TTN_MAX_DIMS];
+} ttn_tensor;
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int ttn_version(void);
+
+/* Static string for a status code. */
+const char* ttn_status_string(ttn_status status);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* ttn_last_error(void);
+
+/* Stream capture on caller-owned memory, the C-side twin of
+ * thin_backend::RuntimeGraph (reference backend.cpp:62-113):
+ * aclmdlRICaptureBegin(THREAD_LOCAL) -> cudaStreamBeginCapture(ThreadLocal),
+ * aclmdlRICaptureEnd -> cudaStreamEndCapture + cudaGraphInstantiate,
+ * aclmdlRIExecuteAsync -> cudaGraphLaunch, aclmdlRIDestroy -> destroy.
+ * A graph stays bound to the stream it was begun on and to the creating thread. */
+typedef struct ttn_graph ttn_graph;
+ttn_status ttn_graph_create(ttn_graph** graph);
+ttn_status ttn_graph_begin(ttn_graph* graph, ttn_stream stream);
+ttn_status ttn_graph_end(ttn_graph* graph);
+ttn_status ttn_graph_replay(ttn_graph* graph);
+ttn_status ttn_graph_close(ttn_graph* graph);   /* idempotent */
+void ttn_graph_destroy(ttn_graph* graph);       /* closes, then frees the handle */
+
+/* ---------------------------------------------------- elementwise (a1-a3) */
+
+/* y = x / (1 + exp(-x)), FP32 math, one rounding; y may alias x (in place).
+ * Replaces silu_impl elementwise.cpp:47-102 and thin_ops::silu_ ops.cpp:498-512;
+ * aten::silu aten_adapter.cpp:98-105. x and y have equal sizes, any strides. */
+ttn_status ttn_silu(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream);
+
+/* y = 1 / (1 + exp(-x)), FP32 math, one rounding (bit-equal to CPU eager).
+ * Replaces sigmoid_impl sigmoid.cpp:6-44, thin::sigmoid backend.cpp:226-244. */
+ttn_status ttn_sigmoid(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream);
+
+/* out = x (op) alpha*y over equal-sized views; broadcast is a stride of 0.
+ * Replaces binary_impl elementwise.cpp:6-45, strided_binary::launch
+ * strided_binary.h:192-222 and its dispatch binary() ops.cpp:464-497. */
+ttn_status ttn_binary(int op, float alpha, const ttn_tensor* x, const ttn_tensor* y,
+                      const ttn_tensor* out, ttn_stream stream);
+
+/* out = x (op) scalar, the scalar rounded to FP32 first (CPU eager "tensor op
+ * python number").  Replaces the fp16 scale multiply whole_blocked.py:101-102. */
+ttn_status ttn_binary_scalar(int op, double scalar, const ttn_tensor* x,
+                             const ttn_tensor* out, ttn_stream stream);
+
+/* Fused y = SiLU(x + b[c]) + r over NC1HWC0 fp16 [n, c1, hw, 16], FP32 math,
+ * one rounding; b is fp16 [c1*16].  The SiLU epilogue of conv_flow.cpp:57-84
+ * plus the Bottleneck residual add (ops.cpp:464-493) in one pass. */
+ttn_status ttn_bias_silu_residual_nc1hwc0_f16(const void* x, const void* bias,
+                                              const void* residual, void* y, int64_t n,
+                                              int64_t c1, int64_t hw, ttn_stream stream);
+
+/* ------------------------------------------------ data movement (a4, a5) */
+
+/* dst = src elementwise copy between equal-sized views of the same dtype.
+ * Replaces thin_ops::copy_strided ops.cpp:31-84 / materialize::copy
+ * ops.cpp:245-288 (device-to-device). */
+ttn_status ttn_copy(const ttn_tensor* src, const ttn_tensor* dst, ttn_stream stream);
+
+/* out = cat(inputs, dim).  Inputs of numel 0 are skipped; out must have the
+ * concatenated sizes.  Replaces cat() ops.cpp:419-462 with its three paths
+ * concatenate::copy :383-416, strided_concat::launch strided_concat.h:163-238
+ * and the copy_strided fallback. */
+ttn_status ttn_cat(int32_t count, const ttn_tensor* inputs, int32_t dim,
+                   const ttn_tensor* out, ttn_stream stream);
+
+/* NC1HWC0 [n, c1, hw, 16] -> NCHW.  Channel c < channels of image b, pixel p
+ * goes to y[b*y_batch_stride + c*y_channel_stride + p]; channels <= c1*16 drops
+ * the zero-padded tail channels.  Replaces unpack layout_blocked.h:60-69 and the
+ * Detect-terminal NCHW restore conv_flow.cpp:87-121 / trim_output :375-403. */
+ttn_status ttn_nc1hwc0_to_nchw_f16(const void* x, int64_t n, int64_t c1, int64_t hw,
+                                   int64_t channels, void* y, int64_t y_batch_stride,
+                                   int64_t y_channel_stride, ttn_stream stream);
+
+/* NCHW [n, channels, hw] -> NC1HWC0 [n, ceil(channels/16), hw, 16], padding
+ * channels with +0.  Replaces pack layout_blocked.h:43-58 and
+ * pack_input_channels conv_flow.cpp:406-458. */
+ttn_status ttn_nchw_to_nc1hwc0_f16(const void* x, int64_t n, int64_t channels,
+                                   int64_t hw, void* y, ttn_stream stream);
+
+/* ------------------------------------------------------- spatial (a6, a7) */
+
+/* Nearest 2x upsample.  NCHW: x [n, c, h, w] -> y [n, c, 2h, 2w];
+ * NC1HWC0: x [n, c1, h, w, 16] -> y [n, c1, 2h, 2w, 16] (pass c = c1).
+ * Contiguous tensors.  Replaces upsample_impl upsample.cpp:5-132,
+ * thin::upsample_nearest2d backend.cpp:266-286 and blocked_flow::upsample
+ * flow_ops.cpp:233-252. */
+ttn_status ttn_upsample2x(int layout, int dtype, const void* x, void* y, int64_t n,
+                          int64_t c, int64_t h, int64_t w, ttn_stream stream);
+
+/* kernel x kernel, stride 1, padding kernel/2 max-pool with -inf padding,
+ * NaN-propagating (CPU F.max_pool2d semantics).  kernel odd, >= 1.
+ * Layouts as ttn_upsample2x.  Replaces maxpool_impl maxpool.cpp:5-191,
+ * thin::maxpool2d backend.cpp:245-265, blocked_flow::maxpool flow_ops.cpp:208-231. */
+ttn_status ttn_maxpool(int layout, int dtype, int32_t kernel, const void* x, void* y,
+                       int64_t n, int64_t c, int64_t h, int64_t w, ttn_stream stream);
+
+/* SPPF tail fused: out = cat(x, p1, p2, p3) along C1 with p(i+1) = maxpool(p(i)),
+ * x NC1HWC0 fp16 [n, c1, h, w, 16], out [n, 4*c1, h, w, 16].  Replaces three
+ * blocked_flow::maxpool calls plus cat (whole_blocked.py:63-64, ops.cpp:419). */
+ttn_status ttn_sppf_f16(const void* x, void* out, int64_t n, int64_t c1, int64_t h,
+                        int64_t w, int32_t kernel, ttn_stream stream);
+
+/* --------------------------------------------------------- softmax (a8, a9) */
+
+/* y = softmax(x * scale, dim) over views of equal sizes.  x: f16 or f32;
+ * y: same dtype or f32 (half_to_float).  scale != 1 first rounds x*scale to
+ * x's dtype (the separate fp16 multiply of whole_blocked.py:101-102).  FP32
+ * internals.  Replaces thin_softmax::softmax softmax_host.cpp:51-89 and the
+ * kernels Softmax softmax.cpp:6-173 / DflSoftmax :175-271. */
+ttn_status ttn_softmax(const ttn_tensor* x, int32_t dim, float scale, const ttn_tensor* y,
+                       ttn_stream stream);
+
+/* Fused Detect decode (v8 DFL / v26).  box: fp16 [n, 4*16, a] logits (element
+ * (b, s*16+i, j) at box[b*box_bs + (s*16+i)*box_cs + j]); cls: fp16 [n, nc, a]
+ * logits with its own strides.  Anchors come from `levels` feature maps of
+ * sizes heights[l] x widths[l] with strides[l] (a = sum h*w, grid cell + 0.5).
+ * out: fp16 [n, 4+nc, a] contiguous = cat(boxes*stride, sigmoid(cls)), boxes
+ * xywh when xywh != 0 else xyxy.  Rounds to fp16 after every step the
+ * reference rounds (whole_blocked.py:118-146; DFL softmax.cpp:175-263). */
+ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs,
+                              const void* cls, int64_t cls_bs, int64_t cls_cs, int64_t n,
+                              int64_t nc, int32_t levels, const int64_t* heights,
+                              const int64_t* widths, const float* strides, int32_t xywh,
+                              void* out, ttn_stream stream);
+
+/* ------------------------------------------------------- selection (a10) */
+
+/* Flags for ttn_select_f16. */
+#define TTN_SELECT_AGNOSTIC 1u     /* one class per anchor (argmax) */
+#define TTN_SELECT_NAN_LAST 2u     /* rank NaN scores below -inf (default: above +inf) */
+#define TTN_SELECT_SIGMOID 4u      /* decoded[...,4:] are logits: apply fp16 sigmoid first */
+
+/* Optional intermediate outputs, each NULL to skip (the 8 stages of
+ * detection_select_trace selection_flow.cpp:385-491). */
+typedef struct ttn_select_trace {
+  uint16_t* class_max;       /* [b, anchors] best score bits per anchor */
+  int64_t* stage1_indices;   /* [b, k] anchors in stage-1 order */
+  uint16_t* gathered_scores; /* [b, k, nc] (class-aware only) */
+  uint16_t* top_values;      /* [b, k] selected score bits */
+  int64_t* stage2_indices;   /* [b, k] flat rank*nc+cls (class-aware only) */
+  int64_t* anchor_indices;   /* [b, k] */
+  int64_t* labels;           /* [b, k] */
+} ttn_select_trace;
+
+/* Bytes of scratch ttn_select_f16 needs (256-byte aligned pointer). */
+size_t ttn_select_workspace_size(int64_t batch, int64_t anchors, int64_t classes,
+                                 int64_t max_det, uint32_t flags);
+
+/* YOLO26 NMS-free selection over decoded fp16 [b, anchors, 4+nc] (any strides):
+ * per-anchor class max, stable top-k anchors, then (class-aware) stable top-k
+ * over the k*nc (anchor, class) pairs; writes out FP32 [b, k, 6] rows
+ * (x1, y1, x2, y2, score, class), k = min(max_det, anchors).  Order is the
+ * reference's total order: score key, then lower index; NaN first.
+ * Replaces detection_selection::run selection_flow.cpp:429-491 and
+ * thin_native_flow::detection_select :493-514. */
+ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t flags,
+                          void* workspace, size_t workspace_bytes, float* out,
+                          const ttn_select_trace* trace, ttn_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TTN_H */

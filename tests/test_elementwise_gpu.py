@@ -1,0 +1,125 @@
+"""GPU parity: SiLU, sigmoid, add/sub/mul/div, and the fused config-1 op vs CPU eager.
+
+Tolerances (north star): fp16 elementwise within 2 ulp of PyTorch CPU eager;
+SiLU and sigmoid are held to bit equality (the kernels reproduce CPU's FP32
+formula and its rounding), binary ops with alpha == 1 as well.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import assert_bits_equal, half_bits, ulp_diff
+from oracle import ops as oops
+
+pytestmark = pytest.mark.gpu
+
+ALL_HALVES = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.float16)
+
+
+@pytest.mark.parametrize("name", ["silu", "sigmoid"])
+def test_unary_exhaustive_fp16_bit_exact(device, name):
+    import thintnpu_b200 as ttn
+    fn = getattr(ttn, name)
+    ref = getattr(oops, name)(ALL_HALVES)
+    # dense aligned path, an odd-length tail, and a strided view
+    assert_bits_equal(fn(ALL_HALVES.to(device)), ref, name)
+    odd = ALL_HALVES[3:].clone()
+    assert_bits_equal(fn(odd.to(device)), getattr(oops, name)(odd), name + " tail")
+    strided = ALL_HALVES.view(256, 256).t()
+    assert_bits_equal(fn(strided.to(device)), getattr(oops, name)(strided), name + " strided")
+
+
+@pytest.mark.parametrize("shape", [(1,), (3,), (7,), (100,), (2047,), (2048,), (2049,), (16385,),
+                                   (65537,), (0,), (), (3, 5, 7)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_binary_sizes(device, shape, dtype):
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(42)
+    a = (torch.rand(shape, generator=g) * 2 - 1).to(dtype)
+    b = (torch.rand(shape, generator=g) + 0.5).to(dtype)
+    for op in ("add", "sub", "mul", "div"):
+        got = getattr(ttn, op)(a.to(device), b.to(device)).cpu()
+        want = oops.binary(op, a, b)
+        if dtype == torch.float16:
+            assert_bits_equal(got, want, f"{op} {shape}")
+        else:
+            torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-6)
+
+
+def test_binary_alpha_strided_broadcast(device):
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(7)
+    a = torch.randn(2, 5, 7, generator=g).half()
+    b = torch.randn(2, 5, 7, generator=g).half() + 2
+    for op in ("sub", "mul", "div"):
+        got = getattr(ttn, op)(a.to(device).transpose(0, 2), b.to(device).transpose(0, 2))
+        assert_bits_equal(got, oops.binary(op, a.transpose(0, 2), b.transpose(0, 2)), op)
+    for alpha in (2.0, -0.5):
+        got = ttn.sub(a.to(device), b.to(device), alpha=alpha)
+        assert ulp_diff(got, torch.sub(a, b, alpha=alpha)).max() <= 2
+    # row, column and scalar broadcast; narrow [...,2] box slices (verify_narrow_binary.py)
+    x = torch.randn(1, 3, 9, 11, 16, generator=g).half()
+    row = torch.randn(1, 1, 1, 11, 16, generator=g).half()
+    col = torch.randn(1, 3, 9, 1, 1, generator=g).half()
+    for other in (row, col, torch.tensor(1.5, dtype=torch.float16)):
+        got = ttn.add(x.to(device), other.to(device))
+        assert_bits_equal(got, x + other, "broadcast")
+    got = ttn.mul(x.to(device)[..., 2:4], x.to(device)[..., :2])
+    assert_bits_equal(got, x[..., 2:4] * x[..., :2], "narrow")
+    got = ttn.mul(x.to(device), 32 ** -0.5)
+    assert_bits_equal(got, x * 32 ** -0.5, "python scalar")
+
+
+def test_silu_inplace_on_strided_parent_and_c2f_chain(device):
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(42)
+    a = torch.randn(2, 7, 5, 7, generator=g).half()
+    x = a.to(device)
+    part = torch.split(x, [3, 4], 1)[1]
+    ptr = part.data_ptr()
+    out = ttn.silu_(part)
+    assert out is part and out.data_ptr() == ptr
+    ref = a.clone()
+    F.silu(torch.split(ref, [3, 4], 1)[1], inplace=True)
+    assert_bits_equal(x, ref, "silu_ strided parent")
+    for channels in (8, 7):
+        a = torch.randn(2, channels, 13, 11, generator=g).half() * 0.5
+        x = a.to(device)
+        p, q = torch.split(x, [channels // 2, channels - channels // 2], 1)
+        rp, rq = torch.split(a.clone(), [channels // 2, channels - channels // 2], 1)
+        ttn.silu_(q)
+        F.silu(rq, inplace=True)
+        z = ttn.cat((p, ttn.add(q, q)), 1)
+        assert_bits_equal(z, torch.cat((rp, rq + rq), 1), "c2f chain")
+
+
+def test_config1_bias_silu_residual(device):
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(1)
+    x = oops.to_blocked(torch.randn(1, 128, 80, 80, generator=g).half())
+    r = oops.to_blocked(torch.randn(1, 128, 80, 80, generator=g).half())
+    b = (torch.randn(128, generator=g) * 0.1).half()
+    got = ttn.bias_silu_residual(x.to(device), b.to(device), r.to(device))
+    want = oops.bias_silu_residual(x, b, r)
+    d = ulp_diff(got, want)
+    assert d.max() <= 2, d.max()
+    assert (d == 0).mean() > 0.99
+
+
+@pytest.mark.parametrize("dtype", [torch.float32])
+def test_unary_float32(device, dtype):
+    import thintnpu_b200 as ttn
+    a = torch.linspace(-8, 8, 65537, dtype=dtype)
+    torch.testing.assert_close(ttn.sigmoid(a.to(device)).cpu(), torch.sigmoid(a), rtol=2e-6, atol=1e-7)
+    torch.testing.assert_close(ttn.silu(a.to(device)).cpu(), F.silu(a), rtol=2e-6, atol=1e-7)
+
+
+def test_unary_nan_payloads_follow_cpu(device):
+    import thintnpu_b200 as ttn
+    vals = [0x7E00, 0xFE00, 0x7C01, 0x7D23, 0xFD23, 0x7FFF, 0xFFFF, 0x7C00, 0xFC00]
+    h = torch.tensor(vals, dtype=torch.int32).to(torch.int16).view(torch.float16)
+    assert np.array_equal(half_bits(ttn.sigmoid(h.to(device))), half_bits(torch.sigmoid(h)))
+    assert np.array_equal(half_bits(ttn.silu(h.to(device))), half_bits(F.silu(h)))

@@ -1,0 +1,95 @@
+"""CPU: pin the oracle against the reference's own golden vectors and KATs."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, selection_case, selection_index
+from oracle import ops as oops
+from oracle import select as osel
+
+
+def nan_canonical_output(rows: np.ndarray) -> np.ndarray:
+    """The golden rows come from torch's CPU ``half.float()``, whose scalar tail
+    loop (x86, torch 2.11) widens every NaN to 0x7fffffff while its vector body
+    and the reference's float_bits (selection_flow.cpp:37-51) keep sign and
+    payload.  Such rows are mapped back to the float_bits value: the reference
+    fixtures only hold the default NaN 0x7e00, whose widening is 0x7fc00000."""
+    rows = rows.copy()
+    rows[rows == 0x7FFFFFFF] = 0x7FC00000
+    return rows
+
+
+def test_torch_scalar_half_widening_quirk_is_the_only_nan_difference():
+    x = torch.full((1,), float("nan"), dtype=torch.float16)
+    assert x.float().view(torch.int32).item() & 0xFFFFFFFF in (0x7FC00000, 0x7FFFFFFF)
+    assert int(osel.float_bits(np.array([0x7E00], np.uint16))[0]) == 0x7FC00000
+
+
+def test_score_key_and_float_bits_match_reference_for_all_halves():
+    with np.load(GOLDEN / "selection_keys.npz") as z:
+        ref_key, ref_bits = z["score_key"], z["float_bits"]
+    halves = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    assert np.array_equal(osel.score_keys(halves), ref_key)
+    assert np.array_equal(osel.float_bits(halves), ref_bits)
+    # the key order is torch's stable descending argsort (verify_selection_flow.py:141-144)
+    t = torch.from_numpy(halves.view(np.int16)).view(torch.float16)
+    order = torch.argsort(t, descending=True, stable=True).numpy()
+    assert np.array_equal(np.argsort(ref_key, kind="stable"), order)
+
+
+def test_float_bits_equals_torch_widening():
+    halves = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    t = torch.from_numpy(halves.view(np.int16)).view(torch.float16)
+    widened = t.float().view(torch.int32).numpy().view(np.uint32)
+    assert np.array_equal(osel.float_bits(halves), widened)
+
+
+def test_nan_last_keys_rank_nan_after_minus_inf():
+    halves = np.array([0x7E00, 0xFC00, 0x3C00, 0xFE01], np.uint16)
+    keys = osel.score_keys(halves, nan_last=True)
+    assert keys[0] > keys[1] and keys[3] > keys[1] and keys[2] < keys[1]
+
+
+@pytest.mark.parametrize("case", [c["name"] for c in selection_index()])
+def test_selection_oracle_matches_reference_fixture(case):
+    meta = next(c for c in selection_index() if c["name"] == case)
+    golden = selection_case(case)
+    got = osel.select(golden["decoded"], meta["max_det"], meta["agnostic"])
+    for name in osel.TRACE_NAMES:
+        want = golden[name]
+        have = got[name]
+        assert have.shape == want.shape, (case, name, have.shape, want.shape)
+        if name == "output":
+            want = nan_canonical_output(want)
+        assert np.array_equal(have.astype(want.dtype), want), (case, name)
+
+
+def test_blocked_layout_round_trip():
+    x = torch.randn(2, 48, 5, 7).half()
+    assert torch.equal(oops.from_blocked(oops.to_blocked(x)), x)
+    padded = oops.pack_padded(x[:, :40])
+    assert padded.shape == (2, 3, 5, 7, 16)
+    assert torch.equal(oops.unpack(padded, 40), x[:, :40].reshape(2, 40, 35))
+
+
+def test_sppf_oracle_equals_chained_pools():
+    x = torch.randn(1, 2, 20, 20, 16).half()
+    y = oops.sppf(x)
+    assert y.shape == (1, 8, 20, 20, 16)
+    p1 = oops.maxpool_blocked(x, 5)
+    assert torch.equal(y[:, 2:4], p1)
+    assert torch.equal(y[:, 4:6], oops.maxpool_blocked(p1, 5))
+
+
+def test_dfl_decode_oracle_shapes_and_anchor_points():
+    shapes, strides = [(8, 8), (4, 4), (2, 2)], [8.0, 16.0, 32.0]
+    a = sum(h * w for h, w in shapes)
+    box = torch.zeros(1, 64, a).half()
+    cls = torch.zeros(1, 3, a).half()
+    out = oops.dfl_decode(box, cls, shapes, strides)
+    assert out.shape == (1, 7, a)
+    # uniform bins -> distance 7.5 per side: w = h = 15 * stride, centre = anchor * stride
+    assert float(out[0, 2, 0]) == 15 * 8 and float(out[0, 0, 0]) == 0.5 * 8
+    assert torch.all(out[0, 4:] == 0.5)

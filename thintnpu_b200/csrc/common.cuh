@@ -1,0 +1,176 @@
+// Shared helpers for the libttn kernels: status reporting, strided-view
+// coalescing, launch sizing and the fp16 rounding rules of PyTorch CPU eager.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/ttn.h"
+
+namespace ttn {
+
+// ------------------------------------------------------------------ status
+
+void set_error(const char* fmt, ...);
+ttn_status fail(ttn_status status, const char* fmt, ...);
+
+// Turns a CUDA runtime error (or a pending launch error) into TTN_CUDA_ERROR.
+inline ttn_status cuda_check(cudaError_t err, const char* what) {
+  if (err == cudaSuccess) return TTN_OK;
+  return fail(TTN_CUDA_ERROR, "%s: %s", what, cudaGetErrorString(err));
+}
+inline ttn_status launch_check(const char* what) {
+  return cuda_check(cudaGetLastError(), what);
+}
+
+#define TTN_TRY(expr)                   \
+  do {                                  \
+    ttn_status _s = (expr);             \
+    if (_s != TTN_OK) return _s;        \
+  } while (0)
+
+// Number of SMs of the current device, cached per device.
+int sm_count();
+
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` on the
+// current device.  Cached per (device, kernel): the CUDA call only happens the
+// first time a larger size is needed, so later calls (e.g. inside stream
+// capture after a warm-up call) touch no runtime API.
+ttn_status ensure_dynamic_smem(const void* kernel, int bytes);
+
+// Largest opt-in dynamic shared memory per block on the current device.
+int max_dynamic_smem();
+
+// Grid size for a grid-stride loop: enough blocks for `work` units of `per_block`,
+// capped at `waves` resident blocks per SM.
+inline unsigned grid_for(int64_t work, int64_t per_block, int waves = 8) {
+  int64_t blocks = (work + per_block - 1) / per_block;
+  int64_t cap = (int64_t)sm_count() * waves;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (unsigned)blocks;
+}
+
+inline size_t dtype_size(int dtype) { return dtype == TTN_F32 ? 4 : 2; }
+
+// ------------------------------------------------------------ view helpers
+
+// A view reduced to its minimal number of dims (size-1 dims dropped, adjacent
+// dims merged where every participating view is contiguous across them).
+// Dims are stored innermost-first.
+struct Coalesced {
+  int ndim = 0;
+  int64_t size[TTN_MAX_DIMS];
+  int64_t stride[4][TTN_MAX_DIMS];  // per operand
+  int64_t numel = 1;
+};
+
+ttn_status validate(const ttn_tensor* t, const char* name);
+bool same_sizes(const ttn_tensor* a, const ttn_tensor* b);
+int64_t numel(const ttn_tensor* t);
+// Coalesce up to 4 equally-sized views into one iteration space.
+Coalesced coalesce(const ttn_tensor* const* views, int count);
+// True when the view is dense row-major (C-contiguous) from its data pointer.
+bool is_contiguous(const ttn_tensor* t);
+
+// Device-side iteration space for up to 6 coalesced dims and 3 operands.
+struct Index6 {
+  int ndim;
+  int64_t size[6];
+  int64_t stride[3][6];
+};
+
+__device__ __forceinline__ void offsets3(const Index6& ix, int64_t linear, int64_t& o0,
+                                         int64_t& o1, int64_t& o2) {
+  o0 = o1 = o2 = 0;
+#pragma unroll
+  for (int d = 0; d < 6; ++d) {
+    if (d >= ix.ndim) break;
+    int64_t q = linear / ix.size[d];
+    int64_t r = linear - q * ix.size[d];
+    linear = q;
+    o0 += r * ix.stride[0][d];
+    o1 += r * ix.stride[1][d];
+    o2 += r * ix.stride[2][d];
+  }
+}
+
+// -------------------------------------------------------- fp16 bit helpers
+
+__device__ __forceinline__ uint16_t hbits(__half h) { return __half_as_ushort(h); }
+__device__ __forceinline__ __half hfrom(uint16_t b) { return __ushort_as_half(b); }
+__device__ __forceinline__ bool hnan_bits(uint16_t b) { return (b & 0x7fffu) > 0x7c00u; }
+__device__ __forceinline__ uint16_t hquiet(uint16_t b) { return (uint16_t)(b | 0x0200u); }
+
+// Exact fp16 -> fp32 widening done on bits (keeps NaN sign/payload, quiets it),
+// the reference's float_bits (selection_flow.cpp:37-51).
+__host__ __device__ __forceinline__ uint32_t float_bits_of_half(uint32_t h) {
+  uint32_t sign = (h & 0x8000u) << 16;
+  uint32_t exponent = (h >> 10) & 31u;
+  uint32_t mantissa = h & 1023u;
+  if (exponent == 31u)
+    return sign | 0x7f800000u | (mantissa << 13) | (mantissa ? 0x00400000u : 0u);
+  if (exponent) return sign | ((exponent + 112u) << 23) | (mantissa << 13);
+  if (!mantissa) return sign;
+  exponent = 113u;
+  while (!(mantissa & 1024u)) {
+    mantissa <<= 1;
+    --exponent;
+  }
+  return sign | (exponent << 23) | ((mantissa & 1023u) << 13);
+}
+
+// True when r sits within ~8 fp32 ulps of the midpoint between the two fp16
+// values around it, i.e. when a few-ulp difference in an fp32 intermediate
+// could flip the final fp16 rounding.
+__device__ __forceinline__ bool near_half_midpoint(float r) {
+  float lo = __half2float(__float2half_rd(r));
+  float hi = __half2float(__float2half_ru(r));
+  if (!(lo < hi)) return false;  // exactly representable, inf or NaN
+  float mid = 0.5f * (lo + hi);  // exact: one more bit than fp16 needs
+  return fabsf(r - mid) <= fabsf(r) * 9.5367431640625e-07f;  // 2^-20
+}
+
+// fp32 exp(-x) correctly rounded: exp in double, then one rounding to fp32.
+__device__ __forceinline__ float exp_neg_cr(float x) { return (float)exp(-(double)x); }
+
+// --- PyTorch CPU eager rules for fp16 unary ops (FP32 math, one rounding) ---
+// CPU computes 1/(1+exp(-x)) and x/(1+exp(-x)) in fp32 with IEEE add/div and
+// rounds once to fp16.  The GPU uses expf and, when the fp32 result lies near an
+// fp16 rounding midpoint, recomputes with a correctly rounded exp so both sides
+// round the same fp32 value.  NaN handling follows x86: sigmoid returns the
+// quieted -x NaN, silu the quieted x NaN, and silu(-inf) is the default NaN.
+
+__device__ __forceinline__ float sigmoid_f32(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+}
+__device__ __forceinline__ float silu_f32(float x) {
+  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
+__device__ __forceinline__ uint16_t sigmoid_h(uint16_t xb) {
+  if (hnan_bits(xb)) return hquiet((uint16_t)(xb ^ 0x8000u));
+  float x = __half2float(hfrom(xb));
+  float r = sigmoid_f32(x);
+  if (near_half_midpoint(r)) r = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_neg_cr(x)));
+  return hbits(__float2half_rn(r));
+}
+
+__device__ __forceinline__ uint16_t silu_h(uint16_t xb) {
+  if (hnan_bits(xb)) return hquiet(xb);
+  if (xb == 0xfc00u) return 0xfe00u;  // -inf / (1 + inf): x86 default NaN
+  float x = __half2float(hfrom(xb));
+  float r = silu_f32(x);
+  if (near_half_midpoint(r)) r = __fdiv_rn(x, __fadd_rn(1.0f, exp_neg_cr(x)));
+  return hbits(__float2half_rn(r));
+}
+
+// fp32 versions for TTN_F32 tensors (no rounding step to protect).
+__device__ __forceinline__ float sigmoid_f(float x) { return sigmoid_f32(x); }
+__device__ __forceinline__ float silu_f(float x) { return silu_f32(x); }
+
+}  // namespace ttn

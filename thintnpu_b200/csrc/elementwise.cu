@@ -1,0 +1,442 @@
+// Elementwise ops of the op pass: SiLU, sigmoid, add/sub/mul/div (tensor or
+// scalar operand, stride-0 broadcast) and the fused NC1HWC0 y = SiLU(x+b)+r.
+//
+// HBM-bound: the contiguous paths move 16 bytes per thread per access (8 fp16
+// lanes, 128-bit loads/stores) with two independent accesses in flight per
+// thread, on a grid-stride loop sized to a few waves of the 148 SMs.  Views
+// that are not dense fall back to one thread per element over a coalesced
+// index space (<= 6 dims).  All arithmetic is FP32 with one rounding to fp16,
+// the rule of PyTorch CPU eager (and of elementwise.cpp:71-86 in the reference).
+#include "common.cuh"
+
+namespace ttn {
+namespace {
+
+constexpr int kThreads = 256;
+
+enum UnaryKind { kSilu = 0, kSigmoid = 1 };
+
+template <int K>
+__device__ __forceinline__ uint16_t unary_h(uint16_t x) {
+  return K == kSilu ? silu_h(x) : sigmoid_h(x);
+}
+template <int K>
+__device__ __forceinline__ float unary_f(float x) {
+  return K == kSilu ? silu_f(x) : sigmoid_f(x);
+}
+
+template <int K>
+__device__ __forceinline__ uint4 unary_vec8(uint4 v) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t lo = unary_h<K>((uint16_t)(w[i] & 0xffffu));
+    uint32_t hi = unary_h<K>((uint16_t)(w[i] >> 16));
+    w[i] = lo | (hi << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Dense fp16, 16-byte aligned: uint4 body plus a scalar tail.  x may equal y.
+template <int K>
+__global__ void __launch_bounds__(kThreads) unary_f16_dense(const uint4* x, uint4* y,
+                                                            int64_t nvec, const uint16_t* xt,
+                                                            uint16_t* yt, int tail) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + stride < nvec; i += 2 * stride) {
+    uint4 a = x[i];
+    uint4 b = x[i + stride];
+    y[i] = unary_vec8<K>(a);
+    y[i + stride] = unary_vec8<K>(b);
+  }
+  if (i < nvec) y[i] = unary_vec8<K>(x[i]);
+  if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = unary_h<K>(xt[threadIdx.x]);
+}
+
+// Any layout (also unaligned dense), one element per thread.
+template <int K, typename T>
+__global__ void __launch_bounds__(kThreads) unary_strided(const T* x, T* y, Index6 ix, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int64_t ox, oy, unused;
+    offsets3(ix, i, ox, oy, unused);
+    if constexpr (sizeof(T) == 2) {
+      reinterpret_cast<uint16_t*>(y)[oy] = unary_h<K>(reinterpret_cast<const uint16_t*>(x)[ox]);
+    } else {
+      y[oy] = unary_f<K>(x[ox]);
+    }
+  }
+}
+
+// Rows of dense fp16 (e.g. channel-block chunks of NC1HWC0 batches): the
+// innermost coalesced dim is unit-stride with a multiple of 8 elements and
+// every outer stride is a multiple of 8, so 16-byte vectors still apply.
+template <int K>
+__global__ void __launch_bounds__(kThreads) unary_f16_rows(const uint16_t* x, uint16_t* y,
+                                                           Index6 outer, int64_t vec_per_row,
+                                                           int64_t nvec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    int64_t row = i / vec_per_row, col = (i - row * vec_per_row) * 8;
+    int64_t ox, oy, unused;
+    offsets3(outer, row, ox, oy, unused);
+    const uint4 a = *reinterpret_cast<const uint4*>(x + ox + col);
+    *reinterpret_cast<uint4*>(y + oy + col) = unary_vec8<K>(a);
+  }
+}
+
+// ---------------------------------------------------------------- binary
+
+// CPU eager semantics per op (FP32 opmath, x86 IEEE): add/sub use one rounding
+// of x +- y when alpha == 1, and fma(y, +-alpha, x) otherwise (the vectorised
+// fmadd of the ATen CPU kernel); mul and div are single IEEE operations.
+struct BinaryParams {
+  int op;
+  float alpha;
+};
+
+__device__ __forceinline__ float binary_f(const BinaryParams& p, float a, float b) {
+  switch (p.op) {
+    case TTN_ADD: return p.alpha == 1.0f ? __fadd_rn(a, b) : __fmaf_rn(b, p.alpha, a);
+    case TTN_SUB: return p.alpha == 1.0f ? __fsub_rn(a, b) : __fmaf_rn(b, -p.alpha, a);
+    case TTN_MUL: return __fmul_rn(a, b);
+    default: return __fdiv_rn(a, b);
+  }
+}
+
+__device__ __forceinline__ uint32_t binary_h2(const BinaryParams& p, uint32_t a, uint32_t b) {
+  __half2 ha = *reinterpret_cast<__half2*>(&a);
+  __half2 hb = *reinterpret_cast<__half2*>(&b);
+  float2 fa = __half22float2(ha), fb = __half22float2(hb);
+  __half2 r = __floats2half2_rn(binary_f(p, fa.x, fb.x), binary_f(p, fa.y, fb.y));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+__global__ void __launch_bounds__(kThreads) binary_f16_dense(BinaryParams p, const uint4* x,
+                                                             const uint4* y, uint4* z,
+                                                             int64_t nvec, const uint16_t* xt,
+                                                             const uint16_t* yt, uint16_t* zt,
+                                                             int tail) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    uint4 a = x[i], b = y[i];
+    uint4 r;
+    r.x = binary_h2(p, a.x, b.x);
+    r.y = binary_h2(p, a.y, b.y);
+    r.z = binary_h2(p, a.z, b.z);
+    r.w = binary_h2(p, a.w, b.w);
+    z[i] = r;
+  }
+  if (blockIdx.x == 0 && (int)threadIdx.x < tail) {
+    float a = __half2float(hfrom(xt[threadIdx.x])), b = __half2float(hfrom(yt[threadIdx.x]));
+    zt[threadIdx.x] = hbits(__float2half_rn(binary_f(p, a, b)));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) binary_f16_rows(BinaryParams p, const uint16_t* x,
+                                                            const uint16_t* y, uint16_t* z,
+                                                            Index6 outer, int64_t vec_per_row,
+                                                            int64_t nvec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    int64_t row = i / vec_per_row, col = (i - row * vec_per_row) * 8;
+    int64_t ox, oy, oz;
+    offsets3(outer, row, ox, oy, oz);
+    uint4 a = *reinterpret_cast<const uint4*>(x + ox + col);
+    uint4 b = *reinterpret_cast<const uint4*>(y + oy + col);
+    uint4 r;
+    r.x = binary_h2(p, a.x, b.x);
+    r.y = binary_h2(p, a.y, b.y);
+    r.z = binary_h2(p, a.z, b.z);
+    r.w = binary_h2(p, a.w, b.w);
+    *reinterpret_cast<uint4*>(z + oz + col) = r;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) binary_strided(BinaryParams p, const T* x, const T* y,
+                                                           T* z, Index6 ix, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int64_t ox, oy, oz;
+    offsets3(ix, i, ox, oy, oz);
+    if constexpr (sizeof(T) == 2) {
+      float a = __half2float(x[ox]), b = __half2float(y[oy]);
+      z[oz] = __float2half_rn(binary_f(p, a, b));
+    } else {
+      z[oz] = binary_f(p, x[ox], y[oy]);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) scalar_strided(BinaryParams p, const T* x, float s,
+                                                           T* z, Index6 ix, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int64_t ox, oz, unused;
+    offsets3(ix, i, ox, oz, unused);
+    if constexpr (sizeof(T) == 2) {
+      z[oz] = __float2half_rn(binary_f(p, __half2float(x[ox]), s));
+    } else {
+      z[oz] = binary_f(p, x[ox], s);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) scalar_f16_dense(BinaryParams p, const uint4* x,
+                                                             float s, uint4* z, int64_t nvec,
+                                                             const uint16_t* xt, uint16_t* zt,
+                                                             int tail) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    uint4 a = x[i];
+    uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __half2 h = *reinterpret_cast<__half2*>(&w[k]);
+      float2 f = __half22float2(h);
+      __half2 r = __floats2half2_rn(binary_f(p, f.x, s), binary_f(p, f.y, s));
+      w[k] = *reinterpret_cast<uint32_t*>(&r);
+    }
+    z[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  if (blockIdx.x == 0 && (int)threadIdx.x < tail)
+    zt[threadIdx.x] =
+        hbits(__float2half_rn(binary_f(p, __half2float(hfrom(xt[threadIdx.x])), s)));
+}
+
+// ------------------------------------------- fused SiLU(x + b) + r, NC1HWC0
+
+// x, r, y: [n, c1, hw, 16] fp16; b: [c1*16].  Each uint4 covers half of one
+// pixel's 16 channel lanes, so its 8 bias values are contiguous in b.
+__global__ void __launch_bounds__(kThreads) bias_silu_residual(const uint4* x, const uint16_t* b,
+                                                               const uint4* r, uint4* y,
+                                                               int64_t nvec, int64_t hw,
+                                                               int64_t c1) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t vec_per_plane = hw * 2;  // 16 lanes = 2 uint4 per pixel
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    uint4 xv = x[i], rv = r[i];
+    int64_t plane = i / vec_per_plane;
+    int channel_block = (int)(plane % c1);
+    int half_sel = (int)(i & 1);
+    const uint4 bv = *reinterpret_cast<const uint4*>(b + channel_block * 16 + half_sel * 8);
+    uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+    uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+    uint32_t out[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 fx = __half22float2(*reinterpret_cast<__half2*>(&xw[k]));
+      float2 fr = __half22float2(*reinterpret_cast<__half2*>(&rw[k]));
+      float2 fb = __half22float2(*reinterpret_cast<__half2*>(&bw[k]));
+      float lo = __fadd_rn(silu_f32(__fadd_rn(fx.x, fb.x)), fr.x);
+      float hi = __fadd_rn(silu_f32(__fadd_rn(fx.y, fb.y)), fr.y);
+      __half2 h = __floats2half2_rn(lo, hi);
+      out[k] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    y[i] = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
+// ----------------------------------------------------------- host helpers
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// Dense when every view is contiguous with identical element order.
+bool dense(const Coalesced& c, int count) {
+  if (c.ndim > 1) return false;
+  if (c.ndim == 0) return true;
+  for (int v = 0; v < count; ++v)
+    if (c.stride[v][0] != 1) return false;
+  return true;
+}
+
+// Vectorisable rows: unit inner stride, inner length and outer strides in
+// multiples of 8 elements, 16-byte aligned bases, at most 6 outer dims.
+bool vec_rows(const Coalesced& c, int count, const void* const* ptrs, Index6& outer,
+              int64_t& vec_per_row) {
+  if (c.ndim < 2 || c.ndim > 7 || c.size[0] % 8) return false;
+  for (int v = 0; v < count; ++v) {
+    if (c.stride[v][0] != 1 || ((uintptr_t)ptrs[v] & 15u)) return false;
+    for (int d = 1; d < c.ndim; ++d)
+      if (c.stride[v][d] % 8) return false;
+  }
+  outer.ndim = c.ndim - 1;
+  for (int d = 0; d < 6; ++d) {
+    outer.size[d] = d + 1 < c.ndim ? c.size[d + 1] : 1;
+    for (int v = 0; v < 3; ++v)
+      outer.stride[v][d] = (d + 1 < c.ndim && v < count) ? c.stride[v][d + 1] : 0;
+  }
+  vec_per_row = c.size[0] / 8;
+  return true;
+}
+
+ttn_status to_index6(const Coalesced& c, int count, Index6& ix, const char* what) {
+  if (c.ndim > 6)
+    return fail(TTN_UNSUPPORTED, "%s: view needs %d dims after coalescing (max 6)", what, c.ndim);
+  ix.ndim = c.ndim;
+  for (int d = 0; d < 6; ++d) {
+    ix.size[d] = d < c.ndim ? c.size[d] : 1;
+    for (int v = 0; v < 3; ++v) ix.stride[v][d] = (d < c.ndim && v < count) ? c.stride[v][d] : 0;
+  }
+  return TTN_OK;
+}
+
+template <int K>
+ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, const char* name) {
+  TTN_TRY(validate(x, name));
+  TTN_TRY(validate(y, name));
+  if (!same_sizes(x, y)) return fail(TTN_INVALID_ARG, "%s: x and y sizes differ", name);
+  if (x->dtype != y->dtype) return fail(TTN_INVALID_ARG, "%s: x and y dtypes differ", name);
+  const ttn_tensor* views[2] = {x, y};
+  Coalesced c = coalesce(views, 2);
+  if (!c.numel) return TTN_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (x->dtype == TTN_F16 && dense(c, 2) && aligned16(x->data) && aligned16(y->data)) {
+    int64_t nvec = c.numel / 8;
+    int tail = (int)(c.numel - nvec * 8);
+    unsigned grid = grid_for(nvec ? nvec : 1, (int64_t)kThreads * 2);
+    unary_f16_dense<K><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x->data, (uint4*)y->data, nvec, (const uint16_t*)x->data + nvec * 8,
+        (uint16_t*)y->data + nvec * 8, tail);
+    return launch_check(name);
+  }
+  Index6 ix;
+  int64_t vpr;
+  const void* ptrs[2] = {x->data, y->data};
+  if (x->dtype == TTN_F16 && vec_rows(c, 2, ptrs, ix, vpr)) {
+    int64_t nvec = c.numel / 8;
+    unary_f16_rows<K><<<grid_for(nvec, kThreads), kThreads, 0, s>>>(
+        (const uint16_t*)x->data, (uint16_t*)y->data, ix, vpr, nvec);
+    return launch_check(name);
+  }
+  TTN_TRY(to_index6(c, 2, ix, name));
+  unsigned grid = grid_for(c.numel, kThreads);
+  if (x->dtype == TTN_F16)
+    unary_strided<K, __half><<<grid, kThreads, 0, s>>>((const __half*)x->data, (__half*)y->data, ix,
+                                                        c.numel);
+  else
+    unary_strided<K, float><<<grid, kThreads, 0, s>>>((const float*)x->data, (float*)y->data, ix,
+                                                       c.numel);
+  return launch_check(name);
+}
+
+}  // namespace
+}  // namespace ttn
+
+using namespace ttn;
+
+extern "C" {
+
+ttn_status ttn_silu(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream) {
+  return unary<kSilu>(x, y, stream, "ttn_silu");
+}
+
+ttn_status ttn_sigmoid(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream) {
+  return unary<kSigmoid>(x, y, stream, "ttn_sigmoid");
+}
+
+ttn_status ttn_binary(int op, float alpha, const ttn_tensor* x, const ttn_tensor* y,
+                      const ttn_tensor* out, ttn_stream stream) {
+  const char* name = "ttn_binary";
+  if (op < TTN_SUB || op > TTN_ADD) return fail(TTN_INVALID_ARG, "%s: unknown op %d", name, op);
+  TTN_TRY(validate(x, name));
+  TTN_TRY(validate(y, name));
+  TTN_TRY(validate(out, name));
+  if (!same_sizes(x, y) || !same_sizes(x, out))
+    return fail(TTN_INVALID_ARG, "%s: operand sizes differ (expand broadcasts first)", name);
+  if (x->dtype != y->dtype || x->dtype != out->dtype)
+    return fail(TTN_INVALID_ARG, "%s: operand dtypes differ", name);
+  const ttn_tensor* views[3] = {x, y, out};
+  Coalesced c = coalesce(views, 3);
+  if (!c.numel) return TTN_OK;
+  BinaryParams p{op, alpha};
+  cudaStream_t s = (cudaStream_t)stream;
+  if (x->dtype == TTN_F16 && dense(c, 3) && aligned16(x->data) && aligned16(y->data) &&
+      aligned16(out->data)) {
+    int64_t nvec = c.numel / 8;
+    int tail = (int)(c.numel - nvec * 8);
+    unsigned grid = grid_for(nvec ? nvec : 1, kThreads);
+    binary_f16_dense<<<grid, kThreads, 0, s>>>(
+        p, (const uint4*)x->data, (const uint4*)y->data, (uint4*)out->data, nvec,
+        (const uint16_t*)x->data + nvec * 8, (const uint16_t*)y->data + nvec * 8,
+        (uint16_t*)out->data + nvec * 8, tail);
+    return launch_check(name);
+  }
+  Index6 ix;
+  int64_t vpr;
+  const void* ptrs[3] = {x->data, y->data, out->data};
+  if (x->dtype == TTN_F16 && vec_rows(c, 3, ptrs, ix, vpr)) {
+    int64_t nvec = c.numel / 8;
+    binary_f16_rows<<<grid_for(nvec, kThreads), kThreads, 0, s>>>(
+        p, (const uint16_t*)x->data, (const uint16_t*)y->data, (uint16_t*)out->data, ix, vpr, nvec);
+    return launch_check(name);
+  }
+  TTN_TRY(to_index6(c, 3, ix, name));
+  unsigned grid = grid_for(c.numel, kThreads);
+  if (x->dtype == TTN_F16)
+    binary_strided<__half><<<grid, kThreads, 0, s>>>(p, (const __half*)x->data,
+                                                      (const __half*)y->data, (__half*)out->data,
+                                                      ix, c.numel);
+  else
+    binary_strided<float><<<grid, kThreads, 0, s>>>(p, (const float*)x->data, (const float*)y->data,
+                                                     (float*)out->data, ix, c.numel);
+  return launch_check(name);
+}
+
+ttn_status ttn_binary_scalar(int op, double scalar, const ttn_tensor* x, const ttn_tensor* out,
+                             ttn_stream stream) {
+  const char* name = "ttn_binary_scalar";
+  if (op < TTN_SUB || op > TTN_ADD) return fail(TTN_INVALID_ARG, "%s: unknown op %d", name, op);
+  TTN_TRY(validate(x, name));
+  TTN_TRY(validate(out, name));
+  if (!same_sizes(x, out)) return fail(TTN_INVALID_ARG, "%s: sizes differ", name);
+  if (x->dtype != out->dtype) return fail(TTN_INVALID_ARG, "%s: dtypes differ", name);
+  const ttn_tensor* views[2] = {x, out};
+  Coalesced c = coalesce(views, 2);
+  if (!c.numel) return TTN_OK;
+  BinaryParams p{op, 1.0f};
+  float s32 = (float)scalar;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (x->dtype == TTN_F16 && dense(c, 2) && aligned16(x->data) && aligned16(out->data)) {
+    int64_t nvec = c.numel / 8;
+    int tail = (int)(c.numel - nvec * 8);
+    unsigned grid = grid_for(nvec ? nvec : 1, kThreads);
+    scalar_f16_dense<<<grid, kThreads, 0, s>>>(p, (const uint4*)x->data, s32, (uint4*)out->data,
+                                               nvec, (const uint16_t*)x->data + nvec * 8,
+                                               (uint16_t*)out->data + nvec * 8, tail);
+    return launch_check(name);
+  }
+  Index6 ix;
+  TTN_TRY(to_index6(c, 2, ix, name));
+  unsigned grid = grid_for(c.numel, kThreads);
+  if (x->dtype == TTN_F16)
+    scalar_strided<__half><<<grid, kThreads, 0, s>>>(p, (const __half*)x->data, s32,
+                                                      (__half*)out->data, ix, c.numel);
+  else
+    scalar_strided<float><<<grid, kThreads, 0, s>>>(p, (const float*)x->data, s32,
+                                                     (float*)out->data, ix, c.numel);
+  return launch_check(name);
+}
+
+ttn_status ttn_bias_silu_residual_nc1hwc0_f16(const void* x, const void* bias,
+                                              const void* residual, void* y, int64_t n,
+                                              int64_t c1, int64_t hw, ttn_stream stream) {
+  const char* name = "ttn_bias_silu_residual_nc1hwc0_f16";
+  if (n < 0 || c1 < 0 || hw < 0) return fail(TTN_INVALID_ARG, "%s: negative size", name);
+  int64_t count = n * c1 * hw * 16;
+  if (!count) return TTN_OK;
+  if (!x || !bias || !residual || !y) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned16(x) || !aligned16(bias) || !aligned16(residual) || !aligned16(y))
+    return fail(TTN_INVALID_ARG, "%s: pointers must be 16-byte aligned", name);
+  int64_t nvec = count / 8;
+  unsigned grid = grid_for(nvec, kThreads);
+  bias_silu_residual<<<grid, kThreads, 0, (cudaStream_t)stream>>>(
+      (const uint4*)x, (const uint16_t*)bias, (const uint4*)residual, (uint4*)y, nvec, hw, c1);
+  return launch_check(name);
+}
+
+}  // extern "C"

@@ -1,0 +1,614 @@
+// YOLO26 NMS-free detection selection (reference: selection_flow.cpp:429-491).
+//
+// Total order (selection_flow.cpp:30-35, 54-57; selection_sort.h:85-89): a
+// score's key is 0 for NaN (or 0xffff with TTN_SELECT_NAN_LAST), 0x7fff for
+// +-0, the raw bits for negatives and 0x7fff - bits for positives; smaller
+// keys rank first and equal keys keep the lower source index.  That order is
+// torch.argsort(descending=True, stable=True) over fp16 scores.
+//
+// Pipeline per call (b images, a anchors, nc classes, k = min(max_det, a)):
+//   1. class_max_*   one pass over the scores: per anchor the first class with
+//                    the smallest key -> 32-bit record (score bits | class<<16).
+//   2. topk_block    one CTA per image: 16-bit radix select of the k-th key,
+//                    index-ordered collection of the k winners (keys below the
+//                    threshold plus the lowest-index ties), bitonic sort of the
+//                    (key<<32 | index) composites in shared memory.  k > 4096
+//                    takes a stable counting sort of every key instead.
+//   3. gather_pairs  (class-aware) the k x nc scores of the stage-1 anchors,
+//                    then topk_block again over the k*nc flat (rank*nc + class).
+//   4. pack          FP32 rows (box bits widened exactly, score, class) and the
+//                    optional trace outputs.
+// Scratch lives in the caller's workspace (ttn_select_workspace_size).
+#include "common.cuh"
+
+namespace ttn {
+namespace {
+
+constexpr int kTopkThreads = 1024;
+constexpr int kSmemSort = 4096;  // largest k sorted in shared memory
+constexpr uint32_t kInvalidKey = 0x10000u;
+
+struct SelectView {
+  const uint16_t* base;  // element [0,0,0]
+  int64_t sb, sa, sc;    // strides in elements
+  int64_t batch, anchors, classes;
+};
+
+__device__ __forceinline__ uint32_t score_key(uint16_t bits, bool nan_last) {
+  uint32_t magnitude = bits & 0x7fffu;
+  if (magnitude > 0x7c00u) return nan_last ? 0xffffu : 0u;
+  if (magnitude == 0) return 0x7fffu;
+  return (bits & 0x8000u) ? bits : (uint32_t)((~(bits ^ 0x8000u)) & 0xffffu);
+}
+
+__device__ __forceinline__ uint16_t score_bits(const SelectView& v, int64_t b, int64_t a, int64_t c,
+                                               bool sigmoid) {
+  uint16_t raw = v.base[b * v.sb + a * v.sa + (c + 4) * v.sc];
+  return sigmoid ? sigmoid_h(raw) : raw;
+}
+
+// ------------------------------------------------------------ 1. class max
+
+// Thread per anchor (coalesced when anchors are the unit-stride dim).
+__global__ void __launch_bounds__(256) class_max_thread(SelectView v, bool nan_last, bool sigmoid,
+                                                        uint32_t* records, int64_t rec_pitch,
+                                                        uint16_t* trace_max) {
+  const int64_t total = v.batch * v.anchors;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    int64_t b = t / v.anchors, a = t % v.anchors;
+    uint32_t best = kInvalidKey, best_bits = 0, best_cls = 0;
+    const uint16_t* p = v.base + b * v.sb + a * v.sa + 4 * v.sc;
+    for (int64_t c = 0; c < v.classes; ++c) {
+      uint16_t bits = p[c * v.sc];
+      if (sigmoid) bits = sigmoid_h(bits);
+      uint32_t key = score_key(bits, nan_last);
+      if (key < best) {
+        best = key;
+        best_bits = bits;
+        best_cls = (uint32_t)c;
+      }
+    }
+    records[b * rec_pitch + a] = best_bits | (best_cls << 16);
+    if (trace_max) trace_max[t] = (uint16_t)best_bits;
+  }
+}
+
+// Channel-planar scores (anchor stride 1, 16-byte aligned rows): 8 anchors per
+// thread with 128-bit loads, one class row at a time.
+__global__ void __launch_bounds__(256) class_max_planar8(SelectView v, bool nan_last, bool sigmoid,
+                                                         uint32_t* records, int64_t rec_pitch,
+                                                         uint16_t* trace_max) {
+  const int64_t groups = v.anchors / 8;
+  const int64_t total = v.batch * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    int64_t b = t / groups, a0 = (t % groups) * 8;
+    uint32_t best[8], bits8[8], cls8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      best[j] = kInvalidKey;
+      bits8[j] = 0;
+      cls8[j] = 0;
+    }
+    const uint16_t* p = v.base + b * v.sb + a0 + 4 * v.sc;
+    int64_t c = 0;
+    for (; c + 1 < v.classes; c += 2) {  // two rows in flight
+      uint4 q0 = *reinterpret_cast<const uint4*>(p + c * v.sc);
+      uint4 q1 = *reinterpret_cast<const uint4*>(p + (c + 1) * v.sc);
+      uint32_t w[2][4] = {{q0.x, q0.y, q0.z, q0.w}, {q1.x, q1.y, q1.z, q1.w}};
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint16_t bits = (uint16_t)((w[r][j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+          if (sigmoid) bits = sigmoid_h(bits);
+          uint32_t key = score_key(bits, nan_last);
+          if (key < best[j]) {
+            best[j] = key;
+            bits8[j] = bits;
+            cls8[j] = (uint32_t)(c + r);
+          }
+        }
+      }
+    }
+    if (c < v.classes) {
+      uint4 q0 = *reinterpret_cast<const uint4*>(p + c * v.sc);
+      uint32_t w[4] = {q0.x, q0.y, q0.z, q0.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint16_t bits = (uint16_t)((w[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+        if (sigmoid) bits = sigmoid_h(bits);
+        uint32_t key = score_key(bits, nan_last);
+        if (key < best[j]) {
+          best[j] = key;
+          bits8[j] = bits;
+          cls8[j] = (uint32_t)c;
+        }
+      }
+    }
+    uint32_t out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = bits8[j] | (cls8[j] << 16);
+    uint4* dst = reinterpret_cast<uint4*>(records + b * rec_pitch + a0);
+    dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+    dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+    if (trace_max) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) trace_max[b * v.anchors + a0 + j] = (uint16_t)bits8[j];
+    }
+  }
+}
+
+// Class-contiguous rows (class stride 1): one warp per anchor, lanes over
+// classes, (key, class) lexicographic warp reduction.
+__global__ void __launch_bounds__(256) class_max_warp(SelectView v, bool nan_last, bool sigmoid,
+                                                      uint32_t* records, int64_t rec_pitch,
+                                                      uint16_t* trace_max) {
+  const int lane = threadIdx.x & 31;
+  const int64_t total = v.batch * v.anchors;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < total; t += warps) {
+    int64_t b = t / v.anchors, a = t % v.anchors;
+    const uint16_t* p = v.base + b * v.sb + a * v.sa + 4 * v.sc;
+    uint32_t best = kInvalidKey, best_cls = 0xffffffffu, best_bits = 0;
+    for (int64_t c = lane; c < v.classes; c += 32) {
+      uint16_t bits = p[c * v.sc];
+      if (sigmoid) bits = sigmoid_h(bits);
+      uint32_t key = score_key(bits, nan_last);
+      if (key < best) {  // lanes walk classes in increasing order
+        best = key;
+        best_cls = (uint32_t)c;
+        best_bits = bits;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      uint32_t ok = __shfl_xor_sync(0xffffffffu, best, o);
+      uint32_t oc = __shfl_xor_sync(0xffffffffu, best_cls, o);
+      uint32_t ob = __shfl_xor_sync(0xffffffffu, best_bits, o);
+      if (ok < best || (ok == best && oc < best_cls)) {
+        best = ok;
+        best_cls = oc;
+        best_bits = ob;
+      }
+    }
+    if (lane == 0) {
+      if (best_cls == 0xffffffffu) best_cls = 0;
+      records[b * rec_pitch + a] = best_bits | (best_cls << 16);
+      if (trace_max) trace_max[t] = (uint16_t)best_bits;
+    }
+  }
+}
+
+// ------------------------------------------------------------- 2. top-k
+
+// Key source for topk_block: stage 1 reads 32-bit records, stage 2 16-bit bits.
+struct KeySource {
+  const uint32_t* records;  // stage 1 (low 16 bits are the score bits)
+  const uint16_t* bits;     // stage 2
+  int64_t pitch;            // elements between images
+  __device__ __forceinline__ uint16_t get(int64_t b, int64_t i) const {
+    return records ? (uint16_t)(records[b * pitch + i] & 0xffffu) : bits[b * pitch + i];
+  }
+};
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Block-wide exclusive prefix of a per-thread 0/1 flag over threads in order.
+// Returns this thread's prefix; *total receives the block total.  Uses
+// scratch[32] and synchronises.
+__device__ __forceinline__ int block_prefix(bool flag, int* scratch, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t mask = __ballot_sync(0xffffffffu, flag);
+  int in_warp = __popc(mask & lanemask_lt());
+  if (lane == 0) scratch[warp] = __popc(mask);
+  __syncthreads();
+  int warps = blockDim.x >> 5;
+  if (warp == 0) {
+    int v = lane < warps ? scratch[lane] : 0;
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
+    }
+    if (lane < warps) scratch[lane] = inc - v;  // exclusive
+    if (lane == 31) scratch[32] = inc;
+  }
+  __syncthreads();
+  int result = scratch[warp] + in_warp;
+  *total = scratch[32];
+  __syncthreads();
+  return result;
+}
+
+// Find the bucket holding the k-th smallest (1-based) of 256 counters: returns
+// the bucket and the count of elements in lower buckets.  Warp 0 only; result
+// through shared memory.
+__device__ __forceinline__ void find_bucket(const uint32_t* hist, uint32_t k, uint32_t base,
+                                            uint32_t* out_bucket, uint32_t* out_below) {
+  const int lane = threadIdx.x & 31;
+  uint32_t local[8], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    local[j] = hist[lane * 8 + j];
+    sum += local[j];
+  }
+  uint32_t inc = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t u = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  uint32_t before = base + inc - sum;
+  // the lane whose range [before, before+sum) contains the k-th element
+  bool mine = before < k && k <= before + sum;
+  if (mine) {
+    uint32_t run = before;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (run < k && k <= run + local[j]) {
+        *out_bucket = (uint32_t)(lane * 8 + j);
+        *out_below = run;
+      }
+      run += local[j];
+    }
+  }
+}
+
+// Sort `count` composites (<= kSmemSort) held in shared memory ascending,
+// padding to a power of two with UINT64_MAX.
+__device__ void bitonic_sort(unsigned long long* data, int count) {
+  int size = 32;
+  while (size < count) size <<= 1;
+  for (int i = count + threadIdx.x; i < size; i += blockDim.x) data[i] = ~0ull;
+  __syncthreads();
+  for (int span = 2; span <= size; span <<= 1) {
+    for (int stride = span >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < size; i += blockDim.x) {
+        int j = i ^ stride;
+        if (j > i) {
+          unsigned long long a = data[i], b = data[j];
+          bool ascending = (i & span) == 0;
+          if ((a > b) == ascending) {
+            data[i] = b;
+            data[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+struct TopkArgs {
+  KeySource src;
+  int64_t n;        // keys per image
+  int64_t k;        // winners per image
+  bool nan_last;
+  unsigned long long* sorted;  // [batch][sorted_pitch] composites (key<<32 | index)
+  int64_t sorted_pitch;
+  uint32_t* hist64k;           // [batch][65536] for the large-k path
+  unsigned long long* scratch; // [batch][n] for the large-k path
+};
+
+__global__ void __launch_bounds__(kTopkThreads) topk_block(TopkArgs args) {
+  __shared__ uint32_t hist[256];
+  __shared__ int scan[33];
+  __shared__ uint32_t sel_bucket, sel_below;
+  __shared__ int collected;
+  extern __shared__ unsigned long long cand[];
+  const int64_t b = blockIdx.x;
+  const int64_t n = args.n, k = args.k;
+  unsigned long long* out = args.sorted + b * args.sorted_pitch;
+  if (k <= 0) return;
+
+  if (k > kSmemSort) {
+    // Stable counting sort of all n keys (index order preserved within a key).
+    uint32_t* h = args.hist64k + b * 65536;
+    for (int i = threadIdx.x; i < 65536; i += blockDim.x) h[i] = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+      atomicAdd(&h[score_key(args.src.get(b, i), args.nan_last)], 1u);
+    __syncthreads();
+    // exclusive scan of 65536 counters: 64 per thread
+    {
+      uint32_t local = 0;
+      const int per = 65536 / kTopkThreads;
+      for (int j = 0; j < per; ++j) local += h[threadIdx.x * per + j];
+      int dummy;
+      // block scan of sums via the prefix helper on 32-bit values
+      __shared__ uint32_t sums[kTopkThreads];
+      sums[threadIdx.x] = local;
+      __syncthreads();
+      for (int o = 1; o < kTopkThreads; o <<= 1) {
+        uint32_t add = threadIdx.x >= o ? sums[threadIdx.x - o] : 0u;
+        __syncthreads();
+        sums[threadIdx.x] += add;
+        __syncthreads();
+      }
+      uint32_t run = sums[threadIdx.x] - local;
+      for (int j = 0; j < per; ++j) {
+        uint32_t c = h[threadIdx.x * per + j];
+        h[threadIdx.x * per + j] = run;
+        run += c;
+      }
+      (void)dummy;
+    }
+    __syncthreads();
+    // ordered scatter by warp 0
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      for (int64_t base = 0; base < n; base += 32) {
+        int64_t i = base + lane;
+        bool valid = i < n;
+        uint32_t key = valid ? score_key(args.src.get(b, i), args.nan_last) : 0xffffffffu;
+        uint32_t peers = __match_any_sync(0xffffffffu, key);
+        int rank = __popc(peers & lanemask_lt());
+        int leader = __ffs(peers) - 1;
+        uint32_t start = 0;
+        if (lane == leader && valid) start = atomicAdd(&h[key], (uint32_t)__popc(peers));
+        start = __shfl_sync(0xffffffffu, start, leader);
+        if (valid) {
+          uint32_t pos = start + rank;
+          args.scratch[b * n + pos] = ((unsigned long long)key << 32) | (unsigned long long)i;
+        }
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) out[i] = args.scratch[b * n + i];
+    return;
+  }
+
+  // --- radix select of the k-th smallest 16-bit key
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+    atomicAdd(&hist[score_key(args.src.get(b, i), args.nan_last) >> 8], 1u);
+  __syncthreads();
+  if (threadIdx.x < 32) find_bucket(hist, (uint32_t)k, 0u, &sel_bucket, &sel_below);
+  __syncthreads();
+  const uint32_t high = sel_bucket, below_high = sel_below;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    uint32_t key = score_key(args.src.get(b, i), args.nan_last);
+    if ((key >> 8) == high) atomicAdd(&hist[key & 255u], 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) find_bucket(hist, (uint32_t)k, below_high, &sel_bucket, &sel_below);
+  __syncthreads();
+  const uint32_t threshold = (high << 8) | sel_bucket;
+  const int64_t need = k - (int64_t)sel_below;  // ties at the threshold to take, lowest index first
+
+  // --- index-ordered collection
+  if (threadIdx.x == 0) collected = 0;
+  __syncthreads();
+  int64_t eq_seen = 0;
+  for (int64_t base = 0; base < n; base += blockDim.x) {
+    int64_t i = base + threadIdx.x;
+    uint32_t key = i < n ? score_key(args.src.get(b, i), args.nan_last) : 0xffffffffu;
+    bool eq = key == threshold;
+    int eq_total;
+    int eq_rank = block_prefix(eq, scan, &eq_total);
+    bool take = key < threshold || (eq && eq_seen + eq_rank < need);
+    if (take) {
+      int pos = atomicAdd(&collected, 1);
+      cand[pos] = ((unsigned long long)key << 32) | (unsigned long long)i;
+    }
+    eq_seen += eq_total;
+  }
+  __syncthreads();
+  bitonic_sort(cand, (int)k);
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) out[i] = cand[i];
+}
+
+// --------------------------------------------------------- 3. pair gather
+
+// pair_bits[b][r*nc + c] = score of class c at the stage-1 anchor of rank r.
+__global__ void __launch_bounds__(256) gather_pairs(SelectView v, bool sigmoid,
+                                                    const unsigned long long* stage1,
+                                                    int64_t s1_pitch, int64_t k, uint16_t* pair_bits,
+                                                    int64_t pair_pitch, uint16_t* trace_gathered) {
+  const int64_t total = v.batch * k * v.classes;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    int64_t b = t / (k * v.classes), flat = t % (k * v.classes);
+    int64_t r = flat / v.classes, c = flat % v.classes;
+    int64_t anchor = (int64_t)(stage1[b * s1_pitch + r] & 0xffffffffull);
+    uint16_t bits = score_bits(v, b, anchor, c, sigmoid);
+    pair_bits[b * pair_pitch + flat] = bits;
+    if (trace_gathered) trace_gathered[t] = bits;
+  }
+}
+
+// ------------------------------------------------------------------ 4. pack
+
+struct PackArgs {
+  SelectView v;
+  bool agnostic;
+  int64_t k;
+  const uint32_t* records;
+  int64_t rec_pitch;
+  const unsigned long long* stage1;
+  int64_t s1_pitch;
+  const unsigned long long* stage2;
+  int64_t s2_pitch;
+  const uint16_t* pair_bits;
+  int64_t pair_pitch;
+  float* out;
+  ttn_select_trace trace;
+};
+
+__global__ void __launch_bounds__(256) pack_rows(PackArgs p) {
+  const int64_t total = p.v.batch * p.k;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    int64_t b = t / p.k, j = t % p.k;
+    int64_t anchor, cls, flat = 0;
+    uint32_t bits;
+    int64_t first = (int64_t)(p.stage1[b * p.s1_pitch + j] & 0xffffffffull);
+    if (p.agnostic) {
+      anchor = first;
+      uint32_t rec = p.records[b * p.rec_pitch + anchor];
+      bits = rec & 0xffffu;
+      cls = rec >> 16;
+    } else {
+      flat = (int64_t)(p.stage2[b * p.s2_pitch + j] & 0xffffffffull);
+      int64_t rank = flat / p.v.classes;
+      cls = flat % p.v.classes;
+      anchor = (int64_t)(p.stage1[b * p.s1_pitch + rank] & 0xffffffffull);
+      bits = p.pair_bits[b * p.pair_pitch + flat];
+    }
+    const uint16_t* box = p.v.base + b * p.v.sb + anchor * p.v.sa;
+    uint32_t* row = reinterpret_cast<uint32_t*>(p.out + t * 6);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) row[c] = float_bits_of_half(box[c * p.v.sc]);
+    row[4] = float_bits_of_half(bits);
+    p.out[t * 6 + 5] = (float)cls;
+    if (p.trace.stage1_indices) p.trace.stage1_indices[t] = first;
+    if (p.trace.top_values) p.trace.top_values[t] = (uint16_t)bits;
+    if (p.trace.stage2_indices && !p.agnostic) p.trace.stage2_indices[t] = flat;
+    if (p.trace.anchor_indices) p.trace.anchor_indices[t] = anchor;
+    if (p.trace.labels) p.trace.labels[t] = cls;
+  }
+}
+
+// --------------------------------------------------------------- host side
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct Workspace {
+  size_t records, stage1, pairs, stage2, hist, scratch, total;
+};
+
+Workspace layout(int64_t batch, int64_t anchors, int64_t classes, int64_t k, bool agnostic) {
+  Workspace w;
+  int64_t kp = k < 1 ? 1 : k;
+  int64_t pairs = agnostic ? 0 : kp * classes;
+  w.records = 0;
+  size_t off = align256((size_t)batch * anchors * 4);
+  w.stage1 = off;
+  off += align256((size_t)batch * kp * 8);
+  w.pairs = off;
+  off += align256((size_t)batch * pairs * 2);
+  w.stage2 = off;
+  off += align256((size_t)batch * kp * 8);
+  w.hist = off;
+  bool large = k > kSmemSort;
+  off += large ? align256((size_t)batch * 65536 * 4) : 0;
+  w.scratch = off;
+  int64_t widest = anchors > pairs ? anchors : pairs;
+  off += large ? align256((size_t)batch * widest * 8) : 0;
+  w.total = off;
+  return w;
+}
+
+}  // namespace
+}  // namespace ttn
+
+using namespace ttn;
+
+extern "C" {
+
+size_t ttn_select_workspace_size(int64_t batch, int64_t anchors, int64_t classes, int64_t max_det,
+                                 uint32_t flags) {
+  if (batch <= 0 || anchors <= 0 || classes <= 0) return 256;
+  int64_t k = max_det < anchors ? max_det : anchors;
+  if (k < 0) k = 0;
+  return layout(batch, anchors, classes, k, (flags & TTN_SELECT_AGNOSTIC) != 0).total;
+}
+
+ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t flags,
+                          void* workspace, size_t workspace_bytes, float* out,
+                          const ttn_select_trace* trace, ttn_stream stream) {
+  const char* name = "ttn_select_f16";
+  TTN_TRY(validate(decoded, name));
+  if (decoded->dtype != TTN_F16 || decoded->ndim != 3)
+    return fail(TTN_INVALID_ARG, "%s: detection_select expects FP16 [B,A,4+nc]", name);
+  if (decoded->sizes[2] <= 4 || max_det < 0)
+    return fail(TTN_INVALID_ARG, "%s: detection_select requires nc > 0 and max_det >= 0", name);
+  if (flags & ~(uint32_t)(TTN_SELECT_AGNOSTIC | TTN_SELECT_NAN_LAST | TTN_SELECT_SIGMOID))
+    return fail(TTN_INVALID_ARG, "%s: unknown flag bits", name);
+  SelectView v;
+  v.base = (const uint16_t*)decoded->data;
+  v.sb = decoded->strides[0];
+  v.sa = decoded->strides[1];
+  v.sc = decoded->strides[2];
+  v.batch = decoded->sizes[0];
+  v.anchors = decoded->sizes[1];
+  v.classes = decoded->sizes[2] - 4;
+  if (v.classes > 65535) return fail(TTN_UNSUPPORTED, "%s: more than 65535 classes", name);
+  if (v.anchors > 0x7fffffffLL) return fail(TTN_UNSUPPORTED, "%s: too many anchors", name);
+  const bool agnostic = flags & TTN_SELECT_AGNOSTIC, nan_last = flags & TTN_SELECT_NAN_LAST;
+  const bool sigmoid = flags & TTN_SELECT_SIGMOID;
+  const int64_t k = max_det < v.anchors ? max_det : v.anchors;
+  if (!v.batch || !v.anchors) return TTN_OK;
+  if (!agnostic && k * v.classes > 0x7fffffffLL)
+    return fail(TTN_UNSUPPORTED, "%s: k*nc exceeds 2^31", name);
+  Workspace w = layout(v.batch, v.anchors, v.classes, k, agnostic);
+  if (!workspace || workspace_bytes < w.total || ((uintptr_t)workspace & 255u))
+    return fail(TTN_INVALID_ARG, "%s: workspace needs %zu bytes, 256-byte aligned", name, w.total);
+  if (k && !out) return fail(TTN_INVALID_ARG, "%s: null output", name);
+  ttn_select_trace tr = trace ? *trace : ttn_select_trace{};
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  uint32_t* records = (uint32_t*)(ws + w.records);
+  unsigned long long* stage1 = (unsigned long long*)(ws + w.stage1);
+  uint16_t* pairs = (uint16_t*)(ws + w.pairs);
+  unsigned long long* stage2 = (unsigned long long*)(ws + w.stage2);
+  uint32_t* hist = (uint32_t*)(ws + w.hist);
+  unsigned long long* scratch = (unsigned long long*)(ws + w.scratch);
+  const int64_t kp = k < 1 ? 1 : k;
+
+  // 1. class max
+  bool planar = v.sa == 1 && v.anchors % 8 == 0 && v.sb % 8 == 0 && v.sc % 8 == 0 &&
+                ((uintptr_t)(v.base + 4 * v.sc) & 15u) == 0;
+  if (planar) {
+    int64_t work = v.batch * (v.anchors / 8);
+    class_max_planar8<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, sigmoid, records,
+                                                             v.anchors, tr.class_max);
+  } else if (v.sc == 1 && v.classes >= 16) {
+    int64_t work = v.batch * v.anchors * 32;
+    class_max_warp<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, sigmoid, records, v.anchors,
+                                                          tr.class_max);
+  } else {
+    int64_t work = v.batch * v.anchors;
+    class_max_thread<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, sigmoid, records,
+                                                            v.anchors, tr.class_max);
+  }
+  TTN_TRY(launch_check("ttn_select_f16 class_max"));
+  if (!k) return TTN_OK;
+
+  const size_t sort_smem = (size_t)(k > kSmemSort ? 32 : 1 << (64 - __builtin_clzll((unsigned long long)(k > 32 ? k - 1 : 31)))) * 8;
+  TTN_TRY(ensure_dynamic_smem((const void*)topk_block, (int)sort_smem));
+  // 2. stage-1 top-k over anchors
+  TopkArgs t1{KeySource{records, nullptr, v.anchors}, v.anchors, k, nan_last, stage1, kp, hist, scratch};
+  topk_block<<<(unsigned)v.batch, kTopkThreads, sort_smem, s>>>(t1);
+  TTN_TRY(launch_check("ttn_select_f16 topk anchors"));
+
+  // 3. class-aware: pairs and stage-2 top-k
+  if (!agnostic) {
+    int64_t work = v.batch * k * v.classes;
+    gather_pairs<<<grid_for(work, 256, 8), 256, 0, s>>>(v, sigmoid, stage1, kp, k, pairs,
+                                                        kp * v.classes, tr.gathered_scores);
+    TTN_TRY(launch_check("ttn_select_f16 gather_pairs"));
+    TopkArgs t2{KeySource{nullptr, pairs, kp * v.classes}, k * v.classes, k, nan_last, stage2, kp,
+                hist, scratch};
+    topk_block<<<(unsigned)v.batch, kTopkThreads, sort_smem, s>>>(t2);
+    TTN_TRY(launch_check("ttn_select_f16 topk pairs"));
+  }
+
+  // 4. pack
+  PackArgs p{v, agnostic, k, records, v.anchors, stage1, kp, stage2, kp, pairs, kp * v.classes, out, tr};
+  pack_rows<<<grid_for(v.batch * k, 256, 8), 256, 0, s>>>(p);
+  return launch_check("ttn_select_f16 pack");
+}
+
+}  // extern "C"

@@ -1,0 +1,477 @@
+// Softmax over any dim of a strided view (attention rows, DFL bins) and the
+// fused Detect decode (DFL softmax + expectation + anchor decode + sigmoid).
+//
+// Softmax follows CPU eager's three IEEE passes: m = max (NaN-propagating),
+// s = sum exp(x - m), y = exp(x - m) * (1/s), all in FP32 with one rounding of
+// y.  So rows holding NaN, +inf or only -inf become NaN exactly as on CPU.
+// Rows with a unit-stride reduction run one warp per row (values held in
+// registers, 16-byte loads when rows are 8-aligned); reductions over a strided
+// dim run one thread per row with consecutive threads on the unit-stride dim,
+// which keeps every pass coalesced.
+#include "common.cuh"
+
+namespace ttn {
+namespace {
+
+__device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b != b) ? b : a; }
+
+template <typename T>
+__device__ __forceinline__ float load_scaled(const T* p, int64_t off, float scale, bool scaled) {
+  if constexpr (sizeof(T) == 2) {
+    float v = __half2float(reinterpret_cast<const __half*>(p)[off]);
+    return scaled ? __half2float(__float2half_rn(__fmul_rn(v, scale))) : v;
+  } else {
+    float v = p[off];
+    return scaled ? __fmul_rn(v, scale) : v;
+  }
+}
+
+template <typename U>
+__device__ __forceinline__ void store_out(U* p, int64_t off, float v) {
+  if constexpr (sizeof(U) == 2) reinterpret_cast<__half*>(p)[off] = __float2half_rn(v);
+  else p[off] = v;
+}
+
+struct RowSpace {  // non-reduced dims (innermost first) with x and y strides
+  int ndim;
+  int64_t size[7];
+  int64_t sx[7];
+  int64_t sy[7];
+};
+
+__device__ __forceinline__ void row_offsets(const RowSpace& rs, int64_t row, int64_t& ox,
+                                            int64_t& oy) {
+  ox = oy = 0;
+#pragma unroll
+  for (int d = 0; d < 7; ++d) {
+    if (d >= rs.ndim) break;
+    int64_t q = row / rs.size[d];
+    int64_t r = row - q * rs.size[d];
+    row = q;
+    ox += r * rs.sx[d];
+    oy += r * rs.sy[d];
+  }
+}
+
+// One warp per row, unit-stride reduction, up to 32*PER elements per row.
+template <typename T, typename U, int PER>
+__global__ void __launch_bounds__(256) softmax_warp_rows(const T* x, U* y, RowSpace rs, int64_t rows,
+                                                         int reduce, float scale, bool scaled) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = warp; row < rows; row += warps) {
+    int64_t ox, oy;
+    row_offsets(rs, row, ox, oy);
+    float v[PER];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      v[k] = e < reduce ? load_scaled(x, ox + e, scale, scaled) : -INFINITY;
+      if (e < reduce) m = nan_max(m, v[k]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = nan_max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      if (e < reduce) {
+        v[k] = expf(__fsub_rn(v[k], m));
+        s = __fadd_rn(s, v[k]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    const float inv = __fdiv_rn(1.0f, s);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      if (e < reduce) store_out(y, oy + e, __fmul_rn(v[k], inv));
+    }
+  }
+}
+
+// fp16 rows with reduce % 8 == 0 and 16-byte aligned rows: each lane owns whole
+// 8-element vectors (element index (k*32 + lane)*8 + j).
+template <int PER>
+__global__ void __launch_bounds__(256) softmax_warp_rows_h8(const uint16_t* x, uint16_t* y, RowSpace rs,
+                                                            int64_t rows, int reduce, float scale,
+                                                            bool scaled) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int nvec = reduce >> 3;
+  for (int64_t row = warp; row < rows; row += warps) {
+    int64_t ox, oy;
+    row_offsets(rs, row, ox, oy);
+    const uint4* xv = reinterpret_cast<const uint4*>(x + ox);
+    uint4* yv = reinterpret_cast<uint4*>(y + oy);
+    float v[PER][8];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      if (e < nvec) {
+        uint4 q = xv[e];
+        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __half22float2(*reinterpret_cast<__half2*>(&w[j]));
+          if (scaled) {
+            f.x = __half2float(__float2half_rn(__fmul_rn(f.x, scale)));
+            f.y = __half2float(__float2half_rn(__fmul_rn(f.y, scale)));
+          }
+          v[k][2 * j] = f.x;
+          v[k][2 * j + 1] = f.y;
+          m = nan_max(nan_max(m, f.x), f.y);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = nan_max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      if (e < nvec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[k][j] = expf(__fsub_rn(v[k][j], m));
+          s = __fadd_rn(s, v[k][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    const float inv = __fdiv_rn(1.0f, s);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      if (e < nvec) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __half2 h = __floats2half2_rn(__fmul_rn(v[k][2 * j], inv), __fmul_rn(v[k][2 * j + 1], inv));
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        yv[e] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+}
+
+// One block per row for long unit-stride rows: three passes through L2.
+template <typename T, typename U>
+__global__ void __launch_bounds__(512) softmax_block_rows(const T* x, U* y, RowSpace rs, int64_t rows,
+                                                          int64_t reduce, int64_t rsx, int64_t rsy,
+                                                          float scale, bool scaled) {
+  __shared__ float red[32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    int64_t ox, oy;
+    row_offsets(rs, row, ox, oy);
+    float m = -INFINITY;
+    for (int64_t e = threadIdx.x; e < reduce; e += blockDim.x)
+      m = nan_max(m, load_scaled(x, ox + e * rsx, scale, scaled));
+    for (int o = 16; o; o >>= 1) m = nan_max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -INFINITY;
+      for (int o = 16; o; o >>= 1) t = nan_max(t, __shfl_xor_sync(0xffffffffu, t, o));
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    m = red[0];
+    __syncthreads();
+    float s = 0.0f;
+    for (int64_t e = threadIdx.x; e < reduce; e += blockDim.x)
+      s = __fadd_rn(s, expf(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)));
+    for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+      for (int o = 16; o; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = __fdiv_rn(1.0f, red[0]);
+    __syncthreads();
+    for (int64_t e = threadIdx.x; e < reduce; e += blockDim.x)
+      store_out(y, oy + e * rsy,
+                __fmul_rn(expf(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)), inv));
+  }
+}
+
+// One thread per row for strided reductions (rows enumerated innermost-first,
+// so neighbouring threads touch neighbouring addresses when a unit stride exists).
+template <typename T, typename U>
+__global__ void __launch_bounds__(256) softmax_thread_rows(const T* x, U* y, RowSpace rs, int64_t rows,
+                                                           int64_t reduce, int64_t rsx, int64_t rsy,
+                                                           float scale, bool scaled) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; row < rows; row += stride) {
+    int64_t ox, oy;
+    row_offsets(rs, row, ox, oy);
+    float m = -INFINITY;
+    for (int64_t e = 0; e < reduce; ++e) m = nan_max(m, load_scaled(x, ox + e * rsx, scale, scaled));
+    float s = 0.0f;
+    for (int64_t e = 0; e < reduce; ++e)
+      s = __fadd_rn(s, expf(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)));
+    const float inv = __fdiv_rn(1.0f, s);
+    for (int64_t e = 0; e < reduce; ++e)
+      store_out(y, oy + e * rsy,
+                __fmul_rn(expf(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)), inv));
+  }
+}
+
+// ------------------------------------------------------------ DFL decode
+
+constexpr int kMaxLevels = 8;
+struct Levels {
+  int count;
+  int64_t start[kMaxLevels];
+  int64_t width[kMaxLevels];
+  float stride[kMaxLevels];
+};
+
+__device__ __forceinline__ float h16(float v) { return __half2float(__float2half_rn(v)); }
+
+// 16-bin softmax of one side (fp16 probabilities, as the separate softmax op
+// stores them) followed by the arange(16) expectation rounded to fp16.
+__device__ __forceinline__ float dfl_side(const float (&v)[16]) {
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m = nan_max(m, v[i]);
+  float e[16], s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    e[i] = expf(__fsub_rn(v[i], m));
+    s = __fadd_rn(s, e[i]);
+  }
+  const float inv = __fdiv_rn(1.0f, s);
+  float d = 0.0f;
+#pragma unroll
+  for (int i = 1; i < 16; ++i) d = __fmaf_rn(h16(__fmul_rn(e[i], inv)), (float)i, d);
+  return h16(d);
+}
+
+template <int APT>
+__global__ void __launch_bounds__(128) dfl_decode(const __half* box, int64_t box_bs, int64_t box_cs,
+                                                  const __half* cls, int64_t cls_bs, int64_t cls_cs,
+                                                  int64_t n, int64_t nc, int64_t anchors, Levels lv,
+                                                  bool xywh, __half* out) {
+  const int64_t groups = (anchors + APT - 1) / APT;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n * groups; t += stride) {
+    const int64_t b = t / groups;
+    const int64_t a0 = (t % groups) * APT;
+    const __half* bx = box + b * box_bs + a0;
+    __half* o = out + b * (4 + nc) * anchors + a0;
+    float dist[4][APT];
+#pragma unroll
+    for (int sd = 0; sd < 4; ++sd) {
+      float v[APT][16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const __half* p = bx + (sd * 16 + i) * box_cs;
+        if constexpr (APT == 2) {
+          float2 f = __half22float2(*reinterpret_cast<const __half2*>(p));
+          v[0][i] = f.x;
+          v[1][i] = f.y;
+        } else {
+          v[0][i] = __half2float(*p);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < APT; ++k) dist[sd][k] = dfl_side(v[k]);
+    }
+    float res[4][APT];
+#pragma unroll
+    for (int k = 0; k < APT; ++k) {
+      int64_t a = a0 + k;
+      if (a >= anchors) {
+        res[0][k] = res[1][k] = res[2][k] = res[3][k] = 0.0f;
+        continue;
+      }
+      int l = 0;
+      while (l + 1 < lv.count && a >= lv.start[l + 1]) ++l;
+      int64_t local = a - lv.start[l];
+      float ax = h16((float)(local % lv.width[l]) + 0.5f);
+      float ay = h16((float)(local / lv.width[l]) + 0.5f);
+      float st = lv.stride[l];
+      float lx = h16(__fsub_rn(ax, dist[0][k])), ly = h16(__fsub_rn(ay, dist[1][k]));
+      float ux = h16(__fadd_rn(ax, dist[2][k])), uy = h16(__fadd_rn(ay, dist[3][k]));
+      float q[4];
+      if (xywh) {
+        q[0] = h16(__fdiv_rn(h16(__fadd_rn(lx, ux)), 2.0f));
+        q[1] = h16(__fdiv_rn(h16(__fadd_rn(ly, uy)), 2.0f));
+        q[2] = h16(__fsub_rn(ux, lx));
+        q[3] = h16(__fsub_rn(uy, ly));
+      } else {
+        q[0] = lx; q[1] = ly; q[2] = ux; q[3] = uy;
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) res[c][k] = __fmul_rn(q[c], st);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if constexpr (APT == 2) {
+        *reinterpret_cast<__half2*>(o + c * anchors) = __floats2half2_rn(res[c][0], res[c][1]);
+      } else {
+        o[c * anchors] = __float2half_rn(res[c][0]);
+      }
+    }
+    const __half* cx = cls + b * cls_bs + a0;
+    for (int64_t c = 0; c < nc; ++c) {
+      if constexpr (APT == 2) {
+        uint32_t w = *reinterpret_cast<const uint32_t*>(cx + c * cls_cs);
+        uint32_t r = (uint32_t)sigmoid_h((uint16_t)(w & 0xffffu)) |
+                     ((uint32_t)sigmoid_h((uint16_t)(w >> 16)) << 16);
+        *reinterpret_cast<uint32_t*>(o + (4 + c) * anchors) = r;
+      } else {
+        reinterpret_cast<uint16_t*>(o)[(4 + c) * anchors] =
+            sigmoid_h(reinterpret_cast<const uint16_t*>(cx)[c * cls_cs]);
+      }
+    }
+  }
+}
+
+template <typename T, typename U>
+ttn_status launch_softmax(const ttn_tensor* x, const ttn_tensor* y, int dim, float scale,
+                          cudaStream_t s) {
+  const bool scaled = scale != 1.0f;
+  RowSpace rs;
+  rs.ndim = 0;
+  int64_t rows = 1;
+  // non-reduced dims, innermost first, merging where both views allow
+  for (int d = x->ndim - 1; d >= 0; --d) {
+    if (d == dim || x->sizes[d] == 1) continue;
+    rows *= x->sizes[d];
+    if (rs.ndim && rs.sx[rs.ndim - 1] * rs.size[rs.ndim - 1] == x->strides[d] &&
+        rs.sy[rs.ndim - 1] * rs.size[rs.ndim - 1] == y->strides[d]) {
+      rs.size[rs.ndim - 1] *= x->sizes[d];
+    } else {
+      if (rs.ndim == 7) return fail(TTN_UNSUPPORTED, "ttn_softmax: too many dims");
+      rs.size[rs.ndim] = x->sizes[d];
+      rs.sx[rs.ndim] = x->strides[d];
+      rs.sy[rs.ndim] = y->strides[d];
+      ++rs.ndim;
+    }
+  }
+  for (int d = 0; d < x->ndim; ++d)
+    if (x->sizes[d] == 0) return TTN_OK;
+  const int64_t reduce = x->ndim ? x->sizes[dim] : 1;
+  const int64_t rsx = x->ndim ? x->strides[dim] : 1, rsy = y->ndim ? y->strides[dim] : 1;
+  if (reduce == 0 || rows == 0) return TTN_OK;
+  const T* xp = (const T*)x->data;
+  U* yp = (U*)y->data;
+  if (rsx == 1 && rsy == 1 && reduce <= 1024) {
+    if constexpr (sizeof(T) == 2 && sizeof(U) == 2) {
+      bool vec = reduce % 8 == 0 && ((uintptr_t)xp & 15u) == 0 && ((uintptr_t)yp & 15u) == 0;
+      for (int d = 0; d < rs.ndim && vec; ++d) vec = rs.sx[d] % 8 == 0 && rs.sy[d] % 8 == 0;
+      if (vec) {
+        unsigned grid = grid_for(rows, 8, 16);
+        int nvec = (int)(reduce / 8);
+        if (nvec <= 32)
+          softmax_warp_rows_h8<1><<<grid, 256, 0, s>>>((const uint16_t*)xp, (uint16_t*)yp, rs, rows,
+                                                       (int)reduce, scale, scaled);
+        else if (nvec <= 64)
+          softmax_warp_rows_h8<2><<<grid, 256, 0, s>>>((const uint16_t*)xp, (uint16_t*)yp, rs, rows,
+                                                       (int)reduce, scale, scaled);
+        else
+          softmax_warp_rows_h8<4><<<grid, 256, 0, s>>>((const uint16_t*)xp, (uint16_t*)yp, rs, rows,
+                                                       (int)reduce, scale, scaled);
+        return launch_check("ttn_softmax");
+      }
+    }
+    unsigned grid = grid_for(rows, 8, 16);
+    if (reduce <= 128)
+      softmax_warp_rows<T, U, 4><<<grid, 256, 0, s>>>(xp, yp, rs, rows, (int)reduce, scale, scaled);
+    else if (reduce <= 256)
+      softmax_warp_rows<T, U, 8><<<grid, 256, 0, s>>>(xp, yp, rs, rows, (int)reduce, scale, scaled);
+    else if (reduce <= 512)
+      softmax_warp_rows<T, U, 16><<<grid, 256, 0, s>>>(xp, yp, rs, rows, (int)reduce, scale, scaled);
+    else
+      softmax_warp_rows<T, U, 32><<<grid, 256, 0, s>>>(xp, yp, rs, rows, (int)reduce, scale, scaled);
+    return launch_check("ttn_softmax");
+  }
+  if (rsx == 1 && rsy == 1) {
+    unsigned grid = grid_for(rows, 1, 4);
+    softmax_block_rows<T, U><<<grid, 512, 0, s>>>(xp, yp, rs, rows, reduce, rsx, rsy, scale, scaled);
+    return launch_check("ttn_softmax");
+  }
+  unsigned grid = grid_for(rows, 256);
+  softmax_thread_rows<T, U><<<grid, 256, 0, s>>>(xp, yp, rs, rows, reduce, rsx, rsy, scale, scaled);
+  return launch_check("ttn_softmax");
+}
+
+}  // namespace
+}  // namespace ttn
+
+using namespace ttn;
+
+extern "C" {
+
+ttn_status ttn_softmax(const ttn_tensor* x, int32_t dim, float scale, const ttn_tensor* y,
+                       ttn_stream stream) {
+  const char* name = "ttn_softmax";
+  TTN_TRY(validate(x, name));
+  TTN_TRY(validate(y, name));
+  if (!same_sizes(x, y)) return fail(TTN_INVALID_ARG, "%s: x and y sizes differ", name);
+  if (x->ndim == 0 ? (dim != 0 && dim != -1) : (dim < 0 || dim >= x->ndim))
+    return fail(TTN_INVALID_ARG, "%s: dim %d out of range", name, dim);
+  if (x->ndim == 0) dim = 0;
+  if (x->dtype == TTN_F32 && y->dtype == TTN_F16)
+    return fail(TTN_INVALID_ARG, "%s: float32 input cannot produce float16 output", name);
+  if (!(scale == scale)) return fail(TTN_INVALID_ARG, "%s: scale is NaN", name);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (x->dtype == TTN_F16 && y->dtype == TTN_F16) return launch_softmax<uint16_t, uint16_t>(x, y, dim, scale, s);
+  if (x->dtype == TTN_F16) return launch_softmax<uint16_t, float>(x, y, dim, scale, s);
+  return launch_softmax<float, float>(x, y, dim, scale, s);
+}
+
+ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs, const void* cls,
+                              int64_t cls_bs, int64_t cls_cs, int64_t n, int64_t nc,
+                              int32_t levels, const int64_t* heights, const int64_t* widths,
+                              const float* strides, int32_t xywh, void* out, ttn_stream stream) {
+  const char* name = "ttn_dfl_decode_f16";
+  if (n < 0 || nc < 0) return fail(TTN_INVALID_ARG, "%s: negative size", name);
+  if (levels < 1 || levels > kMaxLevels || !heights || !widths || !strides)
+    return fail(TTN_INVALID_ARG, "%s: 1..%d levels with heights/widths/strides", name, kMaxLevels);
+  Levels lv;
+  lv.count = levels;
+  int64_t anchors = 0;
+  for (int l = 0; l < levels; ++l) {
+    if (heights[l] <= 0 || widths[l] <= 0 || !(strides[l] > 0.0f))
+      return fail(TTN_INVALID_ARG, "%s: level %d has a non-positive size or stride", name, l);
+    if (heights[l] > 1024 || widths[l] > 1024)
+      return fail(TTN_UNSUPPORTED, "%s: grid side > 1024 is not exact in fp16 anchors", name);
+    lv.start[l] = anchors;
+    lv.width[l] = widths[l];
+    lv.stride[l] = strides[l];
+    anchors += heights[l] * widths[l];
+  }
+  if (!n || !anchors) return TTN_OK;
+  if (!box || !out || (nc && !cls)) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  bool pair = anchors % 2 == 0 && ((uintptr_t)box & 3u) == 0 && ((uintptr_t)out & 3u) == 0 &&
+              box_bs % 2 == 0 && box_cs % 2 == 0 &&
+              (!nc || (((uintptr_t)cls & 3u) == 0 && cls_bs % 2 == 0 && cls_cs % 2 == 0));
+  cudaStream_t s = (cudaStream_t)stream;
+  if (pair) {
+    int64_t work = n * (anchors / 2);
+    dfl_decode<2><<<grid_for(work, 128, 16), 128, 0, s>>>(
+        (const __half*)box, box_bs, box_cs, (const __half*)cls, cls_bs, cls_cs, n, nc, anchors, lv,
+        xywh != 0, (__half*)out);
+  } else {
+    int64_t work = n * anchors;
+    dfl_decode<1><<<grid_for(work, 128, 16), 128, 0, s>>>(
+        (const __half*)box, box_bs, box_cs, (const __half*)cls, cls_bs, cls_cs, n, nc, anchors, lv,
+        xywh != 0, (__half*)out);
+  }
+  return launch_check(name);
+}
+
+}  // extern "C"

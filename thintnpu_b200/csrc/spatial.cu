@@ -1,0 +1,429 @@
+// Spatial/layout ops over fp16 feature maps: NC1HWC0 <-> NCHW transposes,
+// nearest-2x upsample, odd-kernel stride-1 max-pool and the fused SPPF tail.
+//
+// Layout conversions stage a 64-pixel x 16-channel tile in shared memory so
+// both the 32-byte pixel vectors of NC1HWC0 and the 128-byte channel rows of
+// NCHW move as 16-byte accesses.  Max-pool stages a band of rows (plus the
+// halo) in shared memory and runs the separable window horizontally, then
+// vertically, which reproduces CPU F.max_pool2d's row-major scan exactly: the
+// first maximum wins among equal values (so -0 vs +0 keeps the earlier one)
+// and the last NaN in scan order wins, quieted as CPU's fp32 round trip does.
+#include "common.cuh"
+
+namespace ttn {
+namespace {
+
+constexpr int kPix = 64;  // pixels per layout tile
+
+// x: [n, c1, hw, 16] -> y[b*ybs + c*ycs + p] for c < channels.
+__global__ void __launch_bounds__(128) blocked_to_nchw(const uint16_t* x, int64_t n, int64_t c1,
+                                                       int64_t hw, int64_t channels, uint16_t* y,
+                                                       int64_t ybs, int64_t ycs, bool vector_out) {
+  __shared__ __align__(16) uint16_t tile[16][kPix + 8];
+  const int64_t tiles = (hw + kPix - 1) / kPix;
+  for (int64_t job = blockIdx.x; job < n * c1 * tiles; job += gridDim.x) {
+    int64_t plane = job / tiles;  // b*c1 + cb
+    int64_t p0 = (job % tiles) * kPix;
+    int64_t b = plane / c1, cb = plane % c1;
+    int count = (int)(hw - p0 < kPix ? hw - p0 : kPix);
+    const uint16_t* src = x + (plane * hw + p0) * 16;
+    // load: thread t reads pixel t/2, channels (t&1)*8 .. +8
+    for (int v = threadIdx.x; v < count * 2; v += blockDim.x) {
+      uint4 q = reinterpret_cast<const uint4*>(src)[v];
+      int p = v >> 1, c = (v & 1) * 8;
+      uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        tile[c + 2 * k][p] = (uint16_t)(w[k] & 0xffffu);
+        tile[c + 2 * k + 1][p] = (uint16_t)(w[k] >> 16);
+      }
+    }
+    __syncthreads();
+    int valid = (int)(channels - cb * 16 < 16 ? channels - cb * 16 : 16);
+    if (vector_out && count == kPix) {
+      // 16 channels x 8 vectors of 8 pixels
+      int c = threadIdx.x >> 3, v = threadIdx.x & 7;
+      if (c < valid) {
+        uint16_t* dst = y + b * ybs + (cb * 16 + c) * ycs + p0 + v * 8;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&tile[c][v * 8]);
+      }
+    } else {
+      for (int e = threadIdx.x; e < valid * count; e += blockDim.x) {
+        int c = e / count, p = e % count;
+        y[b * ybs + (cb * 16 + c) * ycs + p0 + p] = tile[c][p];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// x: NCHW [n, channels, hw] -> y: [n, ceil(channels/16), hw, 16], zero-padded.
+__global__ void __launch_bounds__(128) nchw_to_blocked(const uint16_t* x, int64_t n,
+                                                       int64_t channels, int64_t hw, uint16_t* y,
+                                                       bool vector_in) {
+  __shared__ __align__(16) uint16_t tile[16][kPix + 8];
+  const int64_t c1 = (channels + 15) / 16;
+  const int64_t tiles = (hw + kPix - 1) / kPix;
+  for (int64_t job = blockIdx.x; job < n * c1 * tiles; job += gridDim.x) {
+    int64_t plane = job / tiles;
+    int64_t p0 = (job % tiles) * kPix;
+    int64_t b = plane / c1, cb = plane % c1;
+    int count = (int)(hw - p0 < kPix ? hw - p0 : kPix);
+    int valid = (int)(channels - cb * 16 < 16 ? channels - cb * 16 : 16);
+    if (vector_in && count == kPix) {
+      int c = threadIdx.x >> 3, v = threadIdx.x & 7;
+      uint4 q = make_uint4(0, 0, 0, 0);
+      if (c < valid)
+        q = *reinterpret_cast<const uint4*>(x + (b * channels + cb * 16 + c) * hw + p0 + v * 8);
+      *reinterpret_cast<uint4*>(&tile[c][v * 8]) = q;
+    } else {
+      for (int e = threadIdx.x; e < 16 * count; e += blockDim.x) {
+        int c = e / count, p = e % count;
+        tile[c][p] = c < valid ? x[(b * channels + cb * 16 + c) * hw + p0 + p] : (uint16_t)0;
+      }
+    }
+    __syncthreads();
+    uint16_t* dst = y + (plane * hw + p0) * 16;
+    for (int v = threadIdx.x; v < count * 2; v += blockDim.x) {
+      int p = v >> 1, c = (v & 1) * 8;
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        w[k] = (uint32_t)tile[c + 2 * k][p] | ((uint32_t)tile[c + 2 * k + 1][p] << 16);
+      reinterpret_cast<uint4*>(dst)[v] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------- upsample
+
+// NC1HWC0 (and any layout whose innermost group is 16 bytes wide per half-pixel):
+// each input 16-byte vector is written to the 4 output pixels it covers.
+__global__ void __launch_bounds__(256) upsample_blocked(const uint4* x, uint4* y, int64_t planes,
+                                                        int64_t h, int64_t w) {
+  const int64_t nvec = planes * h * w * 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    uint4 q = x[v];
+    int64_t p = v >> 1;
+    int j = (int)(v & 1);
+    int64_t col = p % w, rest = p / w;
+    int64_t row = rest % h, plane = rest / h;
+    int64_t base = ((plane * 2 * h + 2 * row) * 2 * w + 2 * col) * 2 + j;
+    y[base] = q;
+    y[base + 2] = q;
+    y[base + 4 * w] = q;
+    y[base + 4 * w + 2] = q;
+  }
+}
+
+// NCHW with w % 4 == 0: read 4 input columns (8 bytes), write 8 output columns
+// (16 bytes) to both output rows.
+__global__ void __launch_bounds__(256) upsample_nchw_vec(const uint2* x, uint4* y, int64_t planes,
+                                                         int64_t h, int64_t w4) {
+  const int64_t nvec = planes * h * w4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    uint2 q = x[v];
+    int64_t col = v % w4, rest = v / w4;
+    uint32_t a = q.x & 0xffffu, b = q.x >> 16, c = q.y & 0xffffu, d = q.y >> 16;
+    uint4 o = make_uint4(a | (a << 16), b | (b << 16), c | (c << 16), d | (d << 16));
+    int64_t row0 = rest * 2;  // rest = plane*h + row
+    y[row0 * w4 * 2 + col] = o;
+    y[(row0 + 1) * w4 * 2 + col] = o;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) upsample_nchw_scalar(const T* x, T* y, int64_t planes,
+                                                            int64_t h, int64_t w) {
+  const int64_t total = planes * h * w * 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += stride) {
+    int64_t col = o % (2 * w), rest = o / (2 * w);
+    int64_t row = rest % (2 * h), plane = rest / (2 * h);
+    y[o] = x[(plane * h + row / 2) * w + col / 2];
+  }
+}
+
+// --------------------------------------------------------------- maxpool
+
+// CPU F.max_pool2d update rule on raw bits: take v when v > m or v is NaN.
+template <typename T>
+struct PoolBits;
+template <>
+struct PoolBits<uint16_t> {
+  static __device__ __forceinline__ float value(uint16_t b) { return __half2float(hfrom(b)); }
+  static __device__ __forceinline__ uint16_t neg_inf() { return 0xfc00u; }
+  static __device__ __forceinline__ uint16_t finish(uint16_t b) { return hnan_bits(b) ? hquiet(b) : b; }
+};
+template <>
+struct PoolBits<uint32_t> {
+  static __device__ __forceinline__ float value(uint32_t b) { return __uint_as_float(b); }
+  static __device__ __forceinline__ uint32_t neg_inf() { return 0xff800000u; }
+  static __device__ __forceinline__ uint32_t finish(uint32_t b) {
+    return ((b & 0x7fffffffu) > 0x7f800000u) ? (b | 0x00400000u) : b;
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ void pool_update(T& m, float& mv, T v) {
+  float vv = PoolBits<T>::value(v);
+  if (vv > mv || vv != vv) {
+    m = v;
+    mv = vv;
+  }
+}
+
+// One block = one plane band: output rows [r0, r0+rows) of plane `plane`,
+// `lanes` interleaved channels per pixel (16 for NC1HWC0, 1 for NCHW).
+// smem: in[(rows+2r) x w x lanes], hmax[(rows+2r) x w x lanes].
+template <typename T>
+__global__ void __launch_bounds__(256) maxpool_band(const T* x, T* y, int64_t planes, int h, int w,
+                                                    int lanes, int radius, int band) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* in = reinterpret_cast<T*>(smem_raw);
+  const int rows_max = band + 2 * radius;
+  T* hmax = in + (size_t)rows_max * w * lanes;
+  const int bands = (h + band - 1) / band;
+  const int row_elems = w * lanes;
+  for (int64_t job = blockIdx.x; job < planes * bands; job += gridDim.x) {
+    int64_t plane = job / bands;
+    int r0 = (int)(job % bands) * band;
+    int rows = h - r0 < band ? h - r0 : band;
+    int in0 = r0 - radius > 0 ? r0 - radius : 0;
+    int in1 = r0 + rows + radius < h ? r0 + rows + radius : h;
+    int in_rows = in1 - in0;
+    const T* src = x + (plane * h + in0) * (int64_t)row_elems;
+    for (int e = threadIdx.x; e < in_rows * row_elems; e += blockDim.x) in[e] = src[e];
+    __syncthreads();
+    // horizontal pass over every staged row
+    for (int e = threadIdx.x; e < in_rows * row_elems; e += blockDim.x) {
+      int lane = e % lanes, col = (e / lanes) % w, row = e / row_elems;
+      int c0 = col - radius > 0 ? col - radius : 0;
+      int c1 = col + radius < w - 1 ? col + radius : w - 1;
+      T m = PoolBits<T>::neg_inf();
+      float mv = -INFINITY;
+      const T* r = in + row * row_elems + lane;
+      for (int c = c0; c <= c1; ++c) pool_update(m, mv, r[c * lanes]);
+      hmax[e] = m;
+    }
+    __syncthreads();
+    // vertical pass for the band's output rows
+    T* dst = y + (plane * h + r0) * (int64_t)row_elems;
+    for (int e = threadIdx.x; e < rows * row_elems; e += blockDim.x) {
+      int row = r0 + e / row_elems, rest = e % row_elems;
+      int q0 = row - radius > 0 ? row - radius : 0;
+      int q1 = row + radius < h - 1 ? row + radius : h - 1;
+      T m = PoolBits<T>::neg_inf();
+      float mv = -INFINITY;
+      for (int q = q0; q <= q1; ++q) pool_update(m, mv, hmax[(q - in0) * row_elems + rest]);
+      dst[e] = PoolBits<T>::finish(m);
+    }
+    __syncthreads();
+  }
+}
+
+// SPPF: per (image, channel block) plane held whole in shared memory;
+// out planes: [x, p1, p2, p3] at channel blocks cb, c1+cb, 2c1+cb, 3c1+cb.
+__global__ void __launch_bounds__(256) sppf_planes(const uint16_t* x, uint16_t* out, int64_t n,
+                                                   int64_t c1, int h, int w, int radius) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int plane_elems = h * w * 16;
+  uint16_t* cur = reinterpret_cast<uint16_t*>(smem_raw);
+  uint16_t* tmp = cur + plane_elems;
+  const int row_elems = w * 16;
+  for (int64_t job = blockIdx.x; job < n * c1; job += gridDim.x) {
+    int64_t b = job / c1, cb = job % c1;
+    const uint4* src = reinterpret_cast<const uint4*>(x + job * plane_elems);
+    for (int v = threadIdx.x; v < plane_elems / 8; v += blockDim.x) {
+      uint4 q = src[v];
+      reinterpret_cast<uint4*>(cur)[v] = q;
+      reinterpret_cast<uint4*>(out + ((b * 4 * c1) + cb) * plane_elems)[v] = q;
+    }
+    __syncthreads();
+    for (int stage = 1; stage <= 3; ++stage) {
+      for (int e = threadIdx.x; e < plane_elems; e += blockDim.x) {
+        int lane = e & 15, col = (e >> 4) % w, row = e / row_elems;
+        int a = col - radius > 0 ? col - radius : 0;
+        int z = col + radius < w - 1 ? col + radius : w - 1;
+        uint16_t m = 0xfc00u;
+        float mv = -INFINITY;
+        const uint16_t* r = cur + row * row_elems + lane;
+        for (int c = a; c <= z; ++c) pool_update(m, mv, r[c * 16]);
+        tmp[e] = m;
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < plane_elems; e += blockDim.x) {
+        int row = e / row_elems, rest = e % row_elems;
+        int a = row - radius > 0 ? row - radius : 0;
+        int z = row + radius < h - 1 ? row + radius : h - 1;
+        uint16_t m = 0xfc00u;
+        float mv = -INFINITY;
+        for (int q = a; q <= z; ++q) pool_update(m, mv, tmp[q * row_elems + rest]);
+        cur[e] = PoolBits<uint16_t>::finish(m);
+      }
+      __syncthreads();
+      uint4* dst = reinterpret_cast<uint4*>(out + ((b * 4 * c1) + stage * c1 + cb) * plane_elems);
+      for (int v = threadIdx.x; v < plane_elems / 8; v += blockDim.x)
+        dst[v] = reinterpret_cast<const uint4*>(cur)[v];
+      __syncthreads();
+    }
+  }
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+
+}  // namespace
+}  // namespace ttn
+
+using namespace ttn;
+
+extern "C" {
+
+ttn_status ttn_nc1hwc0_to_nchw_f16(const void* x, int64_t n, int64_t c1, int64_t hw,
+                                   int64_t channels, void* y, int64_t y_batch_stride,
+                                   int64_t y_channel_stride, ttn_stream stream) {
+  const char* name = "ttn_nc1hwc0_to_nchw_f16";
+  if (n < 0 || c1 < 0 || hw < 0 || channels < 0 || channels > c1 * 16)
+    return fail(TTN_INVALID_ARG, "%s: bad sizes", name);
+  if (!n || !c1 || !hw || !channels) return TTN_OK;
+  if (!x || !y) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned16(x)) return fail(TTN_INVALID_ARG, "%s: x must be 16-byte aligned", name);
+  if (((uintptr_t)y & 1u)) return fail(TTN_INVALID_ARG, "%s: y not 2-byte aligned", name);
+  bool vec = aligned16(y) && y_batch_stride % 8 == 0 && y_channel_stride % 8 == 0;
+  int64_t jobs = n * c1 * ((hw + kPix - 1) / kPix);
+  unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * 16 ? jobs : (int64_t)sm_count() * 16);
+  blocked_to_nchw<<<grid, 128, 0, (cudaStream_t)stream>>>(
+      (const uint16_t*)x, n, c1, hw, (c1 * 16 < channels ? c1 * 16 : channels), (uint16_t*)y,
+      y_batch_stride, y_channel_stride, vec);
+  return launch_check(name);
+}
+
+ttn_status ttn_nchw_to_nc1hwc0_f16(const void* x, int64_t n, int64_t channels, int64_t hw,
+                                   void* y, ttn_stream stream) {
+  const char* name = "ttn_nchw_to_nc1hwc0_f16";
+  if (n < 0 || channels < 0 || hw < 0) return fail(TTN_INVALID_ARG, "%s: bad sizes", name);
+  if (!n || !channels || !hw) return TTN_OK;
+  if (!x || !y) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned16(y)) return fail(TTN_INVALID_ARG, "%s: y must be 16-byte aligned", name);
+  if (((uintptr_t)x & 1u)) return fail(TTN_INVALID_ARG, "%s: x not 2-byte aligned", name);
+  bool vec = aligned16(x) && hw % 8 == 0;
+  int64_t jobs = n * ((channels + 15) / 16) * ((hw + kPix - 1) / kPix);
+  unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * 16 ? jobs : (int64_t)sm_count() * 16);
+  nchw_to_blocked<<<grid, 128, 0, (cudaStream_t)stream>>>((const uint16_t*)x, n, channels, hw,
+                                                          (uint16_t*)y, vec);
+  return launch_check(name);
+}
+
+ttn_status ttn_upsample2x(int layout, int dtype, const void* x, void* y, int64_t n, int64_t c,
+                          int64_t h, int64_t w, ttn_stream stream) {
+  const char* name = "ttn_upsample2x";
+  if (layout != TTN_NCHW && layout != TTN_NC1HWC0) return fail(TTN_INVALID_ARG, "%s: layout", name);
+  if (dtype != TTN_F16 && dtype != TTN_F32) return fail(TTN_UNSUPPORTED, "%s: dtype", name);
+  if (n < 0 || c < 0 || h < 0 || w < 0) return fail(TTN_INVALID_ARG, "%s: negative size", name);
+  if (!n || !c || !h || !w) return TTN_OK;
+  if (!x || !y) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (layout == TTN_NC1HWC0) {
+    if (dtype != TTN_F16) return fail(TTN_UNSUPPORTED, "%s: NC1HWC0 supports float16", name);
+    if (!aligned16(x) || !aligned16(y)) return fail(TTN_INVALID_ARG, "%s: 16-byte alignment", name);
+    int64_t nvec = n * c * h * w * 2;
+    upsample_blocked<<<grid_for(nvec, 256), 256, 0, s>>>((const uint4*)x, (uint4*)y, n * c, h, w);
+    return launch_check(name);
+  }
+  if (dtype == TTN_F16 && w % 4 == 0 && aligned16(y) && ((uintptr_t)x & 7u) == 0) {
+    int64_t nvec = n * c * h * (w / 4);
+    upsample_nchw_vec<<<grid_for(nvec, 256), 256, 0, s>>>((const uint2*)x, (uint4*)y, n * c, h,
+                                                          w / 4);
+  } else if (dtype == TTN_F16) {
+    upsample_nchw_scalar<uint16_t><<<grid_for(n * c * h * w * 4, 256), 256, 0, s>>>(
+        (const uint16_t*)x, (uint16_t*)y, n * c, h, w);
+  } else {
+    upsample_nchw_scalar<uint32_t><<<grid_for(n * c * h * w * 4, 256), 256, 0, s>>>(
+        (const uint32_t*)x, (uint32_t*)y, n * c, h, w);
+  }
+  return launch_check(name);
+}
+
+ttn_status ttn_maxpool(int layout, int dtype, int32_t kernel, const void* x, void* y, int64_t n,
+                       int64_t c, int64_t h, int64_t w, ttn_stream stream) {
+  const char* name = "ttn_maxpool";
+  if (layout != TTN_NCHW && layout != TTN_NC1HWC0) return fail(TTN_INVALID_ARG, "%s: layout", name);
+  if (dtype != TTN_F16 && dtype != TTN_F32) return fail(TTN_UNSUPPORTED, "%s: dtype", name);
+  if (kernel < 1 || kernel % 2 == 0)
+    return fail(TTN_INVALID_ARG, "%s: maxpool kernel must be a positive odd integer", name);
+  if (n < 0 || c < 0 || h < 0 || w < 0) return fail(TTN_INVALID_ARG, "%s: negative size", name);
+  if (!n || !c || !h || !w) return TTN_OK;
+  if (!x || !y) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  if (h > (1 << 20) || w > (1 << 20)) return fail(TTN_UNSUPPORTED, "%s: plane too large", name);
+  if (layout == TTN_NC1HWC0 && dtype != TTN_F16)
+    return fail(TTN_UNSUPPORTED, "%s: NC1HWC0 supports float16", name);
+  const int lanes = layout == TTN_NC1HWC0 ? 16 : 1;
+  const int radius = kernel / 2;
+  const size_t es = dtype_size(dtype);
+  const size_t row_bytes = (size_t)w * lanes * es;
+  const int limit = max_dynamic_smem();
+  // band rows: as many as fit two staged copies of (band + 2r) rows
+  int64_t band = (int64_t)(limit / (2 * row_bytes)) - 2 * radius;
+  if (band < 1) return fail(TTN_UNSUPPORTED, "%s: a row band exceeds shared memory", name);
+  int64_t want = (int64_t)(8192 / (w * lanes)) + 1;  // ~8K outputs per block
+  if (band > want) band = want;
+  if (band > h) band = h;
+  size_t smem = 2 * (size_t)(band + 2 * radius) * row_bytes;
+  int64_t planes = layout == TTN_NC1HWC0 ? n * c : n * c;
+  int64_t jobs = planes * ((h + band - 1) / band);
+  unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * 8 ? jobs : (int64_t)sm_count() * 8);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (es == 2) {
+    TTN_TRY(ensure_dynamic_smem((const void*)maxpool_band<uint16_t>, (int)smem));
+    maxpool_band<uint16_t><<<grid, 256, smem, s>>>((const uint16_t*)x, (uint16_t*)y, planes, (int)h,
+                                                   (int)w, lanes, radius, (int)band);
+  } else {
+    TTN_TRY(ensure_dynamic_smem((const void*)maxpool_band<uint32_t>, (int)smem));
+    maxpool_band<uint32_t><<<grid, 256, smem, s>>>((const uint32_t*)x, (uint32_t*)y, planes, (int)h,
+                                                   (int)w, lanes, radius, (int)band);
+  }
+  return launch_check(name);
+}
+
+ttn_status ttn_sppf_f16(const void* x, void* out, int64_t n, int64_t c1, int64_t h, int64_t w,
+                        int32_t kernel, ttn_stream stream) {
+  const char* name = "ttn_sppf_f16";
+  if (kernel < 1 || kernel % 2 == 0)
+    return fail(TTN_INVALID_ARG, "%s: kernel must be a positive odd integer", name);
+  if (n < 0 || c1 < 0 || h < 0 || w < 0) return fail(TTN_INVALID_ARG, "%s: negative size", name);
+  if (!n || !c1 || !h || !w) return TTN_OK;
+  if (!x || !out) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned16(x) || !aligned16(out)) return fail(TTN_INVALID_ARG, "%s: 16-byte alignment", name);
+  size_t smem = 2 * (size_t)h * w * 16 * 2;
+  cudaStream_t s = (cudaStream_t)stream;
+  if ((int64_t)smem > max_dynamic_smem()) {
+    // Plane too large to hold twice: three chained pools through the output.
+    const int64_t plane = h * w * 16;
+    TTN_TRY(cuda_check(cudaMemcpy2DAsync(out, 4 * c1 * plane * 2, x, c1 * plane * 2, c1 * plane * 2,
+                                         n, cudaMemcpyDeviceToDevice, s),
+                       name));
+    for (int stage = 1; stage <= 3; ++stage) {
+      // pool each image's previous stage slice into the next slice
+      for (int64_t b = 0; b < n; ++b) {
+        const uint16_t* src = (const uint16_t*)out + (b * 4 * c1 + (stage - 1) * c1) * plane;
+        uint16_t* dst = (uint16_t*)out + (b * 4 * c1 + stage * c1) * plane;
+        TTN_TRY(ttn_maxpool(TTN_NC1HWC0, TTN_F16, kernel, src, dst, 1, c1, h, w, stream));
+      }
+    }
+    return TTN_OK;
+  }
+  TTN_TRY(ensure_dynamic_smem((const void*)sppf_planes, (int)smem));
+  int64_t jobs = n * c1;
+  int per_sm = (int)(200 * 1024 / (smem ? smem : 1));
+  if (per_sm < 1) per_sm = 1;
+  unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * per_sm ? jobs : (int64_t)sm_count() * per_sm);
+  sppf_planes<<<grid, 256, smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w,
+                                      kernel / 2);
+  return launch_check(name);
+}
+
+}  // extern "C"

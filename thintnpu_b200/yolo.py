@@ -1,0 +1,313 @@
+"""The YOLOv8s-640 non-conv op pass as a static plan, and its CUDA executor.
+
+Every convolution output is an input of the pass (seeded N(0,1) data at the
+conv's true NC1HWC0 shape); the pass runs everything between the convs, in
+model order:
+
+* SiLU on each of the 57 activated conv outputs (conv_flow.cpp:57-84 fuses it
+  into the conv epilogue in the reference; here it is its own kernel),
+* C2f ``chunk(2, 1)`` as channel-block views and the Bottleneck residual adds,
+* the C2f / neck concats along C1 (ops.cpp:419-462),
+* SPPF: three chained 5x5 max-pools and their concat (flow_ops.cpp:208-231),
+* two nearest-2x upsamples (flow_ops.cpp:233-252),
+* the Detect-terminal NC1HWC0 -> NCHW restore into one [B, 144, 8400] head
+  (conv_flow.cpp:87-121, anchorfree_predictions whole_blocked.py:118-135),
+* the DFL / anchor decode with sigmoid scores (whole_blocked.py:136-146).
+
+Topology: Ultralytics yolov8s (depth 0.33, width 0.50, max 1024 channels),
+restated from the published model definition; channel widths 32/64/128/256/512.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import ops
+
+C0 = 16
+
+
+@dataclass(frozen=True)
+class Ref:
+    """A channel-block slice [start, start+count) of a named NC1HWC0 tensor."""
+    name: str
+    start: int
+    count: int
+
+
+@dataclass(frozen=True)
+class Step:
+    op: str                      # silu | add | cat | sppf | upsample | restore | decode
+    inputs: Tuple[Ref, ...]
+    output: Optional[str]
+    attrs: Tuple = ()
+
+
+@dataclass
+class Plan:
+    imgsz: int
+    nc: int
+    shapes: Dict[str, Tuple[int, int, int]] = field(default_factory=dict)  # name -> (c1, h, w)
+    conv_inputs: List[str] = field(default_factory=list)  # synthetic pass inputs, in model order
+    steps: List[Step] = field(default_factory=list)
+    levels: List[Tuple[int, int]] = field(default_factory=list)
+    strides: List[float] = field(default_factory=list)
+
+    @property
+    def anchors(self) -> int:
+        return sum(h * w for h, w in self.levels)
+
+    def elements(self, name: str) -> int:
+        c1, h, w = self.shapes[name]
+        return c1 * h * w * C0
+
+    def step_bytes(self, step: Step) -> int:
+        """Compulsory bytes of one step for one image (inputs read + output written)."""
+        def ref_elems(r: Ref) -> int:
+            _, h, w = self.shapes[r.name]
+            return r.count * h * w * C0
+        if step.op == "silu":
+            return 2 * 2 * ref_elems(step.inputs[0])
+        if step.op == "add":
+            return 3 * 2 * ref_elems(step.inputs[0])
+        if step.op == "cat":
+            return 2 * 2 * sum(ref_elems(r) for r in step.inputs)
+        if step.op == "sppf":
+            return 2 * (1 + 4) * ref_elems(step.inputs[0])
+        if step.op == "upsample":
+            return 2 * (1 + 4) * ref_elems(step.inputs[0])
+        if step.op == "restore":
+            channels = step.attrs[1]
+            _, h, w = self.shapes[step.inputs[0].name]
+            return 2 * 2 * channels * h * w
+        if step.op == "decode":
+            return 2 * (64 + self.nc + 4 + self.nc) * self.anchors
+        raise ValueError(step.op)
+
+    def bytes_per_image(self) -> Dict[str, int]:
+        out: Dict[str, int] = {}
+        for s in self.steps:
+            out[s.op] = out.get(s.op, 0) + self.step_bytes(s)
+        return out
+
+
+class _Builder:
+    def __init__(self, imgsz: int, nc: int):
+        self.plan = Plan(imgsz=imgsz, nc=nc)
+        self.count = 0
+
+    def _new(self, prefix: str, c1: int, h: int, w: int) -> str:
+        name = f"{prefix}{self.count}"
+        self.count += 1
+        self.plan.shapes[name] = (c1, h, w)
+        return name
+
+    def conv(self, channels: int, h: int, w: int, act: bool = True) -> Ref:
+        c1 = (channels + C0 - 1) // C0
+        raw = self._new("conv", c1, h, w)
+        self.plan.conv_inputs.append(raw)
+        if not act:
+            return Ref(raw, 0, c1)
+        out = self._new("act", c1, h, w)
+        self.plan.steps.append(Step("silu", (Ref(raw, 0, c1),), out))
+        return Ref(out, 0, c1)
+
+    def add(self, a: Ref, b: Ref) -> Ref:
+        _, h, w = self.plan.shapes[a.name]
+        out = self._new("add", a.count, h, w)
+        self.plan.steps.append(Step("add", (a, b), out))
+        return Ref(out, 0, a.count)
+
+    def cat(self, refs: Sequence[Ref]) -> Ref:
+        _, h, w = self.plan.shapes[refs[0].name]
+        total = sum(r.count for r in refs)
+        out = self._new("cat", total, h, w)
+        self.plan.steps.append(Step("cat", tuple(refs), out))
+        return Ref(out, 0, total)
+
+    def upsample(self, x: Ref) -> Ref:
+        _, h, w = self.plan.shapes[x.name]
+        out = self._new("up", x.count, 2 * h, 2 * w)
+        self.plan.steps.append(Step("upsample", (x,), out))
+        return Ref(out, 0, x.count)
+
+    def sppf_pools(self, x: Ref, k: int = 5) -> Ref:
+        _, h, w = self.plan.shapes[x.name]
+        out = self._new("sppf", 4 * x.count, h, w)
+        self.plan.steps.append(Step("sppf", (x,), out, (k,)))
+        return Ref(out, 0, 4 * x.count)
+
+    # --- modules
+    def c2f(self, x_hw: Tuple[int, int], c2: int, n: int, shortcut: bool) -> Ref:
+        h, w = x_hw
+        c = c2 // 2
+        y = self.conv(2 * c, h, w)                       # cv1
+        half = y.count // 2
+        parts = [Ref(y.name, y.start, half), Ref(y.name, y.start + half, half)]
+        last = parts[-1]
+        for _ in range(n):                               # Bottleneck(c, c, shortcut, e=1.0)
+            t = self.conv(c, h, w)
+            t = self.conv(c, h, w)
+            last = self.add(last, t) if shortcut else t
+            parts.append(last)
+        cat = self.cat(parts)
+        del cat
+        return self.conv(c2, h, w)                       # cv2
+
+    def sppf(self, hw: Tuple[int, int], c2: int) -> Ref:
+        h, w = hw
+        a = self.conv(c2 // 2, h, w)                     # cv1
+        self.sppf_pools(a, 5)
+        return self.conv(c2, h, w)                       # cv2
+
+
+def yolov8s_plan(imgsz: int = 640, nc: int = 80) -> Plan:
+    """The non-conv op pass of YOLOv8s at imgsz x imgsz (batch-independent)."""
+    if imgsz % 32:
+        raise ValueError("imgsz must be a multiple of 32")
+    b = _Builder(imgsz, nc)
+    s = imgsz
+    b.conv(32, s // 2, s // 2)                                   # 0 P1/2
+    b.conv(64, s // 4, s // 4)                                   # 1 P2/4
+    b.c2f((s // 4, s // 4), 64, 1, True)                         # 2
+    b.conv(128, s // 8, s // 8)                                  # 3 P3/8
+    p3 = b.c2f((s // 8, s // 8), 128, 2, True)                   # 4
+    b.conv(256, s // 16, s // 16)                                # 5 P4/16
+    p4 = b.c2f((s // 16, s // 16), 256, 2, True)                 # 6
+    b.conv(512, s // 32, s // 32)                                # 7 P5/32
+    b.c2f((s // 32, s // 32), 512, 1, True)                      # 8
+    p5 = b.sppf((s // 32, s // 32), 512)                         # 9
+    up = b.upsample(p5)                                          # 10
+    cat = b.cat([up, p4])                                        # 11
+    h12 = b.c2f((s // 16, s // 16), 256, 1, False)               # 12
+    del cat
+    up = b.upsample(h12)                                         # 13
+    b.cat([up, p3])                                              # 14
+    o3 = b.c2f((s // 8, s // 8), 128, 1, False)                  # 15 (P3 out)
+    d = b.conv(128, s // 16, s // 16)                            # 16
+    b.cat([d, h12])                                              # 17
+    o4 = b.c2f((s // 16, s // 16), 256, 1, False)                # 18 (P4 out)
+    d = b.conv(256, s // 32, s // 32)                            # 19
+    b.cat([d, p5])                                               # 20
+    o5 = b.c2f((s // 32, s // 32), 512, 1, False)                # 21 (P5 out)
+    del o3, o4, o5
+    # 22 Detect(nc, ch=(128, 256, 512)): c2 = max(16, 128//4, 64) = 64, c3 = max(128, min(nc, 100))
+    c3 = max(128, min(nc, 100))
+    anchor = 0
+    for stride in (8, 16, 32):
+        h = w = s // stride
+        b.conv(64, h, w)
+        b.conv(64, h, w)
+        box = b.conv(64, h, w, act=False)
+        b.conv(c3, h, w)
+        b.conv(c3, h, w)
+        cls = b.conv(nc, h, w, act=False)
+        b.plan.steps.append(Step("restore", (box,), None, (0, 64, anchor)))
+        b.plan.steps.append(Step("restore", (cls,), None, (64, nc, anchor)))
+        b.plan.levels.append((h, w))
+        b.plan.strides.append(float(stride))
+        anchor += h * w
+    b.plan.steps.append(Step("decode", (), None, (True,)))
+    return b.plan
+
+
+def synthetic_inputs(plan: Plan, batch: int, device, seed: int = 4) -> Dict[str, torch.Tensor]:
+    """Seeded N(0,1) fp16 conv outputs, one generator per conv (seed + conv index).
+
+    Drawn in FP32 on ``device`` and rounded to fp16 (on CUDA the stream is the
+    Philox generator of that device, on CPU the CPU generator)."""
+    device = torch.device(device)
+    out = {}
+    for index, name in enumerate(plan.conv_inputs):
+        c1, h, w = plan.shapes[name]
+        g = torch.Generator(device=device)
+        g.manual_seed(seed + index)
+        out[name] = torch.randn((batch, c1, h, w, C0), generator=g, device=device,
+                                dtype=torch.float32).half()
+    return out
+
+
+class OpPass:
+    """Executes a Plan on one CUDA device with preallocated buffers.
+
+    ``inputs`` maps conv names to [B, c1, h, w, 16] fp16 CUDA tensors (kept
+    intact: SiLU writes separate activation buffers, so every run of the pass
+    -- and every CUDA-graph replay -- computes the same outputs).
+    ``output`` is the decoded [B, 4+nc, anchors] fp16 tensor."""
+
+    def __init__(self, plan: Plan, inputs: Dict[str, torch.Tensor]):
+        self.plan = plan
+        first = inputs[plan.conv_inputs[0]]
+        self.batch = first.size(0)
+        self.device = first.device
+        self.buffers: Dict[str, torch.Tensor] = dict(inputs)
+        for step in plan.steps:
+            if step.output is not None and step.output not in self.buffers:
+                c1, h, w = plan.shapes[step.output]
+                self.buffers[step.output] = torch.empty((self.batch, c1, h, w, C0),
+                                                        dtype=torch.float16, device=self.device)
+        self.head = torch.empty((self.batch, 64 + plan.nc, plan.anchors), dtype=torch.float16,
+                                device=self.device)
+        self.output = torch.empty((self.batch, 4 + plan.nc, plan.anchors), dtype=torch.float16,
+                                  device=self.device)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+    def view(self, ref: Ref) -> torch.Tensor:
+        t = self.buffers[ref.name]
+        if ref.start == 0 and ref.count == t.size(1):
+            return t
+        return t[:, ref.start:ref.start + ref.count]
+
+    def run_step(self, step: Step) -> None:
+        p = self.plan
+        if step.op == "silu":
+            ops.silu(self.view(step.inputs[0]), out=self.buffers[step.output])
+        elif step.op == "add":
+            ops.binary("add", self.view(step.inputs[0]), self.view(step.inputs[1]),
+                       out=self.buffers[step.output])
+        elif step.op == "cat":
+            ops.cat([self.view(r) for r in step.inputs], 1, out=self.buffers[step.output])
+        elif step.op == "sppf":
+            ops.sppf(self.view(step.inputs[0]), step.attrs[0], out=self.buffers[step.output])
+        elif step.op == "upsample":
+            ops.upsample_blocked(self.view(step.inputs[0]), out=self.buffers[step.output])
+        elif step.op == "restore":
+            channel0, channels, anchor0 = step.attrs
+            ops.unpack(self.view(step.inputs[0]), channels,
+                       out=self.head[:, channel0:channel0 + channels], out_offset=anchor0)
+        elif step.op == "decode":
+            ops.dfl_decode(self.head[:, :64], self.head[:, 64:], p.levels, p.strides,
+                           xywh=step.attrs[0], out=self.output)
+        else:
+            raise ValueError(step.op)
+
+    def run(self) -> torch.Tensor:
+        for step in self.plan.steps:
+            self.run_step(step)
+        return self.output
+
+    def capture(self, warmup: int = 2) -> torch.cuda.CUDAGraph:
+        """Capture the whole pass as one CUDA graph (the FrozenGraph replay path)."""
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.run()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.run()
+        self.graph = graph
+        return graph
+
+    def replay(self) -> torch.Tensor:
+        if self.graph is None:
+            self.capture()
+        self.graph.replay()
+        return self.output
+
+    def launches_per_pass(self) -> int:
+        """Kernels one pass launches (one per step; every op is a single kernel)."""
+        return len(self.plan.steps)
