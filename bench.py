@@ -295,25 +295,35 @@ def silu_traffic_per_launch(plan, batch):
 
 
 def run_e2e(args, plan, op_pass, device, stream, world, barrier, max_over_ranks):
+    """Same pass through the public API with host buffers: every step copies all of
+    the step's conv outputs host->device from pinned memory, replays the pass and
+    reads the decoded output back.  The pinned source is one pool per rank of at
+    most a quarter of the free host RAM split over the local ranks; inputs larger
+    than the pool are copied from it chunk by chunk, so the bytes crossing PCIe
+    per step are always the full input set."""
     import psutil
     import torch
     names = plan.conv_inputs
     step_bytes = sum(op_pass.buffers[n].numel() * 2 for n in names)
     local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
-    available = psutil.virtual_memory().available
-    if step_bytes * local_ranks * 2 > available:
-        return {"value": None, "unit": "images/s", "h2d_bytes_per_step": step_bytes,
-                "d2h_bytes_per_step": op_pass.output.numel() * 2,
-                "skipped": f"pinned host inputs need {step_bytes * local_ranks / 2**30:.1f} GiB; "
-                           f"{available / 2**30:.1f} GiB available"}
-    host = {n: torch.empty(op_pass.buffers[n].shape, dtype=torch.float16, pin_memory=True) for n in names}
-    for n in names:
-        host[n].copy_(op_pass.buffers[n])
+    budget = int(0.25 * psutil.virtual_memory().available / local_ranks)
+    pool_elems = max(1 << 20, min(step_bytes, budget) // 2)
+    pool = torch.empty(pool_elems, dtype=torch.float16, pin_memory=True)
+    pool.copy_(op_pass.buffers[names[0]].reshape(-1)[:pool_elems]
+               if op_pass.buffers[names[0]].numel() >= pool_elems else
+               torch.randn(pool_elems, dtype=torch.float32).half())
     result = torch.empty(op_pass.output.shape, dtype=torch.float16, pin_memory=True)
 
     def step():
+        offset = 0
         for n in names:  # H2D of this step's inputs
-            op_pass.buffers[n].copy_(host[n], non_blocking=True)
+            dst = op_pass.buffers[n].reshape(-1)
+            done = 0
+            while done < dst.numel():
+                take = min(dst.numel() - done, pool_elems - offset)
+                dst[done:done + take].copy_(pool[offset:offset + take], non_blocking=True)
+                done += take
+                offset = (offset + take) % pool_elems
         op_pass.replay()
         result.copy_(op_pass.output, non_blocking=True)  # D2H of the step's result
 
@@ -329,7 +339,8 @@ def run_e2e(args, plan, op_pass, device, stream, world, barrier, max_over_ranks)
     value = world * args.batch * args.e2e_steps / (ms / 1000.0)
     return {"value": value, "unit": "images/s", "h2d_bytes_per_step": step_bytes,
             "d2h_bytes_per_step": result.numel() * 2, "steps": args.e2e_steps,
-            "path": "pinned host -> cudaMemcpyAsync per conv output -> graph replay -> pinned host"}
+            "pinned_pool_bytes": pool_elems * 2,
+            "path": "pinned host pool -> cudaMemcpyAsync per conv output -> graph replay -> pinned host"}
 
 
 if __name__ == "__main__":

@@ -28,7 +28,7 @@ def device():
 
 
 def half_bits(t: torch.Tensor) -> np.ndarray:
-    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+    return t.detach().cpu().contiguous().reshape(-1).view(torch.int16).numpy().view(np.uint16)
 
 
 def ordered(bits: np.ndarray) -> np.ndarray:
@@ -50,8 +50,8 @@ def ulp_diff(a: torch.Tensor, b: torch.Tensor) -> np.ndarray:
 
 def assert_bits_equal(a: torch.Tensor, b: torch.Tensor, what: str = "") -> None:
     assert a.shape == b.shape and a.dtype == b.dtype, (what, a.shape, b.shape, a.dtype, b.dtype)
-    x = a.detach().cpu().contiguous().view(torch.uint8)
-    y = b.detach().cpu().contiguous().view(torch.uint8)
+    x = a.detach().cpu().contiguous().reshape(-1).view(torch.uint8)
+    y = b.detach().cpu().contiguous().reshape(-1).view(torch.uint8)
     assert torch.equal(x, y), f"bit mismatch {what}"
 
 

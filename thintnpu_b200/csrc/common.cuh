@@ -169,6 +169,86 @@ __device__ __forceinline__ uint16_t silu_h(uint16_t xb) {
   return hbits(__float2half_rn(r));
 }
 
+// --- fast path for the same functions on fp16 inputs ---
+// ex2.approx / rcp.approx give r within ~12 fp32 ulps of the exact value.  When
+// r lands in the fp16 normal range more than 16 fp32 ulps (of the 13 bits that
+// fp16 drops) away from a rounding midpoint, CPU's fp32 result (within ~2 ulps
+// of exact) rounds to the same fp16 value, so r is final; otherwise (about 0.4%
+// of inputs, plus subnormal/overflow/non-finite cases) the exact routine above
+// decides.  Both functions take fp16 inputs only, so the exhaustive 65,536-input
+// comparison with CPU eager covers the whole domain.
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// exp(-x) to ~2^-20 relative for |x| <= 25 (ex2.approx of a rounded product).
+__device__ __forceinline__ float exp_neg_fast(float x) { return ex2_approx(x * -1.44269504088896341f); }
+// exp(x) for softmax-style uses (tolerance-gated outputs).
+__device__ __forceinline__ float exp_fast(float x) { return ex2_approx(x * 1.44269504088896341f); }
+
+// True when the fast fp32 result r can be rounded to fp16 directly.
+__device__ __forceinline__ bool fast_rounding_safe(float r) {
+  uint32_t b = __float_as_uint(r) & 0x7fffffffu;
+  bool normal = (b - 0x38800000u) < (0x477fe000u - 0x38800000u);  // 2^-14 <= |r| < 65504
+  return normal && ((b - 0x0ff0u) & 0x1fffu) > 0x20u;               // > 16 ulps off the midpoint
+}
+
+__device__ __forceinline__ float silu_fast_f32(float x) { return x * rcp_approx(1.0f + exp_neg_fast(x)); }
+__device__ __forceinline__ float sigmoid_fast_f32(float x) { return rcp_approx(1.0f + exp_neg_fast(x)); }
+
+// Two fp16 lanes at once, deferring the exact decision: returns the fast fp16
+// pair and sets `unsafe` to a per-lane 0xffff mask where the result must come
+// from the exact routine instead -- where r*(1-2^-18) and r*(1+2^-18) round to
+// different fp16 values (r within ~16-32 fp32 ulps of a midpoint, any range), or
+// the input is +-inf/NaN (whose x86 results the fast formula does not give).
+template <bool kSilu>
+__device__ __forceinline__ uint32_t unary_h2_deferred(uint32_t packed, uint32_t& unsafe) {
+  __half2 h = *reinterpret_cast<__half2*>(&packed);
+  float2 f = __half22float2(h);
+  float r0 = kSilu ? silu_fast_f32(f.x) : sigmoid_fast_f32(f.x);
+  float r1 = kSilu ? silu_fast_f32(f.y) : sigmoid_fast_f32(f.y);
+  __half2 o = __floats2half2_rn(r0, r1);
+  __half2 up = __floats2half2_rn(r0 * 1.000003814697265625f, r1 * 1.000003814697265625f);
+  __half2 dn = __floats2half2_rn(r0 * 0.999996185302734375f, r1 * 0.999996185302734375f);
+  uint32_t uw = *reinterpret_cast<uint32_t*>(&up), dw = *reinterpret_cast<uint32_t*>(&dn);
+  unsafe = __vcmpne2(uw, dw) | __vcmpeq2(packed & 0x7c007c00u, 0x7c007c00u);
+  return *reinterpret_cast<uint32_t*>(&o);
+}
+
+// Two fp16 lanes at once; exact fallback per lane when needed.
+template <bool kSilu>
+__device__ __forceinline__ uint32_t unary_h2_fast(uint32_t packed) {
+  __half2 h = *reinterpret_cast<__half2*>(&packed);
+  float2 f = __half22float2(h);
+  float r0 = kSilu ? silu_fast_f32(f.x) : sigmoid_fast_f32(f.x);
+  float r1 = kSilu ? silu_fast_f32(f.y) : sigmoid_fast_f32(f.y);
+  __half2 o = __floats2half2_rn(r0, r1);
+  uint32_t out = *reinterpret_cast<uint32_t*>(&o);
+  if (!fast_rounding_safe(r0)) {
+    uint16_t x0 = (uint16_t)(packed & 0xffffu);
+    out = (out & 0xffff0000u) | (kSilu ? silu_h(x0) : sigmoid_h(x0));
+  }
+  if (!fast_rounding_safe(r1)) {
+    uint16_t x1 = (uint16_t)(packed >> 16);
+    out = (out & 0x0000ffffu) | ((uint32_t)(kSilu ? silu_h(x1) : sigmoid_h(x1)) << 16);
+  }
+  return out;
+}
+
+__device__ __forceinline__ uint16_t sigmoid_h_fast(uint16_t xb) {
+  float x = __half2float(hfrom(xb));
+  float r = sigmoid_fast_f32(x);
+  if (fast_rounding_safe(r)) return hbits(__float2half_rn(r));
+  return sigmoid_h(xb);
+}
+
 // fp32 versions for TTN_F32 tensors (no rounding step to protect).
 __device__ __forceinline__ float sigmoid_f(float x) { return sigmoid_f32(x); }
 __device__ __forceinline__ float silu_f(float x) { return silu_f32(x); }

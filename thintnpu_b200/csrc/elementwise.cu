@@ -27,30 +27,79 @@ __device__ __forceinline__ float unary_f(float x) {
 
 template <int K>
 __device__ __forceinline__ uint4 unary_vec8(uint4 v) {
-  uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t lo = unary_h<K>((uint16_t)(w[i] & 0xffffu));
-    uint32_t hi = unary_h<K>((uint16_t)(w[i] >> 16));
-    w[i] = lo | (hi << 16);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
+  return make_uint4(unary_h2_fast<K == kSilu>(v.x), unary_h2_fast<K == kSilu>(v.y),
+                    unary_h2_fast<K == kSilu>(v.z), unary_h2_fast<K == kSilu>(v.w));
 }
 
 // Dense fp16, 16-byte aligned: uint4 body plus a scalar tail.  x may equal y.
+// Warp-uniform loop: each lane owns two 16-byte vectors per step (32 bytes in
+// flight per lane).  Lanes whose fast results are not provably the CPU's fp16
+// value (about 1% of elements) queue (index, input bits) in shared memory; the
+// warp then recomputes the queued elements exactly, one element per lane, and
+// overwrites them -- so the exact path costs per flagged element, not per
+// diverged warp step.
+constexpr int kQueue = 64;  // entries per warp
+
 template <int K>
 __global__ void __launch_bounds__(kThreads) unary_f16_dense(const uint4* x, uint4* y,
                                                             int64_t nvec, const uint16_t* xt,
                                                             uint16_t* yt, int tail) {
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  for (; i + stride < nvec; i += 2 * stride) {
-    uint4 a = x[i];
-    uint4 b = x[i + stride];
-    y[i] = unary_vec8<K>(a);
-    y[i + stride] = unary_vec8<K>(b);
+  __shared__ uint32_t q_index[kThreads / 32][kQueue];
+  __shared__ uint16_t q_bits[kThreads / 32][kQueue];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
+  const int64_t step = warps * 64;
+  uint16_t* yh = reinterpret_cast<uint16_t*>(y);
+  for (int64_t base = ((int64_t)blockIdx.x * (kThreads / 32) + warp) * 64; base < nvec; base += step) {
+    const int64_t i0 = base + lane, i1 = base + 32 + lane;
+    uint4 a = i0 < nvec ? x[i0] : make_uint4(0, 0, 0, 0);
+    uint4 b = i1 < nvec ? x[i1] : make_uint4(0, 0, 0, 0);
+    uint32_t in[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t out[8], bad[8];
+    uint32_t flags = 0;  // one bit per element of the two vectors
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      out[k] = unary_h2_deferred<K == kSilu>(in[k], bad[k]);
+      flags |= ((bad[k] & 1u) | ((bad[k] >> 15) & 2u)) << (2 * k);
+    }
+    if (i0 >= nvec) flags &= 0xff00u;
+    if (i1 >= nvec) flags &= 0x00ffu;
+    if (i0 < nvec) y[i0] = make_uint4(out[0], out[1], out[2], out[3]);
+    if (i1 < nvec) y[i1] = make_uint4(out[4], out[5], out[6], out[7]);
+    if (__any_sync(0xffffffffu, flags != 0u)) {
+      // exclusive prefix of per-lane flag counts
+      int mine = __popc(flags), pos = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int v = __shfl_up_sync(0xffffffffu, pos, o);
+        if (lane >= o) pos += v;
+      }
+      const int total = __shfl_sync(0xffffffffu, pos, 31);
+      pos -= mine;
+      for (int done = 0; done < total; done += kQueue) {
+        uint32_t f = flags;
+        int slot = pos;
+        while (f) {
+          int bit = __ffs(f) - 1;
+          f &= f - 1;
+          if (slot >= done && slot < done + kQueue) {
+            int64_t vec = bit < 8 ? i0 : i1;
+            int e = bit & 7;
+            q_index[warp][slot - done] = (uint32_t)(vec * 8 + e - base * 8);
+            q_bits[warp][slot - done] = (uint16_t)(in[(bit >> 1)] >> ((bit & 1) * 16));
+          }
+          ++slot;
+        }
+        __syncwarp();
+        const int chunk = total - done < kQueue ? total - done : kQueue;
+        for (int t = lane; t < chunk; t += 32) {
+          uint16_t xb = q_bits[warp][t];
+          yh[base * 8 + q_index[warp][t]] = unary_h<K>(xb);
+        }
+        __syncwarp();
+      }
+    }
   }
-  if (i < nvec) y[i] = unary_vec8<K>(x[i]);
   if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = unary_h<K>(xt[threadIdx.x]);
 }
 
@@ -75,14 +124,15 @@ __global__ void __launch_bounds__(kThreads) unary_strided(const T* x, T* y, Inde
 template <int K>
 __global__ void __launch_bounds__(kThreads) unary_f16_rows(const uint16_t* x, uint16_t* y,
                                                            Index6 outer, int64_t vec_per_row,
-                                                           int64_t nvec) {
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
-    int64_t row = i / vec_per_row, col = (i - row * vec_per_row) * 8;
+                                                           int64_t rows) {
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
     int64_t ox, oy, unused;
-    offsets3(outer, row, ox, oy, unused);
-    const uint4 a = *reinterpret_cast<const uint4*>(x + ox + col);
-    *reinterpret_cast<uint4*>(y + oy + col) = unary_vec8<K>(a);
+    offsets3(outer, row, ox, oy, unused);  // once per block row
+    const uint4* xs = reinterpret_cast<const uint4*>(x + ox);
+    uint4* ys = reinterpret_cast<uint4*>(y + oy);
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < vec_per_row;
+         v += (int64_t)gridDim.x * blockDim.x)
+      ys[v] = unary_vec8<K>(xs[v]);
   }
 }
 
@@ -137,20 +187,23 @@ __global__ void __launch_bounds__(kThreads) binary_f16_dense(BinaryParams p, con
 __global__ void __launch_bounds__(kThreads) binary_f16_rows(BinaryParams p, const uint16_t* x,
                                                             const uint16_t* y, uint16_t* z,
                                                             Index6 outer, int64_t vec_per_row,
-                                                            int64_t nvec) {
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
-    int64_t row = i / vec_per_row, col = (i - row * vec_per_row) * 8;
+                                                            int64_t rows) {
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
     int64_t ox, oy, oz;
-    offsets3(outer, row, ox, oy, oz);
-    uint4 a = *reinterpret_cast<const uint4*>(x + ox + col);
-    uint4 b = *reinterpret_cast<const uint4*>(y + oy + col);
-    uint4 r;
-    r.x = binary_h2(p, a.x, b.x);
-    r.y = binary_h2(p, a.y, b.y);
-    r.z = binary_h2(p, a.z, b.z);
-    r.w = binary_h2(p, a.w, b.w);
-    *reinterpret_cast<uint4*>(z + oz + col) = r;
+    offsets3(outer, row, ox, oy, oz);  // once per block row
+    const uint4* xs = reinterpret_cast<const uint4*>(x + ox);
+    const uint4* ys = reinterpret_cast<const uint4*>(y + oy);
+    uint4* zs = reinterpret_cast<uint4*>(z + oz);
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < vec_per_row;
+         v += (int64_t)gridDim.x * blockDim.x) {
+      uint4 a = xs[v], b = ys[v];
+      uint4 r;
+      r.x = binary_h2(p, a.x, b.x);
+      r.y = binary_h2(p, a.y, b.y);
+      r.z = binary_h2(p, a.z, b.z);
+      r.w = binary_h2(p, a.w, b.w);
+      zs[v] = r;
+    }
   }
 }
 
@@ -232,8 +285,8 @@ __global__ void __launch_bounds__(kThreads) bias_silu_residual(const uint4* x, c
       float2 fx = __half22float2(*reinterpret_cast<__half2*>(&xw[k]));
       float2 fr = __half22float2(*reinterpret_cast<__half2*>(&rw[k]));
       float2 fb = __half22float2(*reinterpret_cast<__half2*>(&bw[k]));
-      float lo = __fadd_rn(silu_f32(__fadd_rn(fx.x, fb.x)), fr.x);
-      float hi = __fadd_rn(silu_f32(__fadd_rn(fx.y, fb.y)), fr.y);
+      float lo = silu_fast_f32(fx.x + fb.x) + fr.x;
+      float hi = silu_fast_f32(fx.y + fb.y) + fr.y;
       __half2 h = __floats2half2_rn(lo, hi);
       out[k] = *reinterpret_cast<uint32_t*>(&h);
     }
@@ -274,6 +327,18 @@ bool vec_rows(const Coalesced& c, int count, const void* const* ptrs, Index6& ou
   return true;
 }
 
+// 2-D grid for row kernels: y over rows (<= 65535 per pass), x over the
+// vectors of a row, about 8 resident blocks per SM in total.
+dim3 rows_grid(int64_t vec_per_row, int64_t rows) {
+  int64_t gy = rows < 65535 ? rows : 65535;
+  int64_t want = (int64_t)sm_count() * 8;
+  int64_t gx = (vec_per_row + kThreads - 1) / kThreads;
+  int64_t cap = (want + gy - 1) / gy;
+  if (gx > cap) gx = cap;
+  if (gx < 1) gx = 1;
+  return dim3((unsigned)gx, (unsigned)gy);
+}
+
 ttn_status to_index6(const Coalesced& c, int count, Index6& ix, const char* what) {
   if (c.ndim > 6)
     return fail(TTN_UNSUPPORTED, "%s: view needs %d dims after coalescing (max 6)", what, c.ndim);
@@ -298,7 +363,7 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
   if (x->dtype == TTN_F16 && dense(c, 2) && aligned16(x->data) && aligned16(y->data)) {
     int64_t nvec = c.numel / 8;
     int tail = (int)(c.numel - nvec * 8);
-    unsigned grid = grid_for(nvec ? nvec : 1, (int64_t)kThreads * 2);
+    unsigned grid = grid_for(nvec ? nvec : 1, (int64_t)kThreads * 2, 6);
     unary_f16_dense<K><<<grid, kThreads, 0, s>>>(
         (const uint4*)x->data, (uint4*)y->data, nvec, (const uint16_t*)x->data + nvec * 8,
         (uint16_t*)y->data + nvec * 8, tail);
@@ -308,9 +373,9 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
   int64_t vpr;
   const void* ptrs[2] = {x->data, y->data};
   if (x->dtype == TTN_F16 && vec_rows(c, 2, ptrs, ix, vpr)) {
-    int64_t nvec = c.numel / 8;
-    unary_f16_rows<K><<<grid_for(nvec, kThreads), kThreads, 0, s>>>(
-        (const uint16_t*)x->data, (uint16_t*)y->data, ix, vpr, nvec);
+    dim3 grid = rows_grid(vpr, c.numel / 8 / vpr);
+    unary_f16_rows<K><<<grid, kThreads, 0, s>>>((const uint16_t*)x->data, (uint16_t*)y->data, ix,
+                                                vpr, c.numel / 8 / vpr);
     return launch_check(name);
   }
   TTN_TRY(to_index6(c, 2, ix, name));
@@ -370,9 +435,9 @@ ttn_status ttn_binary(int op, float alpha, const ttn_tensor* x, const ttn_tensor
   int64_t vpr;
   const void* ptrs[3] = {x->data, y->data, out->data};
   if (x->dtype == TTN_F16 && vec_rows(c, 3, ptrs, ix, vpr)) {
-    int64_t nvec = c.numel / 8;
-    binary_f16_rows<<<grid_for(nvec, kThreads), kThreads, 0, s>>>(
-        p, (const uint16_t*)x->data, (const uint16_t*)y->data, (uint16_t*)out->data, ix, vpr, nvec);
+    dim3 grid = rows_grid(vpr, c.numel / 8 / vpr);
+    binary_f16_rows<<<grid, kThreads, 0, s>>>(p, (const uint16_t*)x->data, (const uint16_t*)y->data,
+                                              (uint16_t*)out->data, ix, vpr, c.numel / 8 / vpr);
     return launch_check(name);
   }
   TTN_TRY(to_index6(c, 3, ix, name));

@@ -44,7 +44,7 @@ __device__ __forceinline__ uint32_t score_key(uint16_t bits, bool nan_last) {
 __device__ __forceinline__ uint16_t score_bits(const SelectView& v, int64_t b, int64_t a, int64_t c,
                                                bool sigmoid) {
   uint16_t raw = v.base[b * v.sb + a * v.sa + (c + 4) * v.sc];
-  return sigmoid ? sigmoid_h(raw) : raw;
+  return sigmoid ? sigmoid_h_fast(raw) : raw;
 }
 
 // ------------------------------------------------------------ 1. class max
@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(256) class_max_thread(SelectView v, bool nan_l
     const uint16_t* p = v.base + b * v.sb + a * v.sa + 4 * v.sc;
     for (int64_t c = 0; c < v.classes; ++c) {
       uint16_t bits = p[c * v.sc];
-      if (sigmoid) bits = sigmoid_h(bits);
+      if (sigmoid) bits = sigmoid_h_fast(bits);
       uint32_t key = score_key(bits, nan_last);
       if (key < best) {
         best = key;
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(256) class_max_planar8(SelectView v, bool nan_
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           uint16_t bits = (uint16_t)((w[r][j >> 1] >> ((j & 1) * 16)) & 0xffffu);
-          if (sigmoid) bits = sigmoid_h(bits);
+          if (sigmoid) bits = sigmoid_h_fast(bits);
           uint32_t key = score_key(bits, nan_last);
           if (key < best[j]) {
             best[j] = key;
@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(256) class_max_planar8(SelectView v, bool nan_
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         uint16_t bits = (uint16_t)((w[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
-        if (sigmoid) bits = sigmoid_h(bits);
+        if (sigmoid) bits = sigmoid_h_fast(bits);
         uint32_t key = score_key(bits, nan_last);
         if (key < best[j]) {
           best[j] = key;
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(256) class_max_warp(SelectView v, bool nan_las
     uint32_t best = kInvalidKey, best_cls = 0xffffffffu, best_bits = 0;
     for (int64_t c = lane; c < v.classes; c += 32) {
       uint16_t bits = p[c * v.sc];
-      if (sigmoid) bits = sigmoid_h(bits);
+      if (sigmoid) bits = sigmoid_h_fast(bits);
       uint32_t key = score_key(bits, nan_last);
       if (key < best) {  // lanes walk classes in increasing order
         best = key;

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(256) softmax_warp_rows(const T* x, U* y, RowSp
     for (int k = 0; k < PER; ++k) {
       int e = k * 32 + lane;
       if (e < reduce) {
-        v[k] = expf(__fsub_rn(v[k], m));
+        v[k] = exp_fast(__fsub_rn(v[k], m));
         s = __fadd_rn(s, v[k]);
       }
     }
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(256) softmax_warp_rows_h8(const uint16_t* x, u
       if (e < nvec) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          v[k][j] = expf(__fsub_rn(v[k][j], m));
+          v[k][j] = exp_fast(__fsub_rn(v[k][j], m));
           s = __fadd_rn(s, v[k][j]);
         }
       }
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(512) softmax_block_rows(const T* x, U* y, RowS
     __syncthreads();
     float s = 0.0f;
     for (int64_t e = threadIdx.x; e < reduce; e += blockDim.x)
-      s = __fadd_rn(s, expf(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)));
+      s = __fadd_rn(s, exp_fast(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)));
     for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(512) softmax_block_rows(const T* x, U* y, RowS
     __syncthreads();
     for (int64_t e = threadIdx.x; e < reduce; e += blockDim.x)
       store_out(y, oy + e * rsy,
-                __fmul_rn(expf(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)), inv));
+                __fmul_rn(exp_fast(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)), inv));
   }
 }
 
@@ -219,11 +219,11 @@ __global__ void __launch_bounds__(256) softmax_thread_rows(const T* x, U* y, Row
     for (int64_t e = 0; e < reduce; ++e) m = nan_max(m, load_scaled(x, ox + e * rsx, scale, scaled));
     float s = 0.0f;
     for (int64_t e = 0; e < reduce; ++e)
-      s = __fadd_rn(s, expf(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)));
+      s = __fadd_rn(s, exp_fast(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)));
     const float inv = __fdiv_rn(1.0f, s);
     for (int64_t e = 0; e < reduce; ++e)
       store_out(y, oy + e * rsy,
-                __fmul_rn(expf(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)), inv));
+                __fmul_rn(exp_fast(__fsub_rn(load_scaled(x, ox + e * rsx, scale, scaled), m)), inv));
   }
 }
 
@@ -248,7 +248,7 @@ __device__ __forceinline__ float dfl_side(const float (&v)[16]) {
   float e[16], s = 0.0f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    e[i] = expf(__fsub_rn(v[i], m));
+    e[i] = exp_fast(__fsub_rn(v[i], m));
     s = __fadd_rn(s, e[i]);
   }
   const float inv = __fdiv_rn(1.0f, s);
@@ -328,14 +328,88 @@ __global__ void __launch_bounds__(128) dfl_decode(const __half* box, int64_t box
     for (int64_t c = 0; c < nc; ++c) {
       if constexpr (APT == 2) {
         uint32_t w = *reinterpret_cast<const uint32_t*>(cx + c * cls_cs);
-        uint32_t r = (uint32_t)sigmoid_h((uint16_t)(w & 0xffffu)) |
-                     ((uint32_t)sigmoid_h((uint16_t)(w >> 16)) << 16);
+        uint32_t r = unary_h2_fast<false>(w);
         *reinterpret_cast<uint32_t*>(o + (4 + c) * anchors) = r;
       } else {
         reinterpret_cast<uint16_t*>(o)[(4 + c) * anchors] =
-            sigmoid_h(reinterpret_cast<const uint16_t*>(cx)[c * cls_cs]);
+            sigmoid_h_fast(reinterpret_cast<const uint16_t*>(cx)[c * cls_cs]);
       }
     }
+  }
+}
+
+// Tiled decode for 8-aligned anchors: a block stages [64 + nc rows] x 64 anchors
+// of logits in shared memory with 16-byte loads, runs one (anchor, side) DFL
+// reduction per thread and the class sigmoids two lanes at a time, then stores
+// the [4 + nc] x 64 output tile with 16-byte stores.
+constexpr int kTileA = 64;
+
+template <int NC_MAX>
+__global__ void __launch_bounds__(256) dfl_decode_tiled(const __half* box, int64_t box_bs,
+                                                        int64_t box_cs, const __half* cls,
+                                                        int64_t cls_bs, int64_t cls_cs, int64_t n,
+                                                        int nc, int64_t anchors, Levels lv, bool xywh,
+                                                        __half* out) {
+  __shared__ __align__(16) uint16_t in_box[64][kTileA];
+  __shared__ __align__(16) uint16_t io_cls[NC_MAX][kTileA];
+  __shared__ float dist[4][kTileA];
+  __shared__ __align__(16) uint16_t out_box[4][kTileA];
+  const int64_t tiles = anchors / kTileA;
+  const int tid = threadIdx.x;
+  for (int64_t job = blockIdx.x; job < n * tiles; job += gridDim.x) {
+    const int64_t b = job / tiles, a0 = (job % tiles) * kTileA;
+    // load: 8 uint4 per row
+    for (int v = tid; v < (64 + nc) * 8; v += blockDim.x) {
+      int row = v >> 3, col = (v & 7) * 8;
+      const __half* src = row < 64 ? box + b * box_bs + row * box_cs + a0 + col
+                                   : cls + b * cls_bs + (row - 64) * cls_cs + a0 + col;
+      uint4 q = *reinterpret_cast<const uint4*>(src);
+      uint16_t* dst = row < 64 ? &in_box[row][col] : &io_cls[row - 64][col];
+      *reinterpret_cast<uint4*>(dst) = q;
+    }
+    __syncthreads();
+    {  // DFL: thread -> (side, anchor)
+      int side = tid >> 6, a = tid & 63;
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = __half2float(hfrom(in_box[side * 16 + i][a]));
+      dist[side][a] = dfl_side(v);
+    }
+    // sigmoid in place on the class rows, two anchors per step
+    for (int e = tid; e < nc * (kTileA / 2); e += blockDim.x) {
+      int row = e / (kTileA / 2), col = (e % (kTileA / 2)) * 2;
+      uint32_t* p = reinterpret_cast<uint32_t*>(&io_cls[row][col]);
+      *p = unary_h2_fast<false>(*p);
+    }
+    __syncthreads();
+    if (tid < kTileA * 4) {  // box decode: thread -> (coordinate, anchor)
+      int c = tid >> 6, a = tid & 63;
+      int64_t idx = a0 + a;
+      int l = 0;
+      while (l + 1 < lv.count && idx >= lv.start[l + 1]) ++l;
+      int64_t local = idx - lv.start[l];
+      float ax = h16((float)(local % lv.width[l]) + 0.5f);
+      float ay = h16((float)(local / lv.width[l]) + 0.5f);
+      float lx = h16(__fsub_rn(ax, dist[0][a])), ly = h16(__fsub_rn(ay, dist[1][a]));
+      float ux = h16(__fadd_rn(ax, dist[2][a])), uy = h16(__fadd_rn(ay, dist[3][a]));
+      float q;
+      if (xywh) {
+        q = c == 0 ? h16(__fdiv_rn(h16(__fadd_rn(lx, ux)), 2.0f))
+          : c == 1 ? h16(__fdiv_rn(h16(__fadd_rn(ly, uy)), 2.0f))
+          : c == 2 ? h16(__fsub_rn(ux, lx)) : h16(__fsub_rn(uy, ly));
+      } else {
+        q = c == 0 ? lx : c == 1 ? ly : c == 2 ? ux : uy;
+      }
+      out_box[c][a] = hbits(__float2half_rn(__fmul_rn(q, lv.stride[l])));
+    }
+    __syncthreads();
+    __half* o = out + b * (4 + nc) * anchors + a0;
+    for (int v = tid; v < (4 + nc) * 8; v += blockDim.x) {
+      int row = v >> 3, col = (v & 7) * 8;
+      const uint16_t* src = row < 4 ? &out_box[row][col] : &io_cls[row - 4][col];
+      *reinterpret_cast<uint4*>(o + row * anchors + col) = *reinterpret_cast<const uint4*>(src);
+    }
+    __syncthreads();
   }
 }
 
@@ -460,6 +534,17 @@ ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs, c
               box_bs % 2 == 0 && box_cs % 2 == 0 &&
               (!nc || (((uintptr_t)cls & 3u) == 0 && cls_bs % 2 == 0 && cls_cs % 2 == 0));
   cudaStream_t s = (cudaStream_t)stream;
+  bool tiled = nc <= 96 && anchors % kTileA == 0 && ((uintptr_t)box & 15u) == 0 &&
+               ((uintptr_t)out & 15u) == 0 && box_bs % 8 == 0 && box_cs % 8 == 0 &&
+               (!nc || (((uintptr_t)cls & 15u) == 0 && cls_bs % 8 == 0 && cls_cs % 8 == 0));
+  if (tiled) {
+    int64_t jobs = n * (anchors / kTileA);
+    unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * 8 ? jobs : (int64_t)sm_count() * 8);
+    dfl_decode_tiled<96><<<grid, 256, 0, s>>>((const __half*)box, box_bs, box_cs, (const __half*)cls,
+                                               cls_bs, cls_cs, n, (int)nc, anchors, lv, xywh != 0,
+                                               (__half*)out);
+    return launch_check(name);
+  }
   if (pair) {
     int64_t work = n * (anchors / 2);
     dfl_decode<2><<<grid_for(work, 128, 16), 128, 0, s>>>(

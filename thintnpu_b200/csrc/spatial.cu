@@ -129,9 +129,9 @@ __global__ void __launch_bounds__(256) upsample_nchw_vec(const uint2* x, uint4* 
     int64_t col = v % w4, rest = v / w4;
     uint32_t a = q.x & 0xffffu, b = q.x >> 16, c = q.y & 0xffffu, d = q.y >> 16;
     uint4 o = make_uint4(a | (a << 16), b | (b << 16), c | (c << 16), d | (d << 16));
-    int64_t row0 = rest * 2;  // rest = plane*h + row
-    y[row0 * w4 * 2 + col] = o;
-    y[(row0 + 1) * w4 * 2 + col] = o;
+    int64_t row0 = rest * 2;  // output row of input row `rest` (= plane*h + row)
+    y[row0 * w4 + col] = o;
+    y[(row0 + 1) * w4 + col] = o;
   }
 }
 
@@ -225,49 +225,102 @@ __global__ void __launch_bounds__(256) maxpool_band(const T* x, T* y, int64_t pl
   }
 }
 
-// SPPF: per (image, channel block) plane held whole in shared memory;
+// SPPF: per (image, channel block) plane held whole in shared memory, with a
+// 2-pixel -inf border so every 5-wide window is full (-inf never wins under the
+// CPU rule, so this equals clipping the window at the edge).  Planes without NaN
+// or -0 take a half2 max (equal values then have equal bits, so any max is the
+// CPU's first max); planes holding either take the exact per-lane CPU rule.
 // out planes: [x, p1, p2, p3] at channel blocks cb, c1+cb, 2c1+cb, 3c1+cb.
+__device__ __forceinline__ bool special_word(uint32_t w) {
+  uint32_t nan = __vcmpgtu2(w & 0x7fff7fffu, 0x7c007c00u);
+  uint32_t negzero = __vcmpeq2(w, 0x80008000u);
+  return (nan | negzero) != 0u;
+}
+
+__device__ __forceinline__ uint4 hmax4(uint4 a, uint4 b) {
+  __half2 r[4];
+  const __half2* pa = reinterpret_cast<const __half2*>(&a);
+  const __half2* pb = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) r[i] = __hmax2(pa[i], pb[i]);
+  return *reinterpret_cast<uint4*>(r);
+}
+
 __global__ void __launch_bounds__(256) sppf_planes(const uint16_t* x, uint16_t* out, int64_t n,
                                                    int64_t c1, int h, int w, int radius) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int plane_elems = h * w * 16;
-  uint16_t* cur = reinterpret_cast<uint16_t*>(smem_raw);
-  uint16_t* tmp = cur + plane_elems;
-  const int row_elems = w * 16;
+  const int pw = w + 2 * radius, ph = h + 2 * radius;  // padded plane, in pixels
+  const int padded_vec = ph * pw * 2;                 // uint4 per padded plane
+  uint4* cur = reinterpret_cast<uint4*>(smem_raw);
+  uint4* tmp = cur + padded_vec;
+  const int plane_vec = h * w * 2;
+  const uint4 ninf = make_uint4(0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u);
+  for (int v = threadIdx.x; v < 2 * padded_vec; v += blockDim.x) cur[v] = ninf;
+  __syncthreads();
   for (int64_t job = blockIdx.x; job < n * c1; job += gridDim.x) {
     int64_t b = job / c1, cb = job % c1;
-    const uint4* src = reinterpret_cast<const uint4*>(x + job * plane_elems);
-    for (int v = threadIdx.x; v < plane_elems / 8; v += blockDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + job * (int64_t)plane_vec * 8);
+    uint4* dst0 = reinterpret_cast<uint4*>(out + ((b * 4 * c1) + cb) * (int64_t)plane_vec * 8);
+    bool special = false;
+    for (int v = threadIdx.x; v < plane_vec; v += blockDim.x) {
       uint4 q = src[v];
-      reinterpret_cast<uint4*>(cur)[v] = q;
-      reinterpret_cast<uint4*>(out + ((b * 4 * c1) + cb) * plane_elems)[v] = q;
+      dst0[v] = q;
+      int pix = v >> 1, row = pix / w, col = pix % w;
+      cur[((row + radius) * pw + col + radius) * 2 + (v & 1)] = q;
+      special |= special_word(q.x) | special_word(q.y) | special_word(q.z) | special_word(q.w);
     }
-    __syncthreads();
+    special = __syncthreads_or(special);
     for (int stage = 1; stage <= 3; ++stage) {
-      for (int e = threadIdx.x; e < plane_elems; e += blockDim.x) {
-        int lane = e & 15, col = (e >> 4) % w, row = e / row_elems;
-        int a = col - radius > 0 ? col - radius : 0;
-        int z = col + radius < w - 1 ? col + radius : w - 1;
-        uint16_t m = 0xfc00u;
-        float mv = -INFINITY;
-        const uint16_t* r = cur + row * row_elems + lane;
-        for (int c = a; c <= z; ++c) pool_update(m, mv, r[c * 16]);
-        tmp[e] = m;
+      // horizontal: tmp[row][col] over every padded row (border rows stay -inf)
+      for (int v = threadIdx.x; v < plane_vec; v += blockDim.x) {
+        int pix = v >> 1, row = pix / w + radius, col = pix % w + radius, j = v & 1;
+        const uint4* r = cur + (row * pw + col - radius) * 2 + j;
+        uint4 m;
+        if (!special) {
+          m = r[0];
+          for (int k = 1; k <= 2 * radius; ++k) m = hmax4(m, r[2 * k]);
+        } else {
+          uint16_t best[8];
+          float bv[8];
+#pragma unroll
+          for (int l = 0; l < 8; ++l) { best[l] = 0xfc00u; bv[l] = -INFINITY; }
+          for (int k = 0; k <= 2 * radius; ++k) {
+            uint4 q = r[2 * k];
+            const uint16_t* e = reinterpret_cast<const uint16_t*>(&q);
+#pragma unroll
+            for (int l = 0; l < 8; ++l) pool_update(best[l], bv[l], e[l]);
+          }
+          m = *reinterpret_cast<uint4*>(best);
+        }
+        tmp[(row * pw + col) * 2 + j] = m;
       }
       __syncthreads();
-      for (int e = threadIdx.x; e < plane_elems; e += blockDim.x) {
-        int row = e / row_elems, rest = e % row_elems;
-        int a = row - radius > 0 ? row - radius : 0;
-        int z = row + radius < h - 1 ? row + radius : h - 1;
-        uint16_t m = 0xfc00u;
-        float mv = -INFINITY;
-        for (int q = a; q <= z; ++q) pool_update(m, mv, tmp[q * row_elems + rest]);
-        cur[e] = PoolBits<uint16_t>::finish(m);
+      uint4* dst = reinterpret_cast<uint4*>(out + ((b * 4 * c1) + stage * c1 + cb) * (int64_t)plane_vec * 8);
+      for (int v = threadIdx.x; v < plane_vec; v += blockDim.x) {
+        int pix = v >> 1, row = pix / w + radius, col = pix % w + radius, j = v & 1;
+        const uint4* r = tmp + ((row - radius) * pw + col) * 2 + j;
+        uint4 m;
+        if (!special) {
+          m = r[0];
+          for (int k = 1; k <= 2 * radius; ++k) m = hmax4(m, r[2 * k * pw]);
+        } else {
+          uint16_t best[8];
+          float bv[8];
+#pragma unroll
+          for (int l = 0; l < 8; ++l) { best[l] = 0xfc00u; bv[l] = -INFINITY; }
+          for (int k = 0; k <= 2 * radius; ++k) {
+            uint4 q = r[2 * k * pw];
+            const uint16_t* e = reinterpret_cast<const uint16_t*>(&q);
+#pragma unroll
+            for (int l = 0; l < 8; ++l) pool_update(best[l], bv[l], e[l]);
+          }
+#pragma unroll
+          for (int l = 0; l < 8; ++l) best[l] = PoolBits<uint16_t>::finish(best[l]);
+          m = *reinterpret_cast<uint4*>(best);
+        }
+        cur[(row * pw + col) * 2 + j] = m;
+        dst[v] = m;
       }
-      __syncthreads();
-      uint4* dst = reinterpret_cast<uint4*>(out + ((b * 4 * c1) + stage * c1 + cb) * plane_elems);
-      for (int v = threadIdx.x; v < plane_elems / 8; v += blockDim.x)
-        dst[v] = reinterpret_cast<const uint4*>(cur)[v];
       __syncthreads();
     }
   }
@@ -398,7 +451,8 @@ ttn_status ttn_sppf_f16(const void* x, void* out, int64_t n, int64_t c1, int64_t
   if (!n || !c1 || !h || !w) return TTN_OK;
   if (!x || !out) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
   if (!aligned16(x) || !aligned16(out)) return fail(TTN_INVALID_ARG, "%s: 16-byte alignment", name);
-  size_t smem = 2 * (size_t)h * w * 16 * 2;
+  const int64_t r = kernel / 2;
+  size_t smem = 2 * (size_t)(h + 2 * r) * (w + 2 * r) * 16 * 2;
   cudaStream_t s = (cudaStream_t)stream;
   if ((int64_t)smem > max_dynamic_smem()) {
     // Plane too large to hold twice: three chained pools through the output.
