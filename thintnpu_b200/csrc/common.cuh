@@ -45,6 +45,21 @@ ttn_status ensure_dynamic_smem(const void* kernel, int bytes);
 // Largest opt-in dynamic shared memory per block on the current device.
 int max_dynamic_smem();
 
+// Blocks of `kernel` (at `threads` threads, `smem` dynamic bytes) resident per SM
+// on the current device, from the occupancy calculator; cached per (device, kernel).
+int resident_blocks(const void* kernel, int threads, size_t smem);
+
+// Grid for a grid-stride loop that keeps every block resident (one full wave):
+// min(blocks the work needs, SMs x resident blocks per SM).
+template <typename Kernel>
+inline unsigned resident_grid(Kernel kernel, int threads, size_t smem, int64_t work,
+                              int64_t per_block) {
+  int64_t need = (work + per_block - 1) / per_block;
+  int64_t cap = (int64_t)sm_count() * resident_blocks((const void*)kernel, threads, smem);
+  if (need > cap) need = cap;
+  return (unsigned)(need < 1 ? 1 : need);
+}
+
 // Grid size for a grid-stride loop: enough blocks for `work` units of `per_block`,
 // capped at `waves` resident blocks per SM.
 inline unsigned grid_for(int64_t work, int64_t per_block, int waves = 8) {
@@ -205,20 +220,21 @@ __device__ __forceinline__ float sigmoid_fast_f32(float x) { return rcp_approx(1
 
 // Two fp16 lanes at once, deferring the exact decision: returns the fast fp16
 // pair and sets `unsafe` to a per-lane 0xffff mask where the result must come
-// from the exact routine instead -- where r*(1-2^-18) and r*(1+2^-18) round to
-// different fp16 values (r within ~16-32 fp32 ulps of a midpoint, any range), or
+// from the exact routine instead -- where r*(1-2^-19) and r*(1+2^-19) round to
+// different fp16 values (r within 16-32 fp32 ulps of a midpoint, any range), or
 // the input is +-inf/NaN (whose x86 results the fast formula does not give).
 template <bool kSilu>
-__device__ __forceinline__ uint32_t unary_h2_deferred(uint32_t packed, uint32_t& unsafe) {
+__device__ __forceinline__ uint32_t unary_h2_deferred(uint32_t packed, bool& unsafe) {
   __half2 h = *reinterpret_cast<__half2*>(&packed);
   float2 f = __half22float2(h);
   float r0 = kSilu ? silu_fast_f32(f.x) : sigmoid_fast_f32(f.x);
   float r1 = kSilu ? silu_fast_f32(f.y) : sigmoid_fast_f32(f.y);
   __half2 o = __floats2half2_rn(r0, r1);
-  __half2 up = __floats2half2_rn(r0 * 1.000003814697265625f, r1 * 1.000003814697265625f);
-  __half2 dn = __floats2half2_rn(r0 * 0.999996185302734375f, r1 * 0.999996185302734375f);
+  __half2 up = __floats2half2_rn(r0 * 1.0000019073486328125f, r1 * 1.0000019073486328125f);
+  __half2 dn = __floats2half2_rn(r0 * 0.9999980926513671875f, r1 * 0.9999980926513671875f);
   uint32_t uw = *reinterpret_cast<uint32_t*>(&up), dw = *reinterpret_cast<uint32_t*>(&dn);
-  unsafe = __vcmpne2(uw, dw) | __vcmpeq2(packed & 0x7c007c00u, 0x7c007c00u);
+  bool special = (packed & 0x7c00u) == 0x7c00u || (packed & 0x7c000000u) == 0x7c000000u;
+  unsafe = (uw != dw) | special;
   return *reinterpret_cast<uint32_t*>(&o);
 }
 

@@ -33,12 +33,21 @@ __device__ __forceinline__ uint4 unary_vec8(uint4 v) {
 
 // Dense fp16, 16-byte aligned: uint4 body plus a scalar tail.  x may equal y.
 // Warp-uniform loop: each lane owns two 16-byte vectors per step (32 bytes in
-// flight per lane).  Lanes whose fast results are not provably the CPU's fp16
-// value (about 1% of elements) queue (index, input bits) in shared memory; the
-// warp then recomputes the queued elements exactly, one element per lane, and
-// overwrites them -- so the exact path costs per flagged element, not per
-// diverged warp step.
-constexpr int kQueue = 64;  // entries per warp
+// flight per lane).  Pairs whose fast results are not provably the CPU's fp16
+// value (about 0.6% of pairs) queue (element, input bits) in a per-warp
+// shared-memory queue; the warp recomputes queued elements exactly, 32 at a time
+// with every lane busy, only when the queue fills and once at the end -- so the
+// exact path costs per flagged element instead of per diverged warp step.
+// Launches cover fewer than 2^32 elements (the host splits larger tensors).
+constexpr int kQueue = 128;  // entries per warp
+
+template <int K>
+__device__ __forceinline__ void drain_queue(const uint32_t* q_index, const uint16_t* q_bits, int count,
+                                            uint16_t* yh, int lane) {
+  __syncwarp();
+  for (int t = lane; t < count; t += 32) yh[q_index[t]] = unary_h<K>(q_bits[t]);
+  __syncwarp();
+}
 
 template <int K>
 __global__ void __launch_bounds__(kThreads) unary_f16_dense(const uint4* x, uint4* y,
@@ -46,60 +55,72 @@ __global__ void __launch_bounds__(kThreads) unary_f16_dense(const uint4* x, uint
                                                             uint16_t* yt, int tail) {
   __shared__ uint32_t q_index[kThreads / 32][kQueue];
   __shared__ uint16_t q_bits[kThreads / 32][kQueue];
+  __shared__ int q_count[kThreads / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
   const int64_t step = warps * 64;
   uint16_t* yh = reinterpret_cast<uint16_t*>(y);
+  if (lane == 0) q_count[warp] = 0;
+  __syncwarp();
+  int count = 0;  // warp-uniform copy of q_count[warp]
   for (int64_t base = ((int64_t)blockIdx.x * (kThreads / 32) + warp) * 64; base < nvec; base += step) {
     const int64_t i0 = base + lane, i1 = base + 32 + lane;
     uint4 a = i0 < nvec ? x[i0] : make_uint4(0, 0, 0, 0);
     uint4 b = i1 < nvec ? x[i1] : make_uint4(0, 0, 0, 0);
     uint32_t in[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    uint32_t out[8], bad[8];
-    uint32_t flags = 0;  // one bit per element of the two vectors
+    uint32_t out[8];
+    uint32_t flags = 0;  // one bit per fp16 pair (word) of the two vectors
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      out[k] = unary_h2_deferred<K == kSilu>(in[k], bad[k]);
-      flags |= ((bad[k] & 1u) | ((bad[k] >> 15) & 2u)) << (2 * k);
+      bool bad;
+      out[k] = unary_h2_deferred<K == kSilu>(in[k], bad);
+      flags |= bad ? (1u << k) : 0u;
     }
-    if (i0 >= nvec) flags &= 0xff00u;
-    if (i1 >= nvec) flags &= 0x00ffu;
+    if (i0 >= nvec) flags &= 0xf0u;
+    if (i1 >= nvec) flags &= 0x0fu;
     if (i0 < nvec) y[i0] = make_uint4(out[0], out[1], out[2], out[3]);
     if (i1 < nvec) y[i1] = make_uint4(out[4], out[5], out[6], out[7]);
-    if (__any_sync(0xffffffffu, flags != 0u)) {
-      // exclusive prefix of per-lane flag counts
-      int mine = __popc(flags), pos = mine;
+    const int mine = 2 * __popc(flags);
+    const int total = __reduce_add_sync(0xffffffffu, mine);
+    if (total == 0) continue;
+    if (count + total > kQueue) {  // make room
+      drain_queue<K>(q_index[warp], q_bits[warp], count, yh, lane);
+      if (lane == 0) q_count[warp] = 0;
+      __syncwarp();
+      count = 0;
+    }
+    if (total > kQueue) {  // pathological step: handle its pairs in place
+      __syncwarp();
+      for (uint32_t f = flags; f; f &= f - 1) {
+        int word = __ffs(f) - 1;
+        uint32_t bits = 0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        int v = __shfl_up_sync(0xffffffffu, pos, o);
-        if (lane >= o) pos += v;
+        for (int k = 0; k < 8; ++k) bits = word == k ? in[k] : bits;
+        int64_t e = (word < 4 ? i0 : i1) * 8 + (word & 3) * 2;
+        yh[e] = unary_h<K>((uint16_t)(bits & 0xffffu));
+        yh[e + 1] = unary_h<K>((uint16_t)(bits >> 16));
       }
-      const int total = __shfl_sync(0xffffffffu, pos, 31);
-      pos -= mine;
-      for (int done = 0; done < total; done += kQueue) {
-        uint32_t f = flags;
-        int slot = pos;
-        while (f) {
-          int bit = __ffs(f) - 1;
-          f &= f - 1;
-          if (slot >= done && slot < done + kQueue) {
-            int64_t vec = bit < 8 ? i0 : i1;
-            int e = bit & 7;
-            q_index[warp][slot - done] = (uint32_t)(vec * 8 + e - base * 8);
-            q_bits[warp][slot - done] = (uint16_t)(in[(bit >> 1)] >> ((bit & 1) * 16));
-          }
-          ++slot;
-        }
-        __syncwarp();
-        const int chunk = total - done < kQueue ? total - done : kQueue;
-        for (int t = lane; t < chunk; t += 32) {
-          uint16_t xb = q_bits[warp][t];
-          yh[base * 8 + q_index[warp][t]] = unary_h<K>(xb);
-        }
-        __syncwarp();
+      __syncwarp();
+      continue;
+    }
+    if (mine) {
+      int slot = atomicAdd(&q_count[warp], mine);
+      for (uint32_t f = flags; f; f &= f - 1) {
+        int word = __ffs(f) - 1;
+        uint32_t bits = 0;  // in[word] without a runtime register-array index
+#pragma unroll
+        for (int k = 0; k < 8; ++k) bits = word == k ? in[k] : bits;
+        uint32_t e = (uint32_t)((word < 4 ? i0 : i1) * 8 + (word & 3) * 2);
+        q_index[warp][slot] = e;
+        q_bits[warp][slot] = (uint16_t)(bits & 0xffffu);
+        q_index[warp][slot + 1] = e + 1;
+        q_bits[warp][slot + 1] = (uint16_t)(bits >> 16);
+        slot += 2;
       }
     }
+    count += total;
   }
+  drain_queue<K>(q_index[warp], q_bits[warp], count, yh, lane);
   if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = unary_h<K>(xt[threadIdx.x]);
 }
 
@@ -361,13 +382,22 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
   if (!c.numel) return TTN_OK;
   cudaStream_t s = (cudaStream_t)stream;
   if (x->dtype == TTN_F16 && dense(c, 2) && aligned16(x->data) && aligned16(y->data)) {
-    int64_t nvec = c.numel / 8;
-    int tail = (int)(c.numel - nvec * 8);
-    unsigned grid = grid_for(nvec ? nvec : 1, (int64_t)kThreads * 2, 6);
-    unary_f16_dense<K><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x->data, (uint4*)y->data, nvec, (const uint16_t*)x->data + nvec * 8,
-        (uint16_t*)y->data + nvec * 8, tail);
-    return launch_check(name);
+    const int64_t total_vec = c.numel / 8;
+    const int tail = (int)(c.numel - total_vec * 8);
+    const int64_t chunk = (int64_t)1 << 28;  // vectors per launch: 2^31 elements
+    for (int64_t v0 = 0; v0 < total_vec || (v0 == 0 && tail); v0 += chunk) {
+      int64_t nvec = total_vec - v0 < chunk ? total_vec - v0 : chunk;
+      bool last = v0 + chunk >= total_vec;
+      unsigned grid = resident_grid(unary_f16_dense<K>, kThreads, 0, nvec ? nvec : 1,
+                                    (int64_t)kThreads * 2);
+      unary_f16_dense<K><<<grid, kThreads, 0, s>>>(
+          (const uint4*)x->data + v0, (uint4*)y->data + v0, nvec,
+          (const uint16_t*)x->data + total_vec * 8, (uint16_t*)y->data + total_vec * 8,
+          last ? tail : 0);
+      TTN_TRY(launch_check(name));
+      if (last) break;
+    }
+    return TTN_OK;
   }
   Index6 ix;
   int64_t vpr;

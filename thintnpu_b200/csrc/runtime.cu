@@ -5,6 +5,7 @@
 
 #include <cstring>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <thread>
 
@@ -59,6 +60,23 @@ ttn_status ensure_dynamic_smem(const void* kernel, int bytes) {
                      "cudaFuncSetAttribute"));
   granted[key] = bytes;
   return TTN_OK;
+}
+
+int resident_blocks(const void* kernel, int threads, size_t smem) {
+  static std::mutex mutex;
+  static std::map<std::tuple<int, const void*, int, size_t>, int> cache;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return 1;
+  std::lock_guard<std::mutex> lock(mutex);
+  auto key = std::make_tuple(device, kernel, threads, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem) != cudaSuccess ||
+      blocks < 1)
+    blocks = 1;
+  cache[key] = blocks;
+  return blocks;
 }
 
 int max_dynamic_smem() {
