@@ -178,7 +178,8 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
 
-    import thintnpu_b200  # noqa: F401  (fails loudly without libttn.so)
+    import thintnpu_b200
+    thintnpu_b200.load()  # fails loudly without libttn.so
     from thintnpu_b200 import yolo
 
     plan = yolo.yolov8s_plan(args.imgsz)

@@ -23,7 +23,8 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def device():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
-    import thintnpu_b200  # noqa: F401  (fails loudly if libttn.so is missing)
+    import thintnpu_b200
+    thintnpu_b200.load()  # fails loudly if libttn.so is missing
     return torch.device("cuda", 0)
 
 

@@ -2,16 +2,19 @@
 
 ``libttn.so`` (include/ttn.h) is the product: hand-written kernels behind a
 C ABI.  This package binds it with ctypes and exposes the reference's
-``thin_backend`` operator surface on CUDA tensors.  Importing fails loudly when
-the library is missing -- there is no CPU or PyTorch fallback.
+``thin_backend`` operator surface on CUDA tensors.  The library loads on the
+first op call (or ``load()``) and a missing library raises ImportError -- there
+is no CPU or PyTorch fallback.
 """
 from . import _lib
-
-_lib.lib()
-
 from . import ops  # noqa: E402
 from .ops import (add, bias_silu_residual, cat, contiguous, copy_, detection_select,  # noqa: E402,F401
                   dfl_decode, div, maxpool2d, maxpool_blocked, mul, pack, sigmoid, silu, silu_,
                   softmax, sppf, sub, unpack, upsample_blocked, upsample_nearest2d)
 
 __version__ = "0.1.0"
+
+
+def load():
+    """Load libttn.so now (raises ImportError when it is missing or stale)."""
+    return _lib.lib()
