@@ -225,6 +225,18 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
                           void* workspace, size_t workspace_bytes, float* out,
                           const ttn_select_trace* trace, ttn_stream stream);
 
+/* Allocation-free variant of ttn_select_f16 for callers that cannot allocate
+ * device memory (e.g. bindings that only receive raw device pointers from
+ * another runtime, or loops that forbid allocation after start-up).  The scratch
+ * lives in an 8 MiB array compiled into the library (held by every GPU that
+ * loads it until exit); requests needing more (ttn_select_workspace_size) fail
+ * with TTN_UNSUPPORTED.  All calls share that array: calls whose kernels overlap
+ * on the GPU race, calls on one stream are safe.  The first call on a device
+ * resolves the array's address and should come before any stream capture.
+ * This entry point has no counterpart in the reference. */
+ttn_status ttn_select_f16_static(const ttn_tensor* decoded, int64_t max_det, uint32_t flags,
+                                 float* out, const ttn_select_trace* trace, ttn_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,72 @@
+"""GPU: the allocation-free selection entry point (ttn_select_f16_static).
+
+Callers that cannot allocate device memory -- bindings that only receive raw
+device pointers from another runtime, or loops that forbid allocation after
+start-up -- use this entry point; its scratch is an array compiled into the
+library.  Through the C ABI, two calls in a row must give exactly (bit for bit,
+the selection tolerance) what ttn_select_f16 gives with a caller-owned
+workspace; the second call runs on the scratch the first one left behind.
+This file is collected last so a stop-at-first-failure run has already run
+every other test; it also passes alone in a fresh process."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _logits(n: int, seed: int, anchors: int = 8400, nc: int = 80) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(n, 4 + nc, anchors, generator=g) * 2 - 4)
+    x[:, :4] = torch.rand(n, 4, anchors, generator=g) * 640
+    x = x.half()
+    x[:, 4:, :anchors // 50] = x[:, 4:, anchors // 50:2 * (anchors // 50)]  # exact ties
+    return x
+
+
+def _run(lib, fn_name, decoded, max_det, flags, use_static):
+    from thintnpu_b200 import _lib
+    from thintnpu_b200.ops import desc, stream
+    b, a, c = decoded.shape
+    k = min(max_det, a)
+    out = torch.full((b, k, 6), -1.0, dtype=torch.float32, device=decoded.device)
+    d = desc(decoded)
+    if use_static:
+        status = lib.ttn_select_f16_static(ctypes.byref(d), max_det, flags, out.data_ptr(), None,
+                                           stream())
+    else:
+        size = lib.ttn_select_workspace_size(b, a, c - 4, max_det, flags)
+        ws = torch.empty(size, dtype=torch.uint8, device=decoded.device)
+        status = lib.ttn_select_f16(ctypes.byref(d), max_det, flags, ws.data_ptr(), size,
+                                    out.data_ptr(), None, stream())
+    _lib.check(fn_name, status)
+    torch.cuda.synchronize()
+    return out.cpu().view(torch.int32).numpy()
+
+
+@pytest.mark.parametrize("flags", [0, 1, 4, 5])
+def test_static_scratch_matches_workspace_entry_point_twice(device, flags):
+    from thintnpu_b200 import _lib
+    lib = _lib.lib()
+    for call, (n, seed, max_det) in enumerate(((2, 31, 300), (3, 32, 513))):
+        decoded = _logits(n, seed).to(device).transpose(1, 2)  # [n, 8400, 84] view
+        want = _run(lib, "ttn_select_f16", decoded, max_det, flags, use_static=False)
+        got = _run(lib, "ttn_select_f16_static", decoded, max_det, flags, use_static=True)
+        assert np.array_equal(got, want), f"call {call + 1} differs"
+
+
+def test_static_scratch_rejects_oversized_batch(device):
+    from thintnpu_b200 import _lib
+    from thintnpu_b200.ops import desc, stream
+    lib = _lib.lib()
+    decoded = torch.zeros(1, 84, 8400, dtype=torch.float16, device=device).transpose(1, 2)
+    d = desc(decoded)
+    d.sizes[0] = 4096  # describes a batch too large for the static scratch; never launched
+    out = torch.empty(1, dtype=torch.float32, device=device)
+    status = lib.ttn_select_f16_static(ctypes.byref(d), 300, 0, out.data_ptr(), None, stream())
+    assert status == 2  # TTN_UNSUPPORTED
+    assert b"static scratch holds" in lib.ttn_last_error()

@@ -29,7 +29,7 @@ EXPORTS = (
     "ttn_copy", "ttn_cat", "ttn_nc1hwc0_to_nchw_f16", "ttn_nchw_to_nc1hwc0_f16",
     "ttn_upsample2x", "ttn_maxpool", "ttn_sppf_f16",
     "ttn_softmax", "ttn_dfl_decode_f16",
-    "ttn_select_workspace_size", "ttn_select_f16",
+    "ttn_select_workspace_size", "ttn_select_f16", "ttn_select_f16_static",
 )
 
 
@@ -92,6 +92,8 @@ _SIGNATURES = {
     "ttn_select_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, ctypes.c_uint32]),
     "ttn_select_f16": (ctypes.c_int, [_TP, _I64, ctypes.c_uint32, _P, ctypes.c_size_t, _P,
                                       ctypes.POINTER(SelectTrace), _P]),
+    "ttn_select_f16_static": (ctypes.c_int, [_TP, _I64, ctypes.c_uint32, _P,
+                                             ctypes.POINTER(SelectTrace), _P]),
 }
 
 _lib = None
