@@ -155,6 +155,14 @@ ttn_status ttn_nchw_to_nc1hwc0_f16(const void* x, int64_t n, int64_t channels,
 ttn_status ttn_upsample2x(int layout, int dtype, const void* x, void* y, int64_t n,
                           int64_t c, int64_t h, int64_t w, ttn_stream stream);
 
+/* Nearest 2x upsample of NC1HWC0 fp16 images that sit at batch strides
+ * (elements, multiples of 8) inside larger buffers -- e.g. writing straight into
+ * the neck concat's slice (whole_blocked.py:67-68 upsample, then ops.cpp:419
+ * cat, with the copy elided).  Image layout [c1, h, w, 16] -> [c1, 2h, 2w, 16]. */
+ttn_status ttn_upsample2x_nc1hwc0_f16(const void* x, int64_t x_batch_stride, void* y,
+                                      int64_t y_batch_stride, int64_t n, int64_t c1, int64_t h,
+                                      int64_t w, ttn_stream stream);
+
 /* kernel x kernel, stride 1, padding kernel/2 max-pool with -inf padding,
  * NaN-propagating (CPU F.max_pool2d semantics).  kernel odd, >= 1.
  * Layouts as ttn_upsample2x.  Replaces maxpool_impl maxpool.cpp:5-191,

@@ -57,3 +57,24 @@ def test_smaller_resolution_pass(device):
     assert_bits_equal(gpu.head, head, "head")
     _, stride_row = oops.make_anchors(plan.levels, plan.strides)
     _check_decode(out, want, stride_row, plan.nc)
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_concat_in_place_equals_op_by_op(device, batch):
+    """Zero-copy concat plan: same tensors, no concat kernels."""
+    from thintnpu_b200 import yolo
+    plan = yolo.yolov8s_plan(640)
+    inputs = yolo.synthetic_inputs(plan, batch, device, seed=11)
+    plain = yolo.OpPass(plan, inputs)
+    fused = yolo.OpPass(plan, inputs, concat_in_place=True)
+    assert len(fused.elided) == 12 and fused.launches_per_pass() == plain.launches_per_pass() - 12
+    plain.run()
+    fused.run()
+    for step in plan.steps:
+        if step.output is not None:
+            assert_bits_equal(fused.buffers[step.output], plain.buffers[step.output], step.output)
+    assert_bits_equal(fused.output, plain.output, "decoded")
+    fused.capture()
+    fused.replay()
+    torch.cuda.synchronize()
+    assert_bits_equal(fused.output, plain.output, "decoded after replay")

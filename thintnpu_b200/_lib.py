@@ -27,7 +27,7 @@ EXPORTS = (
     "ttn_silu", "ttn_sigmoid", "ttn_binary", "ttn_binary_scalar",
     "ttn_bias_silu_residual_nc1hwc0_f16",
     "ttn_copy", "ttn_cat", "ttn_nc1hwc0_to_nchw_f16", "ttn_nchw_to_nc1hwc0_f16",
-    "ttn_upsample2x", "ttn_maxpool", "ttn_sppf_f16",
+    "ttn_upsample2x", "ttn_upsample2x_nc1hwc0_f16", "ttn_maxpool", "ttn_sppf_f16",
     "ttn_softmax", "ttn_dfl_decode_f16",
     "ttn_select_workspace_size", "ttn_select_f16", "ttn_select_f16_static",
 )
@@ -83,6 +83,7 @@ _SIGNATURES = {
     "ttn_nc1hwc0_to_nchw_f16": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P]),
     "ttn_nchw_to_nc1hwc0_f16": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P]),
     "ttn_upsample2x": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    "ttn_upsample2x_nc1hwc0_f16": (ctypes.c_int, [_P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "ttn_maxpool": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _I32, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "ttn_sppf_f16": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _I64, _I32, _P]),
     "ttn_softmax": (ctypes.c_int, [_TP, _I32, ctypes.c_float, _TP, _P]),

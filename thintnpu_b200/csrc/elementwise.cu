@@ -32,96 +32,106 @@ __device__ __forceinline__ uint4 unary_vec8(uint4 v) {
 }
 
 // Dense fp16, 16-byte aligned: uint4 body plus a scalar tail.  x may equal y.
-// Warp-uniform loop: each lane owns two 16-byte vectors per step (32 bytes in
-// flight per lane).  Pairs whose fast results are not provably the CPU's fp16
-// value (about 0.6% of pairs) queue (element, input bits) in a per-warp
-// shared-memory queue; the warp recomputes queued elements exactly, 32 at a time
-// with every lane busy, only when the queue fills and once at the end -- so the
-// exact path costs per flagged element instead of per diverged warp step.
+// Warp-uniform loop: each lane owns four 16-byte vectors per step (64 bytes in
+// flight per lane).  A pair whose fast result is not provably the CPU's fp16
+// value (about 1.5% of pairs) is stored with its *input* bits unchanged and its
+// element indices go to a per-warp shared-memory queue; when the queue fills
+// (and once at the end) the warp re-reads those inputs and writes the exact
+// results, 32 elements at a time with every lane busy.  So the exact path costs
+// per flagged element rather than per diverged warp step, and works in place.
 // Launches cover fewer than 2^32 elements (the host splits larger tensors).
-constexpr int kQueue = 128;  // entries per warp
+constexpr int kQueue = 256;  // element entries per warp
+constexpr int kVec = 4;      // 16-byte vectors per lane per step
 
 template <int K>
-__device__ __forceinline__ void drain_queue(const uint32_t* q_index, const uint16_t* q_bits, int count,
-                                            uint16_t* yh, int lane) {
+__device__ __forceinline__ void drain_queue(const uint32_t* queue, int count, uint16_t* yh, int lane) {
   __syncwarp();
-  for (int t = lane; t < count; t += 32) yh[q_index[t]] = unary_h<K>(q_bits[t]);
+  for (int t = lane; t < count; t += 32) {
+    uint32_t e = queue[t];
+    yh[e] = unary_h<K>(yh[e]);  // yh[e] still holds the input bits (stored unchanged)
+  }
   __syncwarp();
 }
 
+// rows x vec_per_row 16-byte vectors; row r of x/y starts at the offsets that
+// `outer` gives for r (a single row at offset 0 for dense tensors).  blockIdx.y
+// walks rows, blockIdx.x / warps walk the vectors of a row.  Queue entries are
+// element offsets from y (the host keeps y's extent below 2^32 elements).
 template <int K>
-__global__ void __launch_bounds__(kThreads) unary_f16_dense(const uint4* x, uint4* y,
-                                                            int64_t nvec, const uint16_t* xt,
-                                                            uint16_t* yt, int tail) {
-  __shared__ uint32_t q_index[kThreads / 32][kQueue];
-  __shared__ uint16_t q_bits[kThreads / 32][kQueue];
+__global__ void __launch_bounds__(kThreads) unary_f16_vec(const uint16_t* x, uint16_t* y, Index6 outer,
+                                                          int64_t vec_per_row, int64_t rows,
+                                                          const uint16_t* xt, uint16_t* yt, int tail) {
+  __shared__ uint32_t queue[kThreads / 32][kQueue];
   __shared__ int q_count[kThreads / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
-  const int64_t step = warps * 64;
-  uint16_t* yh = reinterpret_cast<uint16_t*>(y);
+  const int64_t step = (int64_t)gridDim.x * (kThreads / 32) * 32 * kVec;
   if (lane == 0) q_count[warp] = 0;
   __syncwarp();
   int count = 0;  // warp-uniform copy of q_count[warp]
-  for (int64_t base = ((int64_t)blockIdx.x * (kThreads / 32) + warp) * 64; base < nvec; base += step) {
-    const int64_t i0 = base + lane, i1 = base + 32 + lane;
-    uint4 a = i0 < nvec ? x[i0] : make_uint4(0, 0, 0, 0);
-    uint4 b = i1 < nvec ? x[i1] : make_uint4(0, 0, 0, 0);
-    uint32_t in[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    uint32_t out[8];
-    uint32_t flags = 0;  // one bit per fp16 pair (word) of the two vectors
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    int64_t ox = 0, oy = 0, unused;
+    if (outer.ndim) offsets3(outer, row, ox, oy, unused);
+    const uint4* xs = reinterpret_cast<const uint4*>(x + ox);
+    uint4* ys = reinterpret_cast<uint4*>(y + oy);
+    for (int64_t base = ((int64_t)blockIdx.x * (kThreads / 32) + warp) * 32 * kVec; base < vec_per_row;
+         base += step) {
+      uint4 v[kVec];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      bool bad;
-      out[k] = unary_h2_deferred<K == kSilu>(in[k], bad);
-      flags |= bad ? (1u << k) : 0u;
-    }
-    if (i0 >= nvec) flags &= 0xf0u;
-    if (i1 >= nvec) flags &= 0x0fu;
-    if (i0 < nvec) y[i0] = make_uint4(out[0], out[1], out[2], out[3]);
-    if (i1 < nvec) y[i1] = make_uint4(out[4], out[5], out[6], out[7]);
-    const int mine = 2 * __popc(flags);
-    const int total = __reduce_add_sync(0xffffffffu, mine);
-    if (total == 0) continue;
-    if (count + total > kQueue) {  // make room
-      drain_queue<K>(q_index[warp], q_bits[warp], count, yh, lane);
-      if (lane == 0) q_count[warp] = 0;
-      __syncwarp();
-      count = 0;
-    }
-    if (total > kQueue) {  // pathological step: handle its pairs in place
-      __syncwarp();
-      for (uint32_t f = flags; f; f &= f - 1) {
-        int word = __ffs(f) - 1;
-        uint32_t bits = 0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) bits = word == k ? in[k] : bits;
-        int64_t e = (word < 4 ? i0 : i1) * 8 + (word & 3) * 2;
-        yh[e] = unary_h<K>((uint16_t)(bits & 0xffffu));
-        yh[e + 1] = unary_h<K>((uint16_t)(bits >> 16));
+      for (int u = 0; u < kVec; ++u) {
+        int64_t i = base + u * 32 + lane;
+        v[u] = i < vec_per_row ? xs[i] : make_uint4(0, 0, 0, 0);
       }
-      __syncwarp();
-      continue;
-    }
-    if (mine) {
-      int slot = atomicAdd(&q_count[warp], mine);
-      for (uint32_t f = flags; f; f &= f - 1) {
-        int word = __ffs(f) - 1;
-        uint32_t bits = 0;  // in[word] without a runtime register-array index
+      uint32_t flags = 0;  // bit (4u + w): word w of vector u needs the exact routine
 #pragma unroll
-        for (int k = 0; k < 8; ++k) bits = word == k ? in[k] : bits;
-        uint32_t e = (uint32_t)((word < 4 ? i0 : i1) * 8 + (word & 3) * 2);
-        q_index[warp][slot] = e;
-        q_bits[warp][slot] = (uint16_t)(bits & 0xffffu);
-        q_index[warp][slot + 1] = e + 1;
-        q_bits[warp][slot + 1] = (uint16_t)(bits >> 16);
-        slot += 2;
+      for (int u = 0; u < kVec; ++u) {
+        uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          bool bad;
+          uint32_t r = unary_h2_deferred<K == kSilu>(w[k], bad);
+          w[k] = bad ? w[k] : r;  // flagged pairs keep their input bits for the exact pass
+          flags |= bad ? (1u << (4 * u + k)) : 0u;
+        }
+        int64_t i = base + u * 32 + lane;
+        if (i < vec_per_row) ys[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        else flags &= ~(0xfu << (4 * u));
       }
+      const int mine = 2 * __popc(flags);
+      const int total = __reduce_add_sync(0xffffffffu, mine);
+      if (total == 0) continue;
+      if (count + total > kQueue) {  // make room
+        drain_queue<K>(queue[warp], count, y, lane);
+        if (lane == 0) q_count[warp] = 0;
+        __syncwarp();
+        count = 0;
+      }
+      if (total > kQueue) {  // pathological step: finish its pairs right away
+        __syncwarp();
+        for (uint32_t f = flags; f; f &= f - 1) {
+          int bit = __ffs(f) - 1;
+          int64_t e = oy + (base + (bit >> 2) * 32 + lane) * 8 + (bit & 3) * 2;
+          y[e] = unary_h<K>(y[e]);
+          y[e + 1] = unary_h<K>(y[e + 1]);
+        }
+        __syncwarp();
+        continue;
+      }
+      if (mine) {
+        int slot = atomicAdd(&q_count[warp], mine);
+        for (uint32_t f = flags; f; f &= f - 1) {
+          int bit = __ffs(f) - 1;
+          uint32_t e = (uint32_t)(oy + (base + (bit >> 2) * 32 + lane) * 8 + (bit & 3) * 2);
+          queue[warp][slot] = e;
+          queue[warp][slot + 1] = e + 1;
+          slot += 2;
+        }
+      }
+      count += total;
     }
-    count += total;
   }
-  drain_queue<K>(q_index[warp], q_bits[warp], count, yh, lane);
-  if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = unary_h<K>(xt[threadIdx.x]);
+  drain_queue<K>(queue[warp], count, y, lane);
+  if (blockIdx.x == 0 && blockIdx.y == 0 && (int)threadIdx.x < tail)
+    yt[threadIdx.x] = unary_h<K>(xt[threadIdx.x]);
 }
 
 // Any layout (also unaligned dense), one element per thread.
@@ -142,21 +152,6 @@ __global__ void __launch_bounds__(kThreads) unary_strided(const T* x, T* y, Inde
 // Rows of dense fp16 (e.g. channel-block chunks of NC1HWC0 batches): the
 // innermost coalesced dim is unit-stride with a multiple of 8 elements and
 // every outer stride is a multiple of 8, so 16-byte vectors still apply.
-template <int K>
-__global__ void __launch_bounds__(kThreads) unary_f16_rows(const uint16_t* x, uint16_t* y,
-                                                           Index6 outer, int64_t vec_per_row,
-                                                           int64_t rows) {
-  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-    int64_t ox, oy, unused;
-    offsets3(outer, row, ox, oy, unused);  // once per block row
-    const uint4* xs = reinterpret_cast<const uint4*>(x + ox);
-    uint4* ys = reinterpret_cast<uint4*>(y + oy);
-    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < vec_per_row;
-         v += (int64_t)gridDim.x * blockDim.x)
-      ys[v] = unary_vec8<K>(xs[v]);
-  }
-}
-
 // ---------------------------------------------------------------- binary
 
 // CPU eager semantics per op (FP32 opmath, x86 IEEE): add/sub use one rounding
@@ -348,6 +343,13 @@ bool vec_rows(const Coalesced& c, int count, const void* const* ptrs, Index6& ou
   return true;
 }
 
+// True when the largest element offset of operand v is below 2^32.
+bool extent_below_2_32(const Coalesced& c, int v) {
+  int64_t extent = 0;
+  for (int d = 0; d < c.ndim; ++d) extent += (c.size[d] - 1) * (c.stride[v][d] < 0 ? -c.stride[v][d] : c.stride[v][d]);
+  return extent < ((int64_t)1 << 32) - 8;
+}
+
 // 2-D grid for row kernels: y over rows (<= 65535 per pass), x over the
 // vectors of a row, about 8 resident blocks per SM in total.
 dim3 rows_grid(int64_t vec_per_row, int64_t rows) {
@@ -385,13 +387,15 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
     const int64_t total_vec = c.numel / 8;
     const int tail = (int)(c.numel - total_vec * 8);
     const int64_t chunk = (int64_t)1 << 28;  // vectors per launch: 2^31 elements
+    Index6 none;
+    none.ndim = 0;
     for (int64_t v0 = 0; v0 < total_vec || (v0 == 0 && tail); v0 += chunk) {
       int64_t nvec = total_vec - v0 < chunk ? total_vec - v0 : chunk;
       bool last = v0 + chunk >= total_vec;
-      unsigned grid = resident_grid(unary_f16_dense<K>, kThreads, 0, nvec ? nvec : 1,
-                                    (int64_t)kThreads * 2);
-      unary_f16_dense<K><<<grid, kThreads, 0, s>>>(
-          (const uint4*)x->data + v0, (uint4*)y->data + v0, nvec,
+      unsigned grid = resident_grid(unary_f16_vec<K>, kThreads, 0, nvec ? nvec : 1,
+                                    (int64_t)kThreads * kVec);
+      unary_f16_vec<K><<<grid, kThreads, 0, s>>>(
+          (const uint16_t*)x->data + v0 * 8, (uint16_t*)y->data + v0 * 8, none, nvec, 1,
           (const uint16_t*)x->data + total_vec * 8, (uint16_t*)y->data + total_vec * 8,
           last ? tail : 0);
       TTN_TRY(launch_check(name));
@@ -402,10 +406,16 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
   Index6 ix;
   int64_t vpr;
   const void* ptrs[2] = {x->data, y->data};
-  if (x->dtype == TTN_F16 && vec_rows(c, 2, ptrs, ix, vpr)) {
-    dim3 grid = rows_grid(vpr, c.numel / 8 / vpr);
-    unary_f16_rows<K><<<grid, kThreads, 0, s>>>((const uint16_t*)x->data, (uint16_t*)y->data, ix,
-                                                vpr, c.numel / 8 / vpr);
+  if (x->dtype == TTN_F16 && vec_rows(c, 2, ptrs, ix, vpr) && extent_below_2_32(c, 1)) {
+    const int64_t rows = c.numel / 8 / vpr;
+    int64_t cap = (int64_t)sm_count() * resident_blocks((const void*)unary_f16_vec<K>, kThreads, 0);
+    int64_t gy = rows < 65535 ? rows : 65535;
+    int64_t gx = (vpr + kThreads * kVec - 1) / (kThreads * kVec);
+    int64_t fit = (cap + gy - 1) / gy;
+    if (gx > fit) gx = fit;
+    if (gx < 1) gx = 1;
+    unary_f16_vec<K><<<dim3((unsigned)gx, (unsigned)gy), kThreads, 0, s>>>(
+        (const uint16_t*)x->data, (uint16_t*)y->data, ix, vpr, rows, nullptr, nullptr, 0);
     return launch_check(name);
   }
   TTN_TRY(to_index6(c, 2, ix, name));

@@ -98,19 +98,23 @@ __global__ void __launch_bounds__(128) nchw_to_blocked(const uint16_t* x, int64_
 
 // ------------------------------------------------------------- upsample
 
-// NC1HWC0 (and any layout whose innermost group is 16 bytes wide per half-pixel):
-// each input 16-byte vector is written to the 4 output pixels it covers.
-__global__ void __launch_bounds__(256) upsample_blocked(const uint4* x, uint4* y, int64_t planes,
-                                                        int64_t h, int64_t w) {
-  const int64_t nvec = planes * h * w * 2;
+// NC1HWC0: each input 16-byte vector (half a pixel's 16 lanes) is written to the
+// 4 output pixels it covers.  Images may sit at any 16-byte-multiple batch
+// stride (x_bs, y_bs in uint4 units), e.g. inside a concat buffer.
+__global__ void __launch_bounds__(256) upsample_blocked(const uint4* x, uint4* y, int64_t n,
+                                                        int64_t c1, int64_t h, int64_t w,
+                                                        int64_t x_bs, int64_t y_bs) {
+  const int64_t per_image = c1 * h * w * 2;
+  const int64_t nvec = n * per_image;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
-    uint4 q = x[v];
-    int64_t p = v >> 1;
-    int j = (int)(v & 1);
+    int64_t b = v / per_image, local = v - b * per_image;
+    uint4 q = x[b * x_bs + local];
+    int64_t p = local >> 1;
+    int j = (int)(local & 1);
     int64_t col = p % w, rest = p / w;
     int64_t row = rest % h, plane = rest / h;
-    int64_t base = ((plane * 2 * h + 2 * row) * 2 * w + 2 * col) * 2 + j;
+    int64_t base = b * y_bs + ((plane * 2 * h + 2 * row) * 2 * w + 2 * col) * 2 + j;
     y[base] = q;
     y[base + 2] = q;
     y[base + 4 * w] = q;
@@ -384,7 +388,8 @@ ttn_status ttn_upsample2x(int layout, int dtype, const void* x, void* y, int64_t
     if (dtype != TTN_F16) return fail(TTN_UNSUPPORTED, "%s: NC1HWC0 supports float16", name);
     if (!aligned16(x) || !aligned16(y)) return fail(TTN_INVALID_ARG, "%s: 16-byte alignment", name);
     int64_t nvec = n * c * h * w * 2;
-    upsample_blocked<<<grid_for(nvec, 256), 256, 0, s>>>((const uint4*)x, (uint4*)y, n * c, h, w);
+    upsample_blocked<<<grid_for(nvec, 256), 256, 0, s>>>((const uint4*)x, (uint4*)y, n, c, h, w,
+                                                         c * h * w * 2, c * h * w * 8);
     return launch_check(name);
   }
   if (dtype == TTN_F16 && w % 4 == 0 && aligned16(y) && ((uintptr_t)x & 7u) == 0) {
@@ -398,6 +403,23 @@ ttn_status ttn_upsample2x(int layout, int dtype, const void* x, void* y, int64_t
     upsample_nchw_scalar<uint32_t><<<grid_for(n * c * h * w * 4, 256), 256, 0, s>>>(
         (const uint32_t*)x, (uint32_t*)y, n * c, h, w);
   }
+  return launch_check(name);
+}
+
+ttn_status ttn_upsample2x_nc1hwc0_f16(const void* x, int64_t x_batch_stride, void* y,
+                                      int64_t y_batch_stride, int64_t n, int64_t c1, int64_t h,
+                                      int64_t w, ttn_stream stream) {
+  const char* name = "ttn_upsample2x_nc1hwc0_f16";
+  if (n < 0 || c1 < 0 || h < 0 || w < 0) return fail(TTN_INVALID_ARG, "%s: negative size", name);
+  if (!n || !c1 || !h || !w) return TTN_OK;
+  if (!x || !y) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned16(x) || !aligned16(y) || x_batch_stride % 8 || y_batch_stride % 8)
+    return fail(TTN_INVALID_ARG, "%s: pointers and batch strides must be 16-byte multiples", name);
+  if (x_batch_stride < c1 * h * w * 16 || y_batch_stride < c1 * h * w * 64)
+    return fail(TTN_INVALID_ARG, "%s: batch stride smaller than one image", name);
+  int64_t nvec = n * c1 * h * w * 2;
+  upsample_blocked<<<grid_for(nvec, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const uint4*)x, (uint4*)y, n, c1, h, w, x_batch_stride / 8, y_batch_stride / 8);
   return launch_check(name);
 }
 

@@ -256,13 +256,32 @@ def _blocked(x: torch.Tensor, what: str) -> None:
 
 
 def upsample_blocked(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Nearest 2x on NC1HWC0 (reference blocked_flow::upsample, flow_ops.cpp:233-252)."""
-    _blocked(x, "upsample")
+    """Nearest 2x on NC1HWC0 (reference blocked_flow::upsample, flow_ops.cpp:233-252).
+
+    ``x`` and ``out`` may be batch-strided views (each image dense), e.g. a slice
+    of a concat buffer along C1."""
+    _cuda(x, "upsample")
+    _require(x.dim() == 5 and x.size(4) == 16 and x.dtype == torch.float16,
+             "expected aligned contiguous FP16 NC1HWC0 input, C0=16")
+    _require(x.size(1) > 0 and x.size(2) > 0 and x.size(3) > 0,
+             "blocked spatial operators require positive C1/H/W")
     n, c1, h, w, _ = x.shape
     y = torch.empty((n, c1, 2 * h, 2 * w, 16), dtype=x.dtype, device=x.device) if out is None else out
-    _require(tuple(y.shape) == (n, c1, 2 * h, 2 * w, 16) and y.is_contiguous(), "upsample: bad out")
-    call("ttn_upsample2x", _lib.NC1HWC0, _lib.F16, x.data_ptr(), y.data_ptr(), n, c1, h, w, stream())
+    _require(tuple(y.shape) == (n, c1, 2 * h, 2 * w, 16), "upsample: bad out shape")
+    _require(_image_dense(x) and _image_dense(y), "upsample: each image must be dense")
+    call("ttn_upsample2x_nc1hwc0_f16", x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), n, c1, h, w,
+         stream())
     return y
+
+
+def _image_dense(t: torch.Tensor) -> bool:
+    """True when every image (dims 1..) of t is a dense row-major block."""
+    expect = 1
+    for d in range(t.dim() - 1, 0, -1):
+        if t.size(d) != 1 and t.stride(d) != expect:
+            return False
+        expect *= t.size(d)
+    return True
 
 
 def maxpool_blocked(x: torch.Tensor, kernel: int) -> torch.Tensor:

@@ -229,25 +229,72 @@ def synthetic_inputs(plan: Plan, batch: int, device, seed: int = 4) -> Dict[str,
     return out
 
 
+def concat_placements(plan: Plan):
+    """Zero-copy concat plan: for every concat whose inputs are all whole outputs
+    of SiLU / residual-add / upsample steps (a C2f ``chunk`` half counts as part of
+    its producer), place each producer's output as a C1 slice of the concat
+    buffer so it writes there directly, and drop the concat step.
+
+    Returns ({producer: (concat, block offset)}, {elided concat outputs})."""
+    producers = {st.output: st for st in plan.steps if st.output is not None}
+    placed, elided = {}, set()
+    for st in plan.steps:
+        if st.op != "cat":
+            continue
+        local, offset, ok = {}, 0, True
+        for ref in st.inputs:
+            prod = producers.get(ref.name)
+            if prod is None or prod.op not in ("silu", "add", "upsample") or ref.name in placed:
+                ok = False
+                break
+            pos = offset - ref.start
+            if local.setdefault(ref.name, pos) != pos:
+                ok = False
+                break
+            offset += ref.count
+        if ok:  # placed buffers must tile the concat exactly
+            spans = sorted((pos, pos + plan.shapes[name][0]) for name, pos in local.items())
+            ok = spans[0][0] == 0 and spans[-1][1] == plan.shapes[st.output][0] and all(
+                a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        if ok:
+            for name, pos in local.items():
+                placed[name] = (st.output, pos)
+            elided.add(st.output)
+    return placed, elided
+
+
 class OpPass:
     """Executes a Plan on one CUDA device with preallocated buffers.
 
     ``inputs`` maps conv names to [B, c1, h, w, 16] fp16 CUDA tensors (kept
     intact: SiLU writes separate activation buffers, so every run of the pass
     -- and every CUDA-graph replay -- computes the same outputs).
-    ``output`` is the decoded [B, 4+nc, anchors] fp16 tensor."""
+    ``output`` is the decoded [B, 4+nc, anchors] fp16 tensor.
 
-    def __init__(self, plan: Plan, inputs: Dict[str, torch.Tensor]):
+    ``concat_in_place`` turns on the zero-copy concat plan (concat_placements):
+    the same tensors result, every concat buffer filled by its producers."""
+
+    def __init__(self, plan: Plan, inputs: Dict[str, torch.Tensor], concat_in_place: bool = False):
         self.plan = plan
         first = inputs[plan.conv_inputs[0]]
         self.batch = first.size(0)
         self.device = first.device
         self.buffers: Dict[str, torch.Tensor] = dict(inputs)
+        self.placed, self.elided = concat_placements(plan) if concat_in_place else ({}, set())
+
+        def alloc(name):
+            c1, h, w = plan.shapes[name]
+            return torch.empty((self.batch, c1, h, w, C0), dtype=torch.float16, device=self.device)
+
+        for name in self.elided:
+            self.buffers[name] = alloc(name)
+        for name, (cat, pos) in self.placed.items():
+            c1 = plan.shapes[name][0]
+            self.buffers[name] = self.buffers[cat][:, pos:pos + c1]
         for step in plan.steps:
             if step.output is not None and step.output not in self.buffers:
-                c1, h, w = plan.shapes[step.output]
-                self.buffers[step.output] = torch.empty((self.batch, c1, h, w, C0),
-                                                        dtype=torch.float16, device=self.device)
+                self.buffers[step.output] = alloc(step.output)
+        self.steps = [st for st in plan.steps if not (st.op == "cat" and st.output in self.elided)]
         self.head = torch.empty((self.batch, 64 + plan.nc, plan.anchors), dtype=torch.float16,
                                 device=self.device)
         self.output = torch.empty((self.batch, 4 + plan.nc, plan.anchors), dtype=torch.float16,
@@ -284,7 +331,7 @@ class OpPass:
             raise ValueError(step.op)
 
     def run(self) -> torch.Tensor:
-        for step in self.plan.steps:
+        for step in self.steps:
             self.run_step(step)
         return self.output
 
@@ -310,4 +357,4 @@ class OpPass:
 
     def launches_per_pass(self) -> int:
         """Kernels one pass launches (one per step; every op is a single kernel)."""
-        return len(self.plan.steps)
+        return len(self.steps)
