@@ -395,7 +395,7 @@ def workspace_size(batch: int, anchors: int, classes: int, max_det: int, flags: 
 
 def detection_select(decoded: torch.Tensor, max_det: int, agnostic: bool = False, *,
                      nan_last: bool = False, apply_sigmoid: bool = False, trace: bool = False,
-                     workspace: Optional[torch.Tensor] = None):
+                     workspace: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):
     """YOLO26 stable top-k selection (reference detection_selection::run, selection_flow.cpp:429-491).
 
     decoded: fp16 [B, A, 4+nc] view (boxes then scores).  Returns FP32
@@ -410,7 +410,9 @@ def detection_select(decoded: torch.Tensor, max_det: int, agnostic: bool = False
     flags = ((_lib.SELECT_AGNOSTIC if agnostic else 0) | (_lib.SELECT_NAN_LAST if nan_last else 0)
              | (_lib.SELECT_SIGMOID if apply_sigmoid else 0))
     dev = decoded.device
-    output = torch.empty((b, k, 6), dtype=torch.float32, device=dev)
+    output = torch.empty((b, k, 6), dtype=torch.float32, device=dev) if out is None else out
+    _require(tuple(output.shape) == (b, k, 6) and output.dtype == torch.float32 and output.is_contiguous(),
+             "detection_select: out must be contiguous float32 [B, k, 6]")
     tr = _lib.SelectTrace()
     tensors = None
     if trace:
