@@ -176,14 +176,10 @@ def main():
     import torch
     import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from thintnpu_b200 import shard
+    rank, world, local = shard.init("nccl", timeout_s=600)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
 
     import thintnpu_b200
     thintnpu_b200.load()  # fails loudly without libttn.so
@@ -199,14 +195,11 @@ def main():
             dist.barrier()
 
     def max_over_ranks(value: float) -> float:
-        if world == 1:
-            return value
-        t = torch.tensor([value], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(value, device)
 
-    # --- inputs resident in HBM; each rank owns images [rank*B, (rank+1)*B)
-    inputs = yolo.synthetic_inputs(plan, args.batch, device, seed=4 + 1000 * rank)
+    # --- inputs resident in HBM; rank r owns images shard_range(world*B, world, r)
+    images_mine = shard.shard_range(world * args.batch, world, rank)
+    inputs = yolo.synthetic_inputs(plan, len(images_mine), device, seed=4 + images_mine.start)
     op_pass = yolo.OpPass(plan, inputs)
     op_pass.capture(warmup=2)
     stream = torch.cuda.current_stream(device)

@@ -140,6 +140,137 @@ __global__ void __launch_bounds__(256) class_max_planar8(SelectView v, bool nan_
   }
 }
 
+// Fused-sigmoid class max (TTN_SELECT_SIGMOID), planar scores.  fp16 sigmoid
+// is monotone non-decreasing, so the best sigmoid key belongs to the best logit
+// key; only ties in the *sigmoid* value can move the winner to a lower class
+// index (distinct logits that round to one fp16 sigmoid).  Pass 1 keeps the best
+// and second-best logit keys per anchor (no sigmoid at all); the winner is final
+// unless sigmoid(second) has the winner's sigmoid key, in which case the warp
+// rescans that anchor's classes with the exact sigmoid, lanes over classes.
+__device__ __forceinline__ uint16_t bits_of_key(uint32_t key, bool nan_last) {
+  // a representative fp16 value with this key (+0 for the +-0 key, a NaN for the
+  // NaN key): its sigmoid has the key every value with this key has.
+  if (key == (nan_last ? 0xffffu : 0u)) return 0x7e00u;
+  if (key == 0x7fffu) return 0u;
+  return (key & 0x8000u) ? (uint16_t)key : (uint16_t)(0x7fffu - key);
+}
+
+__device__ __forceinline__ void rescan_anchor(const SelectView& v, int64_t b, int64_t a, bool nan_last,
+                                              uint32_t& out_bits, uint32_t& out_cls) {
+  const int lane = threadIdx.x & 31;
+  const uint16_t* p = v.base + b * v.sb + a * v.sa + 4 * v.sc;
+  uint32_t best = kInvalidKey, best_cls = 0xffffffffu, best_bits = 0;
+  for (int64_t c = lane; c < v.classes; c += 32) {
+    uint16_t bits = sigmoid_h_fast(p[c * v.sc]);
+    uint32_t key = score_key(bits, nan_last);
+    if (key < best) {
+      best = key;
+      best_cls = (uint32_t)c;
+      best_bits = bits;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    uint32_t ok = __shfl_xor_sync(0xffffffffu, best, o);
+    uint32_t oc = __shfl_xor_sync(0xffffffffu, best_cls, o);
+    uint32_t ob = __shfl_xor_sync(0xffffffffu, best_bits, o);
+    if (ok < best || (ok == best && oc < best_cls)) {
+      best = ok;
+      best_cls = oc;
+      best_bits = ob;
+    }
+  }
+  out_bits = best_bits;
+  out_cls = best_cls;
+}
+
+__global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, bool nan_last,
+                                                                 uint32_t* records, int64_t rec_pitch,
+                                                                 uint16_t* trace_max) {
+  const int lane = threadIdx.x & 31;
+  const int64_t groups = v.anchors / 8;
+  const int64_t total = v.batch * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  // warp-uniform trip count so the rescan can use the whole warp
+  for (int64_t t0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); t0 < total; t0 += stride) {
+    const int64_t t = t0 + lane;
+    const bool live = t < total;
+    const int64_t b = live ? t / groups : 0, a0 = live ? (t % groups) * 8 : 0;
+    uint32_t best[8], second[8], cls8[8], raw8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      best[j] = kInvalidKey;
+      second[j] = kInvalidKey;
+      cls8[j] = 0;
+      raw8[j] = 0;
+    }
+    if (live) {
+      const uint16_t* p = v.base + b * v.sb + a0 + 4 * v.sc;
+      for (int64_t c = 0; c < v.classes; ++c) {
+        uint4 q = *reinterpret_cast<const uint4*>(p + c * v.sc);
+        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint16_t bits = (uint16_t)((w[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+          uint32_t key = score_key(bits, nan_last);
+          if (key < best[j]) {
+            second[j] = best[j];
+            best[j] = key;
+            cls8[j] = (uint32_t)c;
+            raw8[j] = bits;
+          } else if (key < second[j]) {
+            second[j] = key;
+          }
+        }
+      }
+    }
+    uint32_t out_bits[8], tie = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint16_t s1 = sigmoid_h_fast((uint16_t)raw8[j]);
+      out_bits[j] = s1;
+      if (live && second[j] != kInvalidKey) {
+        uint16_t s2 = sigmoid_h_fast(bits_of_key(second[j], nan_last));
+        if (score_key(s2, nan_last) == score_key(s1, nan_last)) tie |= 1u << j;
+      }
+    }
+    // exact rescans of tied anchors, one anchor at a time with the whole warp
+    uint32_t pending = __ballot_sync(0xffffffffu, tie != 0);
+    while (pending) {
+      const int src = __ffs(pending) - 1;
+      uint32_t src_tie = __shfl_sync(0xffffffffu, tie, src);
+      const int64_t sb = __shfl_sync(0xffffffffu, b, src), sa0 = __shfl_sync(0xffffffffu, a0, src);
+      while (src_tie) {
+        const int j = __ffs(src_tie) - 1;
+        src_tie &= src_tie - 1;
+        uint32_t rb, rc;
+        rescan_anchor(v, sb, sa0 + j, nan_last, rb, rc);
+        if (lane == src) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (k == j) {
+              out_bits[k] = rb;
+              cls8[k] = rc;
+            }
+        }
+      }
+      pending &= pending - 1;
+    }
+    if (live) {
+      uint32_t out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = out_bits[j] | (cls8[j] << 16);
+      uint4* dst = reinterpret_cast<uint4*>(records + b * rec_pitch + a0);
+      dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+      dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+      if (trace_max) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) trace_max[b * v.anchors + a0 + j] = (uint16_t)out_bits[j];
+      }
+    }
+  }
+}
+
 // Class-contiguous rows (class stride 1): one warp per anchor, lanes over
 // classes, (key, class) lexicographic warp reduction.
 __global__ void __launch_bounds__(256) class_max_warp(SelectView v, bool nan_last, bool sigmoid,
@@ -570,7 +701,11 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
   // 1. class max
   bool planar = v.sa == 1 && v.anchors % 8 == 0 && v.sb % 8 == 0 && v.sc % 8 == 0 &&
                 ((uintptr_t)(v.base + 4 * v.sc) & 15u) == 0;
-  if (planar) {
+  if (planar && sigmoid) {
+    int64_t work = v.batch * (v.anchors / 8);
+    class_max_planar8_sigmoid<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, records, v.anchors,
+                                                                     tr.class_max);
+  } else if (planar) {
     int64_t work = v.batch * (v.anchors / 8);
     class_max_planar8<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, sigmoid, records,
                                                              v.anchors, tr.class_max);

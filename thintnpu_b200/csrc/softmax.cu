@@ -15,6 +15,24 @@ namespace {
 
 __device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b != b) ? b : a; }
 
+// Row max for softmax.  A plain max is enough: a NaN anywhere in the row, an
+// +inf (inf - inf), or an all -inf row (-inf - -inf) makes the sum NaN, so the
+// whole row comes out NaN exactly as CPU eager's three passes produce.
+__device__ __forceinline__ float row_max(float a, float b) { return fmaxf(a, b); }
+
+// exp(v - m) as ex2 of v*log2e - m*log2e, with m*log2e carried as hi + lo so the
+// argument keeps full precision even for |m| in the thousands.
+struct ShiftLog2 {
+  float hi, lo;
+};
+__device__ __forceinline__ ShiftLog2 shift_log2(float m) {
+  float hi = m * 1.44269504088896341f;
+  return {hi, __fmaf_rn(m, 1.44269504088896341f, -hi)};
+}
+__device__ __forceinline__ float exp_shifted(float v, ShiftLog2 ml) {
+  return ex2_approx(__fmaf_rn(v, 1.44269504088896341f, -ml.hi) - ml.lo);
+}
+
 template <typename T>
 __device__ __forceinline__ float load_scaled(const T* p, int64_t off, float scale, bool scaled) {
   if constexpr (sizeof(T) == 2) {
@@ -125,12 +143,13 @@ __global__ void __launch_bounds__(256) softmax_warp_rows_h8(const uint16_t* x, u
           }
           v[k][2 * j] = f.x;
           v[k][2 * j + 1] = f.y;
-          m = nan_max(nan_max(m, f.x), f.y);
+          m = row_max(row_max(m, f.x), f.y);
         }
       }
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) m = nan_max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    for (int o = 16; o; o >>= 1) m = row_max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const ShiftLog2 ml = shift_log2(m);
     float s = 0.0f;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
@@ -138,7 +157,7 @@ __global__ void __launch_bounds__(256) softmax_warp_rows_h8(const uint16_t* x, u
       if (e < nvec) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          v[k][j] = exp_fast(__fsub_rn(v[k][j], m));
+          v[k][j] = exp_shifted(v[k][j], ml);
           s = __fadd_rn(s, v[k][j]);
         }
       }
@@ -354,13 +373,15 @@ __global__ void __launch_bounds__(256) dfl_decode_tiled(const __half* box, int64
   __shared__ __align__(16) uint16_t io_cls[NC_MAX][kTileA];
   __shared__ float dist[4][kTileA];
   __shared__ __align__(16) uint16_t out_box[4][kTileA];
-  const int64_t tiles = anchors / kTileA;
+  const int64_t tiles = (anchors + kTileA - 1) / kTileA;
   const int tid = threadIdx.x;
   for (int64_t job = blockIdx.x; job < n * tiles; job += gridDim.x) {
     const int64_t b = job / tiles, a0 = (job % tiles) * kTileA;
-    // load: 8 uint4 per row
+    const int vecs = (int)((anchors - a0 < kTileA ? anchors - a0 : kTileA) / 8);  // 16-byte columns
+    // load: `vecs` uint4 per row
     for (int v = tid; v < (64 + nc) * 8; v += blockDim.x) {
       int row = v >> 3, col = (v & 7) * 8;
+      if ((v & 7) >= vecs) continue;
       const __half* src = row < 64 ? box + b * box_bs + row * box_cs + a0 + col
                                    : cls + b * cls_bs + (row - 64) * cls_cs + a0 + col;
       uint4 q = *reinterpret_cast<const uint4*>(src);
@@ -406,6 +427,7 @@ __global__ void __launch_bounds__(256) dfl_decode_tiled(const __half* box, int64
     __half* o = out + b * (4 + nc) * anchors + a0;
     for (int v = tid; v < (4 + nc) * 8; v += blockDim.x) {
       int row = v >> 3, col = (v & 7) * 8;
+      if ((v & 7) >= vecs) continue;
       const uint16_t* src = row < 4 ? &out_box[row][col] : &io_cls[row - 4][col];
       *reinterpret_cast<uint4*>(o + row * anchors + col) = *reinterpret_cast<const uint4*>(src);
     }
@@ -534,11 +556,11 @@ ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs, c
               box_bs % 2 == 0 && box_cs % 2 == 0 &&
               (!nc || (((uintptr_t)cls & 3u) == 0 && cls_bs % 2 == 0 && cls_cs % 2 == 0));
   cudaStream_t s = (cudaStream_t)stream;
-  bool tiled = nc <= 96 && anchors % kTileA == 0 && ((uintptr_t)box & 15u) == 0 &&
+  bool tiled = nc <= 96 && anchors % 8 == 0 && ((uintptr_t)box & 15u) == 0 &&
                ((uintptr_t)out & 15u) == 0 && box_bs % 8 == 0 && box_cs % 8 == 0 &&
                (!nc || (((uintptr_t)cls & 15u) == 0 && cls_bs % 8 == 0 && cls_cs % 8 == 0));
   if (tiled) {
-    int64_t jobs = n * (anchors / kTileA);
+    int64_t jobs = n * ((anchors + kTileA - 1) / kTileA);
     unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * 8 ? jobs : (int64_t)sm_count() * 8);
     dfl_decode_tiled<96><<<grid, 256, 0, s>>>((const __half*)box, box_bs, box_cs, (const __half*)cls,
                                                cls_bs, cls_cs, n, (int)nc, anchors, lv, xywh != 0,
