@@ -141,20 +141,12 @@ __global__ void __launch_bounds__(256) class_max_planar8(SelectView v, bool nan_
 }
 
 // Fused-sigmoid class max (TTN_SELECT_SIGMOID), planar scores.  fp16 sigmoid
-// is monotone non-decreasing, so the best sigmoid key belongs to the best logit
-// key; only ties in the *sigmoid* value can move the winner to a lower class
-// index (distinct logits that round to one fp16 sigmoid).  Pass 1 keeps the best
-// and second-best logit keys per anchor (no sigmoid at all); the winner is final
-// unless sigmoid(second) has the winner's sigmoid key, in which case the warp
-// rescans that anchor's classes with the exact sigmoid, lanes over classes.
-__device__ __forceinline__ uint16_t bits_of_key(uint32_t key, bool nan_last) {
-  // a representative fp16 value with this key (+0 for the +-0 key, a NaN for the
-  // NaN key): its sigmoid has the key every value with this key has.
-  if (key == (nan_last ? 0xffffu : 0u)) return 0x7e00u;
-  if (key == 0x7fffu) return 0u;
-  return (key & 0x8000u) ? (uint16_t)key : (uint16_t)(0x7fffu - key);
-}
-
+// is monotone non-decreasing, so the best sigmoid belongs to the best logit; only
+// ties in the *sigmoid* value can move the winner to a lower class index
+// (distinct logits that round to one fp16 sigmoid).  Pass 1 keeps the best and
+// second-best logit per anchor (no sigmoid at all); the winner is final unless
+// sigmoid(second) equals sigmoid(best), in which case the warp rescans that
+// anchor's classes with the exact sigmoid, lanes over classes.
 __device__ __forceinline__ void rescan_anchor(const SelectView& v, int64_t b, int64_t a, bool nan_last,
                                               uint32_t& out_bits, uint32_t& out_cls) {
   const int lane = threadIdx.x & 31;
@@ -184,6 +176,21 @@ __device__ __forceinline__ void rescan_anchor(const SelectView& v, int64_t b, in
   out_cls = best_cls;
 }
 
+// Pass 1 works on 32-bit composites (ordered logit key << 16) | (0xffff - class):
+// the ordered key maps fp16 bits to an unsigned value that grows with the value
+// (sign-magnitude to offset binary), so the largest composite is the largest
+// logit and, among equal logits, the lowest class.  Per score that is two
+// integer max/min ops plus the key build, two lanes at a time.  Anchors with any
+// NaN logit, or whose best and second-best logits give the same fp16 sigmoid
+// (this also covers +0/-0), are decided by the exact rescan.
+__device__ __forceinline__ uint32_t ordered_pair(uint32_t w) {
+  const uint32_t sign = (w >> 15) & 0x00010001u;        // 1 per negative lane
+  return w ^ ((sign * 0x7fffu) | 0x80008000u);           // negative: ~h, positive: h | 0x8000
+}
+__device__ __forceinline__ uint16_t unordered(uint32_t key) {
+  return (uint16_t)((key & 0x8000u) ? (key & 0x7fffu) : (~key & 0xffffu));
+}
+
 __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, bool nan_last,
                                                                  uint32_t* records, int64_t rec_pitch,
                                                                  uint16_t* trace_max) {
@@ -196,53 +203,54 @@ __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, b
     const int64_t t = t0 + lane;
     const bool live = t < total;
     const int64_t b = live ? t / groups : 0, a0 = live ? (t % groups) * 8 : 0;
-    uint32_t best[8], second[8], cls8[8], raw8[8];
+    uint32_t best[8], second[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      best[j] = kInvalidKey;
-      second[j] = kInvalidKey;
-      cls8[j] = 0;
-      raw8[j] = 0;
-    }
+    for (int j = 0; j < 8; ++j) best[j] = second[j] = 0u;
+    uint32_t nan_any = 0;  // bit 15 / 31 of word k: a NaN logit in anchor 2k / 2k+1
+    uint32_t nan_word[4] = {0, 0, 0, 0};
     if (live) {
       const uint16_t* p = v.base + b * v.sb + a0 + 4 * v.sc;
       for (int64_t c = 0; c < v.classes; ++c) {
-        uint4 q = *reinterpret_cast<const uint4*>(p + c * v.sc);
-        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        const uint4 q = *reinterpret_cast<const uint4*>(p + c * v.sc);
+        const uint32_t cc = 0xffffu - (uint32_t)c;
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint16_t bits = (uint16_t)((w[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
-          uint32_t key = score_key(bits, nan_last);
-          if (key < best[j]) {
-            second[j] = best[j];
-            best[j] = key;
-            cls8[j] = (uint32_t)c;
-            raw8[j] = bits;
-          } else if (key < second[j]) {
-            second[j] = key;
-          }
+        for (int k = 0; k < 4; ++k) {
+          nan_word[k] |= ((w[k] & 0x7fff7fffu) + 0x03ff03ffu) & 0x80008000u;
+          const uint32_t kw = ordered_pair(w[k]);
+          const uint32_t c0 = __byte_perm(kw, cc, 0x1054), c1 = __byte_perm(kw, cc, 0x3254);
+          second[2 * k] = max(second[2 * k], min(best[2 * k], c0));
+          best[2 * k] = max(best[2 * k], c0);
+          second[2 * k + 1] = max(second[2 * k + 1], min(best[2 * k + 1], c1));
+          best[2 * k + 1] = max(best[2 * k + 1], c1);
         }
       }
     }
-    uint32_t out_bits[8], tie = 0;
+    uint32_t out_bits[8], cls8[8], redo = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      uint16_t s1 = sigmoid_h_fast((uint16_t)raw8[j]);
+      const uint16_t logit = unordered(best[j] >> 16);
+      cls8[j] = 0xffffu - (best[j] & 0xffffu);
+      const uint16_t s1 = sigmoid_h_fast(logit);
       out_bits[j] = s1;
-      if (live && second[j] != kInvalidKey) {
-        uint16_t s2 = sigmoid_h_fast(bits_of_key(second[j], nan_last));
-        if (score_key(s2, nan_last) == score_key(s1, nan_last)) tie |= 1u << j;
+      const bool has_nan = (nan_word[j >> 1] >> ((j & 1) ? 31 : 15)) & 1u;
+      bool tie = false;
+      if (v.classes > 1) {
+        const uint16_t s2 = sigmoid_h_fast(unordered(second[j] >> 16));
+        tie = score_key(s2, nan_last) == score_key(s1, nan_last);
       }
+      if (live && (has_nan || tie)) redo |= 1u << j;
     }
-    // exact rescans of tied anchors, one anchor at a time with the whole warp
-    uint32_t pending = __ballot_sync(0xffffffffu, tie != 0);
+    (void)nan_any;
+    // exact rescans, one anchor at a time with the whole warp
+    uint32_t pending = __ballot_sync(0xffffffffu, redo != 0);
     while (pending) {
       const int src = __ffs(pending) - 1;
-      uint32_t src_tie = __shfl_sync(0xffffffffu, tie, src);
+      uint32_t src_redo = __shfl_sync(0xffffffffu, redo, src);
       const int64_t sb = __shfl_sync(0xffffffffu, b, src), sa0 = __shfl_sync(0xffffffffu, a0, src);
-      while (src_tie) {
-        const int j = __ffs(src_tie) - 1;
-        src_tie &= src_tie - 1;
+      while (src_redo) {
+        const int j = __ffs(src_redo) - 1;
+        src_redo &= src_redo - 1;
         uint32_t rb, rc;
         rescan_anchor(v, sb, sa0 + j, nan_last, rb, rc);
         if (lane == src) {

@@ -373,11 +373,15 @@ __global__ void __launch_bounds__(256) dfl_decode_tiled(const __half* box, int64
   __shared__ __align__(16) uint16_t io_cls[NC_MAX][kTileA];
   __shared__ float dist[4][kTileA];
   __shared__ __align__(16) uint16_t out_box[4][kTileA];
+  constexpr int kFixups = 512;  // queued (class row, anchor pair) fix-ups per tile
+  __shared__ uint16_t fixups[kFixups];
+  __shared__ int queued;
   const int64_t tiles = (anchors + kTileA - 1) / kTileA;
   const int tid = threadIdx.x;
   for (int64_t job = blockIdx.x; job < n * tiles; job += gridDim.x) {
     const int64_t b = job / tiles, a0 = (job % tiles) * kTileA;
     const int vecs = (int)((anchors - a0 < kTileA ? anchors - a0 : kTileA) / 8);  // 16-byte columns
+    if (tid == 0) queued = 0;
     // load: `vecs` uint4 per row
     for (int v = tid; v < (64 + nc) * 8; v += blockDim.x) {
       int row = v >> 3, col = (v & 7) * 8;
@@ -396,13 +400,30 @@ __global__ void __launch_bounds__(256) dfl_decode_tiled(const __half* box, int64
       for (int i = 0; i < 16; ++i) v[i] = __half2float(hfrom(in_box[side * 16 + i][a]));
       dist[side][a] = dfl_side(v);
     }
-    // sigmoid in place on the class rows, two anchors per step
+    // sigmoid in place on the class rows, two anchors per step; pairs the fast
+    // path cannot settle keep their logits and are queued for the exact routine
     for (int e = tid; e < nc * (kTileA / 2); e += blockDim.x) {
       int row = e / (kTileA / 2), col = (e % (kTileA / 2)) * 2;
       uint32_t* p = reinterpret_cast<uint32_t*>(&io_cls[row][col]);
-      *p = unary_h2_fast<false>(*p);
+      bool bad;
+      uint32_t r = unary_h2_deferred<false>(*p, bad);
+      if (bad) {
+        int slot = atomicAdd(&queued, 1);
+        if (slot < kFixups) fixups[slot] = (uint16_t)e;
+        else *p = unary_h2_fast<false>(*p);  // queue full: settle in place
+      } else {
+        *p = r;
+      }
     }
     __syncthreads();
+    {
+      const int n_fix = queued < kFixups ? queued : kFixups;
+      for (int q = tid; q < 2 * n_fix; q += blockDim.x) {
+        int e = fixups[q >> 1];
+        int row = e / (kTileA / 2), col = (e % (kTileA / 2)) * 2 + (q & 1);
+        io_cls[row][col] = sigmoid_h(io_cls[row][col]);
+      }
+    }
     if (tid < kTileA * 4) {  // box decode: thread -> (coordinate, anchor)
       int c = tid >> 6, a = tid & 63;
       int64_t idx = a0 + a;
