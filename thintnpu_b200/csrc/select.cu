@@ -210,9 +210,8 @@ __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, b
     uint32_t nan_word[4] = {0, 0, 0, 0};
     if (live) {
       const uint16_t* p = v.base + b * v.sb + a0 + 4 * v.sc;
-      for (int64_t c = 0; c < v.classes; ++c) {
-        const uint4 q = *reinterpret_cast<const uint4*>(p + c * v.sc);
-        const uint32_t cc = 0xffffu - (uint32_t)c;
+      auto fold = [&](const uint4 q, uint32_t c) {
+        const uint32_t cc = 0xffffu - c;
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -224,7 +223,19 @@ __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, b
           second[2 * k + 1] = max(second[2 * k + 1], min(best[2 * k + 1], c1));
           best[2 * k + 1] = max(best[2 * k + 1], c1);
         }
+      };
+      int64_t c = 0;
+      for (; c + 3 < v.classes; c += 4) {  // four class rows in flight
+        const uint4 q0 = *reinterpret_cast<const uint4*>(p + c * v.sc);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(p + (c + 1) * v.sc);
+        const uint4 q2 = *reinterpret_cast<const uint4*>(p + (c + 2) * v.sc);
+        const uint4 q3 = *reinterpret_cast<const uint4*>(p + (c + 3) * v.sc);
+        fold(q0, (uint32_t)c);
+        fold(q1, (uint32_t)c + 1);
+        fold(q2, (uint32_t)c + 2);
+        fold(q3, (uint32_t)c + 3);
       }
+      for (; c < v.classes; ++c) fold(*reinterpret_cast<const uint4*>(p + c * v.sc), (uint32_t)c);
     }
     uint32_t out_bits[8], cls8[8], redo = 0;
 #pragma unroll
@@ -548,6 +559,134 @@ __global__ void __launch_bounds__(kTopkThreads) topk_block(TopkArgs args) {
   for (int64_t i = threadIdx.x; i < k; i += blockDim.x) out[i] = cand[i];
 }
 
+// k <= 4096: 256-thread CTA per image (eight fit on an SM).
+//  1. radix select of the k-th smallest 16-bit key (two 256-bin histograms);
+//  2. index-ordered collection: warp w owns a contiguous index range, counts its
+//     keys below / equal to the threshold with ballots, one block-wide prefix over
+//     the 8 warp counts places every warp, then each warp writes its winners in
+//     index order (the first `need` threshold ties globally);
+//  3. the k winners sit in index order, so a sort by key alone is stable: bitonic
+//     sort of (key << 12 | slot) 32-bit composites in shared memory.
+constexpr int kSmallThreads = 256;
+constexpr int kSmallWarps = kSmallThreads / 32;
+
+constexpr int kStageKeys = 24576;  // keys staged in shared memory (48 KB)
+
+template <bool kStaged>
+__global__ void __launch_bounds__(kSmallThreads) topk_small(TopkArgs args) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sel_bucket, sel_below;
+  __shared__ int warp_lt[kSmallWarps], warp_eq[kSmallWarps];
+  extern __shared__ uint32_t dyn[];  // [cap] composites, [cap] source indices, [n] staged keys
+  const int64_t b = blockIdx.x, n = args.n, k = args.k;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int cap = 32;
+  while (cap < k) cap <<= 1;
+  uint32_t* comp = dyn;
+  uint32_t* src = dyn + cap;
+  uint16_t* staged = reinterpret_cast<uint16_t*>(dyn + 2 * cap);
+  unsigned long long* out = args.sorted + b * args.sorted_pitch;
+  if (k <= 0) return;
+  if (kStaged) {  // one coalesced, 4-way unrolled pass computes every key once
+    int64_t i = threadIdx.x;
+    for (; i + 3 * kSmallThreads < n; i += 4 * kSmallThreads) {
+      uint16_t h0 = args.src.get(b, i), h1 = args.src.get(b, i + kSmallThreads);
+      uint16_t h2 = args.src.get(b, i + 2 * kSmallThreads), h3 = args.src.get(b, i + 3 * kSmallThreads);
+      staged[i] = (uint16_t)score_key(h0, args.nan_last);
+      staged[i + kSmallThreads] = (uint16_t)score_key(h1, args.nan_last);
+      staged[i + 2 * kSmallThreads] = (uint16_t)score_key(h2, args.nan_last);
+      staged[i + 3 * kSmallThreads] = (uint16_t)score_key(h3, args.nan_last);
+    }
+    for (; i < n; i += kSmallThreads) staged[i] = (uint16_t)score_key(args.src.get(b, i), args.nan_last);
+    __syncthreads();
+  }
+  auto key_at = [&](int64_t i) -> uint32_t {
+    return kStaged ? (uint32_t)staged[i] : score_key(args.src.get(b, i), args.nan_last);
+  };
+  // --- radix select
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+    atomicAdd(&hist[key_at(i) >> 8], 1u);
+  __syncthreads();
+  if (warp == 0) find_bucket(hist, (uint32_t)k, 0u, &sel_bucket, &sel_below);
+  __syncthreads();
+  const uint32_t high = sel_bucket, below_high = sel_below;
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    uint32_t key = key_at(i);
+    if ((key >> 8) == high) atomicAdd(&hist[key & 255u], 1u);
+  }
+  __syncthreads();
+  if (warp == 0) find_bucket(hist, (uint32_t)k, below_high, &sel_bucket, &sel_below);
+  __syncthreads();
+  const uint32_t threshold = (high << 8) | sel_bucket;
+  const int64_t need = k - (int64_t)sel_below;
+  // --- index-ordered collection
+  const int64_t span = ((n + kSmallWarps - 1) / kSmallWarps + 31) / 32 * 32;
+  const int64_t lo = warp * span, hi = lo + span < n ? lo + span : n;
+  int lt = 0, eq = 0;
+  for (int64_t base = lo; base < hi; base += 32) {
+    int64_t i = base + lane;
+    uint32_t key = i < hi ? key_at(i) : 0xffffffffu;
+    lt += __popc(__ballot_sync(0xffffffffu, key < threshold));
+    eq += __popc(__ballot_sync(0xffffffffu, key == threshold));
+  }
+  if (lane == 0) {
+    warp_lt[warp] = lt;
+    warp_eq[warp] = eq;
+  }
+  __syncthreads();
+  int64_t eq_before = 0, taken_before = 0;
+  for (int w = 0; w < warp; ++w) {
+    int64_t take_eq = need - eq_before;
+    take_eq = take_eq < 0 ? 0 : (take_eq > warp_eq[w] ? warp_eq[w] : take_eq);
+    taken_before += warp_lt[w] + take_eq;
+    eq_before += warp_eq[w];
+  }
+  const uint32_t lane_lt = (1u << lane) - 1u;
+  for (int64_t base = lo; base < hi; base += 32) {
+    int64_t i = base + lane;
+    uint32_t key = i < hi ? key_at(i) : 0xffffffffu;
+    uint32_t eq_mask = __ballot_sync(0xffffffffu, key == threshold);
+    int64_t my_eq_rank = eq_before + __popc(eq_mask & lane_lt);
+    bool take = key < threshold || (key == threshold && my_eq_rank < need);
+    uint32_t take_mask = __ballot_sync(0xffffffffu, take);
+    if (take) {
+      int pos = (int)(taken_before + __popc(take_mask & lane_lt));
+      comp[pos] = (key << 12) | (uint32_t)pos;
+      src[pos] = (uint32_t)i;
+    }
+    taken_before += __popc(take_mask);
+    eq_before += __popc(eq_mask);
+  }
+  __syncthreads();
+  // --- stable sort by key (slot order = index order)
+  for (int i = (int)k + threadIdx.x; i < cap; i += blockDim.x) comp[i] = 0xffffffffu;
+  __syncthreads();
+  for (int span2 = 2; span2 <= cap; span2 <<= 1) {
+    for (int stride = span2 >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < cap; i += blockDim.x) {
+        int j = i ^ stride;
+        if (j > i) {
+          uint32_t a = comp[i], c = comp[j];
+          if ((a > c) == ((i & span2) == 0)) {
+            comp[i] = c;
+            comp[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+    uint32_t c = comp[i];
+    out[i] = ((unsigned long long)(c >> 12) << 32) | (unsigned long long)src[c & 0xfffu];
+  }
+}
+
 // --------------------------------------------------------- 3. pair gather
 
 // pair_bits[b][r*nc + c] = score of class c at the stage-1 anchor of rank r.
@@ -626,6 +765,25 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 struct Workspace {
   size_t records, stage1, pairs, stage2, hist, scratch, total;
 };
+
+ttn_status launch_topk(const TopkArgs& args, int64_t batch, int64_t k, cudaStream_t s) {
+  if (k > kSmemSort) {
+    topk_block<<<(unsigned)batch, kTopkThreads, 32 * 8, s>>>(args);
+    return launch_check("ttn_select_f16 topk (large k)");
+  }
+  int cap = 32;
+  while (cap < k) cap <<= 1;
+  if (args.n <= kStageKeys) {
+    const size_t smem = (size_t)cap * 8 + (size_t)(args.n + 1) / 2 * 4;  // + 16-bit staged keys
+    TTN_TRY(ensure_dynamic_smem((const void*)topk_small<true>, (int)smem));
+    topk_small<true><<<(unsigned)batch, kSmallThreads, smem, s>>>(args);
+  } else {
+    const size_t smem = (size_t)cap * 8;  // composites + source indices
+    TTN_TRY(ensure_dynamic_smem((const void*)topk_small<false>, (int)smem));
+    topk_small<false><<<(unsigned)batch, kSmallThreads, smem, s>>>(args);
+  }
+  return launch_check("ttn_select_f16 topk");
+}
 
 Workspace layout(int64_t batch, int64_t anchors, int64_t classes, int64_t k, bool agnostic) {
   Workspace w;
@@ -729,12 +887,9 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
   TTN_TRY(launch_check("ttn_select_f16 class_max"));
   if (!k) return TTN_OK;
 
-  const size_t sort_smem = (size_t)(k > kSmemSort ? 32 : 1 << (64 - __builtin_clzll((unsigned long long)(k > 32 ? k - 1 : 31)))) * 8;
-  TTN_TRY(ensure_dynamic_smem((const void*)topk_block, (int)sort_smem));
   // 2. stage-1 top-k over anchors
   TopkArgs t1{KeySource{records, nullptr, v.anchors}, v.anchors, k, nan_last, stage1, kp, hist, scratch};
-  topk_block<<<(unsigned)v.batch, kTopkThreads, sort_smem, s>>>(t1);
-  TTN_TRY(launch_check("ttn_select_f16 topk anchors"));
+  TTN_TRY(launch_topk(t1, v.batch, k, s));
 
   // 3. class-aware: pairs and stage-2 top-k
   if (!agnostic) {
@@ -744,8 +899,7 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
     TTN_TRY(launch_check("ttn_select_f16 gather_pairs"));
     TopkArgs t2{KeySource{nullptr, pairs, kp * v.classes}, k * v.classes, k, nan_last, stage2, kp,
                 hist, scratch};
-    topk_block<<<(unsigned)v.batch, kTopkThreads, sort_smem, s>>>(t2);
-    TTN_TRY(launch_check("ttn_select_f16 topk pairs"));
+    TTN_TRY(launch_topk(t2, v.batch, k, s));
   }
 
   // 4. pack

@@ -258,22 +258,34 @@ struct Levels {
 
 __device__ __forceinline__ float h16(float v) { return __half2float(__float2half_rn(v)); }
 
+// Round a probability p in [0, 1] (or NaN) to the nearest fp16 value, ties to
+// even, without conversion instructions: on the fp32 bits for the fp16 normal
+// range (drop 13 mantissa bits), by adding and removing 0.5 below it (fp32
+// spacing at 0.5 is the fp16 subnormal quantum 2^-24).
+__device__ __forceinline__ float round_prob_h16(float p) {
+  if (p < 6.103515625e-05f) return __fsub_rn(__fadd_rn(p, 0.5f), 0.5f);
+  uint32_t b = __float_as_uint(p);
+  b = (b + 0x0fffu + ((b >> 13) & 1u)) & 0xffffe000u;
+  return __uint_as_float(b);
+}
+
 // 16-bin softmax of one side (fp16 probabilities, as the separate softmax op
 // stores them) followed by the arange(16) expectation rounded to fp16.
 __device__ __forceinline__ float dfl_side(const float (&v)[16]) {
-  float m = -INFINITY;
+  float m = v[0];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) m = nan_max(m, v[i]);
+  for (int i = 1; i < 16; ++i) m = row_max(m, v[i]);  // NaN/inf reach the sum below
+  const ShiftLog2 ml = shift_log2(m);
   float e[16], s = 0.0f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    e[i] = exp_fast(__fsub_rn(v[i], m));
+    e[i] = exp_shifted(v[i], ml);
     s = __fadd_rn(s, e[i]);
   }
   const float inv = __fdiv_rn(1.0f, s);
   float d = 0.0f;
 #pragma unroll
-  for (int i = 1; i < 16; ++i) d = __fmaf_rn(h16(__fmul_rn(e[i], inv)), (float)i, d);
+  for (int i = 1; i < 16; ++i) d = __fmaf_rn(round_prob_h16(__fmul_rn(e[i], inv)), (float)i, d);
   return h16(d);
 }
 
