@@ -181,6 +181,102 @@ __global__ void __launch_bounds__(256) softmax_warp_rows_h8(const uint16_t* x, u
   }
 }
 
+// Contiguous fp16 rows (row pitch == reduce, 16-byte aligned, reduce % 8 == 0,
+// reduce <= 1024): each warp double-buffers its rows in shared memory with
+// cp.async 16-byte copies, so the next row streams in while the current one is
+// reduced; completion is tracked by cp.async.wait_group (no software spin).
+constexpr int kRowsWarps = 8;
+constexpr int kRowMaxVec = 128;  // 1024 fp16 per row
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+template <int PER>
+__global__ void __launch_bounds__(kRowsWarps * 32) softmax_rows_pipelined(const uint16_t* x, uint16_t* y,
+                                                                          int64_t rows, int reduce,
+                                                                          float scale, bool scaled) {
+  extern __shared__ __align__(16) uint4 rowbuf[];  // [warps][2][nvec]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = reduce >> 3;
+  uint4* buf = rowbuf + (size_t)warp * 2 * nvec;
+  const int64_t warps = (int64_t)gridDim.x * kRowsWarps;
+  int64_t row = (int64_t)blockIdx.x * kRowsWarps + warp;
+  auto prefetch = [&](int64_t r, int slot) {
+    if (r < rows) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + r * reduce);
+      for (int e = lane; e < nvec; e += 32) cp_async16(&buf[slot * nvec + e], &src[e]);
+    }
+    cp_async_commit();
+  };
+  prefetch(row, 0);
+  for (int i = 0; row < rows; row += warps, ++i) {
+    prefetch(row + warps, (i + 1) & 1);
+    cp_async_wait<1>();
+    __syncwarp();
+    const uint4* xv = buf + (i & 1) * nvec;
+    float v[PER][8];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      if (e < nvec) {
+        uint4 q = xv[e];
+        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __half22float2(*reinterpret_cast<__half2*>(&w[j]));
+          if (scaled) {
+            f.x = __half2float(__float2half_rn(__fmul_rn(f.x, scale)));
+            f.y = __half2float(__float2half_rn(__fmul_rn(f.y, scale)));
+          }
+          v[k][2 * j] = f.x;
+          v[k][2 * j + 1] = f.y;
+          m = row_max(row_max(m, f.x), f.y);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = row_max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const ShiftLog2 ml = shift_log2(m);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      if (e < nvec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[k][j] = exp_shifted(v[k][j], ml);
+          s = __fadd_rn(s, v[k][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    const float inv = __fdiv_rn(1.0f, s);
+    uint4* yv = reinterpret_cast<uint4*>(y + row * reduce);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int e = k * 32 + lane;
+      if (e < nvec) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __half2 h = __floats2half2_rn(__fmul_rn(v[k][2 * j], inv), __fmul_rn(v[k][2 * j + 1], inv));
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        yv[e] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    __syncwarp();  // this slot is refilled two rows later
+  }
+  cp_async_wait<0>();
+}
+
 // One block per row for long unit-stride rows: three passes through L2.
 template <typename T, typename U>
 __global__ void __launch_bounds__(512) softmax_block_rows(const T* x, U* y, RowSpace rs, int64_t rows,
@@ -501,6 +597,29 @@ ttn_status launch_softmax(const ttn_tensor* x, const ttn_tensor* y, int dim, flo
     if constexpr (sizeof(T) == 2 && sizeof(U) == 2) {
       bool vec = reduce % 8 == 0 && ((uintptr_t)xp & 15u) == 0 && ((uintptr_t)yp & 15u) == 0;
       for (int d = 0; d < rs.ndim && vec; ++d) vec = rs.sx[d] % 8 == 0 && rs.sy[d] % 8 == 0;
+      bool packed = vec && rs.ndim <= 1 && (rs.ndim == 0 || (rs.sx[0] == reduce && rs.sy[0] == reduce));
+      if (packed && rows >= 1024) {  // contiguous rows: cp.async double buffering
+        int nvec = (int)(reduce / 8);
+        size_t smem = (size_t)kRowsWarps * 2 * nvec * 16;
+        int per = nvec <= 32 ? 1 : nvec <= 64 ? 2 : 4;
+        const void* fn = per == 1 ? (const void*)softmax_rows_pipelined<1>
+                       : per == 2 ? (const void*)softmax_rows_pipelined<2>
+                                  : (const void*)softmax_rows_pipelined<4>;
+        TTN_TRY(ensure_dynamic_smem(fn, (int)smem));
+        unsigned grid = (unsigned)(sm_count() * resident_blocks(fn, kRowsWarps * 32, smem));
+        int64_t need = (rows + kRowsWarps - 1) / kRowsWarps;
+        if ((int64_t)grid > need) grid = (unsigned)need;
+        if (per == 1)
+          softmax_rows_pipelined<1><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
+                                                                       rows, (int)reduce, scale, scaled);
+        else if (per == 2)
+          softmax_rows_pipelined<2><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
+                                                                       rows, (int)reduce, scale, scaled);
+        else
+          softmax_rows_pipelined<4><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
+                                                                       rows, (int)reduce, scale, scaled);
+        return launch_check("ttn_softmax");
+      }
       if (vec) {
         unsigned grid = grid_for(rows, 8, 16);
         int nvec = (int)(reduce / 8);
