@@ -43,6 +43,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-variants", action="store_true")
+    p.add_argument("--sweep", choices=("silu", "sigmoid"),
+                   help="print fp16 unary bandwidth by tensor size (one GPU) and exit")
     p.add_argument("--config", type=int, default=4, choices=(1, 2, 3, 4, 5),
                    help="BASELINE config; 4 (the op pass) is the headline workload")
     return p.parse_args()
@@ -166,6 +168,10 @@ def run_reference(args):
 
 def main():
     args = parse()
+    if args.sweep:
+        from thintnpu_b200 import perf
+        print(json.dumps({"sweep": args.sweep, "unit": "us / GB/s", **perf.unary_sweep(args.sweep)}))
+        return
     if args.config != 4:
         from thintnpu_b200 import perf
         perf.run_config(args)

@@ -24,12 +24,46 @@ def test_unary_exhaustive_fp16_bit_exact(device, name):
     import thintnpu_b200 as ttn
     fn = getattr(ttn, name)
     ref = getattr(oops, name)(ALL_HALVES)
-    # dense aligned path, an odd-length tail, and a strided view
+    # dense aligned arithmetic path, an odd-length tail, and a strided view
     assert_bits_equal(fn(ALL_HALVES.to(device)), ref, name)
     odd = ALL_HALVES[3:].clone()
     assert_bits_equal(fn(odd.to(device)), getattr(oops, name)(odd), name + " tail")
     strided = ALL_HALVES.view(256, 256).t()
     assert_bits_equal(fn(strided.to(device)), getattr(oops, name)(strided), name + " strided")
+    # dense table path (>= 2^25 elements), with a tail, in place and out of place
+    big = ALL_HALVES.repeat(520)[5:]
+    want = ref.repeat(520)[5:]
+    assert_bits_equal(fn(big.to(device)), want, name + " table")
+    if name == "silu":
+        inplace = big.to(device)
+        ttn.silu_(inplace)
+        assert_bits_equal(inplace, want, name + " table in place")
+
+
+@pytest.mark.parametrize("path", ["table", "arithmetic"])
+@pytest.mark.parametrize("name", ["silu", "sigmoid"])
+def test_unary_all_input_pairs_bit_exact(device, name, path):
+    """Every ordered pair of fp16 inputs in one 32-bit word, 2^32 pairs in 16
+    launches of 2^28.  The arithmetic core computes the two lanes of a word
+    together (one shared reciprocal), so its result is a function of the pair;
+    row-strided views take that kernel, dense tensors the table kernel."""
+    import thintnpu_b200 as ttn
+    fn = getattr(ttn, name)
+    table = getattr(oops, name)(ALL_HALVES).view(torch.int16).to(device)  # CPU result per input bits
+    rows = 4096
+    pad = 0 if path == "table" else 8  # a row gap makes the view non-dense
+    buf = torch.empty(rows, 65536 + pad, 2, dtype=torch.int16, device=device)
+    x = buf[:, :65536]
+    x[..., 0] = torch.arange(65536, dtype=torch.int32, device=device).to(torch.int16)
+    for h0 in range(0, 65536, rows):
+        x[..., 1] = torch.arange(h0, h0 + rows, dtype=torch.int32, device=device).to(torch.int16)[:, None]
+        y = fn(x.view(torch.float16)).view(torch.int16)
+        bad = (y[..., 0] != table[None, :]) | (y[..., 1] != table[h0:h0 + rows, None])
+        if bool(bad.any()):
+            r, c = (int(v) for v in bad.nonzero()[0])
+            raise AssertionError(f"{name}/{path}: pair (lo=0x{c:04x}, hi=0x{h0 + r:04x}) -> "
+                                 f"{int(y[r, c, 0]) & 0xffff:04x},{int(y[r, c, 1]) & 0xffff:04x}, "
+                                 f"want {int(table[c]) & 0xffff:04x},{int(table[h0 + r]) & 0xffff:04x}")
 
 
 @pytest.mark.parametrize("shape", [(1,), (3,), (7,), (100,), (2047,), (2048,), (2049,), (16385,),

@@ -106,7 +106,8 @@ def test_materialize_views_and_nan_payloads(device):
 def test_pack_unpack(device):
     import thintnpu_b200 as ttn
     g = torch.Generator().manual_seed(3)
-    for n, c, h, w in ((1, 64, 80, 80), (2, 80, 40, 40), (3, 16, 13, 17), (1, 40, 5, 7)):
+    for n, c, h, w in ((1, 64, 80, 80), (2, 80, 40, 40), (3, 16, 13, 17), (1, 40, 5, 7), (2, 24, 6, 6),
+                       (1, 33, 2, 2)):
         x = torch.randint(-32768, 32768, (n, c, h, w), dtype=torch.int16, generator=g).view(torch.float16)
         packed = ttn.pack(x.to(device))
         assert_bits_equal(packed, oops.pack_padded(x))
@@ -121,6 +122,13 @@ def test_pack_unpack(device):
         offset += b.size(2) * b.size(3)
     want = torch.cat([oops.unpack(b, 64) for b in boxes], -1)
     assert_bits_equal(head[:, :64], want)
+    # odd anchor offset: rows only 2-byte aligned
+    odd = torch.zeros(2, 64, 8401, dtype=torch.float16, device=device)
+    offset = 1
+    for b in boxes:
+        ttn.unpack(b.to(device), 64, out=odd, out_offset=offset)
+        offset += b.size(2) * b.size(3)
+    assert_bits_equal(odd[..., 1:], want)
 
 
 @pytest.mark.parametrize("c,h,w,k", [(256, 20, 20, 5), (128, 40, 40, 5), (512, 20, 20, 5),

@@ -43,11 +43,12 @@ def _worker(rank, world, port, mode, results):
             results[rank] = shard.max_over_ranks(10.0 + rank)
         elif mode == "raise":
             hb.beat(0)
-            hb.check(0)
             if rank == 1:
+                hb.check(0)
                 hb.fail("injected exception in step 1")
                 raise RuntimeError("injected")
-            try:
+            try:  # rank 0 may still be in its step-0 check when the failure lands
+                hb.check(0, wait_s=10)
                 hb.check(1, wait_s=10)
                 results[rank] = "missed"
             except shard.PeerFailure as err:

@@ -37,13 +37,19 @@ inline ttn_status launch_check(const char* what) {
 int sm_count();
 
 // Raise a kernel's dynamic shared-memory limit to at least `bytes` on the
-// current device.  Cached per (device, kernel): the CUDA call only happens the
-// first time a larger size is needed, so later calls (e.g. inside stream
-// capture after a warm-up call) touch no runtime API.
+// current device (the default limit is 48 KB less the kernel's static shared
+// memory).  Cached per (device, kernel): the CUDA calls only happen the first
+// time a kernel is seen or a larger size is needed, so later calls (e.g. inside
+// stream capture after a warm-up call) touch no runtime API.
 ttn_status ensure_dynamic_smem(const void* kernel, int bytes);
 
 // Largest opt-in dynamic shared memory per block on the current device.
 int max_dynamic_smem();
+
+// The 65,536-entry fp16 table of SiLU (kind 0) or sigmoid (kind 1) on the
+// current device, indexed by input bits and equal to silu_h / sigmoid_h for
+// every input; built on `stream` by the first call.
+ttn_status unary_table(int kind, cudaStream_t stream, const uint16_t** table);
 
 // Blocks of `kernel` (at `threads` threads, `smem` dynamic bytes) resident per SM
 // on the current device, from the occupancy calculator; cached per (device, kernel).
@@ -219,23 +225,44 @@ __device__ __forceinline__ float silu_fast_f32(float x) { return x * rcp_approx(
 __device__ __forceinline__ float sigmoid_fast_f32(float x) { return rcp_approx(1.0f + exp_neg_fast(x)); }
 
 // Two fp16 lanes at once, deferring the exact decision: returns the fast fp16
-// pair and sets `unsafe` to a per-lane 0xffff mask where the result must come
-// from the exact routine instead -- where r*(1-2^-19) and r*(1+2^-19) round to
-// different fp16 values (r within 16-32 fp32 ulps of a midpoint, any range), or
-// the input is +-inf/NaN (whose x86 results the fast formula does not give).
+// pair and sets `unsafe` where a lane must come from the exact routine instead.
+//
+// Fast core: a_i = 1 + 2^(-x_i log2 e) (ex2.approx), and the two reciprocals
+// share one rcp.approx: q = 1/(a0 a1), 1/a0 = a1 q, 1/a1 = a0 q; then
+// sigmoid = 1/a_i, silu = x_i / a_i.  Relative error of r wherever r can sit
+// near an fp16 rounding midpoint (|r| >= 2^-25, so |t| < 30 for the ex2
+// argument t = -x log2 e): rounding t costs ln2 |t| 2^-24 < 2^-19.6 (damped by
+// e/(1+e) <= 1), ex2.approx ~2^-22, rcp.approx 2^-23, and the 1 + e, a0 a1,
+// a_j q and x (a_j q) roundings 2^-24 each: below 2^-19 in all.  The result is
+// a deterministic function of the input pair, and the exhaustive test over all
+// 2^32 pairs checks it against the CPU for every one.
+// Bracket: where r*(1-2^-19) and r*(1+2^-19) round to the same fp16 value, the
+// true result lies between them and rounds to it too (rounding is monotonic),
+// so that value is the result; otherwise (r within 16-32 fp32 ulps of a
+// midpoint, any range) the pair is flagged.
+// Also flagged: !(a0 a1 < 2^126) -- a NaN input (NaN propagates into the
+// product), -inf (a = inf; its CPU results take the exact routine), and
+// products so large that q would leave the normal range.  Every other input,
+// +inf included (a = 1: silu inf, sigmoid 1), gives a finite product >= 1 and
+// a result of the right kind.
 template <bool kSilu>
 __device__ __forceinline__ uint32_t unary_h2_deferred(uint32_t packed, bool& unsafe) {
   __half2 h = *reinterpret_cast<__half2*>(&packed);
   float2 f = __half22float2(h);
-  float r0 = kSilu ? silu_fast_f32(f.x) : sigmoid_fast_f32(f.x);
-  float r1 = kSilu ? silu_fast_f32(f.y) : sigmoid_fast_f32(f.y);
-  __half2 o = __floats2half2_rn(r0, r1);
+  const float a0 = 1.0f + exp_neg_fast(f.x);
+  const float a1 = 1.0f + exp_neg_fast(f.y);
+  const float p = a0 * a1;
+  const float q = rcp_approx(p);
+  float r0 = a1 * q, r1 = a0 * q;
+  if (kSilu) {
+    r0 *= f.x;
+    r1 *= f.y;
+  }
   __half2 up = __floats2half2_rn(r0 * 1.0000019073486328125f, r1 * 1.0000019073486328125f);
   __half2 dn = __floats2half2_rn(r0 * 0.9999980926513671875f, r1 * 0.9999980926513671875f);
   uint32_t uw = *reinterpret_cast<uint32_t*>(&up), dw = *reinterpret_cast<uint32_t*>(&dn);
-  bool special = (packed & 0x7c00u) == 0x7c00u || (packed & 0x7c000000u) == 0x7c000000u;
-  unsafe = (uw != dw) | special;
-  return *reinterpret_cast<uint32_t*>(&o);
+  unsafe = (uw != dw) | !(p < 8.50705917302346159e+37f);  // 2^126
+  return uw;
 }
 
 // Two fp16 lanes at once; exact fallback per lane when needed.
@@ -268,5 +295,15 @@ __device__ __forceinline__ uint16_t sigmoid_h_fast(uint16_t xb) {
 // fp32 versions for TTN_F32 tensors (no rounding step to protect).
 __device__ __forceinline__ float sigmoid_f(float x) { return sigmoid_f32(x); }
 __device__ __forceinline__ float silu_f(float x) { return silu_f32(x); }
+
+// 16-byte global -> shared copies tracked by commit/wait groups (LDGSTS): the
+// hardware counts completion, so a streaming ring needs no software spin.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 }  // namespace ttn

@@ -31,11 +31,10 @@ __device__ __forceinline__ uint4 unary_vec8(uint4 v) {
                     unary_h2_fast<K == kSilu>(v.z), unary_h2_fast<K == kSilu>(v.w));
 }
 
-// Dense fp16, 16-byte aligned: uint4 body plus a scalar tail.  x may equal y.
-// Warp-uniform loop: each lane owns four 16-byte vectors per step (64 bytes in
-// flight per lane).  A pair whose fast result is not provably the CPU's fp16
-// value (about 1.5% of pairs) is stored with its *input* bits unchanged and its
-// element indices go to a per-warp shared-memory queue; when the queue fills
+// Vectorised fp16 SiLU / sigmoid (x may equal y).  Warp-uniform loop: each lane
+// owns four 16-byte vectors per step.  A pair whose fast result is not provably
+// the CPU's fp16 value (about 1.5% of pairs) is stored with its *input* bits
+// unchanged and its element indices go to a per-warp shared-memory queue; when the queue fills
 // (and once at the end) the warp re-reads those inputs and writes the exact
 // results, 32 elements at a time with every lane busy.  So the exact path costs
 // per flagged element rather than per diverged warp step, and works in place.
@@ -43,24 +42,99 @@ __device__ __forceinline__ uint4 unary_vec8(uint4 v) {
 constexpr int kQueue = 256;  // element entries per warp
 constexpr int kVec = 4;      // 16-byte vectors per lane per step
 
+// Rewrites the queued elements with the exact routine (yh[e] still holds the
+// input bits, stored unchanged).  Each lane gathers four entries before
+// computing, so a full queue costs two rounds of L2 latency, not eight.
 template <int K>
 __device__ __forceinline__ void drain_queue(const uint32_t* queue, int count, uint16_t* yh, int lane) {
+  constexpr int kBatch = 4;
   __syncwarp();
-  for (int t = lane; t < count; t += 32) {
-    uint32_t e = queue[t];
-    yh[e] = unary_h<K>(yh[e]);  // yh[e] still holds the input bits (stored unchanged)
+  for (int t0 = 0; t0 < count; t0 += 32 * kBatch) {
+    uint32_t e[kBatch];
+    uint16_t v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int t = t0 + j * 32 + lane;
+      e[j] = t < count ? queue[t] : 0xffffffffu;
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (e[j] != 0xffffffffu) v[j] = yh[e[j]];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (e[j] != 0xffffffffu) yh[e[j]] = unary_h<K>(v[j]);
   }
   __syncwarp();
 }
 
+// Applies the fast core to one lane's kVec vectors in place.  Returns bit
+// (4u + w) set where word w of vector u must come from the exact routine; such
+// words keep their input bits for the exact pass.
+template <int K>
+__device__ __forceinline__ uint32_t fast_step(uint4 (&v)[kVec]) {
+  uint32_t flags = 0;
+#pragma unroll
+  for (int u = 0; u < kVec; ++u) {
+    uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      bool bad;
+      uint32_t r = unary_h2_deferred<K == kSilu>(w[k], bad);
+      w[k] = bad ? w[k] : r;
+      flags |= bad ? (1u << (4 * u + k)) : 0u;
+    }
+    v[u] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  return flags;
+}
+
+// Queues the flagged pairs of one warp step whose vectors start at vector
+// `base` of the row at element offset oy of y (draining the queue first when it
+// would overflow; a step with more flagged pairs than the queue holds is
+// finished right away).
+template <int K>
+__device__ __forceinline__ void queue_step(uint32_t flags, int64_t base, int64_t oy, uint16_t* y,
+                                           uint32_t* queue, int* q_count, int& count, int lane) {
+  if (!__any_sync(0xffffffffu, flags)) return;
+  const int mine = 2 * __popc(flags);
+  const int total = __reduce_add_sync(0xffffffffu, mine);
+  if (count + total > kQueue) {  // make room
+    drain_queue<K>(queue, count, y, lane);
+    if (lane == 0) *q_count = 0;
+    __syncwarp();
+    count = 0;
+  }
+  if (total > kQueue) {  // pathological step: finish its pairs right away
+    __syncwarp();
+    for (uint32_t f = flags; f; f &= f - 1) {
+      int bit = __ffs(f) - 1;
+      int64_t e = oy + (base + (bit >> 2) * 32 + lane) * 8 + (bit & 3) * 2;
+      y[e] = unary_h<K>(y[e]);
+      y[e + 1] = unary_h<K>(y[e + 1]);
+    }
+    __syncwarp();
+    return;
+  }
+  if (mine) {
+    int slot = atomicAdd(q_count, mine);
+    for (uint32_t f = flags; f; f &= f - 1) {
+      int bit = __ffs(f) - 1;
+      uint32_t e = (uint32_t)(oy + (base + (bit >> 2) * 32 + lane) * 8 + (bit & 3) * 2);
+      queue[slot] = e;
+      queue[slot + 1] = e + 1;
+      slot += 2;
+    }
+  }
+  count += total;
+}
+
 // rows x vec_per_row 16-byte vectors; row r of x/y starts at the offsets that
-// `outer` gives for r (a single row at offset 0 for dense tensors).  blockIdx.y
-// walks rows, blockIdx.x / warps walk the vectors of a row.  Queue entries are
-// element offsets from y (the host keeps y's extent below 2^32 elements).
+// `outer` gives for r.  blockIdx.y walks rows, blockIdx.x / warps walk the
+// vectors of a row.  Queue entries are element offsets from y (the host keeps
+// y's extent below 2^32 elements).
 template <int K>
 __global__ void __launch_bounds__(kThreads) unary_f16_vec(const uint16_t* x, uint16_t* y, Index6 outer,
-                                                          int64_t vec_per_row, int64_t rows,
-                                                          const uint16_t* xt, uint16_t* yt, int tail) {
+                                                          int64_t vec_per_row, int64_t rows) {
   __shared__ uint32_t queue[kThreads / 32][kQueue];
   __shared__ int q_count[kThreads / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -81,57 +155,122 @@ __global__ void __launch_bounds__(kThreads) unary_f16_vec(const uint16_t* x, uin
         int64_t i = base + u * 32 + lane;
         v[u] = i < vec_per_row ? xs[i] : make_uint4(0, 0, 0, 0);
       }
-      uint32_t flags = 0;  // bit (4u + w): word w of vector u needs the exact routine
+      uint32_t flags = fast_step<K>(v);
 #pragma unroll
       for (int u = 0; u < kVec; ++u) {
-        uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          bool bad;
-          uint32_t r = unary_h2_deferred<K == kSilu>(w[k], bad);
-          w[k] = bad ? w[k] : r;  // flagged pairs keep their input bits for the exact pass
-          flags |= bad ? (1u << (4 * u + k)) : 0u;
-        }
         int64_t i = base + u * 32 + lane;
-        if (i < vec_per_row) ys[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        if (i < vec_per_row) ys[i] = v[u];
         else flags &= ~(0xfu << (4 * u));
       }
-      const int mine = 2 * __popc(flags);
-      const int total = __reduce_add_sync(0xffffffffu, mine);
-      if (total == 0) continue;
-      if (count + total > kQueue) {  // make room
-        drain_queue<K>(queue[warp], count, y, lane);
-        if (lane == 0) q_count[warp] = 0;
-        __syncwarp();
-        count = 0;
-      }
-      if (total > kQueue) {  // pathological step: finish its pairs right away
-        __syncwarp();
-        for (uint32_t f = flags; f; f &= f - 1) {
-          int bit = __ffs(f) - 1;
-          int64_t e = oy + (base + (bit >> 2) * 32 + lane) * 8 + (bit & 3) * 2;
-          y[e] = unary_h<K>(y[e]);
-          y[e + 1] = unary_h<K>(y[e + 1]);
-        }
-        __syncwarp();
-        continue;
-      }
-      if (mine) {
-        int slot = atomicAdd(&q_count[warp], mine);
-        for (uint32_t f = flags; f; f &= f - 1) {
-          int bit = __ffs(f) - 1;
-          uint32_t e = (uint32_t)(oy + (base + (bit >> 2) * 32 + lane) * 8 + (bit & 3) * 2);
-          queue[warp][slot] = e;
-          queue[warp][slot + 1] = e + 1;
-          slot += 2;
-        }
-      }
-      count += total;
+      queue_step<K>(flags, base, oy, y, queue[warp], &q_count[warp], count, lane);
     }
   }
   drain_queue<K>(queue[warp], count, y, lane);
-  if (blockIdx.x == 0 && blockIdx.y == 0 && (int)threadIdx.x < tail)
-    yt[threadIdx.x] = unary_h<K>(xt[threadIdx.x]);
+}
+
+// Dense fp16, 16-byte aligned, arithmetic core (used below the table path's
+// size threshold): nvec 16-byte vectors plus a scalar tail; x may equal y.
+// Warp tiles (32 lanes x kVec vectors) go round-robin over all warps of a
+// one-wave grid, the next tile prefetched into registers while the current one
+// is computed.
+constexpr int kTileVecs = 32 * kVec;
+
+template <int K>
+__global__ void __launch_bounds__(kThreads) unary_f16_dense(const uint16_t* x, uint16_t* y, int nvec,
+                                                               const uint16_t* xt, uint16_t* yt, int tail) {
+  __shared__ uint32_t queue[kThreads / 32][kQueue];
+  __shared__ int q_count[kThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint4* xs = reinterpret_cast<const uint4*>(x) + lane;
+  uint4* ys = reinterpret_cast<uint4*>(y) + lane;
+  const int full = nvec / kTileVecs;
+  const int tiles = (nvec + kTileVecs - 1) / kTileVecs;
+  const int warps = gridDim.x * (kThreads / 32);
+  int tile = blockIdx.x * (kThreads / 32) + warp;
+  if (lane == 0) q_count[warp] = 0;
+  __syncwarp();
+  int count = 0;
+  uint4 next[kVec];
+  auto fetch = [&](int t) {
+    const uint4* src = xs + (size_t)t * kTileVecs;
+    if (t < full) {
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) next[u] = src[u * 32];
+    } else if (t < tiles) {
+#pragma unroll
+      for (int u = 0; u < kVec; ++u)
+        next[u] = t * kTileVecs + u * 32 + lane < nvec ? src[u * 32] : make_uint4(0, 0, 0, 0);
+    }
+  };
+  fetch(tile);
+  for (; tile < tiles; tile += warps) {
+    uint4 v[kVec];
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) v[u] = next[u];
+    fetch(tile + warps);
+    const int base = tile * kTileVecs;
+    uint32_t flags = fast_step<K>(v);
+    if (tile < full) {
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) ys[base + u * 32] = v[u];
+    } else {
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) {
+        if (base + u * 32 + lane < nvec) ys[base + u * 32] = v[u];
+        else flags &= ~(0xfu << (4 * u));
+      }
+    }
+    queue_step<K>(flags, base, 0, y, queue[warp], &q_count[warp], count, lane);
+  }
+  drain_queue<K>(queue[warp], count, y, lane);
+  if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = unary_h<K>(xt[threadIdx.x]);
+}
+
+// Dense fp16, 16-byte aligned, table core: each block (one per SM, 1024
+// threads) copies the 128 KB table of the op into shared memory, then maps
+// 16-byte vectors on a grid-stride loop, four independent vectors per thread in
+// flight; the first four are requested before the table copy to overlap it.  One shared-memory read per element and no transcendental work: the
+// kernel is bound by HBM.  x may equal y.
+constexpr int kLutThreads = 1024;
+constexpr int kLutBytes = 65536 * 2;
+constexpr int64_t kLutMinVecs = (int64_t)4 << 20;  // below ~34M elements the table copy does not pay
+
+__device__ __forceinline__ uint32_t lut_word(const uint16_t* lut, uint32_t w) {
+  return (uint32_t)lut[w & 0xffffu] | ((uint32_t)lut[w >> 16] << 16);
+}
+__device__ __forceinline__ uint4 lut_vec(const uint16_t* lut, uint4 v) {
+  return make_uint4(lut_word(lut, v.x), lut_word(lut, v.y), lut_word(lut, v.z), lut_word(lut, v.w));
+}
+
+__global__ void __launch_bounds__(kLutThreads) unary_f16_lut(const uint16_t* table, const uint16_t* x,
+                                                             uint16_t* y, int64_t nvec, const uint16_t* xt,
+                                                             uint16_t* yt, int tail) {
+  extern __shared__ __align__(16) uint16_t lut[];
+  const uint4* xs = reinterpret_cast<const uint4*>(x);
+  uint4* ys = reinterpret_cast<uint4*>(y);
+  const int64_t stride = (int64_t)gridDim.x * kLutThreads;
+  int64_t i = (int64_t)blockIdx.x * kLutThreads + threadIdx.x;
+  uint4 cur[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) cur[k] = i + k * stride < nvec ? xs[i + k * stride] : make_uint4(0, 0, 0, 0);
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(table);
+    uint4* dst = reinterpret_cast<uint4*>(lut);
+    for (int t = threadIdx.x; t < kLutBytes / 16; t += kLutThreads) dst[t] = src[t];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (i + k * stride < nvec) ys[i + k * stride] = lut_vec(lut, cur[k]);
+  for (i += 4 * stride; i + 3 * stride < nvec; i += 4 * stride) {
+    const uint4 v0 = xs[i], v1 = xs[i + stride], v2 = xs[i + 2 * stride], v3 = xs[i + 3 * stride];
+    ys[i] = lut_vec(lut, v0);
+    ys[i + stride] = lut_vec(lut, v1);
+    ys[i + 2 * stride] = lut_vec(lut, v2);
+    ys[i + 3 * stride] = lut_vec(lut, v3);
+  }
+  for (; i < nvec; i += stride) ys[i] = lut_vec(lut, xs[i]);
+  if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = lut[xt[threadIdx.x]];
 }
 
 // Any layout (also unaligned dense), one element per thread.
@@ -387,17 +526,27 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
     const int64_t total_vec = c.numel / 8;
     const int tail = (int)(c.numel - total_vec * 8);
     const int64_t chunk = (int64_t)1 << 28;  // vectors per launch: 2^31 elements
-    Index6 none;
-    none.ndim = 0;
     for (int64_t v0 = 0; v0 < total_vec || (v0 == 0 && tail); v0 += chunk) {
       int64_t nvec = total_vec - v0 < chunk ? total_vec - v0 : chunk;
       bool last = v0 + chunk >= total_vec;
-      unsigned grid = resident_grid(unary_f16_vec<K>, kThreads, 0, nvec ? nvec : 1,
-                                    (int64_t)kThreads * kVec);
-      unary_f16_vec<K><<<grid, kThreads, 0, s>>>(
-          (const uint16_t*)x->data + v0 * 8, (uint16_t*)y->data + v0 * 8, none, nvec, 1,
-          (const uint16_t*)x->data + total_vec * 8, (uint16_t*)y->data + total_vec * 8,
-          last ? tail : 0);
+      if (nvec >= kLutMinVecs) {
+        const uint16_t* table = nullptr;
+        TTN_TRY(unary_table(K, s, &table));
+        TTN_TRY(ensure_dynamic_smem((const void*)unary_f16_lut, kLutBytes));
+        int64_t want = (nvec + 4 * kLutThreads - 1) / (4 * kLutThreads);
+        unsigned grid = (unsigned)(want < sm_count() ? want : sm_count());
+        unary_f16_lut<<<grid, kLutThreads, kLutBytes, s>>>(
+            table, (const uint16_t*)x->data + v0 * 8, (uint16_t*)y->data + v0 * 8, nvec,
+            (const uint16_t*)x->data + total_vec * 8, (uint16_t*)y->data + total_vec * 8,
+            last ? tail : 0);
+      } else {
+        unsigned grid = resident_grid(unary_f16_dense<K>, kThreads, 0, nvec ? nvec : 1,
+                                      (int64_t)kThreads * kVec);
+        unary_f16_dense<K><<<grid, kThreads, 0, s>>>(
+            (const uint16_t*)x->data + v0 * 8, (uint16_t*)y->data + v0 * 8, (int)nvec,
+            (const uint16_t*)x->data + total_vec * 8, (uint16_t*)y->data + total_vec * 8,
+            last ? tail : 0);
+      }
       TTN_TRY(launch_check(name));
       if (last) break;
     }
@@ -415,7 +564,7 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
     if (gx > fit) gx = fit;
     if (gx < 1) gx = 1;
     unary_f16_vec<K><<<dim3((unsigned)gx, (unsigned)gy), kThreads, 0, s>>>(
-        (const uint16_t*)x->data, (uint16_t*)y->data, ix, vpr, rows, nullptr, nullptr, 0);
+        (const uint16_t*)x->data, (uint16_t*)y->data, ix, vpr, rows);
     return launch_check(name);
   }
   TTN_TRY(to_index6(c, 2, ix, name));

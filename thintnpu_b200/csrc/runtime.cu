@@ -48,17 +48,22 @@ int sm_count() {
 
 ttn_status ensure_dynamic_smem(const void* kernel, int bytes) {
   static std::mutex mutex;
-  static std::map<std::pair<int, const void*>, int> granted;
-  if (bytes <= 48 * 1024) return TTN_OK;
+  static std::map<std::pair<int, const void*>, int> granted;  // dynamic bytes a launch may use
+  if (bytes <= 0) return TTN_OK;
   int device = 0;
   TTN_TRY(cuda_check(cudaGetDevice(&device), "cudaGetDevice"));
   std::lock_guard<std::mutex> lock(mutex);
   auto key = std::make_pair(device, kernel);
   auto it = granted.find(key);
-  if (it != granted.end() && it->second >= bytes) return TTN_OK;
+  if (it == granted.end()) {  // the default: 48 KB less the kernel's static shared memory
+    cudaFuncAttributes attr;
+    TTN_TRY(cuda_check(cudaFuncGetAttributes(&attr, kernel), "cudaFuncGetAttributes"));
+    it = granted.emplace(key, attr.maxDynamicSharedSizeBytes).first;
+  }
+  if (it->second >= bytes) return TTN_OK;
   TTN_TRY(cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                      "cudaFuncSetAttribute"));
-  granted[key] = bytes;
+  it->second = bytes;
   return TTN_OK;
 }
 

@@ -188,14 +188,6 @@ __global__ void __launch_bounds__(256) softmax_warp_rows_h8(const uint16_t* x, u
 constexpr int kRowsWarps = 8;
 constexpr int kRowMaxVec = 128;  // 1024 fp16 per row
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
-
 template <int PER>
 __global__ void __launch_bounds__(kRowsWarps * 32) softmax_rows_pipelined(const uint16_t* x, uint16_t* y,
                                                                           int64_t rows, int reduce,

@@ -57,6 +57,49 @@ __global__ void __launch_bounds__(128) blocked_to_nchw(const uint16_t* x, int64_
   }
 }
 
+// Register-transpose variant for hw % 4 == 0 and 8-byte aligned channel rows:
+// one thread per (plane, 4-pixel group) loads 4 pixels x 16 lanes (128 B,
+// contiguous per thread, consecutive threads contiguous) and writes 16 channel
+// rows of 4 pixels (8 B each; consecutive threads fill consecutive 8 B of a
+// row).  The 4x16 fp16 transpose is 32 byte permutes, no shared memory.
+__global__ void __launch_bounds__(256) blocked_to_nchw_regs(const uint4* x, int64_t n, int64_t c1,
+                                                            int64_t hw, int64_t channels, uint16_t* y,
+                                                            int64_t ybs, int64_t ycs) {
+  const int64_t groups = hw / 4;
+  const int64_t total = n * c1 * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    const int64_t plane = t / groups, g = t - plane * groups;
+    const int64_t b = plane / c1, cb = plane - b * c1;
+    const uint4* src = x + (plane * hw + g * 4) * 2;  // 2 uint4 (16 channels) per pixel
+    uint32_t in[4][8];                                 // [pixel][channel pair]
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint4 lo = src[p * 2], hi = src[p * 2 + 1];
+      in[p][0] = lo.x;
+      in[p][1] = lo.y;
+      in[p][2] = lo.z;
+      in[p][3] = lo.w;
+      in[p][4] = hi.x;
+      in[p][5] = hi.y;
+      in[p][6] = hi.z;
+      in[p][7] = hi.w;
+    }
+    const int valid = (int)(channels - cb * 16 < 16 ? channels - cb * 16 : 16);
+    uint16_t* dst = y + b * ybs + (cb * 16) * ycs + g * 4;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      if (c < valid) {
+        const uint32_t sel = (c & 1) ? 0x7632u : 0x5410u;  // high or low lane of each word
+        uint2 o;
+        o.x = __byte_perm(in[0][c >> 1], in[1][c >> 1], sel);
+        o.y = __byte_perm(in[2][c >> 1], in[3][c >> 1], sel);
+        *reinterpret_cast<uint2*>(dst + c * ycs) = o;
+      }
+    }
+  }
+}
+
 // x: NCHW [n, channels, hw] -> y: [n, ceil(channels/16), hw, 16], zero-padded.
 __global__ void __launch_bounds__(128) nchw_to_blocked(const uint16_t* x, int64_t n,
                                                        int64_t channels, int64_t hw, uint16_t* y,
@@ -351,6 +394,13 @@ ttn_status ttn_nc1hwc0_to_nchw_f16(const void* x, int64_t n, int64_t c1, int64_t
   if (!aligned16(x)) return fail(TTN_INVALID_ARG, "%s: x must be 16-byte aligned", name);
   if (((uintptr_t)y & 1u)) return fail(TTN_INVALID_ARG, "%s: y not 2-byte aligned", name);
   bool vec = aligned16(y) && y_batch_stride % 8 == 0 && y_channel_stride % 8 == 0;
+  if (((uintptr_t)y & 7u) == 0 && y_batch_stride % 4 == 0 && y_channel_stride % 4 == 0 && hw % 4 == 0) {
+    int64_t threads = n * c1 * (hw / 4);
+    blocked_to_nchw_regs<<<grid_for(threads, 256, 8), 256, 0, (cudaStream_t)stream>>>(
+        (const uint4*)x, n, c1, hw, (c1 * 16 < channels ? c1 * 16 : channels), (uint16_t*)y,
+        y_batch_stride, y_channel_stride);
+    return launch_check(name);
+  }
   int64_t jobs = n * c1 * ((hw + kPix - 1) / kPix);
   unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * 16 ? jobs : (int64_t)sm_count() * 16);
   blocked_to_nchw<<<grid, 128, 0, (cudaStream_t)stream>>>(

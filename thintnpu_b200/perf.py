@@ -145,6 +145,35 @@ class Config5:
 CONFIGS = {1: Config1, 2: Config2, 3: Config3, 5: Config5}
 
 
+def unary_sweep(op: str = "silu", sizes_m=(13, 26, 52, 105, 210, 420, 839), reps: int = 10) -> dict:
+    """In-place fp16 SiLU/sigmoid bandwidth by tensor size (4 algorithmic bytes per
+    element): N(0,1) inputs, 3 warm-ups, then the median of `reps` launches each
+    timed with CUDA events after flushing L2 with a 256 MB write."""
+    import thintnpu_b200
+    thintnpu_b200.load()
+    device = torch.device("cuda", torch.cuda.current_device())
+    fn = ops.silu_ if op == "silu" else (lambda t: ops.sigmoid(t, out=t))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    out = {}
+    for m in sizes_m:
+        x = _gen((m * 1000 * 1000,), m, device)
+        for _ in range(3):
+            fn(x)
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn(x)
+            e.record()
+            torch.cuda.synchronize(device)
+            times.append(s.elapsed_time(e))
+        t = sorted(times)[len(times) // 2]
+        out[f"{m}M"] = {"us": round(t * 1000, 1), "gbs": round(4 * x.numel() / t / 1e6)}
+        del x
+    return out
+
+
 def run_config(args):
     import torch.distributed as dist
     cfg = CONFIGS[args.config]()
