@@ -161,3 +161,20 @@ def test_dfl_decode_views_batches_and_odd_grids(device):
     want = oops.dfl_decode(head[:, :64].contiguous(), head[:, 64:].contiguous(), shapes, strides)
     _, stride_row = oops.make_anchors(shapes, strides)
     _check_decode(got, want, stride_row, 17)
+
+
+@pytest.mark.parametrize("batch,nc", [(52, 80), (2, 120)])
+def test_dfl_decode_head_views_tiled(device, batch, nc):
+    """Box and class rows as views of one [B, 64 + nc, 8400] head: the tiled box
+    kernel plus the row-family sigmoid (table kernel at B=52, arithmetic at B=2)."""
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(5 + nc)
+    shapes = [(80, 80), (40, 40), (20, 20)]
+    head = (torch.randn(batch, 64 + nc, 8400, generator=g) * 3).half()
+    strides = [8.0, 16.0, 32.0]
+    dev = head.to(device)
+    got = ttn.dfl_decode(dev[:, :64], dev[:, 64:], shapes, strides)
+    want = oops.dfl_decode(head[:, :64].contiguous(), head[:, 64:].contiguous(), shapes, strides)
+    _, stride_row = oops.make_anchors(shapes, strides)
+    exact = _check_decode(got, want, stride_row, nc)
+    assert exact > 0.98, exact

@@ -46,10 +46,27 @@ ttn_status ensure_dynamic_smem(const void* kernel, int bytes);
 // Largest opt-in dynamic shared memory per block on the current device.
 int max_dynamic_smem();
 
+// Fork/join of an independent branch of one op: branch_fork makes the calling
+// thread's auxiliary stream for the current device wait for the work already on
+// `stream` and returns it; branch_join makes `stream` wait for everything put on
+// the auxiliary stream since.  Under stream capture the branch becomes a
+// parallel path of the graph.  Every fork must be followed by its join.
+ttn_status branch_fork(cudaStream_t stream, cudaStream_t* aux);
+ttn_status branch_join(cudaStream_t stream);
+
 // The 65,536-entry fp16 table of SiLU (kind 0) or sigmoid (kind 1) on the
 // current device, indexed by input bits and equal to silu_h / sigmoid_h for
 // every input; built on `stream` by the first call.
 ttn_status unary_table(int kind, cudaStream_t stream, const uint16_t** table);
+
+// SiLU (kind 0) or sigmoid (kind 1), fp16, over a two-level family of rows:
+// element (i1, i2, c) of x sits at x + i1*xs1 + i2*xs2 + c, of y likewise, for
+// i1 < n1, i2 < n2, c < ncols.  Rows must be 16-byte aligned (x, y 16-byte
+// aligned; strides and ncols multiples of 8).  x may equal y.  Bit-equal to
+// silu_h / sigmoid_h per element.
+ttn_status unary_rows2_f16(int kind, const uint16_t* x, int64_t xs1, int64_t xs2, uint16_t* y,
+                           int64_t ys1, int64_t ys2, int64_t n1, int64_t n2, int64_t ncols,
+                           cudaStream_t stream);
 
 // Blocks of `kernel` (at `threads` threads, `smem` dynamic bytes) resident per SM
 // on the current device, from the occupancy calculator; cached per (device, kernel).
@@ -97,6 +114,22 @@ int64_t numel(const ttn_tensor* t);
 Coalesced coalesce(const ttn_tensor* const* views, int count);
 // True when the view is dense row-major (C-contiguous) from its data pointer.
 bool is_contiguous(const ttn_tensor* t);
+
+// n / d for 32-bit n and a runtime divisor d >= 1 by one multiply-high: with
+// l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1 (which fits 32 bits),
+// floor(n / d) = (mulhi(n, m) + n) >> l for every n < 2^32 (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994).
+struct FastDiv {
+  uint32_t d, m, l;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t divisor) : d(divisor), m(0), l(0) {
+    while ((1ull << l) < d) ++l;
+    m = (uint32_t)((((1ull << 32) * ((1ull << l) - d)) / d) + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    return (uint32_t)(((uint64_t)__umulhi(n, m) + n) >> l);
+  }
+};
 
 // Device-side iteration space for up to 6 coalesced dims and 3 operands.
 struct Index6 {

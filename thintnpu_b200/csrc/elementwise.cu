@@ -273,6 +273,92 @@ __global__ void __launch_bounds__(kLutThreads) unary_f16_lut(const uint16_t* tab
   if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = lut[xt[threadIdx.x]];
 }
 
+// Table core over a two-level family of rows (see unary_rows2_f16): the flat
+// vector index g splits into (row, column) and row into (i1, i2) with
+// multiply-high divisions; four independent vectors per thread in flight.
+__global__ void __launch_bounds__(kLutThreads) unary_f16_lut2d(const uint16_t* table, const uint16_t* x,
+                                                               int64_t xs1, int64_t xs2, uint16_t* y,
+                                                               int64_t ys1, int64_t ys2, FastDiv vpr,
+                                                               FastDiv n2, uint32_t total) {
+  extern __shared__ __align__(16) uint16_t lut[];
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(table);
+    uint4* dst = reinterpret_cast<uint4*>(lut);
+    for (int t = threadIdx.x; t < kLutBytes / 16; t += kLutThreads) dst[t] = src[t];
+  }
+  __syncthreads();
+  auto locate = [&](uint32_t gi, int64_t& ox, int64_t& oy) {
+    const uint32_t row = vpr.div(gi), col = gi - row * vpr.d;
+    const uint32_t i1 = n2.div(row), i2 = row - i1 * n2.d;
+    ox = (int64_t)i1 * xs1 + (int64_t)i2 * xs2 + (int64_t)col * 8;
+    oy = (int64_t)i1 * ys1 + (int64_t)i2 * ys2 + (int64_t)col * 8;
+  };
+  const uint32_t stride = gridDim.x * kLutThreads;  // total < 2^31, so g + 3 * stride fits
+  uint32_t g = blockIdx.x * kLutThreads + threadIdx.x;
+  for (; g + 3 * stride < total; g += 4 * stride) {
+    int64_t ox[4], oy[4];
+    uint4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      locate(g + k * stride, ox[k], oy[k]);
+      v[k] = *reinterpret_cast<const uint4*>(x + ox[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(y + oy[k]) = lut_vec(lut, v[k]);
+  }
+  for (; g < total; g += stride) {
+    int64_t ox, oy;
+    locate(g, ox, oy);
+    *reinterpret_cast<uint4*>(y + oy) = lut_vec(lut, *reinterpret_cast<const uint4*>(x + ox));
+  }
+}
+
+template <int K>
+ttn_status rows2(const uint16_t* x, int64_t xs1, int64_t xs2, uint16_t* y, int64_t ys1, int64_t ys2,
+                 int64_t n1, int64_t n2, int64_t ncols, cudaStream_t s) {
+  const int64_t vpr = ncols / 8, total = n1 * n2 * vpr;
+  if (total >= kLutMinVecs && total < ((int64_t)1 << 31)) {
+    const uint16_t* table = nullptr;
+    TTN_TRY(unary_table(K, s, &table));
+    TTN_TRY(ensure_dynamic_smem((const void*)unary_f16_lut2d, kLutBytes));
+    int64_t want = (total + 4 * kLutThreads - 1) / (4 * kLutThreads);
+    unsigned grid = (unsigned)(want < sm_count() ? want : sm_count());
+    unary_f16_lut2d<<<grid, kLutThreads, kLutBytes, s>>>(table, x, xs1, xs2, y, ys1, ys2,
+                                                         FastDiv((uint32_t)vpr), FastDiv((uint32_t)n2),
+                                                         (uint32_t)total);
+    return launch_check("unary_rows2_f16");
+  }
+  // arithmetic rows kernel; its queue holds 32-bit element offsets from y, so
+  // each launch covers a slice of i1 whose y extent stays below 2^32
+  const int64_t extent = (n2 - 1) * ys2 + ncols;
+  if (extent >= ((int64_t)1 << 32)) return fail(TTN_UNSUPPORTED, "unary_rows2_f16: row family too wide");
+  int64_t per = ys1 > 0 ? (((int64_t)1 << 32) - extent) / ys1 + 1 : n1;
+  if (per < 1) per = 1;
+  for (int64_t i0 = 0; i0 < n1; i0 += per) {
+    const int64_t m1 = n1 - i0 < per ? n1 - i0 : per;
+    Index6 ix;
+    ix.ndim = 2;
+    ix.size[0] = n2;
+    ix.size[1] = m1;
+    ix.stride[0][0] = xs2;
+    ix.stride[0][1] = xs1;
+    ix.stride[1][0] = ys2;
+    ix.stride[1][1] = ys1;
+    ix.stride[2][0] = ix.stride[2][1] = 0;
+    const int64_t rows = m1 * n2;
+    int64_t cap = (int64_t)sm_count() * resident_blocks((const void*)unary_f16_vec<K>, kThreads, 0);
+    int64_t gy = rows < 65535 ? rows : 65535;
+    int64_t gx = (vpr + kThreads * kVec - 1) / (kThreads * kVec);
+    int64_t fit = (cap + gy - 1) / gy;
+    if (gx > fit) gx = fit;
+    if (gx < 1) gx = 1;
+    unary_f16_vec<K><<<dim3((unsigned)gx, (unsigned)gy), kThreads, 0, s>>>(x + i0 * xs1, y + i0 * ys1, ix,
+                                                                          vpr, rows);
+    TTN_TRY(launch_check("unary_rows2_f16"));
+  }
+  return TTN_OK;
+}
+
 // Any layout (also unaligned dense), one element per thread.
 template <int K, typename T>
 __global__ void __launch_bounds__(kThreads) unary_strided(const T* x, T* y, Index6 ix, int64_t n) {
@@ -579,6 +665,19 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
 }
 
 }  // namespace
+
+ttn_status unary_rows2_f16(int kind, const uint16_t* x, int64_t xs1, int64_t xs2, uint16_t* y,
+                           int64_t ys1, int64_t ys2, int64_t n1, int64_t n2, int64_t ncols,
+                           cudaStream_t stream) {
+  if (n1 <= 0 || n2 <= 0 || ncols <= 0) return TTN_OK;
+  if (ncols % 8 || xs1 % 8 || xs2 % 8 || ys1 % 8 || ys2 % 8 || !aligned16(x) || !aligned16(y))
+    return fail(TTN_INVALID_ARG, "unary_rows2_f16: rows must be 16-byte aligned");
+  if (n2 >= ((int64_t)1 << 32) || ncols / 8 >= ((int64_t)1 << 32))
+    return fail(TTN_UNSUPPORTED, "unary_rows2_f16: dimension beyond 2^32");
+  return kind == kSilu ? rows2<kSilu>(x, xs1, xs2, y, ys1, ys2, n1, n2, ncols, stream)
+                       : rows2<kSigmoid>(x, xs1, xs2, y, ys1, ys2, n1, n2, ncols, stream);
+}
+
 }  // namespace ttn
 
 using namespace ttn;

@@ -84,6 +84,38 @@ int resident_blocks(const void* kernel, int threads, size_t smem) {
   return blocks;
 }
 
+namespace {
+struct Branch {
+  cudaStream_t aux = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+thread_local Branch t_branch[64];  // per host thread and device: calls on one thread are ordered
+}  // namespace
+
+ttn_status branch_fork(cudaStream_t stream, cudaStream_t* aux) {
+  int device = 0;
+  TTN_TRY(cuda_check(cudaGetDevice(&device), "cudaGetDevice"));
+  if (device < 0 || device >= 64) return fail(TTN_UNSUPPORTED, "branch_fork: device %d", device);
+  Branch& b = t_branch[device];
+  if (!b.aux) {
+    TTN_TRY(cuda_check(cudaStreamCreateWithFlags(&b.aux, cudaStreamNonBlocking), "cudaStreamCreate"));
+    TTN_TRY(cuda_check(cudaEventCreateWithFlags(&b.fork, cudaEventDisableTiming), "cudaEventCreate"));
+    TTN_TRY(cuda_check(cudaEventCreateWithFlags(&b.join, cudaEventDisableTiming), "cudaEventCreate"));
+  }
+  TTN_TRY(cuda_check(cudaEventRecord(b.fork, stream), "cudaEventRecord"));
+  TTN_TRY(cuda_check(cudaStreamWaitEvent(b.aux, b.fork, 0), "cudaStreamWaitEvent"));
+  *aux = b.aux;
+  return TTN_OK;
+}
+
+ttn_status branch_join(cudaStream_t stream) {
+  int device = 0;
+  TTN_TRY(cuda_check(cudaGetDevice(&device), "cudaGetDevice"));
+  Branch& b = t_branch[device];
+  TTN_TRY(cuda_check(cudaEventRecord(b.join, b.aux), "cudaEventRecord"));
+  return cuda_check(cudaStreamWaitEvent(stream, b.join, 0), "cudaStreamWaitEvent");
+}
+
 int max_dynamic_smem() {
   static std::mutex mutex;
   static int cached[64] = {0};

@@ -457,103 +457,130 @@ __global__ void __launch_bounds__(128) dfl_decode(const __half* box, int64_t box
   }
 }
 
-// Tiled decode for 8-aligned anchors: a block stages [64 + nc rows] x 64 anchors
-// of logits in shared memory with 16-byte loads, runs one (anchor, side) DFL
-// reduction per thread and the class sigmoids two lanes at a time, then stores
-// the [4 + nc] x 64 output tile with 16-byte stores.
-constexpr int kTileA = 64;
+// dfl_side for two anchors at once: w[i] holds bin i of both anchors as a half2.
+// Same rounding points: fp16 probabilities (one packed conversion per bin pair),
+// fp32 expectation accumulated over bins 1..15 in order, rounded to fp16.
+__device__ __forceinline__ float2 dfl_side2(const uint32_t (&w)[16]) {
+  float2 v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+  float m0 = v[0].x, m1 = v[0].y;
+#pragma unroll
+  for (int i = 1; i < 16; ++i) {
+    m0 = row_max(m0, v[i].x);
+    m1 = row_max(m1, v[i].y);
+  }
+  const ShiftLog2 l0 = shift_log2(m0), l1 = shift_log2(m1);
+  float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v[i].x = exp_shifted(v[i].x, l0);
+    v[i].y = exp_shifted(v[i].y, l1);
+    s0 = __fadd_rn(s0, v[i].x);
+    s1 = __fadd_rn(s1, v[i].y);
+  }
+  const float inv0 = __fdiv_rn(1.0f, s0), inv1 = __fdiv_rn(1.0f, s1);
+  float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+  for (int i = 1; i < 16; ++i) {
+    const float2 p = __half22float2(__floats2half2_rn(__fmul_rn(v[i].x, inv0), __fmul_rn(v[i].y, inv1)));
+    d0 = __fmaf_rn(p.x, (float)i, d0);
+    d1 = __fmaf_rn(p.y, (float)i, d1);
+  }
+  return make_float2(h16(d0), h16(d1));
+}
 
-template <int NC_MAX>
-__global__ void __launch_bounds__(256) dfl_decode_tiled(const __half* box, int64_t box_bs,
-                                                        int64_t box_cs, const __half* cls,
-                                                        int64_t cls_bs, int64_t cls_cs, int64_t n,
-                                                        int nc, int64_t anchors, Levels lv, bool xywh,
-                                                        __half* out) {
-  __shared__ __align__(16) uint16_t in_box[64][kTileA];
-  __shared__ __align__(16) uint16_t io_cls[NC_MAX][kTileA];
+// Box half of the decode for 8-aligned anchors: a block walks 128-anchor tiles
+// of the 64 box rows; the next tile streams into the other shared-memory buffer
+// with cp.async while this one is reduced.  Thread (side, anchor pair) runs the
+// two DFL reductions from half2 reads; thread (anchor) then decodes its four
+// coordinates; the 4 x 128 output tile leaves with 16-byte stores.  Index math
+// is 32-bit (anchors < 2^30).  The class rows are a separate elementwise sigmoid
+// (unary_rows2_f16).
+constexpr int kTileA = 128;
+
+__global__ void __launch_bounds__(256) dfl_box_tiled(const __half* box, int64_t box_bs, int64_t box_cs,
+                                                     int n, int anchors, Levels lv, bool xywh,
+                                                     __half* out, int64_t out_bs) {
+  __shared__ __align__(16) uint16_t in_box[2][64][kTileA];
   __shared__ float dist[4][kTileA];
   __shared__ __align__(16) uint16_t out_box[4][kTileA];
-  constexpr int kFixups = 512;  // queued (class row, anchor pair) fix-ups per tile
-  __shared__ uint16_t fixups[kFixups];
-  __shared__ int queued;
-  const int64_t tiles = (anchors + kTileA - 1) / kTileA;
+  const int tiles = (anchors + kTileA - 1) / kTileA;
+  const int jobs = n * tiles;
   const int tid = threadIdx.x;
-  for (int64_t job = blockIdx.x; job < n * tiles; job += gridDim.x) {
-    const int64_t b = job / tiles, a0 = (job % tiles) * kTileA;
-    const int vecs = (int)((anchors - a0 < kTileA ? anchors - a0 : kTileA) / 8);  // 16-byte columns
-    if (tid == 0) queued = 0;
-    // load: `vecs` uint4 per row
-    for (int v = tid; v < (64 + nc) * 8; v += blockDim.x) {
-      int row = v >> 3, col = (v & 7) * 8;
-      if ((v & 7) >= vecs) continue;
-      const __half* src = row < 64 ? box + b * box_bs + row * box_cs + a0 + col
-                                   : cls + b * cls_bs + (row - 64) * cls_cs + a0 + col;
-      uint4 q = *reinterpret_cast<const uint4*>(src);
-      uint16_t* dst = row < 64 ? &in_box[row][col] : &io_cls[row - 64][col];
-      *reinterpret_cast<uint4*>(dst) = q;
-    }
-    __syncthreads();
-    {  // DFL: thread -> (side, anchor)
-      int side = tid >> 6, a = tid & 63;
-      float v[16];
+  auto issue = [&](int job, int buf) {
+    if (job < jobs) {
+      const int b = job / tiles, a0 = (job - b * tiles) * kTileA;
+      const int vecs = (anchors - a0 < kTileA ? anchors - a0 : kTileA) / 8;
+      const __half* src = box + (int64_t)b * box_bs + a0;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = __half2float(hfrom(in_box[side * 16 + i][a]));
-      dist[side][a] = dfl_side(v);
+      for (int v = tid; v < 64 * (kTileA / 8); v += 256) {
+        const int row = v / (kTileA / 8), c = v % (kTileA / 8);
+        if (c < vecs) cp_async16(&in_box[buf][row][c * 8], src + row * box_cs + c * 8);
+      }
     }
-    // sigmoid in place on the class rows, two anchors per step; pairs the fast
-    // path cannot settle keep their logits and are queued for the exact routine
-    for (int e = tid; e < nc * (kTileA / 2); e += blockDim.x) {
-      int row = e / (kTileA / 2), col = (e % (kTileA / 2)) * 2;
-      uint32_t* p = reinterpret_cast<uint32_t*>(&io_cls[row][col]);
-      bool bad;
-      uint32_t r = unary_h2_deferred<false>(*p, bad);
-      if (bad) {
-        int slot = atomicAdd(&queued, 1);
-        if (slot < kFixups) fixups[slot] = (uint16_t)e;
-        else *p = unary_h2_fast<false>(*p);  // queue full: settle in place
+    cp_async_commit();
+  };
+  int buf = 0;
+  issue(blockIdx.x, 0);
+  for (int job = blockIdx.x; job < jobs; job += gridDim.x, buf ^= 1) {
+    issue(job + gridDim.x, buf ^ 1);  // that buffer's last reader finished before the previous sync
+    cp_async_wait<1>();
+    __syncthreads();
+    const int b = job / tiles, a0 = (job - b * tiles) * kTileA;
+    const int vecs = (anchors - a0 < kTileA ? anchors - a0 : kTileA) / 8;
+    {  // DFL: thread -> (side, anchor pair)
+      const int side = tid >> 6, a = (tid & 63) * 2;
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = *reinterpret_cast<const uint32_t*>(&in_box[buf][side * 16 + i][a]);
+      const float2 d = dfl_side2(w);
+      dist[side][a] = d.x;
+      dist[side][a + 1] = d.y;
+    }
+    __syncthreads();
+    if (tid < kTileA) {  // box decode: thread -> anchor
+      const int a = tid, idx = a0 + a;
+      int lstart = 0, lwidth = (int)lv.width[0];
+      float lstride = lv.stride[0];
+#pragma unroll
+      for (int k = 1; k < kMaxLevels; ++k) {  // starts increase: the last level begun holds idx
+        if (k < lv.count && idx >= (int)lv.start[k]) {
+          lstart = (int)lv.start[k];
+          lwidth = (int)lv.width[k];
+          lstride = lv.stride[k];
+        }
+      }
+      const int local = idx - lstart;
+      const int gy = local / lwidth;
+      const float ax = h16((float)(local - gy * lwidth) + 0.5f);
+      const float ay = h16((float)gy + 0.5f);
+      const float lx = h16(__fsub_rn(ax, dist[0][a])), ly = h16(__fsub_rn(ay, dist[1][a]));
+      const float ux = h16(__fadd_rn(ax, dist[2][a])), uy = h16(__fadd_rn(ay, dist[3][a]));
+      float q[4];
+      if (xywh) {  // x / 2 == x * 0.5 exactly (both are the correctly rounded half)
+        q[0] = h16(__fmul_rn(h16(__fadd_rn(lx, ux)), 0.5f));
+        q[1] = h16(__fmul_rn(h16(__fadd_rn(ly, uy)), 0.5f));
+        q[2] = h16(__fsub_rn(ux, lx));
+        q[3] = h16(__fsub_rn(uy, ly));
       } else {
-        *p = r;
+        q[0] = lx;
+        q[1] = ly;
+        q[2] = ux;
+        q[3] = uy;
       }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) out_box[c][a] = hbits(__float2half_rn(__fmul_rn(q[c], lstride)));
     }
     __syncthreads();
-    {
-      const int n_fix = queued < kFixups ? queued : kFixups;
-      for (int q = tid; q < 2 * n_fix; q += blockDim.x) {
-        int e = fixups[q >> 1];
-        int row = e / (kTileA / 2), col = (e % (kTileA / 2)) * 2 + (q & 1);
-        io_cls[row][col] = sigmoid_h(io_cls[row][col]);
-      }
+    if (tid < 4 * (kTileA / 8)) {
+      const int row = tid / (kTileA / 8), c = tid % (kTileA / 8);
+      if (c < vecs)
+        *reinterpret_cast<uint4*>(out + (int64_t)b * out_bs + (int64_t)row * anchors + a0 + c * 8) =
+            *reinterpret_cast<const uint4*>(&out_box[row][c * 8]);
     }
-    if (tid < kTileA * 4) {  // box decode: thread -> (coordinate, anchor)
-      int c = tid >> 6, a = tid & 63;
-      int64_t idx = a0 + a;
-      int l = 0;
-      while (l + 1 < lv.count && idx >= lv.start[l + 1]) ++l;
-      int64_t local = idx - lv.start[l];
-      float ax = h16((float)(local % lv.width[l]) + 0.5f);
-      float ay = h16((float)(local / lv.width[l]) + 0.5f);
-      float lx = h16(__fsub_rn(ax, dist[0][a])), ly = h16(__fsub_rn(ay, dist[1][a]));
-      float ux = h16(__fadd_rn(ax, dist[2][a])), uy = h16(__fadd_rn(ay, dist[3][a]));
-      float q;
-      if (xywh) {
-        q = c == 0 ? h16(__fdiv_rn(h16(__fadd_rn(lx, ux)), 2.0f))
-          : c == 1 ? h16(__fdiv_rn(h16(__fadd_rn(ly, uy)), 2.0f))
-          : c == 2 ? h16(__fsub_rn(ux, lx)) : h16(__fsub_rn(uy, ly));
-      } else {
-        q = c == 0 ? lx : c == 1 ? ly : c == 2 ? ux : uy;
-      }
-      out_box[c][a] = hbits(__float2half_rn(__fmul_rn(q, lv.stride[l])));
-    }
-    __syncthreads();
-    __half* o = out + b * (4 + nc) * anchors + a0;
-    for (int v = tid; v < (4 + nc) * 8; v += blockDim.x) {
-      int row = v >> 3, col = (v & 7) * 8;
-      if ((v & 7) >= vecs) continue;
-      const uint16_t* src = row < 4 ? &out_box[row][col] : &io_cls[row - 4][col];
-      *reinterpret_cast<uint4*>(o + row * anchors + col) = *reinterpret_cast<const uint4*>(src);
-    }
-    __syncthreads();
   }
+  cp_async_wait<0>();
 }
 
 template <typename T, typename U>
@@ -700,16 +727,26 @@ ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs, c
               box_bs % 2 == 0 && box_cs % 2 == 0 &&
               (!nc || (((uintptr_t)cls & 3u) == 0 && cls_bs % 2 == 0 && cls_cs % 2 == 0));
   cudaStream_t s = (cudaStream_t)stream;
-  bool tiled = nc <= 96 && anchors % 8 == 0 && ((uintptr_t)box & 15u) == 0 &&
+  bool tiled = anchors % 8 == 0 && anchors < ((int64_t)1 << 30) &&
+               n * ((anchors + kTileA - 1) / kTileA) < ((int64_t)1 << 31) && ((uintptr_t)box & 15u) == 0 &&
                ((uintptr_t)out & 15u) == 0 && box_bs % 8 == 0 && box_cs % 8 == 0 &&
                (!nc || (((uintptr_t)cls & 15u) == 0 && cls_bs % 8 == 0 && cls_cs % 8 == 0));
   if (tiled) {
     int64_t jobs = n * ((anchors + kTileA - 1) / kTileA);
-    unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * 8 ? jobs : (int64_t)sm_count() * 8);
-    dfl_decode_tiled<96><<<grid, 256, 0, s>>>((const __half*)box, box_bs, box_cs, (const __half*)cls,
-                                               cls_bs, cls_cs, n, (int)nc, anchors, lv, xywh != 0,
-                                               (__half*)out);
-    return launch_check(name);
+    unsigned grid = resident_grid(dfl_box_tiled, 256, 0, jobs, 1);
+    // the class sigmoid (HBM-bound) runs on a forked branch beside the box
+    // reduction (issue-bound); both read disjoint rows and write disjoint rows
+    cudaStream_t aux = s;
+    if (nc) TTN_TRY(branch_fork(s, &aux));
+    ttn_status st = nc ? unary_rows2_f16(1, (const uint16_t*)cls, cls_bs, cls_cs,
+                                         (uint16_t*)out + 4 * anchors, (4 + nc) * anchors, anchors, n,
+                                         nc, anchors, aux)
+                       : TTN_OK;
+    dfl_box_tiled<<<grid, 256, 0, s>>>((const __half*)box, box_bs, box_cs, (int)n, (int)anchors, lv,
+                                       xywh != 0, (__half*)out, (4 + nc) * anchors);
+    ttn_status launched = launch_check(name);
+    ttn_status joined = nc ? branch_join(s) : TTN_OK;
+    return st != TTN_OK ? st : launched != TTN_OK ? launched : joined;
   }
   if (pair) {
     int64_t work = n * (anchors / 2);

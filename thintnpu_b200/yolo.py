@@ -356,5 +356,6 @@ class OpPass:
         return self.output
 
     def launches_per_pass(self) -> int:
-        """Kernels one pass launches (one per step; every op is a single kernel)."""
-        return len(self.steps)
+        """Kernels one pass launches: one per step, two for the decode (the box
+        reduction and the class-row sigmoid, on forked branches)."""
+        return sum(2 if step.op == "decode" else 1 for step in self.steps)
