@@ -46,24 +46,46 @@ def test_unary_all_input_pairs_bit_exact(device, name, path):
     """Every ordered pair of fp16 inputs in one 32-bit word, 2^32 pairs in 16
     launches of 2^28.  The arithmetic core computes the two lanes of a word
     together (one shared reciprocal), so its result is a function of the pair;
-    row-strided views take that kernel, dense tensors the table kernel."""
+    views with three outer dims take that kernel, dense tensors the table kernel."""
     import thintnpu_b200 as ttn
     fn = getattr(ttn, name)
     table = getattr(oops, name)(ALL_HALVES).view(torch.int16).to(device)  # CPU result per input bits
     rows = 4096
-    pad = 0 if path == "table" else 8  # a row gap makes the view non-dense
-    buf = torch.empty(rows, 65536 + pad, 2, dtype=torch.int16, device=device)
-    x = buf[:, :65536]
+    if path == "table":  # dense
+        x = torch.empty(rows, 65536, 2, dtype=torch.int16, device=device)
+    else:  # gaps at three levels: the general row kernel (three outer dims)
+        buf = torch.empty(rows // 4, 3, 3, 65536 + 8, 2, dtype=torch.int16, device=device)
+        x = buf[:, :2, :2, :65536]
     x[..., 0] = torch.arange(65536, dtype=torch.int32, device=device).to(torch.int16)
     for h0 in range(0, 65536, rows):
-        x[..., 1] = torch.arange(h0, h0 + rows, dtype=torch.int32, device=device).to(torch.int16)[:, None]
-        y = fn(x.view(torch.float16)).view(torch.int16)
+        hi = torch.arange(h0, h0 + rows, dtype=torch.int32, device=device).to(torch.int16)
+        x[..., 1] = hi.view(x.shape[:-2])[..., None]
+        y = fn(x.view(torch.float16)).view(torch.int16).reshape(rows, 65536, 2)
         bad = (y[..., 0] != table[None, :]) | (y[..., 1] != table[h0:h0 + rows, None])
         if bool(bad.any()):
             r, c = (int(v) for v in bad.nonzero()[0])
             raise AssertionError(f"{name}/{path}: pair (lo=0x{c:04x}, hi=0x{h0 + r:04x}) -> "
                                  f"{int(y[r, c, 0]) & 0xffff:04x},{int(y[r, c, 1]) & 0xffff:04x}, "
                                  f"want {int(table[c]) & 0xffff:04x},{int(table[h0 + r]) & 0xffff:04x}")
+
+
+@pytest.mark.parametrize("rows", ["one outer dim", "two outer dims"])
+def test_unary_row_family_table_path(device, rows):
+    """Channel slices of a batch (the zero-copy concat views): 16-byte rows with
+    one or two outer dims and >= 2^22 vectors take the row-family table kernel."""
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(17)
+    base = (torch.randn(16, 96, 160, 160, generator=g) * 4).half()
+    def view(t):
+        return t[:, 4:92] if rows == "one outer dim" else t.view(16, 96, 25600)[:, 4:92, :25592]
+    dev = base.to(device)
+    ttn.silu_(view(dev))
+    want = base.clone()
+    want_view = view(want)
+    want_view.copy_(oops.silu(want_view.contiguous()))
+    assert_bits_equal(dev, want, rows)
+    got = ttn.sigmoid(view(base.to(device)))
+    assert_bits_equal(got, oops.sigmoid(view(base).contiguous()), rows + " sigmoid")
 
 
 @pytest.mark.parametrize("shape", [(1,), (3,), (7,), (100,), (2047,), (2048,), (2049,), (16385,),

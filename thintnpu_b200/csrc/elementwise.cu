@@ -638,6 +638,19 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
     }
     return TTN_OK;
   }
+  if (x->dtype == TTN_F16 && c.ndim >= 2 && c.ndim <= 3 && c.stride[0][0] == 1 && c.stride[1][0] == 1 &&
+      c.size[0] % 8 == 0 && aligned16(x->data) && aligned16(y->data) && c.size[1] < ((int64_t)1 << 32) &&
+      c.size[0] / 8 < ((int64_t)1 << 32)) {  // rows with up to two outer dims: table or arithmetic
+    bool rows16 = true;
+    for (int d = 1; d < c.ndim; ++d) rows16 = rows16 && c.stride[0][d] % 8 == 0 && c.stride[1][d] % 8 == 0;
+    if (rows16) {
+      const bool two = c.ndim == 3;
+      ttn_status st = unary_rows2_f16(K, (const uint16_t*)x->data, two ? c.stride[0][2] : 0, c.stride[0][1],
+                                      (uint16_t*)y->data, two ? c.stride[1][2] : 0, c.stride[1][1],
+                                      two ? c.size[2] : 1, c.size[1], c.size[0], s);
+      if (st != TTN_UNSUPPORTED) return st;  // too wide for 32-bit queue offsets: general paths below
+    }
+  }
   Index6 ix;
   int64_t vpr;
   const void* ptrs[2] = {x->data, y->data};
