@@ -505,34 +505,44 @@ __global__ void __launch_bounds__(kThreads) scalar_f16_dense(BinaryParams p, con
 
 // x, r, y: [n, c1, hw, 16] fp16; b: [c1*16].  Each uint4 covers half of one
 // pixel's 16 channel lanes, so its 8 bias values are contiguous in b.
-__global__ void __launch_bounds__(kThreads) bias_silu_residual(const uint4* x, const uint16_t* b,
-                                                               const uint4* r, uint4* y,
-                                                               int64_t nvec, int64_t hw,
-                                                               int64_t c1) {
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t vec_per_plane = hw * 2;  // 16 lanes = 2 uint4 per pixel
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
-    uint4 xv = x[i], rv = r[i];
-    int64_t plane = i / vec_per_plane;
-    int channel_block = (int)(plane % c1);
-    int half_sel = (int)(i & 1);
-    const uint4 bv = *reinterpret_cast<const uint4*>(b + channel_block * 16 + half_sel * 8);
-    uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-    uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-    uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-    uint32_t out[4];
+__device__ __forceinline__ uint4 bias_silu_residual_vec(uint4 xv, uint4 rv, uint4 bv) {
+  uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+  uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+  uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+  uint32_t out[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float2 fx = __half22float2(*reinterpret_cast<__half2*>(&xw[k]));
-      float2 fr = __half22float2(*reinterpret_cast<__half2*>(&rw[k]));
-      float2 fb = __half22float2(*reinterpret_cast<__half2*>(&bw[k]));
-      float lo = silu_fast_f32(fx.x + fb.x) + fr.x;
-      float hi = silu_fast_f32(fx.y + fb.y) + fr.y;
-      __half2 h = __floats2half2_rn(lo, hi);
-      out[k] = *reinterpret_cast<uint32_t*>(&h);
-    }
-    y[i] = make_uint4(out[0], out[1], out[2], out[3]);
+  for (int k = 0; k < 4; ++k) {
+    float2 fx = __half22float2(*reinterpret_cast<__half2*>(&xw[k]));
+    float2 fr = __half22float2(*reinterpret_cast<__half2*>(&rw[k]));
+    float2 fb = __half22float2(*reinterpret_cast<__half2*>(&bw[k]));
+    float lo = silu_fast_f32(fx.x + fb.x) + fr.x;
+    float hi = silu_fast_f32(fx.y + fb.y) + fr.y;
+    __half2 h = __floats2half2_rn(lo, hi);
+    out[k] = *reinterpret_cast<uint32_t*>(&h);
   }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// nvec 16-byte vectors (< 2^31) starting at plane p0; a plane is one (image,
+// channel block) of hw pixels = 2*hw vectors, and its bias block is
+// (p0 + plane) mod c1.  Two vectors per thread per step.
+__global__ void __launch_bounds__(kThreads) bias_silu_residual(const uint4* x, const uint16_t* b,
+                                                               const uint4* r, uint4* y, uint32_t nvec,
+                                                               FastDiv vec_per_plane, FastDiv c1,
+                                                               uint32_t p0) {
+  const uint32_t stride = gridDim.x * blockDim.x;
+  auto bias_of = [&](uint32_t i) {
+    const uint32_t plane = vec_per_plane.div(i) + p0;
+    const uint32_t block = plane - c1.div(plane) * c1.d;
+    return *reinterpret_cast<const uint4*>(b + block * 16 + (i & 1) * 8);
+  };
+  uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + stride < nvec; i += 2 * stride) {
+    const uint4 x0 = x[i], r0 = r[i], x1 = x[i + stride], r1 = r[i + stride];
+    y[i] = bias_silu_residual_vec(x0, r0, bias_of(i));
+    y[i + stride] = bias_silu_residual_vec(x1, r1, bias_of(i + stride));
+  }
+  if (i < nvec) y[i] = bias_silu_residual_vec(x[i], r[i], bias_of(i));
 }
 
 // ----------------------------------------------------------- host helpers
@@ -798,11 +808,22 @@ ttn_status ttn_bias_silu_residual_nc1hwc0_f16(const void* x, const void* bias,
   if (!x || !bias || !residual || !y) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
   if (!aligned16(x) || !aligned16(bias) || !aligned16(residual) || !aligned16(y))
     return fail(TTN_INVALID_ARG, "%s: pointers must be 16-byte aligned", name);
-  int64_t nvec = count / 8;
-  unsigned grid = grid_for(nvec, kThreads);
-  bias_silu_residual<<<grid, kThreads, 0, (cudaStream_t)stream>>>(
-      (const uint4*)x, (const uint16_t*)bias, (const uint4*)residual, (uint4*)y, nvec, hw, c1);
-  return launch_check(name);
+  // launches of whole planes, each below 2^31 vectors (32-bit index math)
+  const int64_t vpp = 2 * hw, planes = n * c1;
+  if (vpp >= ((int64_t)1 << 31) || c1 >= ((int64_t)1 << 31))
+    return fail(TTN_UNSUPPORTED, "%s: plane beyond 2^31 vectors", name);
+  const int64_t per = (((int64_t)1 << 31) - 1) / vpp;
+  for (int64_t p = 0; p < planes; p += per) {
+    const int64_t m = planes - p < per ? planes - p : per;
+    const int64_t nvec = m * vpp;
+    unsigned grid = grid_for(nvec, 2 * kThreads);
+    bias_silu_residual<<<grid, kThreads, 0, (cudaStream_t)stream>>>(
+        (const uint4*)x + p * vpp, (const uint16_t*)bias, (const uint4*)residual + p * vpp,
+        (uint4*)y + p * vpp, (uint32_t)nvec, FastDiv((uint32_t)vpp), FastDiv((uint32_t)c1),
+        (uint32_t)(p % c1));
+    TTN_TRY(launch_check(name));
+  }
+  return TTN_OK;
 }
 
 }  // extern "C"
