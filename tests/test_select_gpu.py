@@ -142,3 +142,42 @@ def test_batch_sharding_is_image_independent(device):
     for b in range(5):
         one = trace_bits(ttn.detection_select(dev[b:b + 1], 300, apply_sigmoid=True))
         assert np.array_equal(whole[b:b + 1], one)
+
+
+def _pair_stage_logits(pattern: str) -> torch.Tensor:
+    g = torch.Generator().manual_seed(31)
+    if pattern == "config5":
+        return config5_logits(2, seed=13)
+    if pattern == "few_anchors":
+        return config5_logits(2, seed=14, anchors=64)
+    nc = 3 if pattern == "few_classes" else 80
+    x = torch.randn(2, 4 + nc, 8400, generator=g) * 2 - 4
+    x[:, :4] = torch.rand(2, 4, 8400, generator=g) * 640
+    if pattern == "all_tied":
+        x[:, 4:] = 0.5
+    elif pattern == "many_high":  # fp16 sigmoid near 1 collapses many classes into ties
+        x[:, 4:] = torch.randn(2, nc, 8400, generator=g) * 0.5 + 3
+    x = x.half()
+    if pattern == "nan_rows":
+        flat = x.view(torch.int16)
+        pick = torch.rand(2, nc, 8400, generator=g) < 0.05
+        flat[:, 4:][pick] = torch.tensor(0x7E01, dtype=torch.int16)
+        flat[:, 4:][pick & (torch.rand(2, nc, 8400, generator=g) < 0.5)] = torch.tensor(-0x0200, dtype=torch.int16)
+    return x
+
+
+@pytest.mark.parametrize("pattern", ["config5", "all_tied", "many_high", "nan_rows", "few_classes", "few_anchors"])
+@pytest.mark.parametrize("nan_last", [False, True])
+def test_class_aware_pair_stage_without_trace(device, pattern, nan_last):
+    """Class-aware selection with the fused sigmoid and no trace (the one-kernel
+    pair stage: candidate pairs from the second-best keys) against the oracle."""
+    import thintnpu_b200 as ttn
+    logits = _pair_stage_logits(pattern)
+    view = logits.transpose(1, 2)
+    scores = view.clone()
+    scores[..., 4:] = torch.sigmoid(scores[..., 4:])
+    bits = scores.contiguous().view(torch.int16).numpy().view(np.uint16)
+    for k in (300, 7):
+        want = osel.select(bits, k, False, nan_last)["output"]
+        got = ttn.detection_select(logits.to(device).transpose(1, 2), k, nan_last=nan_last, apply_sigmoid=True)
+        assert np.array_equal(trace_bits(got), want), (pattern, k)

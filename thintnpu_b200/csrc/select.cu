@@ -176,52 +176,49 @@ __device__ __forceinline__ void rescan_anchor(const SelectView& v, int64_t b, in
   out_cls = best_cls;
 }
 
-// Pass 1 works on 32-bit composites (ordered logit key << 16) | (0xffff - class):
-// the ordered key maps fp16 bits to an unsigned value that grows with the value
-// (sign-magnitude to offset binary), so the largest composite is the largest
-// logit and, among equal logits, the lowest class.  Per score that is two
-// integer max/min ops plus the key build, two lanes at a time.  Anchors with any
-// NaN logit, or whose best and second-best logits give the same fp16 sigmoid
-// (this also covers +0/-0), are decided by the exact rescan.
-__device__ __forceinline__ uint32_t ordered_pair(uint32_t w) {
-  const uint32_t sign = (w >> 15) & 0x00010001u;        // 1 per negative lane
-  return w ^ ((sign * 0x7fffu) | 0x80008000u);           // negative: ~h, positive: h | 0x8000
-}
-__device__ __forceinline__ uint16_t unordered(uint32_t key) {
-  return (uint16_t)((key & 0x8000u) ? (key & 0x7fffu) : (~key & 0xffffu));
-}
-
+// Pass 1 works on the fp16 logits two anchors at a time (half2 lanes), since
+// fp16 sigmoid is monotonic: per class row, best = max(best, x) and second =
+// max(second, min(best, x)) (packed fp16 max/min), and the class moves only on
+// a strictly greater logit (a packed compare mask and one 3-input logic op), so
+// the first class of the largest logit is kept.  An inf or NaN logit makes
+// x * 0 NaN in a per-lane accumulator.  Anchors with such a logit, or whose
+// best and second-best logits give the same fp16 sigmoid (this also covers
+// +0/-0 and equal logits), are decided by the exact rescan.
 __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, bool nan_last,
                                                                  uint32_t* records, int64_t rec_pitch,
-                                                                 uint16_t* trace_max) {
+                                                                 uint16_t* trace_max, uint16_t* second_keys) {
   const int lane = threadIdx.x & 31;
   const int64_t groups = v.anchors / 8;
   const int64_t total = v.batch * groups;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const __half2 zero = __float2half2_rn(0.0f);
+  const __half2 neg_inf = __halves2half2(__ushort_as_half(0xfc00u), __ushort_as_half(0xfc00u));
   // warp-uniform trip count so the rescan can use the whole warp
   for (int64_t t0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); t0 < total; t0 += stride) {
     const int64_t t = t0 + lane;
     const bool live = t < total;
     const int64_t b = live ? t / groups : 0, a0 = live ? (t % groups) * 8 : 0;
-    uint32_t best[8], second[8];
+    __half2 best[4], second[4], special[4];
+    uint32_t cls[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) best[j] = second[j] = 0u;
-    uint32_t nan_any = 0;  // bit 15 / 31 of word k: a NaN logit in anchor 2k / 2k+1
-    uint32_t nan_word[4] = {0, 0, 0, 0};
+    for (int k = 0; k < 4; ++k) {
+      best[k] = second[k] = neg_inf;
+      special[k] = zero;
+      cls[k] = 0;
+    }
     if (live) {
       const uint16_t* p = v.base + b * v.sb + a0 + 4 * v.sc;
       auto fold = [&](const uint4 q, uint32_t c) {
-        const uint32_t cc = 0xffffu - c;
+        const uint32_t cpair = c * 0x00010001u;
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          nan_word[k] |= ((w[k] & 0x7fff7fffu) + 0x03ff03ffu) & 0x80008000u;
-          const uint32_t kw = ordered_pair(w[k]);
-          const uint32_t c0 = __byte_perm(kw, cc, 0x1054), c1 = __byte_perm(kw, cc, 0x3254);
-          second[2 * k] = max(second[2 * k], min(best[2 * k], c0));
-          best[2 * k] = max(best[2 * k], c0);
-          second[2 * k + 1] = max(second[2 * k + 1], min(best[2 * k + 1], c1));
-          best[2 * k + 1] = max(best[2 * k + 1], c1);
+          const __half2 x = *reinterpret_cast<const __half2*>(&w[k]);
+          const uint32_t m = __hgt2_mask(x, best[k]);
+          cls[k] = (cls[k] & ~m) | (cpair & m);
+          second[k] = __hmax2(second[k], __hmin2(best[k], x));
+          best[k] = __hmax2(best[k], x);
+          special[k] = __hfma2(x, zero, special[k]);
         }
       };
       int64_t c = 0;
@@ -238,21 +235,28 @@ __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, b
       for (; c < v.classes; ++c) fold(*reinterpret_cast<const uint4*>(p + c * v.sc), (uint32_t)c);
     }
     uint32_t out_bits[8], cls8[8], redo = 0;
+    uint32_t skey[8];  // key of the best score among the other classes (0xffff: none)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint16_t logit = unordered(best[j] >> 16);
-      cls8[j] = 0xffffu - (best[j] & 0xffffu);
+      const int k = j >> 1, sh = (j & 1) * 16;
+      const uint16_t logit = (uint16_t)(*reinterpret_cast<const uint32_t*>(&best[k]) >> sh);
+      const uint16_t flag = (uint16_t)(*reinterpret_cast<const uint32_t*>(&special[k]) >> sh);
+      cls8[j] = (cls[k] >> sh) & 0xffffu;
       const uint16_t s1 = sigmoid_h_fast(logit);
       out_bits[j] = s1;
-      const bool has_nan = (nan_word[j >> 1] >> ((j & 1) ? 31 : 15)) & 1u;
+      const bool has_special = (flag & 0x7fffu) > 0x7c00u;  // NaN: some logit was inf or NaN
       bool tie = false;
-      if (v.classes > 1) {
-        const uint16_t s2 = sigmoid_h_fast(unordered(second[j] >> 16));
-        tie = score_key(s2, nan_last) == score_key(s1, nan_last);
+      skey[j] = 0xffffu;
+      if (v.classes > 1) {  // sigmoid is monotonic: the second logit gives the second score
+        const uint16_t s2 = sigmoid_h_fast((uint16_t)(*reinterpret_cast<const uint32_t*>(&second[k]) >> sh));
+        skey[j] = score_key(s2, nan_last);
+        tie = skey[j] == score_key(s1, nan_last);
       }
-      if (live && (has_nan || tie)) redo |= 1u << j;
+      if (live && (has_special || tie)) {
+        redo |= 1u << j;
+        skey[j] = 0;  // rescanned anchors always gather every class in the fused pair stage
+      }
     }
-    (void)nan_any;
     // exact rescans, one anchor at a time with the whole warp
     uint32_t pending = __ballot_sync(0xffffffffu, redo != 0);
     while (pending) {
@@ -286,6 +290,10 @@ __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, b
 #pragma unroll
         for (int j = 0; j < 8; ++j) trace_max[b * v.anchors + a0 + j] = (uint16_t)out_bits[j];
       }
+      if (second_keys)
+        *reinterpret_cast<uint4*>(second_keys + b * v.anchors + a0) =
+            make_uint4(skey[0] | (skey[1] << 16), skey[2] | (skey[3] << 16), skey[4] | (skey[5] << 16),
+                       skey[6] | (skey[7] << 16));
     }
   }
 }
@@ -572,37 +580,17 @@ constexpr int kSmallWarps = kSmallThreads / 32;
 
 constexpr int kStageKeys = 24576;  // keys staged in shared memory (48 KB)
 
-template <bool kStaged>
-__global__ void __launch_bounds__(kSmallThreads) topk_small(TopkArgs args) {
+// Top k of n 16-bit keys in one CTA of 32*WARPS threads: radix select of the
+// k-th key, index-ordered collection of the winners, stable bitonic sort of
+// (key << 12 | slot) composites.  comp and src are shared arrays of cap >= k
+// (a power of two >= 32, k <= 4096); out[i] = key << 32 | index for i < k.
+template <int WARPS, typename KeyAt>
+__device__ void cta_topk(int64_t n, int64_t k, int cap, KeyAt key_at, uint32_t* comp, uint32_t* src,
+                         unsigned long long* out) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sel_bucket, sel_below;
-  __shared__ int warp_lt[kSmallWarps], warp_eq[kSmallWarps];
-  extern __shared__ uint32_t dyn[];  // [cap] composites, [cap] source indices, [n] staged keys
-  const int64_t b = blockIdx.x, n = args.n, k = args.k;
+  __shared__ int warp_lt[WARPS], warp_eq[WARPS];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int cap = 32;
-  while (cap < k) cap <<= 1;
-  uint32_t* comp = dyn;
-  uint32_t* src = dyn + cap;
-  uint16_t* staged = reinterpret_cast<uint16_t*>(dyn + 2 * cap);
-  unsigned long long* out = args.sorted + b * args.sorted_pitch;
-  if (k <= 0) return;
-  if (kStaged) {  // one coalesced, 4-way unrolled pass computes every key once
-    int64_t i = threadIdx.x;
-    for (; i + 3 * kSmallThreads < n; i += 4 * kSmallThreads) {
-      uint16_t h0 = args.src.get(b, i), h1 = args.src.get(b, i + kSmallThreads);
-      uint16_t h2 = args.src.get(b, i + 2 * kSmallThreads), h3 = args.src.get(b, i + 3 * kSmallThreads);
-      staged[i] = (uint16_t)score_key(h0, args.nan_last);
-      staged[i + kSmallThreads] = (uint16_t)score_key(h1, args.nan_last);
-      staged[i + 2 * kSmallThreads] = (uint16_t)score_key(h2, args.nan_last);
-      staged[i + 3 * kSmallThreads] = (uint16_t)score_key(h3, args.nan_last);
-    }
-    for (; i < n; i += kSmallThreads) staged[i] = (uint16_t)score_key(args.src.get(b, i), args.nan_last);
-    __syncthreads();
-  }
-  auto key_at = [&](int64_t i) -> uint32_t {
-    return kStaged ? (uint32_t)staged[i] : score_key(args.src.get(b, i), args.nan_last);
-  };
   // --- radix select
   for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -625,7 +613,7 @@ __global__ void __launch_bounds__(kSmallThreads) topk_small(TopkArgs args) {
   const uint32_t threshold = (high << 8) | sel_bucket;
   const int64_t need = k - (int64_t)sel_below;
   // --- index-ordered collection
-  const int64_t span = ((n + kSmallWarps - 1) / kSmallWarps + 31) / 32 * 32;
+  const int64_t span = ((n + WARPS - 1) / WARPS + 31) / 32 * 32;
   const int64_t lo = warp * span, hi = lo + span < n ? lo + span : n;
   int lt = 0, eq = 0;
   for (int64_t base = lo; base < hi; base += 32) {
@@ -687,6 +675,37 @@ __global__ void __launch_bounds__(kSmallThreads) topk_small(TopkArgs args) {
   }
 }
 
+
+template <bool kStaged>
+__global__ void __launch_bounds__(kSmallThreads) topk_small(TopkArgs args) {
+  extern __shared__ uint32_t dyn[];  // [cap] composites, [cap] source indices, [n] staged keys
+  const int64_t b = blockIdx.x, n = args.n, k = args.k;
+  int cap = 32;
+  while (cap < k) cap <<= 1;
+  uint32_t* comp = dyn;
+  uint32_t* src = dyn + cap;
+  uint16_t* staged = reinterpret_cast<uint16_t*>(dyn + 2 * cap);
+  unsigned long long* out = args.sorted + b * args.sorted_pitch;
+  if (k <= 0) return;
+  if (kStaged) {  // one coalesced, 4-way unrolled pass computes every key once
+    int64_t i = threadIdx.x;
+    for (; i + 3 * kSmallThreads < n; i += 4 * kSmallThreads) {
+      uint16_t h0 = args.src.get(b, i), h1 = args.src.get(b, i + kSmallThreads);
+      uint16_t h2 = args.src.get(b, i + 2 * kSmallThreads), h3 = args.src.get(b, i + 3 * kSmallThreads);
+      staged[i] = (uint16_t)score_key(h0, args.nan_last);
+      staged[i + kSmallThreads] = (uint16_t)score_key(h1, args.nan_last);
+      staged[i + 2 * kSmallThreads] = (uint16_t)score_key(h2, args.nan_last);
+      staged[i + 3 * kSmallThreads] = (uint16_t)score_key(h3, args.nan_last);
+    }
+    for (; i < n; i += kSmallThreads) staged[i] = (uint16_t)score_key(args.src.get(b, i), args.nan_last);
+    __syncthreads();
+  }
+  auto key_at = [&](int64_t i) -> uint32_t {
+    return kStaged ? (uint32_t)staged[i] : score_key(args.src.get(b, i), args.nan_last);
+  };
+  cta_topk<kSmallWarps>(n, k, cap, key_at, comp, src, out);
+}
+
 // --------------------------------------------------------- 3. pair gather
 
 // pair_bits[b][r*nc + c] = score of class c at the stage-1 anchor of rank r.
@@ -704,6 +723,112 @@ __global__ void __launch_bounds__(256) gather_pairs(SelectView v, bool sigmoid,
     pair_bits[b * pair_pitch + flat] = bits;
     if (trace_gathered) trace_gathered[t] = bits;
   }
+}
+
+// ------------------------------------- 3'. fused pair stage and pack
+
+// Class-aware stage 2 and pack for one image per CTA, without gathering the
+// k x nc scores.  K1 = the k-th stage-1 key.  The k pairs (rank r, best class of
+// anchor r) all have keys <= K1, so every pair of the final top k has a key
+// <= K1 too; a non-best class of anchor r can qualify only if the best score
+// among its other classes has key <= K1 (the class-max pass records that key,
+// 0 for anchors it rescanned).  Candidates: (r, best class) for every other
+// anchor, and every class with key <= K1 of the anchors that may hold more
+// (read exactly, as gather_pairs does).  Up to kPairCand candidates, as 32-bit
+// composites (key << 15 | r*nc + c), are sorted ascending in shared memory --
+// equal keys in flat-index order, as the stage-2 top-k orders them -- and the
+// first k packed.  More candidates (many ties at K1) take the exact top-k over
+// all k*nc pairs in the same CTA, keys read on the fly.
+constexpr int kPairThreads = 512;
+constexpr int kPairCand = 4096;
+constexpr int64_t kPairFlatMax = 1 << 15;
+
+__global__ void __launch_bounds__(kPairThreads) pairs_fused(SelectView v, bool nan_last, bool sigmoid, int k,
+                                                            const unsigned long long* stage1, int64_t s1_pitch,
+                                                            const uint32_t* records, const uint16_t* second_keys,
+                                                            float* out) {
+  // [kPairCand] composites (reused as k sorted 64-bit results on overflow),
+  // [k] ranks of anchors needing every class, [2 * cap] top-k scratch
+  extern __shared__ uint32_t pair_cand[];
+  __shared__ int count, n_full;
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nc = (int)v.classes;
+  int cap = 32;
+  while (cap < k) cap <<= 1;
+  int* full = reinterpret_cast<int*>(pair_cand + kPairCand);
+  uint32_t* topk_comp = pair_cand + kPairCand + k;
+  const unsigned long long* s1 = stage1 + (int64_t)b * s1_pitch;
+  const uint32_t k1 = (uint32_t)(s1[k - 1] >> 32);
+  if (tid == 0) count = n_full = 0;
+  __syncthreads();
+  for (int r = tid; r < k; r += kPairThreads) {
+    const unsigned long long e = s1[r];
+    const int64_t a = (int64_t)(e & 0xffffffffull);
+    if ((uint32_t)second_keys[(int64_t)b * v.anchors + a] > k1) {  // only the best class can rank
+      const uint32_t cls = records[(int64_t)b * v.anchors + a] >> 16;
+      const int slot = atomicAdd(&count, 1);
+      if (slot < kPairCand) pair_cand[slot] = ((uint32_t)(e >> 32) << 15) | (uint32_t)(r * nc + (int)cls);
+    } else {
+      full[atomicAdd(&n_full, 1)] = r;
+    }
+  }
+  __syncthreads();
+  for (int f = warp; f < n_full; f += kPairThreads / 32) {  // warp per anchor, lanes over classes
+    const int r = full[f];
+    const int64_t a = (int64_t)(s1[r] & 0xffffffffull);
+    for (int c = lane; c < nc; c += 32) {
+      const uint32_t key = score_key(score_bits(v, b, a, c, sigmoid), nan_last);
+      if (key <= k1) {
+        const int slot = atomicAdd(&count, 1);
+        if (slot < kPairCand) pair_cand[slot] = (key << 15) | (uint32_t)(r * nc + c);
+      }
+    }
+  }
+  __syncthreads();
+  const int n = count;  // >= k: the k best-class pairs are always candidates
+  auto pack = [&](int j, int flat) {
+    const int r = flat / nc, c = flat - r * nc;
+    const int64_t anchor = (int64_t)(s1[r] & 0xffffffffull);
+    const uint16_t bits = score_bits(v, b, anchor, c, sigmoid);
+    const uint16_t* box = v.base + (int64_t)b * v.sb + anchor * v.sa;
+    const int64_t t = (int64_t)b * k + j;
+    uint32_t* row = reinterpret_cast<uint32_t*>(out + t * 6);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) row[q] = float_bits_of_half(box[q * v.sc]);
+    row[4] = float_bits_of_half(bits);
+    out[t * 6 + 5] = (float)c;
+  };
+  if (n > kPairCand) {
+    unsigned long long* sorted = reinterpret_cast<unsigned long long*>(pair_cand);
+    auto key_at = [&](int64_t i) -> uint32_t {
+      const int r = (int)(i / nc), c = (int)(i - (int64_t)r * nc);
+      return score_key(score_bits(v, b, (int64_t)(s1[r] & 0xffffffffull), c, sigmoid), nan_last);
+    };
+    cta_topk<kPairThreads / 32>((int64_t)k * nc, k, cap, key_at, topk_comp, topk_comp + cap, sorted);
+    __syncthreads();
+    for (int j = tid; j < k; j += kPairThreads) pack(j, (int)(sorted[j] & 0xffffffffull));
+    return;
+  }
+  int size = 32;
+  while (size < n) size <<= 1;
+  for (int i = n + tid; i < size; i += kPairThreads) pair_cand[i] = 0xffffffffu;
+  __syncthreads();
+  for (int span = 2; span <= size; span <<= 1) {
+    for (int stride = span >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < size; i += kPairThreads) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint32_t x = pair_cand[i], y = pair_cand[j];
+          if ((x > y) == ((i & span) == 0)) {
+            pair_cand[i] = y;
+            pair_cand[j] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int j = tid; j < k; j += kPairThreads) pack(j, (int)(pair_cand[j] & 0x7fffu));
 }
 
 // ------------------------------------------------------------------ 4. pack
@@ -763,7 +888,7 @@ __global__ void __launch_bounds__(256) pack_rows(PackArgs p) {
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct Workspace {
-  size_t records, stage1, pairs, stage2, hist, scratch, total;
+  size_t records, second, stage1, pairs, stage2, hist, scratch, total;
 };
 
 ttn_status launch_topk(const TopkArgs& args, int64_t batch, int64_t k, cudaStream_t s) {
@@ -791,6 +916,8 @@ Workspace layout(int64_t batch, int64_t anchors, int64_t classes, int64_t k, boo
   int64_t pairs = agnostic ? 0 : kp * classes;
   w.records = 0;
   size_t off = align256((size_t)batch * anchors * 4);
+  w.second = off;
+  off += agnostic ? 0 : align256((size_t)batch * anchors * 2);
   w.stage1 = off;
   off += align256((size_t)batch * kp * 8);
   w.pairs = off;
@@ -867,10 +994,19 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
   // 1. class max
   bool planar = v.sa == 1 && v.anchors % 8 == 0 && v.sb % 8 == 0 && v.sc % 8 == 0 &&
                 ((uintptr_t)(v.base + 4 * v.sc) & 15u) == 0;
+  const bool traced = tr.class_max || tr.stage1_indices || tr.gathered_scores || tr.stage2_indices ||
+                      tr.top_values || tr.anchor_indices || tr.labels;
+  int pair_cap = 32;
+  while (pair_cap < k && pair_cap < 4096) pair_cap <<= 1;
+  const size_t pair_smem = (size_t)kPairCand * 4 + (size_t)k * 4 + (size_t)pair_cap * 8;
+  // k <= 2048: the overflow path's k 64-bit results fit the candidate array
+  const bool fused = planar && sigmoid && !agnostic && !traced && k >= 1 && k <= 2048 &&
+                     k * v.classes <= kPairFlatMax && (int64_t)pair_smem <= max_dynamic_smem();
+  uint16_t* second = fused ? (uint16_t*)(ws + w.second) : nullptr;
   if (planar && sigmoid) {
     int64_t work = v.batch * (v.anchors / 8);
     class_max_planar8_sigmoid<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, records, v.anchors,
-                                                                     tr.class_max);
+                                                                     tr.class_max, second);
   } else if (planar) {
     int64_t work = v.batch * (v.anchors / 8);
     class_max_planar8<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, sigmoid, records,
@@ -890,6 +1026,14 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
   // 2. stage-1 top-k over anchors
   TopkArgs t1{KeySource{records, nullptr, v.anchors}, v.anchors, k, nan_last, stage1, kp, hist, scratch};
   TTN_TRY(launch_topk(t1, v.batch, k, s));
+
+  // 3'. class-aware without trace: candidate pairs, sort and pack in one kernel
+  if (fused) {
+    TTN_TRY(ensure_dynamic_smem((const void*)pairs_fused, (int)pair_smem));
+    pairs_fused<<<(unsigned)v.batch, kPairThreads, pair_smem, s>>>(v, nan_last, sigmoid, (int)k, stage1, kp,
+                                                                   records, second, out);
+    return launch_check("ttn_select_f16 pairs");
+  }
 
   // 3. class-aware: pairs and stage-2 top-k
   if (!agnostic) {
