@@ -20,17 +20,17 @@ __device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b 
 // whole row comes out NaN exactly as CPU eager's three passes produce.
 __device__ __forceinline__ float row_max(float a, float b) { return fmaxf(a, b); }
 
-// exp(v - m) as ex2 of v*log2e - m*log2e, with m*log2e carried as hi + lo so the
-// argument keeps full precision even for |m| in the thousands.
+// exp(v - m') as ex2 of one FMA, v*log2e - hi with hi = fl(m*log2e): the shift
+// m' = hi/log2e differs from m by at most one rounding of m*log2e, and a shift
+// common to a whole row cancels in the softmax ratio, so only the FMA's own
+// rounding (2^-24 of the argument) reaches the probabilities.  The row maximum
+// still maps to an argument within that rounding of 0, so nothing overflows.
 struct ShiftLog2 {
-  float hi, lo;
+  float hi;
 };
-__device__ __forceinline__ ShiftLog2 shift_log2(float m) {
-  float hi = m * 1.44269504088896341f;
-  return {hi, __fmaf_rn(m, 1.44269504088896341f, -hi)};
-}
+__device__ __forceinline__ ShiftLog2 shift_log2(float m) { return {m * 1.44269504088896341f}; }
 __device__ __forceinline__ float exp_shifted(float v, ShiftLog2 ml) {
-  return ex2_approx(__fmaf_rn(v, 1.44269504088896341f, -ml.hi) - ml.lo);
+  return ex2_approx(__fmaf_rn(v, 1.44269504088896341f, -ml.hi));
 }
 
 template <typename T>
