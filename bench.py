@@ -107,29 +107,50 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def cpu_pass_rate(imgsz: int, budget_s: float = 12.0):
-    """CPU-eager op pass (the oracle) on the host cores: images/s over a bounded sample."""
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), or "unknown"."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_pass_rate(imgsz: int, budget_s: float = 12.0, one_thread_s: float = 5.0):
+    """CPU-eager op pass (the oracle) on the host cores: images/s over a bounded
+    sample with every core, plus a shorter sample on one thread."""
     import torch
     from oracle import yolo as oyolo
     from thintnpu_b200 import yolo
 
-    torch.set_num_threads(os.cpu_count() or 1)
     plan = yolo.yolov8s_plan(imgsz)
     batch = 2
     inputs = yolo.synthetic_inputs(plan, batch, "cpu", seed=4)
-    with torch.inference_mode():
-        oyolo.run_pass(plan, inputs)  # warm-up
-        done, start = 0, time.perf_counter()
-        while True:
-            oyolo.run_pass(plan, inputs)
-            done += batch
-            elapsed = time.perf_counter() - start
-            if elapsed >= budget_s:
-                break
-    return {"value": done / elapsed, "unit": "images/s", "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"{done} images ({batch} per pass) of the same 640 op pass, PyTorch CPU eager, "
-                      f"{elapsed:.1f} s"}
+
+    def rate(threads: int, budget: float):
+        torch.set_num_threads(threads)
+        with torch.inference_mode():
+            oyolo.run_pass(plan, inputs)  # warm-up
+            done, start = 0, time.perf_counter()
+            while True:
+                oyolo.run_pass(plan, inputs)
+                done += batch
+                elapsed = time.perf_counter() - start
+                if elapsed >= budget:
+                    return done, elapsed
+
+    cores = os.cpu_count() or 1
+    done, elapsed = rate(cores, budget_s)
+    done1, elapsed1 = rate(1, one_thread_s)
+    torch.set_num_threads(cores)
+    return {"value": done / elapsed, "unit": "images/s", "cores": cores, "kind": "port",
+            "sample": f"{done} images ({batch} per pass) of the same {imgsz} op pass, PyTorch CPU eager, "
+                      f"{elapsed:.1f} s",
+            "one_thread": {"value": done1 / elapsed1, "unit": "images/s",
+                           "sample": f"{done1} images, {elapsed1:.1f} s"},
+            "cpu_model": cpu_model()}
 
 
 def run_reference(args):
