@@ -19,6 +19,8 @@
 //   4. pack          FP32 rows (box bits widened exactly, score, class) and the
 //                    optional trace outputs.
 // Scratch lives in the caller's workspace (ttn_select_workspace_size).
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace ttn {
@@ -184,11 +186,17 @@ __device__ __forceinline__ void rescan_anchor(const SelectView& v, int64_t b, in
 // x * 0 NaN in a per-lane accumulator.  Anchors with such a logit, or whose
 // best and second-best logits give the same fp16 sigmoid (this also covers
 // +0/-0 and equal logits), are decided by the exact rescan.
-__global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, bool nan_last,
-                                                                 uint32_t* records, int64_t rec_pitch,
-                                                                 uint16_t* trace_max, uint16_t* second_keys) {
+// APT anchors per thread (2, 4 or 8: 4-, 8- or 16-byte loads per class row),
+// 32/APT class rows in flight per thread.
+template <int APT>
+__global__ void __launch_bounds__(256) class_max_planar_sigmoid(SelectView v, bool nan_last,
+                                                                uint32_t* records, int64_t rec_pitch,
+                                                                uint16_t* trace_max, uint16_t* second_keys) {
+  constexpr int W = APT / 2;      // half2 words per class row
+  constexpr int ROWS = 32 / APT;  // class rows in flight
+  using Vec = typename std::conditional<W == 4, uint4, typename std::conditional<W == 2, uint2, uint32_t>::type>::type;
   const int lane = threadIdx.x & 31;
-  const int64_t groups = v.anchors / 8;
+  const int64_t groups = v.anchors / APT;
   const int64_t total = v.batch * groups;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const __half2 zero = __float2half2_rn(0.0f);
@@ -197,22 +205,22 @@ __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, b
   for (int64_t t0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); t0 < total; t0 += stride) {
     const int64_t t = t0 + lane;
     const bool live = t < total;
-    const int64_t b = live ? t / groups : 0, a0 = live ? (t % groups) * 8 : 0;
-    __half2 best[4], second[4], special[4];
-    uint32_t cls[4];
+    const int64_t b = live ? t / groups : 0, a0 = live ? (t % groups) * APT : 0;
+    __half2 best[W], second[W], special[W];
+    uint32_t cls[W];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < W; ++k) {
       best[k] = second[k] = neg_inf;
       special[k] = zero;
       cls[k] = 0;
     }
     if (live) {
       const uint16_t* p = v.base + b * v.sb + a0 + 4 * v.sc;
-      auto fold = [&](const uint4 q, uint32_t c) {
+      auto fold = [&](const Vec q, uint32_t c) {
         const uint32_t cpair = c * 0x00010001u;
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&q);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < W; ++k) {
           const __half2 x = *reinterpret_cast<const __half2*>(&w[k]);
           const uint32_t m = __hgt2_mask(x, best[k]);
           cls[k] = (cls[k] & ~m) | (cpair & m);
@@ -222,26 +230,23 @@ __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, b
         }
       };
       int64_t c = 0;
-      for (; c + 3 < v.classes; c += 4) {  // four class rows in flight
-        const uint4 q0 = *reinterpret_cast<const uint4*>(p + c * v.sc);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(p + (c + 1) * v.sc);
-        const uint4 q2 = *reinterpret_cast<const uint4*>(p + (c + 2) * v.sc);
-        const uint4 q3 = *reinterpret_cast<const uint4*>(p + (c + 3) * v.sc);
-        fold(q0, (uint32_t)c);
-        fold(q1, (uint32_t)c + 1);
-        fold(q2, (uint32_t)c + 2);
-        fold(q3, (uint32_t)c + 3);
-      }
-      for (; c < v.classes; ++c) fold(*reinterpret_cast<const uint4*>(p + c * v.sc), (uint32_t)c);
-    }
-    uint32_t out_bits[8], cls8[8], redo = 0;
-    uint32_t skey[8];  // key of the best score among the other classes (0xffff: none)
+      for (; c + ROWS - 1 < v.classes; c += ROWS) {  // ROWS class rows in flight
+        Vec q[ROWS];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+        for (int u = 0; u < ROWS; ++u) q[u] = *reinterpret_cast<const Vec*>(p + (c + u) * v.sc);
+#pragma unroll
+        for (int u = 0; u < ROWS; ++u) fold(q[u], (uint32_t)(c + u));
+      }
+      for (; c < v.classes; ++c) fold(*reinterpret_cast<const Vec*>(p + c * v.sc), (uint32_t)c);
+    }
+    uint32_t out_bits[APT], clsj[APT], redo = 0;
+    uint32_t skey[APT];  // key of the best score among the other classes (0xffff: none)
+#pragma unroll
+    for (int j = 0; j < APT; ++j) {
       const int k = j >> 1, sh = (j & 1) * 16;
       const uint16_t logit = (uint16_t)(*reinterpret_cast<const uint32_t*>(&best[k]) >> sh);
       const uint16_t flag = (uint16_t)(*reinterpret_cast<const uint32_t*>(&special[k]) >> sh);
-      cls8[j] = (cls[k] >> sh) & 0xffffu;
+      clsj[j] = (cls[k] >> sh) & 0xffffu;
       const uint16_t s1 = sigmoid_h_fast(logit);
       out_bits[j] = s1;
       const bool has_special = (flag & 0x7fffu) > 0x7c00u;  // NaN: some logit was inf or NaN
@@ -270,30 +275,37 @@ __global__ void __launch_bounds__(256) class_max_planar8_sigmoid(SelectView v, b
         rescan_anchor(v, sb, sa0 + j, nan_last, rb, rc);
         if (lane == src) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
+          for (int k = 0; k < APT; ++k)
             if (k == j) {
               out_bits[k] = rb;
-              cls8[k] = rc;
+              clsj[k] = rc;
             }
         }
       }
       pending &= pending - 1;
     }
     if (live) {
-      uint32_t out[8];
+      uint32_t out[APT];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) out[j] = out_bits[j] | (cls8[j] << 16);
-      uint4* dst = reinterpret_cast<uint4*>(records + b * rec_pitch + a0);
-      dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-      dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+      for (int j = 0; j < APT; ++j) out[j] = out_bits[j] | (clsj[j] << 16);
+      if constexpr (APT >= 4) {
+        uint4* dst = reinterpret_cast<uint4*>(records + b * rec_pitch + a0);
+#pragma unroll
+        for (int h = 0; h < APT / 4; ++h)
+          dst[h] = make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
+      } else {
+        *reinterpret_cast<uint2*>(records + b * rec_pitch + a0) = make_uint2(out[0], out[1]);
+      }
       if (trace_max) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) trace_max[b * v.anchors + a0 + j] = (uint16_t)out_bits[j];
+        for (int j = 0; j < APT; ++j) trace_max[b * v.anchors + a0 + j] = (uint16_t)out_bits[j];
       }
-      if (second_keys)
-        *reinterpret_cast<uint4*>(second_keys + b * v.anchors + a0) =
-            make_uint4(skey[0] | (skey[1] << 16), skey[2] | (skey[3] << 16), skey[4] | (skey[5] << 16),
-                       skey[6] | (skey[7] << 16));
+      if (second_keys) {
+        uint32_t sw[W];
+#pragma unroll
+        for (int k = 0; k < W; ++k) sw[k] = skey[2 * k] | (skey[2 * k + 1] << 16);
+        *reinterpret_cast<Vec*>(second_keys + b * v.anchors + a0) = *reinterpret_cast<const Vec*>(sw);
+      }
     }
   }
 }
@@ -1004,9 +1016,9 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
                      k * v.classes <= kPairFlatMax && (int64_t)pair_smem <= max_dynamic_smem();
   uint16_t* second = fused ? (uint16_t*)(ws + w.second) : nullptr;
   if (planar && sigmoid) {
-    int64_t work = v.batch * (v.anchors / 8);
-    class_max_planar8_sigmoid<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, records, v.anchors,
-                                                                     tr.class_max, second);
+    int64_t work = v.batch * (v.anchors / 4);
+    class_max_planar_sigmoid<4><<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, records, v.anchors,
+                                                                       tr.class_max, second);
   } else if (planar) {
     int64_t work = v.batch * (v.anchors / 8);
     class_max_planar8<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, sigmoid, records,
