@@ -177,9 +177,23 @@ def test_upsample_blocked(device, c, h, w):
     assert_bits_equal(ttn.upsample_blocked(xb.to(device)), oops.upsample_blocked(xb))
 
 
-@pytest.mark.parametrize("n,c1,hw", [(1, 16, 20), (4, 16, 20), (2, 3, 13), (1, 2, 40), (1, 1, 64)])
+@pytest.mark.parametrize("n,c1,hw", [(1, 16, 20), (4, 16, 20), (2, 3, 13), (1, 2, 40), (1, 1, 64), (3, 2, 1),
+                                     (2, 2, 16), (1, 3, 22)])
 def test_sppf(device, n, c1, hw):
     import thintnpu_b200 as ttn
     g = torch.Generator().manual_seed(9)
     x = torch.randn(n, c1, hw, hw, 16, generator=g).half()
+    assert_bits_equal(ttn.sppf(x.to(device), 5), oops.sppf(x, 5))
+
+
+@pytest.mark.parametrize("hw", [20, 7])
+def test_sppf_nan_and_negative_zero_planes(device, hw):
+    """Planes holding NaN (with payloads) or -0 take the exact per-lane CPU rule."""
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(19)
+    x = torch.randn(2, 4, hw, hw, 16, generator=g).half()
+    bits = x.view(torch.int16)
+    bits[0, 1, hw // 2, 3 % hw, 5] = 0x7E05
+    bits[0, 1, 0, 0, 6] = -0x0200  # 0xFE00
+    bits[1, 2].masked_fill_(torch.rand(hw, hw, 16, generator=g) < 0.3, -0x8000)  # -0
     assert_bits_equal(ttn.sppf(x.to(device), 5), oops.sppf(x, 5))

@@ -373,6 +373,105 @@ __global__ void __launch_bounds__(256) sppf_planes(const uint16_t* x, uint16_t* 
   }
 }
 
+// sppf_planes for planes of at most 4 * 256 16-byte vectors (e.g. the 20x20
+// SPPF of a 640 model): every plane has the same geometry, so each thread
+// computes the padded shared-memory position of its (at most VPT) vectors once,
+// and the three stages run without any index division.
+template <int VPT>
+__global__ void __launch_bounds__(256) sppf_planes_small(const uint16_t* x, uint16_t* out, int64_t n,
+                                                         int64_t c1, int h, int w, int radius) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int pw = w + 2 * radius, ph = h + 2 * radius;  // padded plane, in pixels
+  const int padded_vec = ph * pw * 2;                 // uint4 per padded plane
+  uint4* cur = reinterpret_cast<uint4*>(smem_raw);
+  uint4* tmp = cur + padded_vec;
+  const int plane_vec = h * w * 2;
+  const uint4 ninf = make_uint4(0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u);
+  int pos[VPT];  // padded position of vector tid + k*256 (-1: none)
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int v = threadIdx.x + k * 256;
+    const int pix = v >> 1, row = pix / w, col = pix - row * w;
+    pos[k] = v < plane_vec ? ((row + radius) * pw + col + radius) * 2 + (v & 1) : -1;
+  }
+  for (int v = threadIdx.x; v < 2 * padded_vec; v += blockDim.x) cur[v] = ninf;
+  __syncthreads();
+  const int row_step = 2 * pw;
+  for (int64_t job = blockIdx.x; job < n * c1; job += gridDim.x) {
+    const int64_t b = job / c1, cb = job - b * c1;
+    const uint4* src = reinterpret_cast<const uint4*>(x + job * (int64_t)plane_vec * 8);
+    uint4* dst0 = reinterpret_cast<uint4*>(out + ((b * 4 * c1) + cb) * (int64_t)plane_vec * 8);
+    bool special = false;
+    uint4 q[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+      if (pos[k] >= 0) q[k] = src[threadIdx.x + k * 256];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (pos[k] >= 0) {
+        dst0[threadIdx.x + k * 256] = q[k];
+        cur[pos[k]] = q[k];
+        special |= special_word(q[k].x) | special_word(q[k].y) | special_word(q[k].z) | special_word(q[k].w);
+      }
+    }
+    special = __syncthreads_or(special);
+    for (int stage = 1; stage <= 3; ++stage) {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {  // horizontal: tmp[row][col] (border rows stay -inf)
+        if (pos[k] < 0) continue;
+        const uint4* r = cur + pos[k] - 2 * radius;
+        uint4 m;
+        if (!special) {
+          m = r[0];
+          for (int t = 1; t <= 2 * radius; ++t) m = hmax4(m, r[2 * t]);
+        } else {
+          uint16_t best[8];
+          float bv[8];
+#pragma unroll
+          for (int l = 0; l < 8; ++l) { best[l] = 0xfc00u; bv[l] = -INFINITY; }
+          for (int t = 0; t <= 2 * radius; ++t) {
+            uint4 e4 = r[2 * t];
+            const uint16_t* e = reinterpret_cast<const uint16_t*>(&e4);
+#pragma unroll
+            for (int l = 0; l < 8; ++l) pool_update(best[l], bv[l], e[l]);
+          }
+          m = *reinterpret_cast<uint4*>(best);
+        }
+        tmp[pos[k]] = m;
+      }
+      __syncthreads();
+      uint4* dst = reinterpret_cast<uint4*>(out + ((b * 4 * c1) + stage * c1 + cb) * (int64_t)plane_vec * 8);
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {  // vertical, into cur and the stage's output slice
+        if (pos[k] < 0) continue;
+        const uint4* r = tmp + pos[k] - radius * row_step;
+        uint4 m;
+        if (!special) {
+          m = r[0];
+          for (int t = 1; t <= 2 * radius; ++t) m = hmax4(m, r[t * row_step]);
+        } else {
+          uint16_t best[8];
+          float bv[8];
+#pragma unroll
+          for (int l = 0; l < 8; ++l) { best[l] = 0xfc00u; bv[l] = -INFINITY; }
+          for (int t = 0; t <= 2 * radius; ++t) {
+            uint4 e4 = r[t * row_step];
+            const uint16_t* e = reinterpret_cast<const uint16_t*>(&e4);
+#pragma unroll
+            for (int l = 0; l < 8; ++l) pool_update(best[l], bv[l], e[l]);
+          }
+#pragma unroll
+          for (int l = 0; l < 8; ++l) best[l] = PoolBits<uint16_t>::finish(best[l]);
+          m = *reinterpret_cast<uint4*>(best);
+        }
+        cur[pos[k]] = m;
+        dst[threadIdx.x + k * 256] = m;
+      }
+      __syncthreads();
+    }
+  }
+}
+
 bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 
@@ -542,8 +641,27 @@ ttn_status ttn_sppf_f16(const void* x, void* out, int64_t n, int64_t c1, int64_t
     }
     return TTN_OK;
   }
-  TTN_TRY(ensure_dynamic_smem((const void*)sppf_planes, (int)smem));
   int64_t jobs = n * c1;
+  const int64_t plane_vec = h * w * 2;
+  if (plane_vec <= 4 * 256) {  // fixed per-thread positions
+    const int vpt = (int)((plane_vec + 255) / 256);
+    const void* fn = vpt == 1 ? (const void*)sppf_planes_small<1>
+                   : vpt == 2 ? (const void*)sppf_planes_small<2>
+                   : vpt == 3 ? (const void*)sppf_planes_small<3>
+                              : (const void*)sppf_planes_small<4>;
+    TTN_TRY(ensure_dynamic_smem(fn, (int)smem));
+    unsigned grid = resident_grid(fn, 256, smem, jobs, 1);
+    if (vpt == 1)
+      sppf_planes_small<1><<<grid, 256, smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w, (int)r);
+    else if (vpt == 2)
+      sppf_planes_small<2><<<grid, 256, smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w, (int)r);
+    else if (vpt == 3)
+      sppf_planes_small<3><<<grid, 256, smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w, (int)r);
+    else
+      sppf_planes_small<4><<<grid, 256, smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w, (int)r);
+    return launch_check(name);
+  }
+  TTN_TRY(ensure_dynamic_smem((const void*)sppf_planes, (int)smem));
   int per_sm = (int)(200 * 1024 / (smem ? smem : 1));
   if (per_sm < 1) per_sm = 1;
   unsigned grid = (unsigned)(jobs < (int64_t)sm_count() * per_sm ? jobs : (int64_t)sm_count() * per_sm);
