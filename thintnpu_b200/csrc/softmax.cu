@@ -457,9 +457,39 @@ __global__ void __launch_bounds__(128) dfl_decode(const __half* box, int64_t box
   }
 }
 
+// Paired fp32 arithmetic (Blackwell f32x2 instructions): one instruction does
+// the same IEEE round-to-nearest operation on both halves of a 64-bit pair.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // dfl_side for two anchors at once: w[i] holds bin i of both anchors as a half2.
 // Same rounding points: fp16 probabilities (one packed conversion per bin pair),
-// fp32 expectation accumulated over bins 1..15 in order, rounded to fp16.
+// fp32 expectation accumulated over bins 1..15 in order, rounded to fp16.  The
+// two anchors' fp32 chains run as the halves of paired f32x2 operations.
 __device__ __forceinline__ float2 dfl_side2(const uint32_t (&w)[16]) {
   float2 v[16];
 #pragma unroll
@@ -471,23 +501,26 @@ __device__ __forceinline__ float2 dfl_side2(const uint32_t (&w)[16]) {
     m1 = row_max(m1, v[i].y);
   }
   const ShiftLog2 l0 = shift_log2(m0), l1 = shift_log2(m1);
-  float s0 = 0.0f, s1 = 0.0f;
+  const unsigned long long log2e = f2_pack(1.44269504088896341f, 1.44269504088896341f);
+  const unsigned long long shift = f2_pack(-l0.hi, -l1.hi);
+  unsigned long long e[16], sum = f2_pack(0.0f, 0.0f);
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    v[i].x = exp_shifted(v[i].x, l0);
-    v[i].y = exp_shifted(v[i].y, l1);
-    s0 = __fadd_rn(s0, v[i].x);
-    s1 = __fadd_rn(s1, v[i].y);
+  for (int i = 0; i < 16; ++i) {  // exp(v - m') per anchor, as exp_shifted does
+    const float2 arg = f2_unpack(f2_fma(f2_pack(v[i].x, v[i].y), log2e, shift));
+    e[i] = f2_pack(ex2_approx(arg.x), ex2_approx(arg.y));
+    sum = f2_add(sum, e[i]);
   }
-  const float inv0 = __fdiv_rn(1.0f, s0), inv1 = __fdiv_rn(1.0f, s1);
-  float d0 = 0.0f, d1 = 0.0f;
+  const float2 s = f2_unpack(sum);
+  const unsigned long long inv = f2_pack(__fdiv_rn(1.0f, s.x), __fdiv_rn(1.0f, s.y));
+  unsigned long long d = f2_pack(0.0f, 0.0f);
 #pragma unroll
   for (int i = 1; i < 16; ++i) {
-    const float2 p = __half22float2(__floats2half2_rn(__fmul_rn(v[i].x, inv0), __fmul_rn(v[i].y, inv1)));
-    d0 = __fmaf_rn(p.x, (float)i, d0);
-    d1 = __fmaf_rn(p.y, (float)i, d1);
+    const float2 pr = f2_unpack(f2_mul(e[i], inv));
+    const float2 p = __half22float2(__floats2half2_rn(pr.x, pr.y));
+    d = f2_fma(f2_pack(p.x, p.y), f2_pack((float)i, (float)i), d);
   }
-  return make_float2(h16(d0), h16(d1));
+  const float2 dd = f2_unpack(d);
+  return make_float2(h16(dd.x), h16(dd.y));
 }
 
 // Box half of the decode for 8-aligned anchors: a block walks 128-anchor tiles
