@@ -137,3 +137,14 @@ def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes, strides, xywh: bool
     else:
         boxes = torch.cat((lower, upper), 1) * stride_row
     return torch.cat((boxes, cls.sigmoid()), 1)
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+    """C2PSA Attention core in CPU eager fp16 (whole_blocked.py:91-110):
+    attn = (q^T @ k) * scale; attn = softmax(attn, -1); out = v @ attn^T.
+
+    q, k [B, h, kd, N], v [B, h, hd, N] fp16; every op rounds to fp16 as the
+    reference's separate ATen ops do."""
+    attn = (q.transpose(-2, -1) @ k) * scale
+    attn = attn.softmax(dim=-1)
+    return v @ attn.transpose(-2, -1)

@@ -353,6 +353,44 @@ def softmax(x: torch.Tensor, dim: int = -1, half_to_float: bool = False, scale: 
     return y
 
 
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused C2PSA attention: v @ softmax((q^T @ k) * scale)^T per (image, head),
+    rounding as the reference's separate fp16 ops do (whole_blocked.py:91-110).
+
+    q, k: fp16 [B, heads, key_dim, N] and v: [B, heads, head_dim, N] views with
+    the token dim contiguous -- e.g. the split of the qkv conv output
+    ``qkv.view(B, heads, 2*key_dim + head_dim, N).split(...)``.  Returns (or
+    fills) out [B, heads, head_dim, N]."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _cuda(t, "attention")
+        _require(t.dtype == torch.float16 and t.dim() == 4 and t.stride(3) == 1,
+                 f"attention: {name} must be fp16 [B, heads, C, N] with the token dim contiguous")
+    b, h, kd, n = q.shape
+    hd = v.size(2)
+    _require(tuple(k.shape) == (b, h, kd, n) and tuple(v.shape[:2]) == (b, h) and v.size(3) == n,
+             "attention: q, k, v shapes disagree")
+    if out is None:
+        out = torch.empty((b, h, hd, n), dtype=torch.float16, device=q.device)
+    _require(tuple(out.shape) == (b, h, hd, n) and out.dtype == torch.float16 and out.stride(3) == 1,
+             "attention: out must be fp16 [B, heads, head_dim, N] with the token dim contiguous")
+
+    def strides(t):
+        return (ctypes.c_int64 * 3)(t.stride(0), t.stride(1), t.stride(2))
+
+    if q.numel() and v.numel():
+        call("ttn_attention_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, h, n, kd, hd,
+             strides(q), strides(k), strides(v), strides(out), float(scale), stream())
+    return out
+
+
+def attention_fault() -> int:
+    """Reads and clears the attention kernel's fault word (0 = no launch gave up)."""
+    word = ctypes.c_uint32(0)
+    call("ttn_attention_fault_f16", ctypes.byref(word))
+    return int(word.value)
+
+
 def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes: Sequence[tuple],
                strides: Sequence[float], xywh: bool = True,
                out: Optional[torch.Tensor] = None) -> torch.Tensor:
