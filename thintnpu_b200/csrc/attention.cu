@@ -7,37 +7,49 @@
 //
 // Layouts, as the reference's split of the qkv conv output gives them: q, k
 // [kd, n] and v [hd, n] per head with the token dim contiguous; out [hd, n].
-// Work item = (image, head, block of 128 queries).  A persistent CTA of 8 warps
-// per SM walks the items; while it computes one, cp.async brings the next
-// item's operands into the other half of a two-stage shared-memory ring.
-//  1. q (128 queries x kd), k (np x kd) and v (hd x np) land in shared memory in
-//     the no-swizzle UMMA canonical layouts (8-row x 16-byte core matrices):
-//     q and k MN-major (tokens contiguous), v K-major; np = n rounded up to 16,
-//     padding zero-filled by the copies.
-//  2. One thread issues S = q^T k as M=128 x N<=256 x K=16 tcgen05.mma steps
-//     into TMEM columns [0, np).
-//  3. Warp w reads TMEM lanes 32(w%4).. (its 32 queries) and every other
-//     32-column chunk (w/4 picks which).  Everything stays in TMEM and in the
-//     chunk's own columns, so the two warps on a lane quarter never touch each
-//     other's data: pass 1 turns S into packed fp16 z (16 columns) and the
-//     row max; pass 2 turns z into fp32 e = 2^(z log2e - max log2e) (32 columns)
-//     and the row sum; pass 3 turns e into packed fp16 P = e / sum (16
-//     columns).  Row max and sum are combined over the two warps in shared memory.
-//  4. One thread issues out^T = P v^T with A = P read from TMEM (K=16 step s
-//     takes the 8 columns at 32(s/2) + 8(s%2)) and B = v from shared memory,
-//     into the last hd of the CTA's TMEM columns; the warps store the rows.
+// Work item = (image, head, block of 128 queries).  A persistent CTA of 16 warps
+// per SM walks its items; thread 0 runs the copies and the tensor cores, the
+// warps run the softmax and the stores:
+//  1. TMA brings q (128 queries x kd), k (kd x n) and v (hd x n) into a
+//     two-stage shared-memory ring as boxes of 64 tokens (128 bytes, the
+//     128-byte swizzle) by all channels: the UMMA canonical 128-byte-swizzled
+//     layouts, q and k MN-major (the next 64 tokens one box further, the next
+//     8 channels 1024 bytes further), v K-major (8-channel groups 1024 bytes
+//     apart, a K=16 step 32 bytes along the row).  Tokens past n are
+//     zero-filled.  Item k+2's copies are issued as soon as item k's output
+//     product has released its stage.
+//  2. S = q^T k as M=128 x N<=256 x K=16 tcgen05.mma steps into TMEM columns
+//     [0, np); item k+1's product is issued before item k's output stores.
+//  3. Warp w reads TMEM lanes 32(w%4).. (its 32 queries) and every fourth
+//     32-column chunk (w/4 picks which).  Pass 1 turns S into packed fp16 z
+//     (kept in registers) and the row max; pass 2 turns z into fp32
+//     e = 2^(z log2e - max log2e), stored in the chunk's own TMEM columns, and
+//     the row sum; pass 3 turns e into packed fp16 P = e / sum, stored in the
+//     first 16 of the chunk's columns.  Row max and sum are combined over the
+//     four warps of a lane quarter in shared memory.
+//  4. out^T = P v^T with A = P read from TMEM (K=16 step s takes the 8 columns
+//     at 32(s/2) + 8(s%2)) and B = v from shared memory, into the last hd of the
+//     CTA's TMEM columns; the warps store their rows.
 // Every wait is bounded (200 ms of wall time): on a timeout the CTA records
 // which wait gave up in a device word (ttn_attention_fault_f16: 1 = the score
-// product, 2 = the output product), drains its copies, frees its TMEM and
-// returns.  Warp-collective tensor-memory loads and stores run on every lane of
-// a warp; only global stores are guarded per row.
+// product, 2 = the output product, 4 = an operand copy), waits (bounded) for
+// its copies in flight, frees its TMEM and returns.  Warp-collective
+// tensor-memory loads and stores run on every lane of a warp; only global
+// stores are guarded per row.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 
 namespace ttn {
 namespace {
 
 constexpr int kAttnRows = 128;     // queries per item (UMMA M, TMEM lanes)
-constexpr int kAttnThreads = 256;  // two warps per TMEM lane quarter
+constexpr int kAttnThreads = 512;  // four warps (column groups) per TMEM lane quarter
+constexpr int kGroups = kAttnThreads / 128;
+constexpr int kChunksPerWarp = 4;  // 32-column chunks per warp: np <= 512 columns
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // give up on a tensor-core wait after 200 ms
 constexpr float kLog2e = 1.44269504088896341f;
@@ -53,18 +65,24 @@ struct AttnArgs {
   int64_t k_bs, k_hs, k_cs;
   int64_t v_bs, v_hs, v_cs;
   int64_t o_bs, o_hs, o_cs;
-  int n, np, kd, hd, heads, tiles;
+  int n, np, nb, kd, hd, heads, tiles;  // nb = 64-token blocks
   int cols;    // TMEM columns: a power of two >= np + hd
   int stages;  // operand buffers in shared memory (2: the next item loads during this one)
   int64_t items;
   float scale;
 };
+// Tensor maps over q, k, v as 4-D fp16 tensors (token, channel, head, image), boxes of
+// 64 tokens x all channels, 128-byte swizzle.
+struct AttnMaps {
+  CUtensorMap q, k, v;
+};
 
-// Shared-memory matrix descriptor, no swizzle (tcgen05 "version 1"): start
-// address, leading-dimension and stride-dimension byte offsets, each >> 4.
+// Shared-memory matrix descriptor (tcgen05 "version 1"), 128-byte swizzle
+// (layout type 2): start address, leading- and stride-dimension byte offsets,
+// each >> 4.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46);
+         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46) | (2ull << 61);
 }
 // Instruction descriptor: f16 x f16 -> f32, M x N, operand majors (1 = MN-major).
 __device__ __forceinline__ uint32_t umma_idesc(int m, int n, bool a_mn, bool b_mn) {
@@ -122,15 +140,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
@@ -151,70 +160,82 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// 16-byte cp.async that writes zeros when `valid` is false (source size 0)
-__device__ __forceinline__ void cp_async16_zfill(uint32_t saddr, const void* gmem, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(gmem), "r"(valid ? 16 : 0)
-               : "memory");
+__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
+}
+// TMA tile load of one box of a 4-D tensor map into shared memory, completing on `mbar`
+__device__ __forceinline__ void tma_load4(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                          uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(mbar)
+      : "memory");
 }
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t b) { return *reinterpret_cast<__half2*>(&b); }
 
-__global__ void __launch_bounds__(kAttnThreads, 1) attention_tc(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attention_tc(AttnArgs a, const __grid_constant__ AttnMaps maps) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ __align__(8) uint64_t mbar[2];
+  __shared__ __align__(8) uint64_t mbar[4];  // score product, output product, stage 0 and 1 copies
   __shared__ uint32_t tmem_base_slot;
-  __shared__ float red_max[2][kAttnRows], red_sum[2][kAttnRows];
+  __shared__ float red_max[kGroups][kAttnRows], red_sum[kGroups][kAttnRows];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, group = warp >> 2, row = quarter * 32 + lane;
   const int kd = a.kd, hd = a.hd, np = a.np, n = a.n;
-  const int chunks = (np + 31) / 32;
-  // shared-memory operands per stage (byte offsets; all multiples of 512)
-  const uint32_t q_bytes = kAttnRows * kd * 2, k_bytes = np * kd * 2, v_bytes = hd * np * 2;
+  const int chunks = (np + 31) / 32;  // <= 15 (np <= 480): at most kChunksPerWarp per column group
+  // shared-memory operands per stage: boxes of 64 tokens x all channels, 128 bytes
+  // per channel (all multiples of 1024 bytes)
+  const uint32_t lbo_qk = (uint32_t)kd * 128, box_v = (uint32_t)hd * 128;  // one box of q or k, of v
+  const uint32_t q_bytes = 2 * lbo_qk, k_bytes = a.nb * lbo_qk, v_bytes = a.nb * box_v;
   const uint32_t stage_bytes = q_bytes + k_bytes + v_bytes;
-  const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(smem);
-  const uint32_t sbo_qk = (uint32_t)(kd / 8) * 128;  // MN-major: next 8 tokens
-  const uint32_t sbo_v = (uint32_t)(np / 8) * 128;   // K-major: next 8 channels
+  const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem) + 1023u) & ~1023u;
   const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&mbar[0]);
   const uint32_t bar1 = (uint32_t)__cvta_generic_to_shared(&mbar[1]);
+  const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(&mbar[2]);  // stage st: full0 + 8 st
+  const int64_t stride = gridDim.x;
+  const int count = a.items > (int64_t)blockIdx.x ? (int)((a.items - blockIdx.x + stride - 1) / stride) : 0;
 
-  // copies of one item's operands (16-byte chunks of 8 consecutive tokens) into stage `st`
-  auto load_item = [&](int64_t item, int st) {
+  // thread 0: copies of this CTA's item j into stage st, and the score product of the item in stage st
+  uint32_t fills[2] = {0, 0}, waited[2] = {0, 0};
+  auto load_item = [&](int j, int st) {
+    const int64_t item = blockIdx.x + j * stride;
     const int t = (int)(item % a.tiles);
     const int64_t bh = item / a.tiles;
     const int h = (int)(bh % a.heads), b = (int)(bh / a.heads);
-    const int i0 = t * kAttnRows;
-    const uint16_t* q = a.q + b * a.q_bs + h * a.q_hs;
-    const uint16_t* k = a.k + b * a.k_bs + h * a.k_hs;
-    const uint16_t* v = a.v + b * a.v_bs + h * a.v_hs;
-    const uint32_t sq = smem0 + st * stage_bytes, sk = sq + q_bytes, sv = sk + k_bytes;
-    for (int c = tid; c < kd * (kAttnRows / 8); c += kAttnThreads) {  // q^T block, MN-major
-      const int d = c / (kAttnRows / 8), t8 = (c % (kAttnRows / 8)) * 8, i = i0 + t8;
-      const bool valid = i < n;
-      cp_async16_zfill(sq + (t8 / 8) * sbo_qk + (d / 8) * 128 + (d % 8) * 16, valid ? q + d * a.q_cs + i : q,
-                       valid);
+    const uint32_t full = full0 + 8 * st, sq = smem0 + st * stage_bytes, sk = sq + q_bytes, sv = sk + k_bytes;
+    mbar_expect_tx(full, stage_bytes);
+    tma_load4(sq, &maps.q, t * kAttnRows, 0, h, b, full);
+    tma_load4(sq + lbo_qk, &maps.q, t * kAttnRows + 64, 0, h, b, full);
+    for (int blk = 0; blk < a.nb; ++blk) {
+      tma_load4(sk + blk * lbo_qk, &maps.k, 64 * blk, 0, h, b, full);
+      tma_load4(sv + blk * box_v, &maps.v, 64 * blk, 0, h, b, full);
     }
-    for (int c = tid; c < kd * (np / 8); c += kAttnThreads) {  // k, MN-major
-      const int d = c / (np / 8), j8 = (c % (np / 8)) * 8;
-      const bool valid = j8 < n;
-      cp_async16_zfill(sk + (j8 / 8) * sbo_qk + (d / 8) * 128 + (d % 8) * 16, valid ? k + d * a.k_cs + j8 : k,
-                       valid);
+    ++fills[st];
+  };
+  auto score_product = [&](int st, uint32_t& fault) {
+    if (!mbar_wait(full0 + 8 * st, waited[st]++ & 1)) {
+      fault |= 4u;  // no commit: the warps' wait for the product gives up too
+      return;
     }
-    for (int c = tid; c < hd * (np / 8); c += kAttnThreads) {  // v, K-major (K = tokens)
-      const int ch = c / (np / 8), j8 = (c % (np / 8)) * 8;
-      const bool valid = j8 < n;
-      cp_async16_zfill(sv + (ch / 8) * sbo_v + (j8 / 8) * 128 + (ch % 8) * 16, valid ? v + ch * a.v_cs + j8 : v,
-                       valid);
+    tc_fence_after();
+    const uint32_t sq = smem0 + st * stage_bytes, sk = sq + q_bytes;
+    for (int col = 0; col < np; col += 256) {
+      const int nc = np - col < 256 ? np - col : 256;
+      const uint32_t idesc = umma_idesc(kAttnRows, nc, true, true);
+      for (int s = 0; s < kd / 16; ++s)  // K=16 channels = two 1024-byte swizzle atoms
+        umma_ss(tmem_base_slot + col, umma_desc(sq + s * 2048, lbo_qk, 1024),
+                umma_desc(sk + (col / 64) * lbo_qk + s * 2048, lbo_qk, 1024), idesc, s > 0);
     }
+    umma_commit(bar0);
   };
 
   if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0));
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar1));
+    for (int i = 0; i < 4; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&mbar[i])));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  int64_t item = blockIdx.x;
-  if (item < a.items) load_item(item, 0);
-  cp_async_commit();
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      (uint32_t)__cvta_generic_to_shared(&tmem_base_slot)),
@@ -227,98 +248,99 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_tc(AttnArgs a) {
   const uint32_t tmem = tmem_base_slot;
   const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
   const uint32_t ocol = a.cols - hd;  // >= np rounded up to 32
+  const __half2 neg_inf2 = bits_h2(0xfc00fc00u);
   uint32_t fault = 0;
+  if (tid == 0 && count > 0) {
+    load_item(0, 0);
+    if (count > 1 && a.stages == 2) load_item(1, 1);
+    score_product(0, fault);
+  }
 
-  for (int it = 0; item < a.items; ++it, item += gridDim.x) {
-    const int st = a.stages == 2 ? (it & 1) : 0;
-    const int64_t next = item + gridDim.x;
-    if (a.stages == 2) {
-      if (next < a.items) load_item(next, st ^ 1);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // copies -> tensor-core reads
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+  for (int j = 0; j < count; ++j) {
+    const int st = a.stages == 2 ? (j & 1) : 0;
+    const int64_t item = blockIdx.x + j * stride;
     const int t = (int)(item % a.tiles);
     const int64_t bh = item / a.tiles;
     const int h = (int)(bh % a.heads), b = (int)(bh / a.heads);
     const int i0 = t * kAttnRows;
-    const uint32_t sq = smem0 + st * stage_bytes, sk = sq + q_bytes, sv = sk + k_bytes;
+    const uint32_t sv = smem0 + st * stage_bytes + q_bytes + k_bytes;
 
-    // 2. S = q^T k into TMEM columns [0, np): N chunks of at most 256
-    if (tid == 0) {
-      for (int col = 0; col < np; col += 256) {
-        const int nc = np - col < 256 ? np - col : 256;
-        const uint32_t idesc = umma_idesc(kAttnRows, nc, true, true);
-        for (int s = 0; s < kd / 16; ++s)
-          umma_ss(tmem + col, umma_desc(sq + s * 256, 128, sbo_qk),
-                  umma_desc(sk + (col / 8) * sbo_qk + s * 256, 128, sbo_qk), idesc, s > 0);
-      }
-      umma_commit(bar0);
-    }
-    bool ok = mbar_wait(bar0, it & 1);
+    bool ok = mbar_wait(bar0, j & 1);  // S of item j in TMEM columns [0, np)
     if (!ok) fault |= 1u;
     ok = __syncthreads_and(ok);
     if (!ok) break;
     tc_fence_after();
 
-    // 3. softmax over this warp's chunks; warps whose 32 queries all lie past n skip it
+    // 3. softmax over this warp's chunks c = group + kGroups i; warps whose 32
+    //    queries all lie past n skip it
     const bool live = i0 + quarter * 32 < n;
-    __half2 mx2 = bits_h2(0xfc00fc00u);  // -inf, -inf
+    uint32_t z[kChunksPerWarp][16];  // packed fp16 z of this warp's chunks
+    __half2 mx2 = neg_inf2;
     if (live) {
-      for (int c = group; c < chunks; c += 2) {  // pass 1: S -> packed z, row max
-        uint32_t r[32], z[16];
-        tmem_ld32(lane_addr + c * 32, r);
 #pragma unroll
-        for (int p = 0; p < 16; ++p) {
-          const float2 s = __half22float2(__floats2half2_rn(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1])));
-          __half2 zz = __floats2half2_rn(__fmul_rn(s.x, a.scale), __fmul_rn(s.y, a.scale));
-          if (c * 32 + 2 * p >= n) zz = bits_h2(0xfc00fc00u);  // n is even: a pair is valid or not
-          mx2 = __hmax2(mx2, zz);
-          z[p] = h2_bits(zz);
+      for (int i = 0; i < kChunksPerWarp; ++i) {  // pass 1: S -> z (registers), row max
+        const int c = group + kGroups * i;
+        if (c < chunks) {
+          uint32_t r[32];
+          tmem_ld32(lane_addr + c * 32, r);
+          const bool tail = c * 32 + 32 > n;
+#pragma unroll
+          for (int p = 0; p < 16; ++p) {
+            const float2 s = __half22float2(__floats2half2_rn(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1])));
+            __half2 zz = __floats2half2_rn(__fmul_rn(s.x, a.scale), __fmul_rn(s.y, a.scale));
+            if (tail && c * 32 + 2 * p >= n) zz = neg_inf2;  // n is even: a pair is valid or not
+            mx2 = __hmax2(mx2, zz);
+            z[i][p] = h2_bits(zz);
+          }
         }
-        tmem_st16(lane_addr + c * 32, z);
       }
     }
     red_max[group][row] = fmaxf(__low2float(mx2), __high2float(mx2));
-    tmem_wait_st();
     __syncthreads();
-    const float m = fmaxf(red_max[0][row], red_max[1][row]);
+    float m = red_max[0][row];
+#pragma unroll
+    for (int g = 1; g < kGroups; ++g) m = fmaxf(m, red_max[g][row]);
     const float hi = m * kLog2e;
     float sum = 0.0f;
     if (live) {
-      for (int c = group; c < chunks; c += 2) {  // pass 2: z -> fp32 e, row sum
-        uint32_t z[16], e[32];
-        tmem_ld16(lane_addr + c * 32, z);
 #pragma unroll
-        for (int p = 0; p < 16; ++p) {
-          const float2 zf = __half22float2(bits_h2(z[p]));
-          const float e0 = ex2_approx(__fmaf_rn(zf.x, kLog2e, -hi));
-          const float e1 = ex2_approx(__fmaf_rn(zf.y, kLog2e, -hi));
-          sum = __fadd_rn(__fadd_rn(sum, e0), e1);
-          e[2 * p] = __float_as_uint(e0);
-          e[2 * p + 1] = __float_as_uint(e1);
+      for (int i = 0; i < kChunksPerWarp; ++i) {  // pass 2: z -> fp32 e (TMEM), row sum
+        const int c = group + kGroups * i;
+        if (c < chunks) {
+          uint32_t e[32];
+#pragma unroll
+          for (int p = 0; p < 16; ++p) {
+            const float2 zf = __half22float2(bits_h2(z[i][p]));
+            const float e0 = ex2_approx(__fmaf_rn(zf.x, kLog2e, -hi));
+            const float e1 = ex2_approx(__fmaf_rn(zf.y, kLog2e, -hi));
+            sum = __fadd_rn(__fadd_rn(sum, e0), e1);
+            e[2 * p] = __float_as_uint(e0);
+            e[2 * p + 1] = __float_as_uint(e1);
+          }
+          tmem_st32(lane_addr + c * 32, e);
         }
-        tmem_st32(lane_addr + c * 32, e);
       }
     }
     red_sum[group][row] = sum;
     tmem_wait_st();
     __syncthreads();
-    const float inv = __fdiv_rn(1.0f, __fadd_rn(red_sum[0][row], red_sum[1][row]));
-    if (live) {
-      for (int c = group; c < chunks; c += 2) {  // pass 3: e -> packed fp16 P
-        uint32_t e[32], pp[16];
-        tmem_ld32(lane_addr + c * 32, e);
+    float total = red_sum[0][row];
 #pragma unroll
-        for (int p = 0; p < 16; ++p)
-          pp[p] = h2_bits(__floats2half2_rn(__fmul_rn(__uint_as_float(e[2 * p]), inv),
-                                            __fmul_rn(__uint_as_float(e[2 * p + 1]), inv)));
-        tmem_st16(lane_addr + c * 32, pp);
+    for (int g = 1; g < kGroups; ++g) total = __fadd_rn(total, red_sum[g][row]);
+    const float inv = __fdiv_rn(1.0f, total);
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < kChunksPerWarp; ++i) {  // pass 3: e -> packed fp16 P (TMEM)
+        const int c = group + kGroups * i;
+        if (c < chunks) {
+          uint32_t e[32], pp[16];
+          tmem_ld32(lane_addr + c * 32, e);
+#pragma unroll
+          for (int p = 0; p < 16; ++p)
+            pp[p] = h2_bits(__floats2half2_rn(__fmul_rn(__uint_as_float(e[2 * p]), inv),
+                                              __fmul_rn(__uint_as_float(e[2 * p + 1]), inv)));
+          tmem_st16(lane_addr + c * 32, pp);
+        }
       }
     }
     tmem_wait_st();
@@ -329,35 +351,42 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_tc(AttnArgs a) {
     // 4. out^T = P v^T into TMEM columns [ocol, ocol + hd)
     if (tid == 0) {
       const uint32_t idesc = umma_idesc(kAttnRows, hd, false, false);
-      for (int s = 0; s < np / 16; ++s)
-        umma_ts(tmem + ocol, tmem + (uint32_t)(32 * (s / 2) + 8 * (s % 2)), umma_desc(sv + s * 256, 128, sbo_v),
-                idesc, s > 0);
+      for (int s = 0; s < np / 16; ++s)  // K=16 tokens: 32 bytes along the 128-byte rows of box s/4
+        umma_ts(tmem + ocol, tmem + (uint32_t)(32 * (s / 2) + 8 * (s % 2)),
+                umma_desc(sv + (s / 4) * box_v + (s % 4) * 32, 16, 1024), idesc, s > 0);
       umma_commit(bar1);
     }
-    ok = mbar_wait(bar1, it & 1);
+    ok = mbar_wait(bar1, j & 1);
     if (!ok) fault |= 2u;
     ok = __syncthreads_and(ok);
     if (!ok) break;
     tc_fence_after();
-    if (a.stages == 1 && next < a.items) {  // the only stage is free once the output product is done
-      load_item(next, 0);
-      cp_async_commit();
+    // item j's stage and TMEM columns [0, np) are free: refill the stage, start item j+1's scores
+    if (tid == 0 && j + 1 < count) {
+      if (a.stages == 2) {
+        if (j + 2 < count) load_item(j + 2, st);
+        score_product(st ^ 1, fault);
+      } else {
+        load_item(j + 1, 0);
+        score_product(0, fault);
+      }
     }
-    if (live) {
-      uint16_t* out = a.out + b * a.o_bs + h * a.o_hs;
-      for (int c = group; c < hd / 32; c += 2) {
-        uint32_t r[32];
-        tmem_ld32(lane_addr + ocol + c * 32, r);
-        if (i0 + row < n) {
+    if (live && group < hd / 32) {  // output chunk `group` of this warp's 32 queries
+      uint16_t* out = a.out + b * a.o_bs + h * a.o_hs + (int64_t)(group * 32) * a.o_cs + i0 + row;
+      uint32_t r[32];
+      tmem_ld32(lane_addr + ocol + group * 32, r);
+      if (i0 + row < n) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            out[(int64_t)(c * 32 + e) * a.o_cs + i0 + row] = __half_as_ushort(__float2half_rn(__uint_as_float(r[e])));
-        }
+        for (int e = 0; e < 32; ++e) out[(int64_t)e * a.o_cs] = __half_as_ushort(__float2half_rn(__uint_as_float(r[e])));
       }
     }
     tc_fence_before();
   }
-  cp_async_wait<0>();
+  if (tid == 0) {  // copies still in flight after an early exit: wait for them (bounded)
+    for (int st = 0; st < 2; ++st)
+      while (waited[st] < fills[st])
+        if (!mbar_wait(full0 + 8 * st, waited[st]++ & 1)) fault |= 4u;
+  }
   if (fault) atomicOr(&g_attention_fault, fault);
   tc_fence_before();
   __syncthreads();
@@ -371,6 +400,44 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_tc(AttnArgs a) {
 }  // namespace ttn
 
 using namespace ttn;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult found;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &found) ==
+            cudaSuccess &&
+        found == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor map over a [batch, heads, channels, tokens] fp16 view (token stride 1) as the
+// 4-D tensor (token, channel, head, image), box (64 tokens, box_c channels, 1, 1) with
+// the 128-byte swizzle: one box lands as box_c swizzled 128-byte rows.
+ttn_status encode_operand(CUtensorMap* map, const void* base, int64_t batch, int64_t heads, int64_t channels,
+                          int64_t tokens, const int64_t* strides, int box_c, const char* name) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return fail(TTN_CUDA_ERROR, "%s: cuTensorMapEncodeTiled is not available", name);
+  const cuuint64_t dims[4] = {(cuuint64_t)tokens, (cuuint64_t)channels, (cuuint64_t)heads, (cuuint64_t)batch};
+  // byte strides of dims 1..3; a dim of extent 1 gets any valid stride
+  const cuuint64_t str[3] = {(cuuint64_t)strides[2] * 2, heads > 1 ? (cuuint64_t)strides[1] * 2 : 16,
+                             batch > 1 ? (cuuint64_t)strides[0] * 2 : 16};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_c, 1, 1};
+  const cuuint32_t unit[4] = {1, 1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, str, box, unit,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TTN_UNSUPPORTED, "%s: cuTensorMapEncodeTiled returned %d", name, (int)r);
+  return TTN_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -391,20 +458,25 @@ ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* 
     return fail(TTN_UNSUPPORTED, "%s: tokens must be a multiple of 8 with tokens + head_dim <= 512", name);
   const int64_t* all[4] = {q_strides, k_strides, v_strides, out_strides};
   const void* ptrs[4] = {q, k, v, out};
+  const int64_t extents[3] = {batch, heads, 0};
   for (int t = 0; t < 4; ++t) {
     if (((uintptr_t)ptrs[t] & 15u) || all[t][0] % 8 || all[t][1] % 8 || all[t][2] % 8)
       return fail(TTN_INVALID_ARG, "%s: 16-byte aligned bases and strides that are multiples of 8", name);
+    for (int d = 0; d < 3; ++d)
+      if (all[t][d] <= 0 && (d == 2 || extents[d] > 1))
+        return fail(TTN_INVALID_ARG, "%s: batch, head and channel strides must be positive", name);
   }
-  const size_t stage = (size_t)kAttnRows * key_dim * 2 + (size_t)np * key_dim * 2 + (size_t)head_dim * np * 2;
+  const int64_t nb = (tokens + 63) / 64;  // 64-token boxes of k and v
+  const size_t stage = (size_t)(2 + nb) * key_dim * 128 + (size_t)nb * head_dim * 128;
   cudaFuncAttributes attr;
   TTN_TRY(cuda_check(cudaFuncGetAttributes(&attr, (const void*)attention_tc), "cudaFuncGetAttributes"));
-  const int64_t budget = (int64_t)max_dynamic_smem() - (int64_t)attr.sharedSizeBytes;
+  const int64_t budget = (int64_t)max_dynamic_smem() - (int64_t)attr.sharedSizeBytes - 1024;  // 1 KB: alignment
   if ((int64_t)stage > budget)
     return fail(TTN_UNSUPPORTED, "%s: needs %zu bytes of shared memory", name, stage);
   if (batch > INT32_MAX || heads > INT32_MAX) return fail(TTN_UNSUPPORTED, "%s: batch or heads beyond 2^31", name);
   AttnArgs a;
   a.stages = (int64_t)(2 * stage) <= budget ? 2 : 1;
-  const size_t smem = stage * a.stages;
+  const size_t smem = stage * a.stages + 1024;
   TTN_TRY(ensure_dynamic_smem((const void*)attention_tc, (int)smem));
   a.q = (const uint16_t*)q;
   a.k = (const uint16_t*)k;
@@ -414,14 +486,19 @@ ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* 
   a.k_bs = k_strides[0], a.k_hs = k_strides[1], a.k_cs = k_strides[2];
   a.v_bs = v_strides[0], a.v_hs = v_strides[1], a.v_cs = v_strides[2];
   a.o_bs = out_strides[0], a.o_hs = out_strides[1], a.o_cs = out_strides[2];
-  a.n = (int)tokens, a.np = (int)np, a.kd = (int)key_dim, a.hd = (int)head_dim, a.heads = (int)heads;
+  a.n = (int)tokens, a.np = (int)np, a.nb = (int)nb, a.kd = (int)key_dim, a.hd = (int)head_dim;
+  a.heads = (int)heads;
   a.tiles = (int)((tokens + kAttnRows - 1) / kAttnRows);
   a.items = batch * heads * a.tiles;
   a.cols = 32;
   while (a.cols < np + head_dim) a.cols <<= 1;
   a.scale = scale;
+  AttnMaps maps;
+  TTN_TRY(encode_operand(&maps.q, q, batch, heads, key_dim, tokens, q_strides, (int)key_dim, name));
+  TTN_TRY(encode_operand(&maps.k, k, batch, heads, key_dim, tokens, k_strides, (int)key_dim, name));
+  TTN_TRY(encode_operand(&maps.v, v, batch, heads, head_dim, tokens, v_strides, (int)head_dim, name));
   const int64_t grid = a.items < sm_count() ? a.items : sm_count();  // one resident CTA per SM
-  attention_tc<<<(unsigned)grid, kAttnThreads, smem, (cudaStream_t)stream>>>(a);
+  attention_tc<<<(unsigned)grid, kAttnThreads, smem, (cudaStream_t)stream>>>(a, maps);
   return launch_check(name);
 }
 

@@ -1,4 +1,5 @@
-"""Per-config measurements for BASELINE configs 1, 2, 3 and 5 (``bench.py --config N``).
+"""Per-config measurements for BASELINE configs 1, 2, 3 and 5, and 6 = the fused
+C2PSA attention built on config 3's softmax (``bench.py --config N``).
 
 Each config is one kernel family on its own batch, inputs resident in HBM
 (every batch is far above the 126 MB L2), timed with CUDA events on the
@@ -142,7 +143,37 @@ class Config5:
         osel.select(s.contiguous().view(torch.int16).numpy().view(np.uint16), self.k)
 
 
-CONFIGS = {1: Config1, 2: Config2, 3: Config3, 5: Config5}
+class Config6:
+    """Fused C2PSA attention (beyond the softmax of config 3): q^T k, * 32^-0.5,
+    softmax, v attn^T from the qkv conv output [B, 4*(32+32+64), 400]."""
+    name = "config 6: fused C2PSA attention, qkv [B,512,400] -> [B,4,64,400], 4 heads, key_dim 32"
+    batch, cpu_batch = 512, 8
+    heads, kd, hd, n = 4, 32, 64, 400
+    scale = 32 ** -0.5
+    bytes_per_image = 2 * heads * (2 * kd + hd) * n + 2 * heads * hd * n  # qkv read, out written
+    flops_per_image = heads * (2 * n * n * kd + 2 * n * n * hd)
+
+    def _split(self, qkv):
+        return qkv.view(qkv.shape[0], self.heads, 2 * self.kd + self.hd, self.n).split([self.kd, self.kd, self.hd], 2)
+
+    def setup(self, batch, device, seed):
+        self.qkv = _gen((batch, self.heads * (2 * self.kd + self.hd), self.n), seed, device)
+        self.q, self.k, self.v = self._split(self.qkv)
+        self.out = torch.empty((batch, self.heads, self.hd, self.n), dtype=torch.float16, device=device)
+        return [self.qkv], [self.out]
+
+    def step(self):
+        ops.attention(self.q, self.k, self.v, self.scale, out=self.out)
+
+    def cpu_step(self, batch):
+        from oracle import ops as oops
+        if not hasattr(self, "cqkv"):
+            g = torch.Generator().manual_seed(6)
+            self.cqkv = torch.randn(batch, self.heads * (2 * self.kd + self.hd), self.n, generator=g).half()
+        oops.attention(*self._split(self.cqkv), self.scale)
+
+
+CONFIGS = {1: Config1, 2: Config2, 3: Config3, 5: Config5, 6: Config6}
 
 
 def unary_sweep(op: str = "silu", sizes_m=(13, 26, 52, 105, 210, 420, 839), reps: int = 10) -> dict:
@@ -269,7 +300,8 @@ def run_config(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": cfg.name, "batch_per_gpu": batch,
                        "l2": "inputs larger than L2 (no flush needed)",
-                       "algorithmic_bytes_per_image": cfg.bytes_per_image},
+                       "algorithmic_bytes_per_image": cfg.bytes_per_image,
+                       **({"tensor_flops_per_image": cfg.flops_per_image} if hasattr(cfg, "flops_per_image") else {})},
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s",
                          "frac": per_gpu / peak, "peak_kind": kind, "traffic": None},
             "gpu_launches": args.steps * (4 if args.config == 5 else 1),
