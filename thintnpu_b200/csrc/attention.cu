@@ -8,16 +8,18 @@
 // Layouts, as the reference's split of the qkv conv output gives them: q, k
 // [kd, n] and v [hd, n] per head with the token dim contiguous; out [hd, n].
 // Work item = (image, head, block of 128 queries).  A persistent CTA of 16 warps
-// per SM walks its items; thread 0 runs the copies and the tensor cores, the
-// warps run the softmax and the stores:
+// per SM walks its items; thread 0 issues the tensor-core products and threads
+// 32 and 64 the copies, all 16 warps run the softmax and the stores:
 //  1. TMA brings q (128 queries x kd), k (kd x n) and v (hd x n) into a
 //     two-stage shared-memory ring as boxes of 64 tokens (128 bytes, the
 //     128-byte swizzle) by all channels: the UMMA canonical 128-byte-swizzled
 //     layouts, q and k MN-major (the next 64 tokens one box further, the next
 //     8 channels 1024 bytes further), v K-major (8-channel groups 1024 bytes
 //     apart, a K=16 step 32 bytes along the row).  Tokens past n are
-//     zero-filled.  Item k+2's copies are issued as soon as item k's output
-//     product has released its stage.
+//     zero-filled.  Each stage has one barrier for q+k and one for v; threads
+//     32 and 64 issue the copies while thread 0 issues item k's output product:
+//     item k+2's q and k (item k's score product is done with them) and item
+//     k+1's v (item k-1's output product is done with it).
 //  2. S = q^T k as M=128 x N<=256 x K=16 tcgen05.mma steps into TMEM columns
 //     [0, np); item k+1's product is issued before item k's output stores.
 //  3. Warp w reads TMEM lanes 32(w%4).. (its 32 queries) and every fourth
@@ -50,6 +52,8 @@ constexpr int kAttnRows = 128;     // queries per item (UMMA M, TMEM lanes)
 constexpr int kAttnThreads = 512;  // four warps (column groups) per TMEM lane quarter
 constexpr int kGroups = kAttnThreads / 128;
 constexpr int kChunksPerWarp = 4;  // 32-column chunks per warp: np <= 512 columns
+constexpr int kCopierQK = 32;  // the threads that issue the TMA copies of q+k and of v (lane 0 of
+constexpr int kCopierV = 64;   // warps 1 and 2, idle while thread 0 issues the output product)
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // give up on a tensor-core wait after 200 ms
 constexpr float kLog2e = 1.44269504088896341f;
@@ -178,7 +182,7 @@ __device__ __forceinline__ __half2 bits_h2(uint32_t b) { return *reinterpret_cas
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_tc(AttnArgs a, const __grid_constant__ AttnMaps maps) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ __align__(8) uint64_t mbar[4];  // score product, output product, stage 0 and 1 copies
+  __shared__ __align__(8) uint64_t mbar[6];  // score product, output product, q+k copies x2, v copies x2
   __shared__ uint32_t tmem_base_slot;
   __shared__ float red_max[kGroups][kAttnRows], red_sum[kGroups][kAttnRows];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -193,29 +197,42 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem) + 1023u) & ~1023u;
   const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&mbar[0]);
   const uint32_t bar1 = (uint32_t)__cvta_generic_to_shared(&mbar[1]);
-  const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(&mbar[2]);  // stage st: full0 + 8 st
+  const uint32_t qk_full0 = (uint32_t)__cvta_generic_to_shared(&mbar[2]);  // stage st: + 8 st
+  const uint32_t v_full0 = (uint32_t)__cvta_generic_to_shared(&mbar[4]);
   const int64_t stride = gridDim.x;
   const int count = a.items > (int64_t)blockIdx.x ? (int)((a.items - blockIdx.x + stride - 1) / stride) : 0;
 
-  // thread 0: copies of this CTA's item j into stage st, and the score product of the item in stage st
-  uint32_t fills[2] = {0, 0}, waited[2] = {0, 0};
-  auto load_item = [&](int j, int st) {
+  // threads kCopierQK, kCopierV: copies of this CTA's item j into stage st; thread 0: waits for
+  // them and issues the products.  Counters per barrier: q+k of stage 0, 1; v of stage 0, 1.
+  uint32_t fills[4] = {0, 0, 0, 0}, waited[4] = {0, 0, 0, 0};
+  auto item_coords = [&](int j, int& t, int& h, int& b) {
     const int64_t item = blockIdx.x + j * stride;
-    const int t = (int)(item % a.tiles);
+    t = (int)(item % a.tiles);
     const int64_t bh = item / a.tiles;
-    const int h = (int)(bh % a.heads), b = (int)(bh / a.heads);
-    const uint32_t full = full0 + 8 * st, sq = smem0 + st * stage_bytes, sk = sq + q_bytes, sv = sk + k_bytes;
-    mbar_expect_tx(full, stage_bytes);
+    h = (int)(bh % a.heads), b = (int)(bh / a.heads);
+  };
+  auto load_qk = [&](int j, int st) {
+    int t, h, b;
+    item_coords(j, t, h, b);
+    const uint32_t full = qk_full0 + 8 * st, sq = smem0 + st * stage_bytes, sk = sq + q_bytes;
+    mbar_expect_tx(full, q_bytes + k_bytes);
     tma_load4(sq, &maps.q, t * kAttnRows, 0, h, b, full);
     tma_load4(sq + lbo_qk, &maps.q, t * kAttnRows + 64, 0, h, b, full);
-    for (int blk = 0; blk < a.nb; ++blk) {
-      tma_load4(sk + blk * lbo_qk, &maps.k, 64 * blk, 0, h, b, full);
-      tma_load4(sv + blk * box_v, &maps.v, 64 * blk, 0, h, b, full);
-    }
+    for (int blk = 0; blk < a.nb; ++blk) tma_load4(sk + blk * lbo_qk, &maps.k, 64 * blk, 0, h, b, full);
     ++fills[st];
   };
+  auto load_v = [&](int j, int st) {
+    int t, h, b;
+    item_coords(j, t, h, b);
+    const uint32_t full = v_full0 + 8 * st, sv = smem0 + st * stage_bytes + q_bytes + k_bytes;
+    mbar_expect_tx(full, v_bytes);
+    for (int blk = 0; blk < a.nb; ++blk) tma_load4(sv + blk * box_v, &maps.v, 64 * blk, 0, h, b, full);
+    ++fills[2 + st];
+  };
+  // which = 0, 1: q+k of stage 0, 1; 2, 3: v of stage 0, 1 (the four barriers are adjacent)
+  auto wait_copies = [&](int which) { return mbar_wait(qk_full0 + 8 * which, waited[which]++ & 1); };
   auto score_product = [&](int st, uint32_t& fault) {
-    if (!mbar_wait(full0 + 8 * st, waited[st]++ & 1)) {
+    if (!wait_copies(st)) {
       fault |= 4u;  // no commit: the warps' wait for the product gives up too
       return;
     }
@@ -232,7 +249,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   };
 
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 6; ++i)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&mbar[i])));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -250,11 +267,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t ocol = a.cols - hd;  // >= np rounded up to 32
   const __half2 neg_inf2 = bits_h2(0xfc00fc00u);
   uint32_t fault = 0;
-  if (tid == 0 && count > 0) {
-    load_item(0, 0);
-    if (count > 1 && a.stages == 2) load_item(1, 1);
-    score_product(0, fault);
+  if (tid == kCopierQK && count > 0) {
+    load_qk(0, 0);
+    if (count > 1 && a.stages == 2) load_qk(1, 1);
   }
+  if (tid == kCopierV && count > 0) load_v(0, 0);
+  if (tid == 0 && count > 0) score_product(0, fault);
 
   for (int j = 0; j < count; ++j) {
     const int st = a.stages == 2 ? (j & 1) : 0;
@@ -350,27 +368,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
     // 4. out^T = P v^T into TMEM columns [ocol, ocol + hd)
     if (tid == 0) {
-      const uint32_t idesc = umma_idesc(kAttnRows, hd, false, false);
-      for (int s = 0; s < np / 16; ++s)  // K=16 tokens: 32 bytes along the 128-byte rows of box s/4
-        umma_ts(tmem + ocol, tmem + (uint32_t)(32 * (s / 2) + 8 * (s % 2)),
-                umma_desc(sv + (s / 4) * box_v + (s % 4) * 32, 16, 1024), idesc, s > 0);
-      umma_commit(bar1);
+      if (!wait_copies(2 + st)) {
+        fault |= 4u;  // no commit on a failed copy: the warps' wait below gives up too
+      } else {
+        tc_fence_after();
+        const uint32_t idesc = umma_idesc(kAttnRows, hd, false, false);
+        for (int s = 0; s < np / 16; ++s)  // K=16 tokens: 32 bytes along the 128-byte rows of box s/4
+          umma_ts(tmem + ocol, tmem + (uint32_t)(32 * (s / 2) + 8 * (s % 2)),
+                  umma_desc(sv + (s / 4) * box_v + (s % 4) * 32, 16, 1024), idesc, s > 0);
+        umma_commit(bar1);
+      }
     }
+    // copies into buffers the tensor cores are done with: item j+2's q+k into this stage, item
+    // j+1's v into the other (one stage: item j+1's q+k now, its v after the output product)
+    if (tid == kCopierQK && j + (a.stages == 2 ? 2 : 1) < count) load_qk(j + (a.stages == 2 ? 2 : 1), st);
+    if (tid == kCopierV && a.stages == 2 && j + 1 < count) load_v(j + 1, st ^ 1);
     ok = mbar_wait(bar1, j & 1);
     if (!ok) fault |= 2u;
     ok = __syncthreads_and(ok);
     if (!ok) break;
     tc_fence_after();
-    // item j's stage and TMEM columns [0, np) are free: refill the stage, start item j+1's scores
-    if (tid == 0 && j + 1 < count) {
-      if (a.stages == 2) {
-        if (j + 2 < count) load_item(j + 2, st);
-        score_product(st ^ 1, fault);
-      } else {
-        load_item(j + 1, 0);
-        score_product(0, fault);
-      }
-    }
+    // TMEM columns [0, np) are free: start item j+1's scores
+    if (a.stages == 1 && tid == kCopierV && j + 1 < count) load_v(j + 1, 0);
+    if (tid == 0 && j + 1 < count) score_product(a.stages == 2 ? st ^ 1 : 0, fault);
     if (live && group < hd / 32) {  // output chunk `group` of this warp's 32 queries
       uint16_t* out = a.out + b * a.o_bs + h * a.o_hs + (int64_t)(group * 32) * a.o_cs + i0 + row;
       uint32_t r[32];
@@ -382,10 +402,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     tc_fence_before();
   }
-  if (tid == 0) {  // copies still in flight after an early exit: wait for them (bounded)
-    for (int st = 0; st < 2; ++st)
-      while (waited[st] < fills[st])
-        if (!mbar_wait(full0 + 8 * st, waited[st]++ & 1)) fault |= 4u;
+  if (tid == kCopierQK || tid == kCopierV) {  // copies in flight after an early exit: wait (bounded)
+    for (int which = 0; which < 4; ++which)  // at most one fill per barrier is outstanding
+      if (fills[which] && !mbar_wait(qk_full0 + 8 * which, (fills[which] - 1) & 1)) fault |= 4u;
   }
   if (fault) atomicOr(&g_attention_fault, fault);
   tc_fence_before();
