@@ -187,22 +187,27 @@ ttn_status ttn_softmax(const ttn_tensor* x, int32_t dim, float scale, const ttn_
                        ttn_stream stream);
 
 /* Fused C2PSA attention (the next step either side of the row softmax):
- * out = v @ softmax(fp16(fp16(q^T @ k) * scale))^T per (image, head), with
+ * out = v @ softmax(Z)^T per (image, head) with Z = fp16(fp16(q^T @ k) * scale)
+ * (YOLO11 order), or with TTN_ATTENTION_PRESCALE Z = fp16(fp16(q * scale)^T @ k)
+ * (the YOLO26 order: the query is scaled and rounded before the product).
  * q, k: fp16 [key_dim, tokens] and v, out: fp16 [head_dim, tokens] per head,
  * token dim contiguous; element (b, h, c, t) of each at
  * ptr[b*strides[0] + h*strides[1] + c*strides[2] + t].  The probabilities are
  * rounded to fp16 as the softmax op stores them; both products accumulate in
  * FP32 on the tensor cores (tcgen05, TMEM) and round once to fp16.  Replaces
- * the chain q.transpose @ k, * scale, softmax, v @ attn.transpose of
- * whole_blocked.py:91-110 (layout_bmm / channel_select bmm_flow.cpp:343-358
- * around thin_softmax::softmax softmax_host.cpp:51-89).  key_dim: 16..64 in
- * steps of 16; head_dim: 32..128 in steps of 32; tokens a multiple of 8 with
- * tokens + head_dim <= 512; 16-byte aligned bases, strides multiples of 8. */
+ * the chain of attention_forward whole_blocked.py:91-103 (both branches of
+ * _thin_attention_prescale: channel_select * scale or layout_bmm * scale, then
+ * softmax, then the second layout_bmm; layout_bmm/channel_select
+ * bmm_flow.cpp:256-358 around thin_softmax::softmax softmax_host.cpp:51-89).
+ * key_dim: 16..64 in steps of 16; head_dim: 32..128 in steps of 32; tokens a
+ * multiple of 8 with tokens + head_dim <= 512; 16-byte aligned bases, strides
+ * positive multiples of 8. */
+#define TTN_ATTENTION_PRESCALE 1u
 ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* out, int64_t batch,
                              int64_t heads, int64_t tokens, int64_t key_dim, int64_t head_dim,
                              const int64_t* q_strides, const int64_t* k_strides,
                              const int64_t* v_strides, const int64_t* out_strides, float scale,
-                             ttn_stream stream);
+                             uint32_t flags, ttn_stream stream);
 
 /* Reads and clears the attention kernel's fault word: nonzero when a launch
  * gave up waiting for its tensor-core work (it then freed its tensor memory

@@ -139,12 +139,18 @@ def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes, strides, xywh: bool
     return torch.cat((boxes, cls.sigmoid()), 1)
 
 
-def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
-    """C2PSA Attention core in CPU eager fp16 (whole_blocked.py:91-110):
-    attn = (q^T @ k) * scale; attn = softmax(attn, -1); out = v @ attn^T.
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+              prescale: bool = False) -> torch.Tensor:
+    """C2PSA Attention core in CPU eager fp16 (attention_forward whole_blocked.py:91-103):
+    attn = (q^T @ k) * scale, or with ``prescale`` (attention_scale_before_matmul,
+    whole_blocked.py:96-99) attn = (q * scale)^T @ k; attn = softmax(attn, -1);
+    out = v @ attn^T.
 
     q, k [B, h, kd, N], v [B, h, hd, N] fp16; every op rounds to fp16 as the
     reference's separate ATen ops do."""
-    attn = (q.transpose(-2, -1) @ k) * scale
+    if prescale:
+        attn = (q * scale).transpose(-2, -1) @ k
+    else:
+        attn = (q.transpose(-2, -1) @ k) * scale
     attn = attn.softmax(dim=-1)
     return v @ attn.transpose(-2, -1)

@@ -56,6 +56,24 @@ def test_attention_matches_cpu_chain(device, b, heads, kd, hd, n):
     _check(got, oops.attention(q, k, v, scale), q, k, v, scale)
 
 
+@pytest.mark.parametrize("b,heads,kd,hd,n", [(2, 4, 32, 64, 400), (1, 2, 64, 64, 448), (48, 4, 32, 64, 400)])
+def test_attention_prescale_matches_cpu_chain(device, b, heads, kd, hd, n):
+    """The YOLO26 order (attention_scale_before_matmul, whole_blocked.py:96-99):
+    the query is rounded to fp16(q * scale) before the product."""
+    import thintnpu_b200 as ttn
+    scale = kd ** -0.5
+    qkv, q, k, v = _qkv(b, heads, kd, hd, n, seed=7 * n + kd)
+    dev = qkv.to(device)
+    dq, dk, dv = dev.view(b, heads, 2 * kd + hd, n).split([kd, kd, hd], dim=2)
+    got = ttn.attention(dq, dk, dv, scale, prescale=True)
+    torch.cuda.synchronize()
+    assert ttn.ops.attention_fault() == 0
+    want = oops.attention(q, k, v, scale, prescale=True)
+    assert not torch.equal(want, oops.attention(q, k, v, scale))  # the two orders differ on these inputs
+    _check(got, want, q, k, v, scale)
+    assert torch.equal(dev, qkv.to(device))  # the input is not modified (q is scaled in shared memory)
+
+
 def test_attention_contiguous_inputs_and_out_view(device):
     import thintnpu_b200 as ttn
     _, q, k, v = _qkv(2, 4, 32, 64, 400, seed=3, std=2.0)

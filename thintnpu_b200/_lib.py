@@ -15,6 +15,7 @@ F16, F32 = 0, 1
 SUB, MUL, DIV, ADD = 0, 1, 2, 3
 NCHW, NC1HWC0 = 0, 1
 SELECT_AGNOSTIC, SELECT_NAN_LAST, SELECT_SIGMOID = 1, 2, 4
+ATTENTION_PRESCALE = 1
 
 STATUS = {0: "TTN_OK", 1: "TTN_INVALID_ARG", 2: "TTN_UNSUPPORTED", 3: "TTN_CUDA_ERROR",
           4: "TTN_TIMEOUT", 5: "TTN_DEVICE_FAULT_FLAG"}
@@ -92,7 +93,7 @@ _SIGNATURES = {
                                           ctypes.POINTER(ctypes.c_float), _I32, _P, _P]),
     "ttn_attention_f16": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, ctypes.POINTER(_I64),
                                          ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
-                                         ctypes.c_float, _P]),
+                                         ctypes.c_float, ctypes.c_uint32, _P]),
     "ttn_attention_fault_f16": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "ttn_select_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, ctypes.c_uint32]),
     "ttn_select_f16": (ctypes.c_int, [_TP, _I64, ctypes.c_uint32, _P, ctypes.c_size_t, _P,

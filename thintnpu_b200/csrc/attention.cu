@@ -21,7 +21,9 @@
 //     item k+2's q and k (item k's score product is done with them) and item
 //     k+1's v (item k-1's output product is done with it).
 //  2. S = q^T k as M=128 x N<=256 x K=16 tcgen05.mma steps into TMEM columns
-//     [0, np); item k+1's product is issued before item k's output stores.
+//     [0, np); item k+1's product is issued before item k's output stores.  In
+//     the prescale order (TTN_ATTENTION_PRESCALE) the warps first round the q
+//     tile to fp16(q scale) in shared memory and z is fp16(S).
 //  3. Warp w reads TMEM lanes 32(w%4).. (its 32 queries) and every fourth
 //     32-column chunk (w/4 picks which).  Pass 1 turns S into packed fp16 z
 //     (kept in registers) and the row max; pass 2 turns z into fp32
@@ -179,6 +181,7 @@ __device__ __forceinline__ void tma_load4(uint32_t dst, const CUtensorMap* map, 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t b) { return *reinterpret_cast<__half2*>(&b); }
 
+template <bool kPrescale>  // TTN_ATTENTION_PRESCALE: z = fp16(fp16(q scale)^T k), else fp16(fp16(q^T k) scale)
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_tc(AttnArgs a, const __grid_constant__ AttnMaps maps) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -231,6 +234,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   };
   // which = 0, 1: q+k of stage 0, 1; 2, 3: v of stage 0, 1 (the four barriers are adjacent)
   auto wait_copies = [&](int which) { return mbar_wait(qk_full0 + 8 * which, waited[which]++ & 1); };
+  // prescale order: every thread waits for item jj's q+k copies and rounds its share of
+  // the q tile to fp16(q * scale) in place before the score product reads it
+  unsigned char* const sbase = smem + (smem0 - (uint32_t)__cvta_generic_to_shared(smem));
+  auto prescale_q = [&](int jj) -> bool {
+    const int st = a.stages == 2 ? (jj & 1) : 0;
+    const uint32_t fill = a.stages == 2 ? (uint32_t)(jj >> 1) : (uint32_t)jj;
+    const bool ok = mbar_wait(qk_full0 + 8 * st, fill & 1);
+    if (ok) {
+      uint4* qv = reinterpret_cast<uint4*>(sbase + st * stage_bytes);
+      for (int i = tid; i < (int)(q_bytes / 16); i += kAttnThreads) {
+        uint4 w = qv[i];
+        uint32_t* h = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(bits_h2(h[e]));
+          h[e] = h2_bits(__floats2half2_rn(__fmul_rn(f.x, a.scale), __fmul_rn(f.y, a.scale)));
+        }
+        qv[i] = w;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+    }
+    return __syncthreads_and(ok);
+  };
   auto score_product = [&](int st, uint32_t& fault) {
     if (!wait_copies(st)) {
       fault |= 4u;  // no commit: the warps' wait for the product gives up too
@@ -272,9 +298,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (count > 1 && a.stages == 2) load_qk(1, 1);
   }
   if (tid == kCopierV && count > 0) load_v(0, 0);
-  if (tid == 0 && count > 0) score_product(0, fault);
+  bool run = true;
+  if (kPrescale && count > 0 && !prescale_q(0)) {
+    run = false;
+    fault |= 4u;
+  }
+  if (tid == 0 && count > 0 && run) score_product(0, fault);
 
-  for (int j = 0; j < count; ++j) {
+  for (int j = 0; j < count && run; ++j) {
     const int st = a.stages == 2 ? (j & 1) : 0;
     const int64_t item = blockIdx.x + j * stride;
     const int t = (int)(item % a.tiles);
@@ -304,8 +335,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const bool tail = c * 32 + 32 > n;
 #pragma unroll
           for (int p = 0; p < 16; ++p) {
-            const float2 s = __half22float2(__floats2half2_rn(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1])));
-            __half2 zz = __floats2half2_rn(__fmul_rn(s.x, a.scale), __fmul_rn(s.y, a.scale));
+            const __half2 sh = __floats2half2_rn(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1]));
+            const float2 s = __half22float2(sh);
+            __half2 zz = kPrescale ? sh : __floats2half2_rn(__fmul_rn(s.x, a.scale), __fmul_rn(s.y, a.scale));
             if (tail && c * 32 + 2 * p >= n) zz = neg_inf2;  // n is even: a pair is valid or not
             mx2 = __hmax2(mx2, zz);
             z[i][p] = h2_bits(zz);
@@ -390,6 +422,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tc_fence_after();
     // TMEM columns [0, np) are free: start item j+1's scores
     if (a.stages == 1 && tid == kCopierV && j + 1 < count) load_v(j + 1, 0);
+    if (kPrescale && j + 1 < count && !prescale_q(j + 1)) {
+      fault |= 4u;
+      break;
+    }
     if (tid == 0 && j + 1 < count) score_product(a.stages == 2 ? st ^ 1 : 0, fault);
     if (live && group < hd / 32) {  // output chunk `group` of this warp's 32 queries
       uint16_t* out = a.out + b * a.o_bs + h * a.o_hs + (int64_t)(group * 32) * a.o_cs + i0 + row;
@@ -463,9 +499,10 @@ extern "C" {
 ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* out, int64_t batch,
                              int64_t heads, int64_t tokens, int64_t key_dim, int64_t head_dim,
                              const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
-                             const int64_t* out_strides, float scale, ttn_stream stream) {
+                             const int64_t* out_strides, float scale, uint32_t flags, ttn_stream stream) {
   const char* name = "ttn_attention_f16";
   if (batch < 0 || heads < 0 || tokens < 0) return fail(TTN_INVALID_ARG, "%s: negative size", name);
+  if (flags & ~TTN_ATTENTION_PRESCALE) return fail(TTN_INVALID_ARG, "%s: unknown flags %u", name, flags);
   if (!batch || !heads || !tokens) return TTN_OK;
   if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides || !out_strides)
     return fail(TTN_INVALID_ARG, "%s: null pointer", name);
@@ -488,7 +525,9 @@ ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* 
   const int64_t nb = (tokens + 63) / 64;  // 64-token boxes of k and v
   const size_t stage = (size_t)(2 + nb) * key_dim * 128 + (size_t)nb * head_dim * 128;
   cudaFuncAttributes attr;
-  TTN_TRY(cuda_check(cudaFuncGetAttributes(&attr, (const void*)attention_tc), "cudaFuncGetAttributes"));
+  const void* kernel =
+      (flags & TTN_ATTENTION_PRESCALE) ? (const void*)attention_tc<true> : (const void*)attention_tc<false>;
+  TTN_TRY(cuda_check(cudaFuncGetAttributes(&attr, kernel), "cudaFuncGetAttributes"));
   const int64_t budget = (int64_t)max_dynamic_smem() - (int64_t)attr.sharedSizeBytes - 1024;  // 1 KB: alignment
   if ((int64_t)stage > budget)
     return fail(TTN_UNSUPPORTED, "%s: needs %zu bytes of shared memory", name, stage);
@@ -496,7 +535,7 @@ ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* 
   AttnArgs a;
   a.stages = (int64_t)(2 * stage) <= budget ? 2 : 1;
   const size_t smem = stage * a.stages + 1024;
-  TTN_TRY(ensure_dynamic_smem((const void*)attention_tc, (int)smem));
+  TTN_TRY(ensure_dynamic_smem(kernel, (int)smem));
   a.q = (const uint16_t*)q;
   a.k = (const uint16_t*)k;
   a.v = (const uint16_t*)v;
@@ -517,7 +556,10 @@ ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* 
   TTN_TRY(encode_operand(&maps.k, k, batch, heads, key_dim, tokens, k_strides, (int)key_dim, name));
   TTN_TRY(encode_operand(&maps.v, v, batch, heads, head_dim, tokens, v_strides, (int)head_dim, name));
   const int64_t grid = a.items < sm_count() ? a.items : sm_count();  // one resident CTA per SM
-  attention_tc<<<(unsigned)grid, kAttnThreads, smem, (cudaStream_t)stream>>>(a, maps);
+  if (flags & TTN_ATTENTION_PRESCALE)
+    attention_tc<true><<<(unsigned)grid, kAttnThreads, smem, (cudaStream_t)stream>>>(a, maps);
+  else
+    attention_tc<false><<<(unsigned)grid, kAttnThreads, smem, (cudaStream_t)stream>>>(a, maps);
   return launch_check(name);
 }
 

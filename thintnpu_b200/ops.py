@@ -354,9 +354,11 @@ def softmax(x: torch.Tensor, dim: int = -1, half_to_float: bool = False, scale: 
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
-              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, prescale: bool = False) -> torch.Tensor:
     """Fused C2PSA attention: v @ softmax((q^T @ k) * scale)^T per (image, head),
-    rounding as the reference's separate fp16 ops do (whole_blocked.py:91-110).
+    rounding as the reference's separate fp16 ops do (whole_blocked.py:91-103);
+    ``prescale`` is the reference's ``attention_scale_before_matmul`` order
+    (YOLO26): ``(q * scale)^T @ k`` with the scaled query rounded to fp16.
 
     q, k: fp16 [B, heads, key_dim, N] and v: [B, heads, head_dim, N] views with
     the token dim contiguous -- e.g. the split of the qkv conv output
@@ -380,7 +382,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
 
     if q.numel() and v.numel():
         call("ttn_attention_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, h, n, kd, hd,
-             strides(q), strides(k), strides(v), strides(out), float(scale), stream())
+             strides(q), strides(k), strides(v), strides(out), float(scale),
+             _lib.ATTENTION_PRESCALE if prescale else 0, stream())
     return out
 
 
