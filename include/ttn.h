@@ -214,6 +214,38 @@ ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* 
  * and left its output unwritten).  Synchronous. */
 ttn_status ttn_attention_fault_f16(uint32_t* fault);
 
+/* Dense 2-D convolution with the reference's fused epilogue, on the tensor cores
+ * (tcgen05 implicit GEMM, FP32 accumulation): out = fp16(silu(conv(x, w) + bias))
+ * with TTN_CONV_SILU (silu(s) = s / (1 + exp(-s)) in FP32), else fp16(conv + bias).
+ * x: NC1HWC0 fp16 [batch, c1, h, w, 16] (image i at x + i*x_batch_stride; input
+ * channels past the real count must be zero, as the reference's pack_input pads).
+ * packed_weights: the reference's prepared layout [c1][kernel^2][co64][16] with
+ * packed[cb][tap][o][c] = w[o][16 cb + c][tap] (co64 = co rounded up to 64, zero
+ * padded; ttn_conv2d_pack_weights_f16 builds it from OIHW).  bias: fp16 [co] or
+ * NULL.  kernel 1 (stride 1) or 3 / 6 (stride 1 or 2), zero padding (kernel-1)/2.
+ * out: NC1HWC0 [batch, co/16, oh, ow, 16] (co % 16 == 0), or NCHW [batch, co, oh,
+ * ow] with TTN_CONV_NCHW, image i at out + i*out_batch_stride (a batch stride
+ * larger than one image writes into a concat buffer).  Replaces
+ * thin_native_flow::conv conv_flow.cpp:594-646 (kernel convolution_native
+ * :123-372, epilogue :45-121) and thin_blocked::conv conv_blocked.cpp. */
+#define TTN_CONV_SILU 1u
+#define TTN_CONV_NCHW 2u
+ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int64_t h, int64_t w,
+                                  int64_t x_batch_stride, const void* packed_weights, const void* bias,
+                                  int64_t co, int32_t kernel, int32_t stride, uint32_t flags, void* out,
+                                  int64_t out_batch_stride, ttn_stream stream);
+
+/* Packs OIHW fp16 weights [co, ci, kernel, kernel] into the layout above
+ * (the reference's prepare(), conv_img.cpp:321-383). packed holds
+ * ceil(ci/16) * kernel^2 * co64 * 16 elements. */
+ttn_status ttn_conv2d_pack_weights_f16(const void* weights, int64_t co, int64_t ci, int32_t kernel,
+                                       void* packed, ttn_stream stream);
+
+/* Reads and clears the convolution kernel's fault word: nonzero when a launch
+ * gave up waiting (1 = an input copy, 2 = a free ring stage, 4 = an
+ * accumulator); its output is then incomplete.  Synchronous. */
+ttn_status ttn_conv2d_fault_f16(uint32_t* fault);
+
 /* Fused Detect decode (v8 DFL / v26).  box: fp16 [n, 4*16, a] logits (element
  * (b, s*16+i, j) at box[b*box_bs + (s*16+i)*box_cs + j]); cls: fp16 [n, nc, a]
  * logits with its own strides.  Anchors come from `levels` feature maps of

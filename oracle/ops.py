@@ -154,3 +154,27 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
         attn = (q.transpose(-2, -1) @ k) * scale
     attn = attn.softmax(dim=-1)
     return v @ attn.transpose(-2, -1)
+
+
+def conv_pack_weights(w: torch.Tensor) -> torch.Tensor:
+    """OIHW [co, ci, k, k] -> the reference's prepared layout [ceil(ci/16), k*k, co64, 16]
+    (blocked_c2f.py:66: reshape(co, ci/16, 16, k*k).permute(1, 3, 0, 2), co padded to 64
+    as prepare() does, conv_img.cpp:371-383; ci padded to 16 with zeros)."""
+    co, ci, k, _ = w.shape
+    cip, cop = (ci + 15) // 16 * 16, (co + 63) // 64 * 64
+    full = torch.zeros(cop, cip, k, k, dtype=w.dtype)
+    full[:co, :ci] = w
+    return full.reshape(cop, cip // 16, 16, k * k).permute(1, 3, 0, 2).contiguous()
+
+
+def conv2d(x: torch.Tensor, w: torch.Tensor, bias, stride: int, silu: bool) -> torch.Tensor:
+    """The reference's fused conv (convolution_native conv_flow.cpp:45-121) on the CPU:
+    x NC1HWC0 fp16 [n, c1, h, w, 16] (zero channels past w's ci), w OIHW fp16, bias fp16
+    [co] or None; FP32 conv + bias, then s / (1 + exp(-s)) in FP32 when ``silu``, one
+    rounding to fp16.  Returns NCHW fp16 [n, co, oh, ow]."""
+    xn = from_blocked(x).float()[:, : w.shape[1]]
+    k = w.shape[-1]
+    s = F.conv2d(xn, w.float(), None if bias is None else bias.float(), stride=stride, padding=(k - 1) // 2)
+    if silu:
+        s = s / (1.0 + torch.exp(-s))
+    return s.half()

@@ -1,0 +1,99 @@
+"""GPU parity: the fused convolution (tcgen05 implicit GEMM, TMEM, TMA) against the
+reference's conv + epilogue on the CPU: FP32 conv + bias, s / (1 + exp(-s)) in FP32,
+one rounding to fp16 (convolution_native conv_flow.cpp:45-121).
+
+The tensor cores sum the products in another order than the CPU conv, so an output
+can round to a neighbouring fp16 value, and outputs near zero can differ by the FP32
+accumulation error (proportional to sum |x| |w|).  Measured on the CPU: the reference
+computation itself, with the input channels summed in a permuted order, moves by one
+fp16 step plus at most 0.23 * 2^-23 * sum |x| |w| (20 seeded cases).  Gate: every
+output within one fp16 step + 2^-21 * sum |x| |w|, and at least 99.5% - 5e-6 K of the
+outputs bit-equal, K = ci * k * k products per output (measured on a B200: 99.98% at
+K = 16, 99.7% at K = 576, 99.0% at K = 2304; the CPU with a permuted channel order
+keeps 99.7% at K = 2304, so the tensor cores' FP32 accumulation is a little coarser
+than sequential round-to-nearest adds)."""
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import ops as oops
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(b, ci, co, h, w, k, seed, bias=True):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(b, ci, h, w, generator=g).half()
+    wt = (torch.randn(co, ci, k, k, generator=g) * (1.0 / (ci * k * k) ** 0.5)).half()
+    bs = (torch.randn(co, generator=g) * 0.1).half() if bias else None
+    return x, wt, bs
+
+
+def _check(got_nchw, x, wt, bs, stride, silu):
+    want = oops.conv2d(oops.pack_padded(x), wt, bs, stride, silu).float()
+    got = got_nchw.cpu().float()
+    k = wt.shape[-1]
+    mag = F.conv2d(x.float().abs(), wt.float().abs(), None, stride=stride, padding=(k - 1) // 2)
+    ulp = 2.0 ** torch.floor(torch.log2(want.abs().clamp(min=2.0 ** -14))) * 2.0 ** -10
+    err = (got - want).abs()
+    bound = ulp + mag * 2.0 ** -21
+    assert torch.all(err <= bound), float((err - bound).max())
+    exact = (got == want).float().mean().item()
+    assert exact >= 0.995 - 5e-6 * wt.shape[1] * k * k, exact
+
+
+def _run(device, b, ci, co, h, w, k, stride, silu=True, bias=True, nchw=False, seed=0):
+    import thintnpu_b200 as ttn
+    x, wt, bs = _case(b, ci, co, h, w, k, seed, bias)
+    xd = oops.pack_padded(x).to(device)
+    packed = ttn.conv2d_pack_weights(wt.to(device))
+    assert torch.equal(packed.cpu(), oops.conv_pack_weights(wt))
+    out = ttn.conv2d(xd, packed, None if bs is None else bs.to(device), co, k, stride, silu=silu, nchw=nchw)
+    torch.cuda.synchronize()
+    assert ttn.ops.conv2d_fault() == 0
+    got = out if nchw else oops.from_blocked(out.cpu())
+    _check(got, x, wt, bs, stride, silu)
+
+
+@pytest.mark.parametrize("b,ci,co,h,w,k,stride", [
+    (2, 64, 128, 40, 40, 1, 1), (1, 32, 32, 80, 80, 1, 1), (3, 128, 256, 20, 20, 1, 1), (1, 128, 512, 20, 20, 1, 1),
+    (2, 64, 64, 40, 40, 3, 1), (1, 16, 32, 20, 20, 3, 1), (2, 32, 64, 80, 80, 3, 2), (1, 256, 256, 20, 20, 3, 2),
+    (1, 32, 48, 13, 13, 3, 1), (1, 32, 64, 13, 13, 3, 2), (1, 3, 32, 64, 64, 6, 2), (2, 80, 96, 24, 24, 3, 1)])
+def test_conv_matches_cpu(device, b, ci, co, h, w, k, stride):
+    _run(device, b, ci, co, h, w, k, stride)
+
+
+def test_conv_without_bias_or_silu(device):
+    _run(device, 2, 64, 64, 20, 20, 3, 1, silu=False, bias=False, seed=3)
+    _run(device, 1, 32, 64, 40, 40, 1, 1, silu=False, bias=True, seed=4)
+
+
+def test_conv_nchw_output(device):
+    _run(device, 2, 64, 80, 20, 20, 1, 1, nchw=True, seed=5)  # the Detect terminals: co = 64 + 16 classes
+    _run(device, 1, 32, 40, 20, 20, 3, 1, nchw=True, seed=6)
+
+
+def test_conv_into_concat_slice(device):
+    """out = a channel slice of a wider NC1HWC0 concat buffer (batch stride > one image)."""
+    import thintnpu_b200 as ttn
+    x, wt, bs = _case(2, 64, 64, 20, 20, 3, seed=7)
+    buf = torch.full((2, 12, 20, 20, 16), 7.0, dtype=torch.float16, device=device)
+    ttn.conv2d(oops.pack_padded(x).to(device), ttn.conv2d_pack_weights(wt.to(device)), bs.to(device), 64, 3, 1,
+               out=buf[:, 4:8])
+    torch.cuda.synchronize()
+    assert ttn.ops.conv2d_fault() == 0
+    assert torch.all(buf[:, :4] == 7.0) and torch.all(buf[:, 8:] == 7.0)
+    _check(oops.from_blocked(buf[:, 4:8].cpu()), x, wt, bs, 1, True)
+
+
+def test_conv_rejects_unsupported(device):
+    import thintnpu_b200 as ttn
+    from thintnpu_b200._lib import TtnError
+    x = torch.zeros(1, 2, 8, 8, 16, dtype=torch.float16, device=device)
+    packed = torch.zeros(2, 25, 64, 16, dtype=torch.float16, device=device)
+    with pytest.raises(TtnError, match="stride"):
+        ttn.conv2d(x, packed, None, 64, 5, 1)
+    with pytest.raises(TtnError, match="co % 16"):
+        ttn.conv2d(x, torch.zeros(2, 1, 64, 16, dtype=torch.float16, device=device), None, 40, 1, 1)

@@ -16,6 +16,7 @@ SUB, MUL, DIV, ADD = 0, 1, 2, 3
 NCHW, NC1HWC0 = 0, 1
 SELECT_AGNOSTIC, SELECT_NAN_LAST, SELECT_SIGMOID = 1, 2, 4
 ATTENTION_PRESCALE = 1
+CONV_SILU, CONV_NCHW = 1, 2
 
 STATUS = {0: "TTN_OK", 1: "TTN_INVALID_ARG", 2: "TTN_UNSUPPORTED", 3: "TTN_CUDA_ERROR",
           4: "TTN_TIMEOUT", 5: "TTN_DEVICE_FAULT_FLAG"}
@@ -30,6 +31,7 @@ EXPORTS = (
     "ttn_copy", "ttn_cat", "ttn_nc1hwc0_to_nchw_f16", "ttn_nchw_to_nc1hwc0_f16",
     "ttn_upsample2x", "ttn_upsample2x_nc1hwc0_f16", "ttn_maxpool", "ttn_sppf_f16",
     "ttn_softmax", "ttn_dfl_decode_f16", "ttn_attention_f16", "ttn_attention_fault_f16",
+    "ttn_conv2d_nc1hwc0_f16", "ttn_conv2d_pack_weights_f16", "ttn_conv2d_fault_f16",
     "ttn_select_workspace_size", "ttn_select_f16", "ttn_select_f16_static",
 )
 
@@ -95,6 +97,10 @@ _SIGNATURES = {
                                          ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
                                          ctypes.c_float, ctypes.c_uint32, _P]),
     "ttn_attention_fault_f16": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+    "ttn_conv2d_nc1hwc0_f16": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32, _I32,
+                                              ctypes.c_uint32, _P, _I64, _P]),
+    "ttn_conv2d_pack_weights_f16": (ctypes.c_int, [_P, _I64, _I64, _I32, _P, _P]),
+    "ttn_conv2d_fault_f16": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "ttn_select_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, ctypes.c_uint32]),
     "ttn_select_f16": (ctypes.c_int, [_TP, _I64, ctypes.c_uint32, _P, ctypes.c_size_t, _P,
                                       ctypes.POINTER(SelectTrace), _P]),

@@ -40,15 +40,12 @@
 // its copies in flight, frees its TMEM and returns.  Warp-collective
 // tensor-memory loads and stores run on every lane of a warp; only global
 // stores are guarded per row.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
-
-#include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace ttn {
 namespace {
+
+using namespace tc;
 
 constexpr int kAttnRows = 128;     // queries per item (UMMA M, TMEM lanes)
 constexpr int kAttnThreads = 512;  // four warps (column groups) per TMEM lane quarter
@@ -57,7 +54,6 @@ constexpr int kChunksPerWarp = 4;  // 32-column chunks per warp: np <= 512 colum
 constexpr int kCopierQK = 32;  // the threads that issue the TMA copies of q+k and of v (lane 0 of
 constexpr int kCopierV = 64;   // warps 1 and 2, idle while thread 0 issues the output product)
 constexpr int kTmemCols = 512;
-constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // give up on a tensor-core wait after 200 ms
 constexpr float kLog2e = 1.44269504088896341f;
 
 __device__ uint32_t g_attention_fault;
@@ -82,104 +78,6 @@ struct AttnArgs {
 struct AttnMaps {
   CUtensorMap q, k, v;
 };
-
-// Shared-memory matrix descriptor (tcgen05 "version 1"), 128-byte swizzle
-// (layout type 2): start address, leading- and stride-dimension byte offsets,
-// each >> 4.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46) | (2ull << 61);
-}
-// Instruction descriptor: f16 x f16 -> f32, M x N, operand majors (1 = MN-major).
-__device__ __forceinline__ uint32_t umma_idesc(int m, int n, bool a_mn, bool b_mn) {
-  return (1u << 4) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) |
-         ((uint32_t)(m >> 4) << 24);
-}
-// D (TMEM) [+]= A (shared memory) x B (shared memory)
-__device__ __forceinline__ void umma_ss(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)acc));
-}
-// D (TMEM) [+]= A (TMEM, K-major, two fp16 per column) x B (shared memory)
-__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, bool acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(b), "r"(idesc), "r"((uint32_t)acc));
-}
-__device__ __forceinline__ void umma_commit(uint32_t mbar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
-               : "memory");
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Waits for phase `phase` of the mbarrier, at most kWaitNs of wall time.
-__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t phase) {
-  const uint64_t start = global_ns();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(done)
-        : "r"(mbar), "r"(phase)
-        : "memory");
-    if (done) return true;
-    if (global_ns() - start > kWaitNs) return false;
-  }
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-      "%14, %15, %16};\n" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
-      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
-      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
-}
-// TMA tile load of one box of a 4-D tensor map into shared memory, completing on `mbar`
-__device__ __forceinline__ void tma_load4(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                          uint32_t mbar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-      "[%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(mbar)
-      : "memory");
-}
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 bits_h2(uint32_t b) { return *reinterpret_cast<__half2*>(&b); }
 
 template <bool kPrescale>  // TTN_ATTENTION_PRESCALE: z = fp16(fp16(q scale)^T k), else fp16(fp16(q^T k) scale)
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -268,23 +166,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int nc = np - col < 256 ? np - col : 256;
       const uint32_t idesc = umma_idesc(kAttnRows, nc, true, true);
       for (int s = 0; s < kd / 16; ++s)  // K=16 channels = two 1024-byte swizzle atoms
-        umma_ss(tmem_base_slot + col, umma_desc(sq + s * 2048, lbo_qk, 1024),
-                umma_desc(sk + (col / 64) * lbo_qk + s * 2048, lbo_qk, 1024), idesc, s > 0);
+        umma_ss(tmem_base_slot + col, smem_desc(sq + s * 2048, lbo_qk, 1024, kSwizzle128B),
+                smem_desc(sk + (col / 64) * lbo_qk + s * 2048, lbo_qk, 1024, kSwizzle128B), idesc, s > 0);
     }
     umma_commit(bar0);
   };
 
   if (tid == 0) {
-    for (int i = 0; i < 6; ++i)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&mbar[i])));
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < 6; ++i) mbar_init((uint32_t)__cvta_generic_to_shared(&mbar[i]), 1);
+    mbar_init_fence();
   }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     (uint32_t)__cvta_generic_to_shared(&tmem_base_slot)),
-                 "r"(a.cols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
-  }
+  if (warp == 0) tmem_alloc((uint32_t)__cvta_generic_to_shared(&tmem_base_slot), a.cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -407,7 +299,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t idesc = umma_idesc(kAttnRows, hd, false, false);
         for (int s = 0; s < np / 16; ++s)  // K=16 tokens: 32 bytes along the 128-byte rows of box s/4
           umma_ts(tmem + ocol, tmem + (uint32_t)(32 * (s / 2) + 8 * (s % 2)),
-                  umma_desc(sv + (s / 4) * box_v + (s % 4) * 32, 16, 1024), idesc, s > 0);
+                  smem_desc(sv + (s / 4) * box_v + (s % 4) * 32, 16, 1024, kSwizzle128B), idesc, s > 0);
         umma_commit(bar1);
       }
     }
@@ -447,7 +339,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.cols));
+    tmem_dealloc(tmem, a.cols);
   }
 }
 
@@ -457,20 +349,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 using namespace ttn;
 
 namespace {
-
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult found;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &found) ==
-            cudaSuccess &&
-        found == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
 
 // Tensor map over a [batch, heads, channels, tokens] fp16 view (token stride 1) as the
 // 4-D tensor (token, channel, head, image), box (64 tokens, box_c channels, 1, 1) with

@@ -1,0 +1,363 @@
+// Dense 2-D convolution on the 5th-generation tensor cores (tcgen05 + TMEM + TMA),
+// NC1HWC0 fp16 in, fp16 out (NC1HWC0 or NCHW), FP32 accumulation, with the
+// reference's fused epilogue: y = fp16(silu(acc + bias)) or fp16(acc + bias), the
+// FP32 SiLU being s / (1 + exp(-s)) and one rounding at the end
+// (convolution_native conv_flow.cpp:45-121, host conv() :594-646).
+//
+// Implicit GEMM: D[pixel, co] = sum over (tap, ci) of x[pixel shifted by tap, ci] *
+// w[co, ci, tap].  A tile is 128 output pixels (a wt x ht rectangle of one image,
+// wt = gcd(ow, 128)) by up to 256 output channels; K runs over (tap, group of up
+// to 4 16-channel blocks), 16 channels per tcgen05.mma.  Persistent CTAs, one per
+// SM, warp-specialised:
+//  * warp 0, lane 0: TMA producer.  Per K step one box of the input — 16 channels
+//    x (wt x ht pixels, element stride = the conv stride) x 4 channel blocks,
+//    started at the tap's offset (the zero padding comes from the out-of-bounds
+//    fill) — and one box of the reference's packed weights [c1][k*k][co64][16]
+//    (16 channels x up to 256 output channels x 4 channel blocks), both with the
+//    32-byte swizzle: every 16-channel row is one K=16 slice of a K-major UMMA
+//    operand (8-row groups 256 bytes apart).  A 4-stage ring with full/empty
+//    mbarriers.
+//  * warp 1, lane 0: MMA issuer into one of two TMEM accumulators (2 x 256
+//    columns), committing each stage back to its empty barrier and each finished
+//    tile to the accumulator's full barrier.
+//  * warps 2-9: epilogue.  Warp w reads TMEM lanes 32(w%4).. (its 32 pixels) and
+//    half of the tile's columns, adds the bias, applies the SiLU, rounds once and
+//    stores 32-byte NC1HWC0 rows (or NCHW elements); then frees the accumulator,
+//    so tile t's stores overlap tile t+1's products.
+// Every wait is bounded (200 ms of wall time); a role that gives up records the
+// reason in a device word (ttn_conv2d_fault_f16: 1 = copy, 2 = stage, 4 =
+// accumulator), stops, and the CTA drains its copies and frees its TMEM.
+#include "tcgen05.cuh"
+
+namespace ttn {
+namespace {
+
+using namespace tc;
+
+constexpr int kConvM = 128;          // output pixels per tile (UMMA M, TMEM lanes)
+constexpr int kConvMaxN = 256;       // output channels per tile (UMMA N, TMEM columns per accumulator)
+constexpr int kConvStages = 4;       // shared-memory ring depth
+constexpr int kConvBlocksPerStep = 4;  // 16-channel blocks (K=16 each) per ring stage
+constexpr int kConvEpiWarps = 8;
+constexpr int kConvThreads = 64 + 32 * kConvEpiWarps;
+
+__device__ uint32_t g_conv_fault;
+
+struct ConvArgs {
+  const uint16_t* bias;  // fp16 [co] or null
+  uint16_t* out;
+  int64_t out_bs;        // elements between images of the output
+  int c1, oh, ow, co, kernel, stride, pad;
+  int wt, ht;            // output tile: wt x ht pixels, wt * ht = 128
+  int tiles_w, tiles_h, co_tiles, tile_n;
+  int blocks;            // channel blocks per step: min(4, c1)
+  int groups;            // steps per tap: ceil(c1 / blocks)
+  int64_t tiles;         // batch * tiles_h * tiles_w * co_tiles
+  int silu, nchw;
+};
+struct ConvMaps {
+  CUtensorMap x, w;
+};
+
+__device__ __forceinline__ float silu_epilogue(float s) { return __fdiv_rn(s, __fadd_rn(1.0f, expf(-s))); }
+
+__global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __grid_constant__ ConvMaps maps) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bars[2 * kConvStages + 4];  // full[s], empty[s], acc_full[2], acc_empty[2]
+  __shared__ uint32_t tmem_slot;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t a_bytes = (uint32_t)a.blocks * kConvM * 32;      // input boxes of one stage
+  const uint32_t b_bytes = (uint32_t)a.blocks * a.tile_n * 32;    // weight boxes of one stage
+  const uint32_t stage_bytes = (a_bytes + b_bytes + 1023u) & ~1023u;
+  const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem) + 1023u) & ~1023u;
+  const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
+  auto full_bar = [&](int s) { return bar0 + 8 * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8 * (kConvStages + s); };
+  auto acc_full = [&](int i) { return bar0 + 8 * (2 * kConvStages + i); };
+  auto acc_empty = [&](int i) { return bar0 + 8 * (2 * kConvStages + 2 + i); };
+  const int64_t stride = gridDim.x;
+  const int count = a.tiles > (int64_t)blockIdx.x ? (int)((a.tiles - blockIdx.x + stride - 1) / stride) : 0;
+  const int taps = a.kernel * a.kernel, steps = taps * a.groups;
+  // tile j of this CTA -> image, output-pixel origin, first output channel
+  auto tile_coords = [&](int j, int& img, int& oh0, int& ow0, int& n0) {
+    int64_t t = blockIdx.x + (int64_t)j * stride;
+    n0 = (int)(t % a.co_tiles) * a.tile_n;
+    t /= a.co_tiles;
+    ow0 = (int)(t % a.tiles_w) * a.wt;
+    t /= a.tiles_w;
+    oh0 = (int)(t % a.tiles_h) * a.ht;
+    img = (int)(t / a.tiles_h);
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < kConvStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(acc_full(i), 1);
+      mbar_init(acc_empty(i), kConvEpiWarps);
+    }
+    mbar_init_fence();
+  }
+  if (warp == 1) tmem_alloc((uint32_t)__cvta_generic_to_shared(&tmem_slot), 2 * kConvMaxN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  uint32_t fault = 0;
+
+  if (warp == 0 && lane == 0) {  // TMA producer
+    uint32_t fills[kConvStages] = {0, 0, 0, 0};
+    int s = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int j = 0; j < count && ok; ++j) {
+      int img, oh0, ow0, n0;
+      tile_coords(j, img, oh0, ow0, n0);
+      for (int step = 0; step < steps; ++step) {
+        if (!mbar_wait(empty_bar(s), phase ^ 1)) {  // a fresh barrier counts as freed
+          fault |= 2u;
+          ok = false;
+          break;
+        }
+        const int tap = step / a.groups, cb = (step % a.groups) * a.blocks;
+        const int kh = tap / a.kernel, kw = tap % a.kernel;
+        const uint32_t sa = smem0 + s * stage_bytes, sb = sa + a_bytes;
+        mbar_expect_tx(full_bar(s), a_bytes + b_bytes);
+        tma_load5(sa, &maps.x, 0, ow0 * a.stride + kw - a.pad, oh0 * a.stride + kh - a.pad, cb, img, full_bar(s));
+        tma_load4(sb, &maps.w, 0, n0, tap, cb, full_bar(s));
+        ++fills[s];
+        if (++s == kConvStages) s = 0, phase ^= 1;
+      }
+    }
+    for (int i = 0; i < kConvStages; ++i)  // copies in flight after an early exit (bounded)
+      if (fills[i] && !mbar_wait(full_bar(i), (fills[i] - 1) & 1)) fault |= 1u;
+  } else if (warp == 1 && lane == 0) {  // MMA issuer
+    const uint32_t idesc = umma_idesc(kConvM, a.tile_n, false, false);
+    int s = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int j = 0; j < count && ok; ++j) {
+      const int acc = j & 1;
+      if (!mbar_wait(acc_empty(acc), ((j >> 1) & 1) ^ 1)) {
+        fault |= 4u;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + acc * kConvMaxN;
+      for (int step = 0; step < steps; ++step) {
+        if (!mbar_wait(full_bar(s), phase)) {
+          fault |= 1u;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem0 + s * stage_bytes, sb = sa + a_bytes;
+        for (int i = 0; i < a.blocks; ++i)
+          umma_ss(d, smem_desc(sa + i * kConvM * 32, 16, 256, kSwizzle32B),
+                  smem_desc(sb + i * a.tile_n * 32, 16, 256, kSwizzle32B), idesc, step > 0 || i > 0);
+        umma_commit(empty_bar(s));  // the stage is free once these products have read it
+        if (++s == kConvStages) s = 0, phase ^= 1;
+      }
+      if (ok) umma_commit(acc_full(acc));
+    }
+  } else if (warp >= 2) {  // epilogue
+    const int quarter = warp & 3, half = (warp - 2) >> 2, m = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int th = m / a.wt, tw = m % a.wt;
+    const int cols = a.tile_n / 2;  // this warp's columns: [half * cols, half * cols + cols)
+    for (int j = 0; j < count; ++j) {
+      const int acc = j & 1;
+      if (!mbar_wait(acc_full(acc), (j >> 1) & 1)) {
+        fault |= 4u;
+        break;
+      }
+      tc_fence_after();
+      int img, oh0, ow0, n0;
+      tile_coords(j, img, oh0, ow0, n0);
+      const int oh = oh0 + th, ow = ow0 + tw;
+      const bool pixel = oh < a.oh;  // ow < a.ow always: wt divides ow
+      uint16_t* out = a.out + img * a.out_bs;
+      for (int c = 0; c < cols; c += 32) {
+        uint32_t r[32];
+        __syncwarp();  // the tensor-memory load is warp-collective: reconverge after the stores
+        tmem_ld32(lane_addr + acc * kConvMaxN + half * cols + c, r);
+        const int co0 = n0 + half * cols + c;
+        if (!pixel || co0 >= a.co) continue;
+        uint32_t packed[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float s0 = __uint_as_float(r[e]), s1 = __uint_as_float(r[e + 1]);
+          if (a.bias && co0 + e < a.co) s0 = __fadd_rn(s0, __half2float(__ushort_as_half(a.bias[co0 + e])));
+          if (a.bias && co0 + e + 1 < a.co) s1 = __fadd_rn(s1, __half2float(__ushort_as_half(a.bias[co0 + e + 1])));
+          if (a.silu) s0 = silu_epilogue(s0), s1 = silu_epilogue(s1);
+          packed[e / 2] = h2_bits(__floats2half2_rn(s0, s1));
+        }
+        if (a.nchw) {
+          const int64_t plane = (int64_t)a.oh * a.ow;
+          uint16_t* o = out + (int64_t)co0 * plane + (int64_t)oh * a.ow + ow;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (co0 + e < a.co) o[e * plane] = (uint16_t)(packed[e / 2] >> (16 * (e & 1)));
+        } else {  // co is a multiple of 16: both 16-channel blocks are whole
+#pragma unroll
+          for (int blk = 0; blk < 2; ++blk) {
+            if (co0 + 16 * blk >= a.co) break;
+            uint4* o = reinterpret_cast<uint4*>(
+                out + ((((int64_t)(co0 / 16 + blk) * a.oh + oh) * a.ow + ow) << 4));
+            o[0] = make_uint4(packed[8 * blk], packed[8 * blk + 1], packed[8 * blk + 2], packed[8 * blk + 3]);
+            o[1] = make_uint4(packed[8 * blk + 4], packed[8 * blk + 5], packed[8 * blk + 6], packed[8 * blk + 7]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(acc));
+    }
+  }
+  if (fault) atomicOr(&g_conv_fault, fault);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * kConvMaxN);
+  }
+}
+
+// packed[cb][tap][co64][16] = w[co][cb * 16 + c][tap], zero where co >= co or ci >= ci
+// (the reference's prepare(): conv_img.cpp:321-383, blocked_c2f.py:66).
+__global__ void conv_pack_weights(const uint16_t* __restrict__ w, uint16_t* __restrict__ packed, int co, int ci,
+                                  int taps, int co_pad, int64_t total) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % 16);
+    int64_t t = i / 16;
+    const int o = (int)(t % co_pad);
+    t /= co_pad;
+    const int tap = (int)(t % taps);
+    const int cb = (int)(t / taps);
+    const int cin = cb * 16 + c;
+    packed[i] = (o < co && cin < ci) ? w[((int64_t)o * ci + cin) * taps + tap] : (uint16_t)0;
+  }
+}
+
+int gcd_int(int x, int y) {
+  while (y) {
+    const int t = x % y;
+    x = y;
+    y = t;
+  }
+  return x;
+}
+
+}  // namespace
+}  // namespace ttn
+
+using namespace ttn;
+
+extern "C" {
+
+ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int64_t h, int64_t w,
+                                  int64_t x_batch_stride, const void* packed_weights, const void* bias,
+                                  int64_t co, int32_t kernel, int32_t stride, uint32_t flags, void* out,
+                                  int64_t out_batch_stride, ttn_stream stream) {
+  const char* name = "ttn_conv2d_nc1hwc0_f16";
+  if (flags & ~(TTN_CONV_SILU | TTN_CONV_NCHW)) return fail(TTN_INVALID_ARG, "%s: unknown flags %u", name, flags);
+  if (batch < 0 || c1 <= 0 || h <= 0 || w <= 0 || co <= 0)
+    return fail(TTN_INVALID_ARG, "%s: sizes must be positive (batch >= 0)", name);
+  if (!((kernel == 1 && stride == 1) || ((kernel == 3 || kernel == 6) && (stride == 1 || stride == 2))))
+    return fail(TTN_UNSUPPORTED, "%s: 1x1 stride 1, or 3x3 / 6x6 stride 1 or 2", name);
+  const bool nchw = flags & TTN_CONV_NCHW;
+  if (!nchw && co % 16) return fail(TTN_UNSUPPORTED, "%s: NC1HWC0 output needs co % 16 == 0", name);
+  const int pad = (kernel - 1) / 2;
+  const int64_t oh = (h + 2 * pad - kernel) / stride + 1, ow = (w + 2 * pad - kernel) / stride + 1;
+  if (oh <= 0 || ow <= 0) return fail(TTN_INVALID_ARG, "%s: kernel exceeds the padded input", name);
+  if (!batch) return TTN_OK;
+  if (!x || !packed_weights || !out) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  if (((uintptr_t)x | (uintptr_t)packed_weights | (uintptr_t)out) & 15u || x_batch_stride % 8 ||
+      out_batch_stride % 8 || (bias && ((uintptr_t)bias & 1u)))
+    return fail(TTN_INVALID_ARG, "%s: 16-byte aligned tensors and batch strides that are multiples of 8", name);
+  const int64_t per_image = c1 * h * w * 16, out_image = (nchw ? co : co / 16 * 16) * oh * ow;
+  if (x_batch_stride < per_image && batch > 1)
+    return fail(TTN_INVALID_ARG, "%s: input images overlap", name);
+  if (out_batch_stride < out_image && batch > 1)
+    return fail(TTN_INVALID_ARG, "%s: output images overlap", name);
+  if (c1 > 65535 || h > 65535 || w > 65535 || co > 65536 || batch > INT32_MAX)
+    return fail(TTN_UNSUPPORTED, "%s: shape beyond the supported range", name);
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return fail(TTN_CUDA_ERROR, "%s: cuTensorMapEncodeTiled is not available", name);
+
+  ConvArgs a;
+  a.bias = (const uint16_t*)bias;
+  a.out = (uint16_t*)out;
+  a.out_bs = out_batch_stride;
+  a.c1 = (int)c1, a.oh = (int)oh, a.ow = (int)ow, a.co = (int)co;
+  a.kernel = kernel, a.stride = stride, a.pad = pad;
+  a.wt = gcd_int((int)ow, kConvM);
+  a.ht = kConvM / a.wt;
+  a.tiles_w = (int)(ow / a.wt);
+  a.tiles_h = (int)((oh + a.ht - 1) / a.ht);
+  const int64_t co_pad = (co + 63) / 64 * 64;
+  a.tile_n = (int)(co_pad < kConvMaxN ? co_pad : kConvMaxN);
+  a.co_tiles = (int)((co_pad + a.tile_n - 1) / a.tile_n);
+  a.blocks = (int)(c1 < kConvBlocksPerStep ? c1 : kConvBlocksPerStep);
+  a.groups = (int)((c1 + a.blocks - 1) / a.blocks);
+  a.tiles = batch * a.tiles_h * a.tiles_w * a.co_tiles;
+  a.silu = (flags & TTN_CONV_SILU) ? 1 : 0;
+  a.nchw = nchw ? 1 : 0;
+
+  ConvMaps maps;
+  {  // input: (16 channels, w, h, c1, image), boxes of 16 x (wt, ht) pixels at the conv stride x blocks
+    const cuuint64_t dims[5] = {16, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)c1, (cuuint64_t)batch};
+    const cuuint64_t str[4] = {32, (cuuint64_t)w * 32, (cuuint64_t)(h * w * 32),
+                               batch > 1 ? (cuuint64_t)x_batch_stride * 2 : 16};  // bytes: dims 1..4
+    const cuuint32_t box[5] = {16, (cuuint32_t)(a.wt * stride), (cuuint32_t)(a.ht * stride), (cuuint32_t)a.blocks, 1};
+    const cuuint32_t unit[5] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1, 1};
+    const CUresult r = encode(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(x), dims, str, box, unit,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TTN_UNSUPPORTED, "%s: input tensor map: cuTensorMapEncodeTiled %d", name, (int)r);
+  }
+  {  // packed weights: (16 channels, co64, tap, c1), boxes of 16 x tile_n x 1 x blocks
+    const int taps = kernel * kernel;
+    const cuuint64_t dims[4] = {16, (cuuint64_t)co_pad, (cuuint64_t)taps, (cuuint64_t)c1};
+    const cuuint64_t str[3] = {32, (cuuint64_t)(co_pad * 32), (cuuint64_t)(taps * co_pad * 32)};
+    const cuuint32_t box[4] = {16, (cuuint32_t)a.tile_n, 1, (cuuint32_t)a.blocks};
+    const cuuint32_t unit[4] = {1, 1, 1, 1};
+    const CUresult r = encode(&maps.w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(packed_weights), dims,
+                              str, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(TTN_UNSUPPORTED, "%s: weight tensor map: cuTensorMapEncodeTiled %d", name, (int)r);
+  }
+  const size_t stage = ((size_t)a.blocks * kConvM * 32 + (size_t)a.blocks * a.tile_n * 32 + 1023) / 1024 * 1024;
+  const size_t smem = stage * kConvStages + 1024;
+  TTN_TRY(ensure_dynamic_smem((const void*)conv_tc, (int)smem));
+  const int64_t grid = a.tiles < sm_count() ? a.tiles : sm_count();
+  conv_tc<<<(unsigned)grid, kConvThreads, smem, (cudaStream_t)stream>>>(a, maps);
+  return launch_check(name);
+}
+
+ttn_status ttn_conv2d_pack_weights_f16(const void* weights, int64_t co, int64_t ci, int32_t kernel, void* packed,
+                                       ttn_stream stream) {
+  const char* name = "ttn_conv2d_pack_weights_f16";
+  if (co <= 0 || ci <= 0 || !(kernel == 1 || kernel == 3 || kernel == 6))
+    return fail(TTN_INVALID_ARG, "%s: positive co, ci and kernel 1, 3 or 6", name);
+  if (!weights || !packed) return fail(TTN_INVALID_ARG, "%s: null pointer", name);
+  const int64_t co_pad = (co + 63) / 64 * 64, taps = (int64_t)kernel * kernel;
+  const int64_t total = (ci + 15) / 16 * taps * co_pad * 16;
+  const int threads = 256;
+  const int64_t blocks = (total + threads - 1) / threads < 4096 ? (total + threads - 1) / threads : 4096;
+  conv_pack_weights<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
+      (const uint16_t*)weights, (uint16_t*)packed, (int)co, (int)ci, (int)taps, (int)co_pad, total);
+  return launch_check(name);
+}
+
+ttn_status ttn_conv2d_fault_f16(uint32_t* fault) {
+  if (!fault) return fail(TTN_INVALID_ARG, "ttn_conv2d_fault_f16: null output");
+  TTN_TRY(cuda_check(cudaMemcpyFromSymbol(fault, g_conv_fault, sizeof(uint32_t)), "ttn_conv2d_fault_f16"));
+  const uint32_t zero = 0;
+  return cuda_check(cudaMemcpyToSymbol(g_conv_fault, &zero, sizeof(uint32_t)), "ttn_conv2d_fault_f16");
+}
+
+}  // extern "C"

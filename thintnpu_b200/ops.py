@@ -394,6 +394,57 @@ def attention_fault() -> int:
     return int(word.value)
 
 
+def conv2d_pack_weights(w: torch.Tensor) -> torch.Tensor:
+    """OIHW fp16 weights [co, ci, k, k] (k = 1, 3 or 6) on the GPU -> the reference's
+    prepared layout [ceil(ci/16), k*k, co64, 16] (conv_img.cpp:321-383)."""
+    _cuda(w, "conv2d_pack_weights")
+    _require(w.dtype == torch.float16 and w.dim() == 4 and w.size(2) == w.size(3) and w.is_contiguous(),
+             "conv2d_pack_weights: expected contiguous fp16 OIHW weights")
+    co, ci, k, _ = w.shape
+    packed = torch.empty(((ci + 15) // 16, k * k, (co + 63) // 64 * 64, 16), dtype=torch.float16, device=w.device)
+    call("ttn_conv2d_pack_weights_f16", w.data_ptr(), co, ci, k, packed.data_ptr(), stream())
+    return packed
+
+
+def conv2d(x: torch.Tensor, packed: torch.Tensor, bias: Optional[torch.Tensor], co: int, kernel: int,
+           stride: int = 1, silu: bool = True, nchw: bool = False,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The reference's fused convolution (thin_native_flow::conv, conv_flow.cpp:594-646) on
+    the tensor cores: x NC1HWC0 fp16 [B, C1, H, W, 16] (images may be strided), packed
+    weights from ``conv2d_pack_weights``, bias fp16 [co] or None; returns (or fills)
+    NC1HWC0 [B, co/16, OH, OW, 16], or NCHW [B, co, OH, OW] with ``nchw``.  ``out`` may
+    be a batch-strided view, e.g. a channel slice of a concat buffer."""
+    _cuda(x, "conv2d")
+    _require(x.dtype == torch.float16 and x.dim() == 5 and x.size(4) == 16 and x[0].is_contiguous(),
+             "conv2d: x must be fp16 NC1HWC0 [B, C1, H, W, 16] with dense images")
+    b, c1, h, w, _ = x.shape
+    _require(packed.dtype == torch.float16 and packed.is_contiguous() and packed.dim() == 4 and
+             tuple(packed.shape) == (c1, kernel * kernel, (co + 63) // 64 * 64, 16),
+             "conv2d: packed weights must be [C1, k*k, co64, 16] (conv2d_pack_weights)")
+    if bias is not None:
+        _require(bias.dtype == torch.float16 and bias.is_contiguous() and bias.numel() >= co,
+                 "conv2d: bias must be contiguous fp16 with at least co elements")
+    pad = (kernel - 1) // 2
+    oh, ow = (h + 2 * pad - kernel) // stride + 1, (w + 2 * pad - kernel) // stride + 1
+    shape = (b, co, oh, ow) if nchw else (b, co // 16, oh, ow, 16)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float16, device=x.device)
+    _require(tuple(out.shape) == shape and out.dtype == torch.float16 and out[0].is_contiguous(),
+             f"conv2d: out must be fp16 {shape} with dense images")
+    flags = (_lib.CONV_SILU if silu else 0) | (_lib.CONV_NCHW if nchw else 0)
+    call("ttn_conv2d_nc1hwc0_f16", x.data_ptr(), b, c1, h, w, x.stride(0) if b > 1 else c1 * h * w * 16,
+         packed.data_ptr(), None if bias is None else bias.data_ptr(), co, kernel, stride, flags, out.data_ptr(),
+         out.stride(0) if b > 1 else out[0].numel(), stream())
+    return out
+
+
+def conv2d_fault() -> int:
+    """Reads and clears the convolution kernel's fault word (0 = no launch gave up)."""
+    word = ctypes.c_uint32(0)
+    call("ttn_conv2d_fault_f16", ctypes.byref(word))
+    return int(word.value)
+
+
 def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes: Sequence[tuple],
                strides: Sequence[float], xywh: bool = True,
                out: Optional[torch.Tensor] = None) -> torch.Tensor:
