@@ -8,15 +8,17 @@
 // w[co, ci, tap].  A tile is 128 output pixels (a wt x ht rectangle of one image,
 // wt = gcd(ow, 128)) by up to 256 output channels; K runs over (tap, group of up
 // to 4 16-channel blocks), 16 channels per tcgen05.mma.  Persistent CTAs, one per
-// SM, warp-specialised:
+// SM, warp-specialised.  When a tile has at most 128 output channels it covers two
+// 128-pixel sub-tiles (the next ht rows) that share every weight stage, halving the
+// weight traffic per product:
 //  * warp 0, lane 0: TMA producer.  Per K step one box of the input — 16 channels
 //    x (wt x ht pixels, element stride = the conv stride) x 4 channel blocks,
 //    started at the tap's offset (the zero padding comes from the out-of-bounds
 //    fill) — and one box of the reference's packed weights [c1][k*k][co64][16]
 //    (16 channels x up to 256 output channels x 4 channel blocks), both with the
 //    32-byte swizzle: every 16-channel row is one K=16 slice of a K-major UMMA
-//    operand (8-row groups 256 bytes apart).  A 4-stage ring with full/empty
-//    mbarriers.
+//    operand (8-row groups 256 bytes apart).  A ring of as many stages as fit
+//    in shared memory (up to 8), with full/empty mbarriers.
 //  * warp 1, lane 0: MMA issuer into one of two TMEM accumulators (2 x 256
 //    columns), committing each stage back to its empty barrier and each finished
 //    tile to the accumulator's full barrier.
@@ -36,7 +38,7 @@ using namespace tc;
 
 constexpr int kConvM = 128;          // output pixels per tile (UMMA M, TMEM lanes)
 constexpr int kConvMaxN = 256;       // output channels per tile (UMMA N, TMEM columns per accumulator)
-constexpr int kConvStages = 4;       // shared-memory ring depth
+constexpr int kConvMaxStages = 8;    // shared-memory ring depth: as many stages as fit, up to 8
 constexpr int kConvBlocksPerStep = 4;  // 16-channel blocks (K=16 each) per ring stage
 constexpr int kConvEpiWarps = 8;
 constexpr int kConvThreads = 64 + 32 * kConvEpiWarps;
@@ -54,6 +56,8 @@ struct ConvArgs {
   int groups;            // steps per tap: ceil(c1 / blocks)
   int64_t tiles;         // batch * tiles_h * tiles_w * co_tiles
   int silu, nchw;
+  int stages;            // ring depth
+  int sub;               // pixel sub-tiles per tile (2 when tile_n <= 128: they share each weight stage)
 };
 struct ConvMaps {
   CUtensorMap x, w;
@@ -63,18 +67,20 @@ __device__ __forceinline__ float silu_epilogue(float s) { return __fdiv_rn(s, __
 
 __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __grid_constant__ ConvMaps maps) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ __align__(8) uint64_t bars[2 * kConvStages + 4];  // full[s], empty[s], acc_full[2], acc_empty[2]
+  __shared__ __align__(8) uint64_t bars[2 * kConvMaxStages + 4];  // full[s], empty[s], acc_full[2], acc_empty[2]
   __shared__ uint32_t tmem_slot;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t a_bytes = (uint32_t)a.blocks * kConvM * 32;      // input boxes of one stage
+  const uint32_t a_box = (uint32_t)a.blocks * kConvM * 32;        // one input box (one sub-tile)
+  const uint32_t a_bytes = a_box * a.sub;                          // input boxes of one stage
   const uint32_t b_bytes = (uint32_t)a.blocks * a.tile_n * 32;    // weight boxes of one stage
   const uint32_t stage_bytes = (a_bytes + b_bytes + 1023u) & ~1023u;
   const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem) + 1023u) & ~1023u;
   const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
   auto full_bar = [&](int s) { return bar0 + 8 * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8 * (kConvStages + s); };
-  auto acc_full = [&](int i) { return bar0 + 8 * (2 * kConvStages + i); };
-  auto acc_empty = [&](int i) { return bar0 + 8 * (2 * kConvStages + 2 + i); };
+  const int stages = a.stages;
+  auto empty_bar = [&](int s) { return bar0 + 8 * (kConvMaxStages + s); };
+  auto acc_full = [&](int i) { return bar0 + 8 * (2 * kConvMaxStages + i); };
+  auto acc_empty = [&](int i) { return bar0 + 8 * (2 * kConvMaxStages + 2 + i); };
   const int64_t stride = gridDim.x;
   const int count = a.tiles > (int64_t)blockIdx.x ? (int)((a.tiles - blockIdx.x + stride - 1) / stride) : 0;
   const int taps = a.kernel * a.kernel, steps = taps * a.groups;
@@ -85,12 +91,12 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
     t /= a.co_tiles;
     ow0 = (int)(t % a.tiles_w) * a.wt;
     t /= a.tiles_w;
-    oh0 = (int)(t % a.tiles_h) * a.ht;
+    oh0 = (int)(t % a.tiles_h) * a.ht * a.sub;
     img = (int)(t / a.tiles_h);
   };
 
   if (tid == 0) {
-    for (int s = 0; s < kConvStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
@@ -108,7 +114,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
   uint32_t fault = 0;
 
   if (warp == 0 && lane == 0) {  // TMA producer
-    uint32_t fills[kConvStages] = {0, 0, 0, 0};
+    uint32_t fills[kConvMaxStages] = {0, 0, 0, 0, 0, 0, 0, 0};
     int s = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -125,13 +131,15 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
         const int kh = tap / a.kernel, kw = tap % a.kernel;
         const uint32_t sa = smem0 + s * stage_bytes, sb = sa + a_bytes;
         mbar_expect_tx(full_bar(s), a_bytes + b_bytes);
-        tma_load5(sa, &maps.x, 0, ow0 * a.stride + kw - a.pad, oh0 * a.stride + kh - a.pad, cb, img, full_bar(s));
+        for (int u = 0; u < a.sub; ++u)
+          tma_load5(sa + u * a_box, &maps.x, 0, ow0 * a.stride + kw - a.pad, (oh0 + u * a.ht) * a.stride + kh - a.pad,
+                    cb, img, full_bar(s));
         tma_load4(sb, &maps.w, 0, n0, tap, cb, full_bar(s));
         ++fills[s];
-        if (++s == kConvStages) s = 0, phase ^= 1;
+        if (++s == stages) s = 0, phase ^= 1;
       }
     }
-    for (int i = 0; i < kConvStages; ++i)  // copies in flight after an early exit (bounded)
+    for (int i = 0; i < stages; ++i)  // copies in flight after an early exit (bounded)
       if (fills[i] && !mbar_wait(full_bar(i), (fills[i] - 1) & 1)) fault |= 1u;
   } else if (warp == 1 && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc(kConvM, a.tile_n, false, false);
@@ -145,7 +153,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
         break;
       }
       tc_fence_after();
-      const uint32_t d = tmem + acc * kConvMaxN;
+      const uint32_t d = tmem + acc * kConvMaxN;  // sub-tile u at d + u * tile_n (sub = 2: tile_n <= 128)
       for (int step = 0; step < steps; ++step) {
         if (!mbar_wait(full_bar(s), phase)) {
           fault |= 1u;
@@ -154,11 +162,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
         }
         tc_fence_after();
         const uint32_t sa = smem0 + s * stage_bytes, sb = sa + a_bytes;
-        for (int i = 0; i < a.blocks; ++i)
-          umma_ss(d, smem_desc(sa + i * kConvM * 32, 16, 256, kSwizzle32B),
-                  smem_desc(sb + i * a.tile_n * 32, 16, 256, kSwizzle32B), idesc, step > 0 || i > 0);
+        for (int i = 0; i < a.blocks; ++i) {
+          const uint64_t bdesc = smem_desc(sb + i * a.tile_n * 32, 16, 256, kSwizzle32B);
+          for (int u = 0; u < a.sub; ++u)
+            umma_ss(d + u * a.tile_n, smem_desc(sa + u * a_box + i * kConvM * 32, 16, 256, kSwizzle32B), bdesc, idesc,
+                    step > 0 || i > 0);
+        }
         umma_commit(empty_bar(s));  // the stage is free once these products have read it
-        if (++s == kConvStages) s = 0, phase ^= 1;
+        if (++s == stages) s = 0, phase ^= 1;
       }
       if (ok) umma_commit(acc_full(acc));
     }
@@ -166,7 +177,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
     const int quarter = warp & 3, half = (warp - 2) >> 2, m = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const int th = m / a.wt, tw = m % a.wt;
-    const int cols = a.tile_n / 2;  // this warp's columns: [half * cols, half * cols + cols)
+    // sub = 1: this warp's columns [half * cols, half * cols + cols) of the one sub-tile;
+    // sub = 2: all columns of sub-tile `half`
+    const int cols = a.sub == 2 ? a.tile_n : a.tile_n / 2, col0 = a.sub == 2 ? half * a.tile_n : half * cols;
+    const int row0 = a.sub == 2 ? half * a.ht : 0;
     for (int j = 0; j < count; ++j) {
       const int acc = j & 1;
       if (!mbar_wait(acc_full(acc), (j >> 1) & 1)) {
@@ -176,14 +190,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
       tc_fence_after();
       int img, oh0, ow0, n0;
       tile_coords(j, img, oh0, ow0, n0);
-      const int oh = oh0 + th, ow = ow0 + tw;
+      const int oh = oh0 + row0 + th, ow = ow0 + tw;
       const bool pixel = oh < a.oh;  // ow < a.ow always: wt divides ow
       uint16_t* out = a.out + img * a.out_bs;
       for (int c = 0; c < cols; c += 32) {
         uint32_t r[32];
         __syncwarp();  // the tensor-memory load is warp-collective: reconverge after the stores
-        tmem_ld32(lane_addr + acc * kConvMaxN + half * cols + c, r);
-        const int co0 = n0 + half * cols + c;
+        tmem_ld32(lane_addr + acc * kConvMaxN + col0 + c, r);
+        const int co0 = n0 + (a.sub == 2 ? 0 : col0) + c;
         if (!pixel || co0 >= a.co) continue;
         uint32_t packed[16];
 #pragma unroll
@@ -296,9 +310,13 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
   a.wt = gcd_int((int)ow, kConvM);
   a.ht = kConvM / a.wt;
   a.tiles_w = (int)(ow / a.wt);
-  a.tiles_h = (int)((oh + a.ht - 1) / a.ht);
   const int64_t co_pad = (co + 63) / 64 * 64;
   a.tile_n = (int)(co_pad < kConvMaxN ? co_pad : kConvMaxN);
+  {  // two sub-tiles share the weight stages when they fit the accumulators and pad no extra rows
+    const int64_t rows1 = (oh + a.ht - 1) / a.ht * a.ht, rows2 = (oh + 2 * a.ht - 1) / (2 * a.ht) * (2 * a.ht);
+    a.sub = a.tile_n <= kConvMaxN / 2 && rows2 <= rows1 ? 2 : 1;
+  }
+  a.tiles_h = (int)((oh + a.sub * a.ht - 1) / (a.sub * a.ht));
   a.co_tiles = (int)((co_pad + a.tile_n - 1) / a.tile_n);
   a.blocks = (int)(c1 < kConvBlocksPerStep ? c1 : kConvBlocksPerStep);
   a.groups = (int)((c1 + a.blocks - 1) / a.blocks);
@@ -330,8 +348,14 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
     if (r != CUDA_SUCCESS)
       return fail(TTN_UNSUPPORTED, "%s: weight tensor map: cuTensorMapEncodeTiled %d", name, (int)r);
   }
-  const size_t stage = ((size_t)a.blocks * kConvM * 32 + (size_t)a.blocks * a.tile_n * 32 + 1023) / 1024 * 1024;
-  const size_t smem = stage * kConvStages + 1024;
+  const size_t stage =
+      ((size_t)a.sub * a.blocks * kConvM * 32 + (size_t)a.blocks * a.tile_n * 32 + 1023) / 1024 * 1024;
+  cudaFuncAttributes attr;
+  TTN_TRY(cuda_check(cudaFuncGetAttributes(&attr, (const void*)conv_tc), "cudaFuncGetAttributes"));
+  const int64_t budget = (int64_t)max_dynamic_smem() - (int64_t)attr.sharedSizeBytes - 1024;  // 1 KB: alignment
+  a.stages = (int)(budget / (int64_t)stage < kConvMaxStages ? budget / (int64_t)stage : kConvMaxStages);
+  if (a.stages < 2) return fail(TTN_UNSUPPORTED, "%s: a ring stage of %zu bytes does not fit twice", name, stage);
+  const size_t smem = stage * a.stages + 1024;
   TTN_TRY(ensure_dynamic_smem((const void*)conv_tc, (int)smem));
   const int64_t grid = a.tiles < sm_count() ? a.tiles : sm_count();
   conv_tc<<<(unsigned)grid, kConvThreads, smem, (cudaStream_t)stream>>>(a, maps);

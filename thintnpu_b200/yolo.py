@@ -213,6 +213,78 @@ def yolov8s_plan(imgsz: int = 640, nc: int = 80) -> Plan:
     return b.plan
 
 
+@dataclass(frozen=True)
+class ConvSpec:
+    """One convolution of the model: input channels, output channels, kernel, stride,
+    input height/width, and whether the SiLU epilogue follows (Ultralytics Conv)."""
+    cin: int
+    cout: int
+    k: int
+    s: int
+    h: int
+    w: int
+    act: bool = True
+
+    @property
+    def out_hw(self) -> Tuple[int, int]:
+        p = (self.k - 1) // 2
+        return (self.h + 2 * p - self.k) // self.s + 1, (self.w + 2 * p - self.k) // self.s + 1
+
+    @property
+    def flops(self) -> int:
+        oh, ow = self.out_hw
+        return 2 * self.cin * self.cout * self.k * self.k * oh * ow
+
+
+def yolov8s_convs(imgsz: int = 640, nc: int = 80) -> List[ConvSpec]:
+    """The 63 convolutions of YOLOv8s at imgsz x imgsz in model order (the same
+    topology as yolov8s_plan: C2f cv1 1x1 -> n bottlenecks of two 3x3 -> cv2 1x1 over
+    the (2+n) chunks; SPPF 1x1 -> 1x1 over 4 chunks; Detect cv2/cv3 towers of two 3x3 and
+    a 1x1 without activation).  The stem's 3 input channels are zero-padded to 16."""
+    s = imgsz
+    convs: List[ConvSpec] = []
+
+    def conv(cin, cout, k, st, hw, act=True):
+        convs.append(ConvSpec(cin, cout, k, st, hw, hw, act))
+        return (hw + 2 * ((k - 1) // 2) - k) // st + 1
+
+    def c2f(cin, cout, n, hw):
+        c = cout // 2
+        conv(cin, 2 * c, 1, 1, hw)
+        for _ in range(n):
+            conv(c, c, 3, 1, hw)
+            conv(c, c, 3, 1, hw)
+        conv((2 + n) * c, cout, 1, 1, hw)
+
+    hw = conv(3, 32, 3, 2, s)            # 0
+    hw = conv(32, 64, 3, 2, hw)          # 1
+    c2f(64, 64, 1, hw)                   # 2
+    hw = conv(64, 128, 3, 2, hw)         # 3
+    c2f(128, 128, 2, hw)                 # 4
+    hw = conv(128, 256, 3, 2, hw)        # 5
+    c2f(256, 256, 2, hw)                 # 6
+    hw = conv(256, 512, 3, 2, hw)        # 7
+    c2f(512, 512, 1, hw)                 # 8
+    conv(512, 256, 1, 1, hw)             # 9 SPPF cv1
+    conv(1024, 512, 1, 1, hw)            #   SPPF cv2
+    c2f(768, 256, 1, s // 16)            # 12
+    c2f(384, 128, 1, s // 8)             # 15
+    conv(128, 128, 3, 2, s // 8)         # 16
+    c2f(384, 256, 1, s // 16)            # 18
+    conv(256, 256, 3, 2, s // 16)        # 19
+    c2f(768, 512, 1, s // 32)            # 21
+    c3 = max(128, min(nc, 100))
+    for ch, stride in ((128, 8), (256, 16), (512, 32)):
+        hw = s // stride
+        conv(ch, 64, 3, 1, hw)
+        conv(64, 64, 3, 1, hw)
+        conv(64, 64, 1, 1, hw, act=False)
+        conv(ch, c3, 3, 1, hw)
+        conv(c3, c3, 3, 1, hw)
+        conv(c3, nc, 1, 1, hw, act=False)
+    return convs
+
+
 def synthetic_inputs(plan: Plan, batch: int, device, seed: int = 4) -> Dict[str, torch.Tensor]:
     """Seeded N(0,1) fp16 conv outputs, one generator per conv (seed + conv index).
 
