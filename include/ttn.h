@@ -235,6 +235,19 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
                                   int64_t co, int32_t kernel, int32_t stride, uint32_t flags, void* out,
                                   int64_t out_batch_stride, ttn_stream stream);
 
+/* Depthwise 2-D convolution (one filter per channel) with the same fused epilogue:
+ * acc = sum over (ky, kx) in that order of x * w (FP32, each product and sum rounded),
+ * + bias, then silu with TTN_CONV_SILU, one rounding to fp16.  x: NC1HWC0 fp16 [batch,
+ * c1, h, w, 16] (image i at x + i*x_batch_stride); packed_weights: [c1][kernel][kernel][16]
+ * fp16 (w[c][0][ky][kx] at [c/16][ky][kx][c%16], verify_depthwise_flow.py:27-30);
+ * bias: fp16 [16*c1] or NULL; odd kernel 1..7, stride 1 or 2, zero padding kernel/2;
+ * out: NC1HWC0 [batch, c1, oh, ow, 16] at out + i*out_batch_stride.  Replaces
+ * thin_native_flow::depthwise depthwise_flow.cpp:164-226 (kernel :23-162). */
+ttn_status ttn_depthwise_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int64_t h, int64_t w,
+                                     int64_t x_batch_stride, const void* packed_weights, const void* bias,
+                                     int32_t kernel, int32_t stride, uint32_t flags, void* out,
+                                     int64_t out_batch_stride, ttn_stream stream);
+
 /* Packs OIHW fp16 weights [co, ci, kernel, kernel] into the layout above
  * (the reference's prepare(), conv_img.cpp:321-383). packed holds
  * ceil(ci/16) * kernel^2 * co64 * 16 elements. */

@@ -178,3 +178,25 @@ def conv2d(x: torch.Tensor, w: torch.Tensor, bias, stride: int, silu: bool) -> t
     if silu:
         s = s / (1.0 + torch.exp(-s))
     return s.half()
+
+
+def depthwise(x: torch.Tensor, w: torch.Tensor, bias, kernel: int, stride: int, silu: bool) -> torch.Tensor:
+    """The reference's depthwise kernel (depthwise_flow.cpp:60-162) on the CPU in its own
+    operation order: acc = 0, then for ky, for kx: acc = acc + x * w (FP32 tensors, each
+    product and sum rounded), + bias, s / (1 + exp(-s)) when ``silu``, one rounding to fp16.
+    x NC1HWC0 fp16 [n, c1, h, w, 16], w [C, 1, k, k] fp16.  Returns NC1HWC0."""
+    n, c1, h, wd, _ = x.shape
+    pad = kernel // 2
+    xp = F.pad(x.float(), (0, 0, pad, pad, pad, pad))  # zero border in W and H
+    oh, ow = (h + 2 * pad - kernel) // stride + 1, (wd + 2 * pad - kernel) // stride + 1
+    wt = w.float().reshape(c1, 16, kernel, kernel)
+    acc = torch.zeros(n, c1, oh, ow, 16)
+    for ky in range(kernel):
+        for kx in range(kernel):
+            src = xp[:, :, ky: ky + (oh - 1) * stride + 1: stride, kx: kx + (ow - 1) * stride + 1: stride, :]
+            acc = acc + src * wt[:, :, ky, kx].reshape(1, c1, 1, 1, 16)
+    if bias is not None:
+        acc = acc + bias.float().reshape(1, c1, 1, 1, 16)
+    if silu:
+        acc = acc / (1.0 + torch.exp(-acc))
+    return acc.half()

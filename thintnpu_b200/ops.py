@@ -438,6 +438,40 @@ def conv2d(x: torch.Tensor, packed: torch.Tensor, bias: Optional[torch.Tensor], 
     return out
 
 
+def depthwise_pack_weights(w: torch.Tensor) -> torch.Tensor:
+    """Depthwise weights [C, 1, k, k] fp16 -> [C/16, k, k, 16] (verify_depthwise_flow.py:27-30)."""
+    c, one, k, k2 = w.shape
+    _require(one == 1 and k == k2 and c % 16 == 0, "depthwise_pack_weights: expected [C, 1, k, k] with C % 16 == 0")
+    return w.reshape(c // 16, 16, k, k).permute(0, 2, 3, 1).contiguous()
+
+
+def depthwise(x: torch.Tensor, packed: torch.Tensor, bias: Optional[torch.Tensor], kernel: int, stride: int = 1,
+              silu: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The reference's depthwise conv (thin_native_flow::depthwise, depthwise_flow.cpp:164-226)
+    over NC1HWC0 fp16 [B, C1, H, W, 16]; packed weights [C1, k, k, 16]; bias fp16 [16*C1]
+    or None; returns (or fills) NC1HWC0 [B, C1, OH, OW, 16]."""
+    _cuda(x, "depthwise")
+    _require(x.dtype == torch.float16 and x.dim() == 5 and x.size(4) == 16 and x[0].is_contiguous(),
+             "depthwise: x must be fp16 NC1HWC0 [B, C1, H, W, 16] with dense images")
+    b, c1, h, w, _ = x.shape
+    _require(packed.dtype == torch.float16 and packed.is_contiguous() and
+             tuple(packed.shape) == (c1, kernel, kernel, 16), "depthwise: packed weights must be [C1, k, k, 16]")
+    if bias is not None:
+        _require(bias.dtype == torch.float16 and bias.is_contiguous() and bias.numel() == 16 * c1,
+                 "depthwise: bias must be contiguous fp16 [16*C1]")
+    pad = kernel // 2
+    oh, ow = (h + 2 * pad - kernel) // stride + 1, (w + 2 * pad - kernel) // stride + 1
+    shape = (b, c1, oh, ow, 16)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float16, device=x.device)
+    _require(tuple(out.shape) == shape and out.dtype == torch.float16 and out[0].is_contiguous(),
+             f"depthwise: out must be fp16 {shape} with dense images")
+    call("ttn_depthwise_nc1hwc0_f16", x.data_ptr(), b, c1, h, w, x.stride(0) if b > 1 else x[0].numel(),
+         packed.data_ptr(), None if bias is None else bias.data_ptr(), kernel, stride,
+         _lib.CONV_SILU if silu else 0, out.data_ptr(), out.stride(0) if b > 1 else out[0].numel(), stream())
+    return out
+
+
 def conv2d_fault() -> int:
     """Reads and clears the convolution kernel's fault word (0 = no launch gave up)."""
     word = ctypes.c_uint32(0)
