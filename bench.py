@@ -45,8 +45,8 @@ def parse():
     p.add_argument("--no-variants", action="store_true")
     p.add_argument("--sweep", choices=("silu", "sigmoid"),
                    help="print fp16 unary bandwidth by tensor size (one GPU) and exit")
-    p.add_argument("--config", type=int, default=4, choices=(1, 2, 3, 4, 5, 6, 7),
-                   help="BASELINE config; 4 (the op pass) is the headline workload; 6 = fused C2PSA attention; 7 = YOLOv8s conv pass")
+    p.add_argument("--config", type=int, default=4, choices=(1, 2, 3, 4, 5, 6, 7, 8),
+                   help="BASELINE config; 4 (the op pass) is the headline workload; 6 = fused C2PSA attention; 7 = YOLOv8s conv pass; 8 = YOLO11s depthwise convs")
     return p.parse_args()
 
 

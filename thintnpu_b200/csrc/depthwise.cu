@@ -8,6 +8,7 @@
 // HBM-bound CUDA-core work.  One CTA per (image, channel block, band of output rows):
 // the band's input rows, with a zero border of `pad` pixels, are staged in shared
 // memory as fp16 16-channel vectors; the block's k*k*16 weights and 16 biases as FP32.
+// The band is staged with cp.async (all copies in flight; the border by zero fill).
 // Thread = (output pixel, 8 channels): k*k 16-byte shared-memory reads, one 16-byte
 // store.  Bands are sized so a CTA stages at most ~48 KB.
 #include "common.cuh"
@@ -18,7 +19,6 @@ namespace {
 constexpr int kDwThreads = 256;
 constexpr int kDwMaxKernel = 7;
 
-__device__ __forceinline__ float dw_silu(float s) { return __fdiv_rn(s, __fadd_rn(1.0f, expf(-s))); }
 
 __global__ void __launch_bounds__(kDwThreads) depthwise_nc1hwc0(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ wts, const uint16_t* __restrict__ bias,
@@ -36,14 +36,18 @@ __global__ void __launch_bounds__(kDwThreads) depthwise_nc1hwc0(
     sw[i] = __half2float(__ushort_as_half(wts[(int64_t)cb * k * k * 16 + i]));
   if (threadIdx.x < 16) sb[threadIdx.x] = bias ? __half2float(__ushort_as_half(bias[cb * 16 + threadIdx.x])) : 0.0f;
   const int top = r0 * s - pad;  // input row of tile row 0
-  for (int i = threadIdx.x; i < rows_in * wp * 2; i += blockDim.x) {
+  const uint32_t tile_s = (uint32_t)__cvta_generic_to_shared(tile);
+  for (int i = threadIdx.x; i < rows_in * wp * 2; i += blockDim.x) {  // all copies in flight, zero border
     const int half = i & 1, p = i >> 1, tr = p / wp, tc = p % wp;
     const int ir = top + tr, ic = tc - pad;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (ir >= 0 && ir < h && ic >= 0 && ic < w)
-      v = reinterpret_cast<const uint4*>(xin + ((int64_t)ir * w + ic) * 16)[half];
-    tile[i] = v;
+    const bool inside = ir >= 0 && ir < h && ic >= 0 && ic < w;
+    const uint16_t* src = inside ? xin + ((int64_t)ir * w + ic) * 16 + half * 8 : xin;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(tile_s + 16u * i), "l"(src),
+                 "r"(inside ? 16 : 0)
+                 : "memory");
   }
+  cp_async_commit();
+  cp_async_wait<0>();
   __syncthreads();
   const int rows = min(band, oh - r0);
   for (int i = threadIdx.x; i < rows * ow * 2; i += blockDim.x) {
@@ -69,7 +73,7 @@ __global__ void __launch_bounds__(kDwThreads) depthwise_nc1hwc0(
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       float a0 = __fadd_rn(acc[2 * c], sb[half * 8 + 2 * c]), a1 = __fadd_rn(acc[2 * c + 1], sb[half * 8 + 2 * c + 1]);
-      if (silu) a0 = dw_silu(a0), a1 = dw_silu(a1);
+      if (silu) a0 = silu_f32_for_f16(a0), a1 = silu_f32_for_f16(a1);
       const __half2 hv = __floats2half2_rn(a0, a1);
       out[c] = *reinterpret_cast<const uint32_t*>(&hv);
     }

@@ -235,7 +235,51 @@ class Config7:
             oops.conv2d(x, w, b, sp.s, sp.act)
 
 
-CONFIGS = {1: Config1, 2: Config2, 3: Config3, 5: Config5, 6: Config6, 7: Config7}
+class Config8:
+    """The depthwise convs of YOLO11s's Detect head at 640 (cv3 towers: DWConv 3x3 + SiLU on
+    the level's channels, then on c3 = 128): (128, 80x80) x2, (256 and 128, 40x40),
+    (512 and 128, 20x20), NC1HWC0 fp16, one graph replay per step."""
+    name = "config 8: YOLO11s-640 Detect depthwise convs, 6 x DWConv 3x3 + SiLU, NC1HWC0 fp16"
+    batch, cpu_batch = 64, 2
+    shapes = [(128, 80), (128, 80), (256, 40), (128, 40), (512, 20), (128, 20)]
+    bytes_per_image = sum(2 * 2 * c * hw * hw for c, hw in shapes)  # read once, written once
+    specs = shapes
+
+    def _layer(self, c, hw, batch, seed, device):
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(batch, c // 16, hw, hw, 16, generator=g).half()
+        w = (torch.randn(c, 1, 3, 3, generator=g) / 3).half()
+        b = (torch.randn(c, generator=g) * 0.1).half()
+        return x.to(device), w.to(device), b.to(device)
+
+    def setup(self, batch, device, seed):
+        self.layers = []
+        for i, (c, hw) in enumerate(self.shapes):
+            x, w, b = self._layer(c, hw, batch, seed + i, device)
+            self.layers.append((x, ops.depthwise_pack_weights(w), b, torch.empty_like(x)))
+        self._run()
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._run()
+        return [layer[0] for layer in self.layers], [layer[3] for layer in self.layers]
+
+    def _run(self):
+        for x, packed, b, out in self.layers:
+            ops.depthwise(x, packed, b, 3, 1, silu=True, out=out)
+
+    def step(self):
+        self.graph.replay()
+
+    def cpu_step(self, batch):
+        from oracle import ops as oops
+        if not hasattr(self, "clayers"):
+            self.clayers = [self._layer(c, hw, batch, 11 + i, "cpu") for i, (c, hw) in enumerate(self.shapes)]
+        for x, w, b in self.clayers:
+            oops.depthwise(x, w, b, 3, 1, True)
+
+
+CONFIGS = {1: Config1, 2: Config2, 3: Config3, 5: Config5, 6: Config6, 7: Config7, 8: Config8}
 
 
 def unary_sweep(op: str = "silu", sizes_m=(13, 26, 52, 105, 210, 420, 839), reps: int = 10) -> dict:
