@@ -27,8 +27,8 @@
 //  3. Warp w reads TMEM lanes 32(w%4).. (its 32 queries) and every fourth
 //     32-column chunk (w/4 picks which).  Pass 1 turns S into packed fp16 z
 //     (kept in registers) and the row max; pass 2 turns z into fp32
-//     e = 2^(z log2e - max log2e) (three pairs in four on the XU's ex2, one on the
-//     FMA pipe), stored in the chunk's own TMEM columns, and the row sum; pass 3 turns e into packed fp16 P = e / sum, stored in the
+//     e = 2^(z log2e - max log2e), stored in the chunk's own TMEM columns, and
+//     the row sum; pass 3 turns e into packed fp16 P = e / sum, stored in the
 //     first 16 of the chunk's columns.  Row max and sum are combined over the
 //     four warps of a lane quarter in shared memory.
 //  4. out^T = P v^T with A = P read from TMEM (K=16 step s takes the 8 columns
@@ -78,27 +78,6 @@ struct AttnArgs {
 struct AttnMaps {
   CUtensorMap q, k, v;
 };
-
-// 2^t on the FMA pipe, for part of the softmax exps (the XU pipe's ex2 is the pass's
-// bound): t = n + f with n = rint(t) from the 1.5 * 2^23 shift, 2^f by a degree-5
-// least-squares fit on [-0.5, 0.5] (fitted here on 4001 Chebyshev-spaced points,
-// relative weight; max relative error 2.0e-7 in fp32 Horner, like ex2.approx), and
-// 2^n added to the exponent field.  t is clamped at -125 so the result stays normal
-// (a masked column's -inf gives 2^-125, whose probability rounds to 0); NaN stays NaN.
-__device__ __forceinline__ float exp2_poly(float t) {
-  const float tc = t < -125.0f ? -125.0f : t;  // false for NaN: tc = NaN
-  const float r = __fadd_rn(tc, 12582912.0f);
-  const float n = __fsub_rn(r, 12582912.0f);
-  const float f = __fsub_rn(tc, n);
-  float p = 1.3266975292935967e-3f;
-  p = __fmaf_rn(p, f, 9.67546459287405e-3f);
-  p = __fmaf_rn(p, f, 5.550742521882057e-2f);
-  p = __fmaf_rn(p, f, 0.24022121727466583f);
-  p = __fmaf_rn(p, f, 0.6931469440460205f);
-  p = __fmaf_rn(p, f, 1.0000001192092896f);
-  const uint32_t scaled = __float_as_uint(p) + ((uint32_t)(__float_as_int(r) - 0x4B400000) << 23);
-  return tc == tc ? __uint_as_float(scaled) : tc;
-}
 
 template <bool kPrescale>  // TTN_ATTENTION_PRESCALE: z = fp16(fp16(q scale)^T k), else fp16(fp16(q^T k) scale)
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -274,10 +253,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int p = 0; p < 16; ++p) {
             const float2 zf = __half22float2(bits_h2(z[i][p]));
-            const float t0 = __fmaf_rn(zf.x, kLog2e, -hi), t1 = __fmaf_rn(zf.y, kLog2e, -hi);
-            const bool fma_pipe = (p & 3) == 3;  // one pair in four: balances the XU and issue
-            const float e0 = fma_pipe ? exp2_poly(t0) : ex2_approx(t0);
-            const float e1 = fma_pipe ? exp2_poly(t1) : ex2_approx(t1);
+            const float e0 = ex2_approx(__fmaf_rn(zf.x, kLog2e, -hi));
+            const float e1 = ex2_approx(__fmaf_rn(zf.y, kLog2e, -hi));
             sum = __fadd_rn(__fadd_rn(sum, e0), e1);
             e[2 * p] = __float_as_uint(e0);
             e[2 * p + 1] = __float_as_uint(e1);

@@ -255,18 +255,6 @@ __device__ __forceinline__ bool fast_rounding_safe(float r) {
 }
 
 __device__ __forceinline__ float silu_fast_f32(float x) { return x * rcp_approx(1.0f + exp_neg_fast(x)); }
-// FP32 SiLU of an FP32 value (a conv accumulator) for a single rounding to fp16: the
-// fast core when its fp16 rounding is certain (|x| < 16 carries the same argument
-// error as the fp16 inputs tested exhaustively; beyond it the result is x, or below
-// the fp16 normal range and decided exactly), else x / (1 + expf(-x)) with IEEE
-// add and divide, and a correctly rounded exp when that lands near a midpoint.
-__device__ __forceinline__ float silu_f32_for_f16(float x) {
-  float r = silu_fast_f32(x);
-  if (fast_rounding_safe(r)) return r;
-  r = silu_f32(x);
-  if (near_half_midpoint(r)) r = __fdiv_rn(x, __fadd_rn(1.0f, exp_neg_cr(x)));
-  return r;
-}
 __device__ __forceinline__ float sigmoid_fast_f32(float x) { return rcp_approx(1.0f + exp_neg_fast(x)); }
 
 // Two fp16 lanes at once, deferring the exact decision: returns the fast fp16

@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
           float s0 = __uint_as_float(r[e]), s1 = __uint_as_float(r[e + 1]);
           if (a.bias && co0 + e < a.co) s0 = __fadd_rn(s0, __half2float(__ushort_as_half(a.bias[co0 + e])));
           if (a.bias && co0 + e + 1 < a.co) s1 = __fadd_rn(s1, __half2float(__ushort_as_half(a.bias[co0 + e + 1])));
-          if (a.silu) s0 = silu_f32_for_f16(s0), s1 = silu_f32_for_f16(s1);
+          if (a.silu) s0 = silu_f32(s0), s1 = silu_f32(s1);
           packed[e / 2] = h2_bits(__floats2half2_rn(s0, s1));
         }
         if (a.nchw) {

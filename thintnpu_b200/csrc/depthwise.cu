@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(kDwThreads) depthwise_nc1hwc0(
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       float a0 = __fadd_rn(acc[2 * c], sb[half * 8 + 2 * c]), a1 = __fadd_rn(acc[2 * c + 1], sb[half * 8 + 2 * c + 1]);
-      if (silu) a0 = silu_f32_for_f16(a0), a1 = silu_f32_for_f16(a1);
+      if (silu) a0 = silu_f32(a0), a1 = silu_f32(a1);
       const __half2 hv = __floats2half2_rn(a0, a1);
       out[c] = *reinterpret_cast<const uint32_t*>(&hv);
     }
