@@ -10,7 +10,11 @@
 // to 4 16-channel blocks), 16 channels per tcgen05.mma.  Persistent CTAs, one per
 // SM, warp-specialised.  When a tile has at most 128 output channels it covers two
 // 128-pixel sub-tiles (the next ht rows) that share every weight stage, halving the
-// weight traffic per product:
+// weight traffic per product.  A 3x3 stride-1 conv uses 8 x 16-pixel tiles and loads,
+// per 16-channel block, one halo box (16 x (16 sub + 2) pixels from column ow0 - 1)
+// and the block's weights for all nine taps: each tap is the same box seen through a
+// shifted operand descriptor (start ((row + kh) * 16 + kw) * 32 bytes, 8-row groups
+// 512 bytes apart), so the input is copied about 1.8 times instead of nine:
 //  * warp 0, lane 0: TMA producer.  Per K step one box of the input — 16 channels
 //    x (wt x ht pixels, element stride = the conv stride) x 4 channel blocks,
 //    started at the tap's offset (the zero padding comes from the out-of-bounds
@@ -41,6 +45,8 @@ constexpr int kConvMaxN = 256;       // output channels per tile (UMMA N, TMEM c
 constexpr int kConvMaxStages = 8;    // shared-memory ring depth: as many stages as fit, up to 8
 constexpr int kConvBlocksPerStep = 4;  // 16-channel blocks (K=16 each) per ring stage
 constexpr int kConvEpiWarps = 8;
+constexpr int kHaloW = 16;  // halo box width (pixels) for 8-pixel-wide 3x3 tiles: 512-byte rows keep
+                            // every 8-row operand group on a 256-byte swizzle atom
 constexpr int kConvThreads = 64 + 32 * kConvEpiWarps;
 
 __device__ uint32_t g_conv_fault;
@@ -58,6 +64,9 @@ struct ConvArgs {
   int silu, nchw;
   int stages;            // ring depth
   int sub;               // pixel sub-tiles per tile (2 when tile_n <= 128: they share each weight stage)
+  int halo;              // 3x3 stride 1: one halo box per channel block, the taps as shifted descriptors
+  int steps;             // ring stages per tile
+  uint32_t a_box, a_bytes, b_off, b_bytes, stage_bytes;  // shared-memory layout of one stage
 };
 struct ConvMaps {
   CUtensorMap x, w;
@@ -69,10 +78,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
   __shared__ __align__(8) uint64_t bars[2 * kConvMaxStages + 4];  // full[s], empty[s], acc_full[2], acc_empty[2]
   __shared__ uint32_t tmem_slot;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t a_box = (uint32_t)a.blocks * kConvM * 32;        // one input box (one sub-tile)
-  const uint32_t a_bytes = a_box * a.sub;                          // input boxes of one stage
-  const uint32_t b_bytes = (uint32_t)a.blocks * a.tile_n * 32;    // weight boxes of one stage
-  const uint32_t stage_bytes = (a_bytes + b_bytes + 1023u) & ~1023u;
+  const uint32_t a_box = a.a_box, a_bytes = a.a_bytes, b_off = a.b_off, b_bytes = a.b_bytes;
+  const uint32_t stage_bytes = a.stage_bytes;
   const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem) + 1023u) & ~1023u;
   const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
   auto full_bar = [&](int s) { return bar0 + 8 * s; };
@@ -82,7 +89,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
   auto acc_empty = [&](int i) { return bar0 + 8 * (2 * kConvMaxStages + 2 + i); };
   const int64_t stride = gridDim.x;
   const int count = a.tiles > (int64_t)blockIdx.x ? (int)((a.tiles - blockIdx.x + stride - 1) / stride) : 0;
-  const int taps = a.kernel * a.kernel, steps = taps * a.groups;
+  const int steps = a.steps;
   // tile j of this CTA -> image, output-pixel origin, first output channel
   auto tile_coords = [&](int j, int& img, int& oh0, int& ow0, int& n0) {
     int64_t t = blockIdx.x + (int64_t)j * stride;
@@ -126,14 +133,19 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
           ok = false;
           break;
         }
-        const int tap = step / a.groups, cb = (step % a.groups) * a.blocks;
-        const int kh = tap / a.kernel, kw = tap % a.kernel;
-        const uint32_t sa = smem0 + s * stage_bytes, sb = sa + a_bytes;
+        const uint32_t sa = smem0 + s * stage_bytes, sb = sa + b_off;
         mbar_expect_tx(full_bar(s), a_bytes + b_bytes);
-        for (int u = 0; u < a.sub; ++u)
-          tma_load5(sa + u * a_box, &maps.x, 0, ow0 * a.stride + kw - a.pad, (oh0 + u * a.ht) * a.stride + kh - a.pad,
-                    cb, img, full_bar(s));
-        tma_load4(sb, &maps.w, 0, n0, tap, cb, full_bar(s));
+        if (a.halo) {  // step = channel block: its 16 x (sub*ht+2) halo and its weights of all 9 taps
+          tma_load5(sa, &maps.x, 0, ow0 - 1, oh0 - 1, step, img, full_bar(s));
+          tma_load4(sb, &maps.w, 0, n0, 0, step, full_bar(s));
+        } else {
+          const int tap = step / a.groups, cb = (step % a.groups) * a.blocks;
+          const int kh = tap / a.kernel, kw = tap % a.kernel;
+          for (int u = 0; u < a.sub; ++u)
+            tma_load5(sa + u * a_box, &maps.x, 0, ow0 * a.stride + kw - a.pad,
+                      (oh0 + u * a.ht) * a.stride + kh - a.pad, cb, img, full_bar(s));
+          tma_load4(sb, &maps.w, 0, n0, tap, cb, full_bar(s));
+        }
         ++fills[s];
         if (++s == stages) s = 0, phase ^= 1;
       }
@@ -160,12 +172,24 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem0 + s * stage_bytes, sb = sa + a_bytes;
-        for (int i = 0; i < a.blocks; ++i) {
-          const uint64_t bdesc = smem_desc(sb + i * a.tile_n * 32, 16, 256, kSwizzle32B);
-          for (int u = 0; u < a.sub; ++u)
-            umma_ss(d + u * a.tile_n, smem_desc(sa + u * a_box + i * kConvM * 32, 16, 256, kSwizzle32B), bdesc, idesc,
-                    step > 0 || i > 0);
+        const uint32_t sa = smem0 + s * stage_bytes, sb = sa + b_off;
+        if (a.halo) {  // tap (kh, kw) of sub-tile u: the halo shifted by (u*ht + kh) rows and kw pixels;
+                       // 8-pixel tile rows are the operand's 8-row groups, kHaloW*32 bytes apart
+          const uint32_t pitch = (uint32_t)kHaloW * 32;
+          for (int tap = 0; tap < 9; ++tap) {
+            const int kh = tap / 3, kw = tap % 3;
+            const uint64_t bdesc = smem_desc(sb + tap * a.tile_n * 32, 16, 256, kSwizzle32B);
+            for (int u = 0; u < a.sub; ++u)
+              umma_ss(d + u * a.tile_n, smem_desc(sa + ((u * a.ht + kh) * kHaloW + kw) * 32, 16, pitch, kSwizzle32B),
+                      bdesc, idesc, step > 0 || tap > 0);
+          }
+        } else {
+          for (int i = 0; i < a.blocks; ++i) {
+            const uint64_t bdesc = smem_desc(sb + i * a.tile_n * 32, 16, 256, kSwizzle32B);
+            for (int u = 0; u < a.sub; ++u)
+              umma_ss(d + u * a.tile_n, smem_desc(sa + u * a_box + i * kConvM * 32, 16, 256, kSwizzle32B), bdesc,
+                      idesc, step > 0 || i > 0);
+          }
         }
         umma_commit(empty_bar(s));  // the stage is free once these products have read it
         if (++s == stages) s = 0, phase ^= 1;
@@ -190,7 +214,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
       int img, oh0, ow0, n0;
       tile_coords(j, img, oh0, ow0, n0);
       const int oh = oh0 + row0 + th, ow = ow0 + tw;
-      const bool pixel = oh < a.oh;  // ow < a.ow always: wt divides ow
+      const bool pixel = oh < a.oh && ow < a.ow;
       uint16_t* out = a.out + img * a.out_bs;
       for (int c = 0; c < cols; c += 32) {
         uint32_t r[32];
@@ -306,9 +330,12 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
   a.out_bs = out_batch_stride;
   a.c1 = (int)c1, a.oh = (int)oh, a.ow = (int)ow, a.co = (int)co;
   a.kernel = kernel, a.stride = stride, a.pad = pad;
-  a.wt = gcd_int((int)ow, kConvM);
+  // halo tiles are 8 pixels wide; where the plain path gets 16-pixel-wide tiles sharing their weight
+  // stages (ow a multiple of 16 below 128, e.g. 80) it measured faster on a B200, elsewhere slower
+  a.halo = kernel == 3 && stride == 1 && !(ow % 16 == 0 && ow < 128);
+  a.wt = a.halo ? 8 : gcd_int((int)ow, kConvM);  // halo: one 8-pixel row per 8-row operand group
   a.ht = kConvM / a.wt;
-  a.tiles_w = (int)(ow / a.wt);
+  a.tiles_w = (int)((ow + a.wt - 1) / a.wt);
   const int64_t co_pad = (co + 63) / 64 * 64;
   a.tile_n = (int)(co_pad < kConvMaxN ? co_pad : kConvMaxN);
   {  // two sub-tiles share the weight stages when they fit the accumulators and pad no extra rows
@@ -317,8 +344,19 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
   }
   a.tiles_h = (int)((oh + a.sub * a.ht - 1) / (a.sub * a.ht));
   a.co_tiles = (int)((co_pad + a.tile_n - 1) / a.tile_n);
-  a.blocks = (int)(c1 < kConvBlocksPerStep ? c1 : kConvBlocksPerStep);
+  a.blocks = a.halo ? 1 : (int)(c1 < kConvBlocksPerStep ? c1 : kConvBlocksPerStep);
   a.groups = (int)((c1 + a.blocks - 1) / a.blocks);
+  a.steps = a.halo ? (int)c1 : kernel * kernel * a.groups;
+  if (a.halo) {
+    a.a_box = a.a_bytes = (uint32_t)((a.sub * a.ht + 2) * kHaloW * 32);
+    a.b_bytes = (uint32_t)(9 * a.tile_n * 32);
+  } else {
+    a.a_box = (uint32_t)(a.blocks * kConvM * 32);
+    a.a_bytes = a.a_box * a.sub;
+    a.b_bytes = (uint32_t)(a.blocks * a.tile_n * 32);
+  }
+  a.b_off = (a.a_bytes + 1023u) & ~1023u;
+  a.stage_bytes = (a.b_off + a.b_bytes + 1023u) & ~1023u;
   a.tiles = batch * a.tiles_h * a.tiles_w * a.co_tiles;
   a.silu = (flags & TTN_CONV_SILU) ? 1 : 0;
   a.nchw = nchw ? 1 : 0;
@@ -328,7 +366,8 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
     const cuuint64_t dims[5] = {16, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)c1, (cuuint64_t)batch};
     const cuuint64_t str[4] = {32, (cuuint64_t)w * 32, (cuuint64_t)(h * w * 32),
                                batch > 1 ? (cuuint64_t)x_batch_stride * 2 : 16};  // bytes: dims 1..4
-    const cuuint32_t box[5] = {16, (cuuint32_t)(a.wt * stride), (cuuint32_t)(a.ht * stride), (cuuint32_t)a.blocks, 1};
+    const cuuint32_t box[5] = {16, (cuuint32_t)(a.halo ? kHaloW : a.wt * stride),
+                               (cuuint32_t)(a.halo ? a.sub * a.ht + 2 : a.ht * stride), (cuuint32_t)a.blocks, 1};
     const cuuint32_t unit[5] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1, 1};
     const CUresult r = encode(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(x), dims, str, box, unit,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
@@ -339,7 +378,7 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
     const int taps = kernel * kernel;
     const cuuint64_t dims[4] = {16, (cuuint64_t)co_pad, (cuuint64_t)taps, (cuuint64_t)c1};
     const cuuint64_t str[3] = {32, (cuuint64_t)(co_pad * 32), (cuuint64_t)(taps * co_pad * 32)};
-    const cuuint32_t box[4] = {16, (cuuint32_t)a.tile_n, 1, (cuuint32_t)a.blocks};
+    const cuuint32_t box[4] = {16, (cuuint32_t)a.tile_n, (cuuint32_t)(a.halo ? 9 : 1), (cuuint32_t)a.blocks};
     const cuuint32_t unit[4] = {1, 1, 1, 1};
     const CUresult r = encode(&maps.w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(packed_weights), dims,
                               str, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
@@ -347,8 +386,7 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
     if (r != CUDA_SUCCESS)
       return fail(TTN_UNSUPPORTED, "%s: weight tensor map: cuTensorMapEncodeTiled %d", name, (int)r);
   }
-  const size_t stage =
-      ((size_t)a.sub * a.blocks * kConvM * 32 + (size_t)a.blocks * a.tile_n * 32 + 1023) / 1024 * 1024;
+  const size_t stage = a.stage_bytes;
   cudaFuncAttributes attr;
   TTN_TRY(cuda_check(cudaFuncGetAttributes(&attr, (const void*)conv_tc), "cudaFuncGetAttributes"));
   const int64_t budget = (int64_t)max_dynamic_smem() - (int64_t)attr.sharedSizeBytes - 1024;  // 1 KB: alignment
