@@ -173,23 +173,32 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
         }
         tc_fence_after();
         const uint32_t sa = smem0 + s * stage_bytes, sb = sa + b_off;
+        // Descriptors are built once per stage and stepped by adding (byte offset >> 4) to the start
+        // field (shared-memory addresses stay below 256 KB: no carry); one thread issues every
+        // product, so its per-product instruction count sets the issue rate.
+        const bool acc0 = step > 0;
         if (a.halo) {  // tap (kh, kw) of sub-tile u: the halo shifted by (u*ht + kh) rows and kw pixels;
                        // 8-pixel tile rows are the operand's 8-row groups, kHaloW*32 bytes apart
-          const uint32_t pitch = (uint32_t)kHaloW * 32;
+          const uint64_t a0 = smem_desc(sa, 16, kHaloW * 32, kSwizzle32B), b0 = smem_desc(sb, 16, 256, kSwizzle32B);
+          const uint32_t sub_off = (uint32_t)(a.ht * kHaloW * 32) >> 4, bn = (uint32_t)(a.tile_n * 32) >> 4;
+#pragma unroll
           for (int tap = 0; tap < 9; ++tap) {
-            const int kh = tap / 3, kw = tap % 3;
-            const uint64_t bdesc = smem_desc(sb + tap * a.tile_n * 32, 16, 256, kSwizzle32B);
-            for (int u = 0; u < a.sub; ++u)
-              umma_ss(d + u * a.tile_n, smem_desc(sa + ((u * a.ht + kh) * kHaloW + kw) * 32, 16, pitch, kSwizzle32B),
-                      bdesc, idesc, step > 0 || tap > 0);
+            const uint64_t ad = a0 + ((tap / 3) * kHaloW * 2 + (tap % 3) * 2), bd = b0 + tap * bn;
+            const bool acc = acc0 || tap > 0;
+            umma_ss(d, ad, bd, idesc, acc);
+            if (a.sub == 2) umma_ss(d + a.tile_n, ad + sub_off, bd, idesc, acc);
           }
         } else {
-          for (int i = 0; i < a.blocks; ++i) {
-            const uint64_t bdesc = smem_desc(sb + i * a.tile_n * 32, 16, 256, kSwizzle32B);
-            for (int u = 0; u < a.sub; ++u)
-              umma_ss(d + u * a.tile_n, smem_desc(sa + u * a_box + i * kConvM * 32, 16, 256, kSwizzle32B), bdesc,
-                      idesc, step > 0 || i > 0);
-          }
+          const uint64_t a0 = smem_desc(sa, 16, 256, kSwizzle32B), b0 = smem_desc(sb, 16, 256, kSwizzle32B);
+          const uint32_t bi = (uint32_t)(a.tile_n * 32) >> 4, ab = a_box >> 4;
+#pragma unroll
+          for (int i = 0; i < kConvBlocksPerStep; ++i)
+            if (i < a.blocks) {
+              const uint64_t ad = a0 + i * (kConvM * 32 / 16), bd = b0 + i * bi;
+              const bool acc = acc0 || i > 0;
+              umma_ss(d, ad, bd, idesc, acc);
+              if (a.sub == 2) umma_ss(d + a.tile_n, ad + ab, bd, idesc, acc);
+            }
         }
         umma_commit(empty_bar(s));  // the stage is free once these products have read it
         if (++s == stages) s = 0, phase ^= 1;
