@@ -49,3 +49,40 @@ def test_depthwise_silu_matches_cpu(device, b, c, h, w, k, s):
 def test_depthwise_without_bias(device):
     got, want = _run(device, 1, 32, 24, 24, 3, 1, silu=False, bias=False, seed=9)
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+def test_depthwise_silu_every_fp16_input(device):
+    """1x1 kernel, weight 1, no bias: the accumulator is each fp16 value itself, so the
+    SiLU epilogue sees all 65,536 inputs (NaNs, infinities, subnormals, signed zeros)."""
+    import thintnpu_b200 as ttn
+    x = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.float16).reshape(1, 16, 16, 16, 16)
+    wt = torch.ones(256, 1, 1, 1, dtype=torch.float16)
+    got = ttn.depthwise(x.to(device), ttn.depthwise_pack_weights(wt.to(device)), None, 1, 1, silu=True).cpu()
+    want = oops.depthwise(x, wt, None, 1, 1, True)
+    g, wv = got.float(), want.float()
+    nan = torch.isnan(wv)
+    assert torch.equal(torch.isnan(g), nan)
+    g, wv = g[~nan], wv[~nan]
+    assert torch.equal(torch.isinf(g), torch.isinf(wv))
+    fin = torch.isfinite(wv)
+    ulp = 2.0 ** torch.floor(torch.log2(wv[fin].abs().clamp(min=2.0 ** -14))) * 2.0 ** -10
+    assert torch.all((g[fin] - wv[fin]).abs() <= ulp)
+    assert (g == wv).float().mean().item() >= 0.999
+
+
+@pytest.mark.parametrize("scale", [0.01, 1.0, 6.0, 30.0])
+def test_depthwise_silu_rounds_like_fp32_silu(device, scale):
+    """The epilogue's fast SiLU either settles a value by its error bracket or takes
+    the IEEE-divide path, so every output must equal fp16(silu(acc)) computed by the
+    library's FP32 SiLU.  With a 1x1 kernel and no bias, acc = x * w exactly (two fp16
+    values), which gives FP32 accumulators of every magnitude at the chosen scale."""
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(int(scale * 100))
+    x = (torch.randn(2, 8, 32, 32, 16, generator=g) * scale).half()
+    wt = torch.randn(128, 1, 1, 1, generator=g).half()
+    xd, wd = x.to(device), wt.to(device)
+    got = ttn.depthwise(xd, ttn.depthwise_pack_weights(wd), None, 1, 1, silu=True)
+    acc = xd.float() * wd.float().reshape(1, 8, 1, 1, 16) + 0.0  # 0 + x*w: a -0 product sums to +0
+    want = ttn.silu(acc).half()
+    bad = got.view(torch.int16) != want.view(torch.int16)
+    assert not bad.any(), (int(bad.sum()), acc[bad][:4].tolist(), got[bad][:4].tolist(), want[bad][:4].tolist())
