@@ -235,6 +235,20 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
                                   int64_t co, int32_t kernel, int32_t stride, uint32_t flags, void* out,
                                   int64_t out_batch_stride, ttn_stream stream);
 
+/* The convolution above with a residual added after its epilogue, as the
+ * reference's residual C2f bottleneck does (blocked_c2f.py:20-24: y.append(y[-1] +
+ * value), value the cv2 conv's fp16 output): out = fp16(float(residual) +
+ * float(y)) with y the fp16 result of ttn_conv2d_nc1hwc0_f16, bit-identical to the
+ * conv followed by the separate fp16 add.  residual: NC1HWC0 [batch, co/16, oh,
+ * ow, 16], 16-byte aligned, image i at residual + i*residual_batch_stride (a
+ * multiple of 8); it may be `out` itself (same pointer and batch stride), any other
+ * overlap is undefined.  NC1HWC0 output only (TTN_CONV_NCHW is rejected). */
+ttn_status ttn_conv2d_residual_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int64_t h, int64_t w,
+                                           int64_t x_batch_stride, const void* packed_weights, const void* bias,
+                                           int64_t co, int32_t kernel, int32_t stride, uint32_t flags,
+                                           const void* residual, int64_t residual_batch_stride, void* out,
+                                           int64_t out_batch_stride, ttn_stream stream);
+
 /* Depthwise 2-D convolution (one filter per channel) with the same fused epilogue:
  * acc = sum over (ky, kx) in that order of x * w (FP32, each product and sum rounded),
  * + bias, then silu with TTN_CONV_SILU, one rounding to fp16.  x: NC1HWC0 fp16 [batch,

@@ -98,3 +98,81 @@ def test_conv_rejects_unsupported(device):
         ttn.conv2d(x, packed, None, 64, 5, 1)
     with pytest.raises(TtnError, match="co % 16"):
         ttn.conv2d(x, torch.zeros(2, 1, 64, 16, dtype=torch.float16, device=device), None, 40, 1, 1)
+
+
+# ---- residual epilogue and the C2f region (blocked_c2f.py:20-24) ----
+
+@pytest.mark.parametrize("b,c,h,w", [(2, 128, 40, 40), (1, 32, 37, 23), (3, 64, 20, 20)])
+def test_conv_residual_equals_conv_then_add(device, b, c, h, w):
+    """The residual epilogue gives fp16(res + y) with y the plain conv's fp16 output:
+    bit-identical to the conv followed by the separate fp16 add (the reference's
+    y[-1] + value), also when the residual is the output buffer itself."""
+    import thintnpu_b200 as ttn
+    x, wt, bs = _case(b, c, c, h, w, 3, seed=c + h)
+    g = torch.Generator().manual_seed(7)
+    res = torch.randn(b, c // 16, h, w, 16, generator=g).half().to(device)
+    xd, packed, bd = oops.pack_padded(x).to(device), ttn.conv2d_pack_weights(wt.to(device)), bs.to(device)
+    plain = ttn.conv2d(xd, packed, bd, c, 3)
+    want = ttn.add(res, plain)
+    fused = ttn.conv2d(xd, packed, bd, c, 3, residual=res)
+    inplace = res.clone()
+    ttn.conv2d(xd, packed, bd, c, 3, out=inplace, residual=inplace)
+    torch.cuda.synchronize()
+    assert ttn.ops.conv2d_fault() == 0
+    assert torch.equal(fused.view(torch.int16), want.view(torch.int16))
+    assert torch.equal(inplace.view(torch.int16), want.view(torch.int16))
+    # and the add itself against the CPU rule, fp16(float(res) + float(y))
+    cpu = (res.cpu().float() + plain.cpu().float()).half()
+    assert torch.equal(fused.cpu().view(torch.int16), cpu.view(torch.int16))
+
+
+def test_conv_residual_rejects_nchw(device):
+    import thintnpu_b200 as ttn
+    x = torch.zeros(1, 2, 8, 8, 16, dtype=torch.float16, device=device)
+    packed = ttn.conv2d_pack_weights(torch.zeros(32, 32, 1, 1, dtype=torch.float16, device=device))
+    with pytest.raises(Exception, match="NC1HWC0"):
+        ttn.conv2d(x, packed, None, 32, 1, nchw=True, residual=torch.zeros(1, 32, 8, 8, dtype=torch.float16,
+                                                                          device=device))
+
+
+def _c2f_weights(c_in, c, n, c_out, seed):
+    g = torch.Generator().manual_seed(seed)
+
+    def conv(co, ci, k):
+        return ((torch.randn(co, ci, k, k, generator=g) * (1.0 / (ci * k * k) ** 0.5)).half(),
+                (torch.randn(co, generator=g) * 0.1).half())
+    return conv(2 * c, c_in, 1), [(conv(c, c, 3), conv(c, c, 3)) for _ in range(n)], conv(c_out, (2 + n) * c, 1)
+
+
+@pytest.mark.parametrize("b,c_in,c,n,c_out,hw", [(2, 256, 128, 2, 256, 40), (1, 64, 32, 1, 64, 80)])
+def test_c2f_region_equals_reference_op_sequence(device, b, c_in, c, n, c_out, hw):
+    """model.6's region (blocked_c2f.py:20-24; 256 -> 256 at 40x40, two bottlenecks) and
+    a smaller one: the fused region against the same op sequence run op by op on the
+    GPU (pack, conv, chunk, conv, conv, add, cat, conv, unpack), bit for bit, and
+    against the CPU FP32 chain within fp16 accumulation noise."""
+    import thintnpu_b200 as ttn
+    from thintnpu_b200.yolo import C2fRegion
+    cv1, m, cv2 = _c2f_weights(c_in, c, n, c_out, seed=c_in + n)
+    dev = lambda wb: (wb[0].to(device), wb[1].to(device))
+    region = C2fRegion(dev(cv1), [(dev(a), dev(bb)) for a, bb in m], dev(cv2))
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(b, c_in, hw, hw, generator=g).half()
+    got = region(x.to(device))
+    # op by op on the GPU, as blocked_forward does
+    conv = lambda t, wb, k, nchw=False: ttn.conv2d(t, ttn.conv2d_pack_weights(wb[0].to(device)),
+                                                    wb[1].to(device), wb[0].shape[0], k, nchw=nchw)
+    y = list(conv(ttn.pack(x.to(device)), cv1, 1).chunk(2, 1))
+    for a, bb in m:
+        y.append(ttn.add(y[-1].contiguous(), conv(conv(y[-1].contiguous(), a, 3), bb, 3)))
+    want = ttn.unpack(conv(torch.cat([t.contiguous() for t in y], 1), cv2, 1))
+    torch.cuda.synchronize()
+    assert ttn.ops.conv2d_fault() == 0
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    # the CPU chain (FP32 convs, one fp16 rounding each, fp16 adds)
+    ccv = lambda t, wb: oops.conv2d(oops.pack_padded(t), wb[0], wb[1], 1, True)
+    ys = list(ccv(x, cv1).chunk(2, 1))
+    for a, bb in m:
+        ys.append((ys[-1].float() + ccv(ccv(ys[-1], a), bb).float()).half())
+    cpu = ccv(torch.cat(ys, 1), cv2).float()
+    diff = (got.cpu().float() - cpu).norm() / cpu.norm()
+    assert diff < 2e-3, float(diff)

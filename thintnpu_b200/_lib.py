@@ -31,7 +31,8 @@ EXPORTS = (
     "ttn_copy", "ttn_cat", "ttn_nc1hwc0_to_nchw_f16", "ttn_nchw_to_nc1hwc0_f16",
     "ttn_upsample2x", "ttn_upsample2x_nc1hwc0_f16", "ttn_maxpool", "ttn_sppf_f16",
     "ttn_softmax", "ttn_dfl_decode_f16", "ttn_attention_f16", "ttn_attention_fault_f16",
-    "ttn_conv2d_nc1hwc0_f16", "ttn_conv2d_pack_weights_f16", "ttn_conv2d_fault_f16", "ttn_depthwise_nc1hwc0_f16",
+    "ttn_conv2d_nc1hwc0_f16", "ttn_conv2d_residual_nc1hwc0_f16", "ttn_conv2d_pack_weights_f16",
+    "ttn_conv2d_fault_f16", "ttn_depthwise_nc1hwc0_f16",
     "ttn_select_workspace_size", "ttn_select_f16", "ttn_select_f16_static",
 )
 
@@ -99,6 +100,8 @@ _SIGNATURES = {
     "ttn_attention_fault_f16": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "ttn_conv2d_nc1hwc0_f16": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32, _I32,
                                               ctypes.c_uint32, _P, _I64, _P]),
+    "ttn_conv2d_residual_nc1hwc0_f16": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32, _I32,
+                                                       ctypes.c_uint32, _P, _I64, _P, _I64, _P]),
     "ttn_conv2d_pack_weights_f16": (ctypes.c_int, [_P, _I64, _I64, _I32, _P, _P]),
     "ttn_conv2d_fault_f16": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "ttn_depthwise_nc1hwc0_f16": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I32, _I32,

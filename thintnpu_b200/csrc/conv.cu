@@ -53,8 +53,10 @@ __device__ uint32_t g_conv_fault;
 
 struct ConvArgs {
   const uint16_t* bias;  // fp16 [co] or null
+  const uint16_t* res;   // NC1HWC0 residual of the output's shape, or null
   uint16_t* out;
   int64_t out_bs;        // elements between images of the output
+  int64_t res_bs;        // elements between images of the residual
   int c1, oh, ow, co, kernel, stride, pad;
   int wt, ht;            // output tile: wt x ht pixels, wt * ht = 128
   int tiles_w, tiles_h, co_tiles, tile_n;
@@ -73,6 +75,7 @@ struct ConvMaps {
 };
 
 
+template <bool kResidual>
 __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __grid_constant__ ConvMaps maps) {
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[2 * kConvMaxStages + 4];  // full[s], empty[s], acc_full[2], acc_empty[2]
@@ -250,8 +253,19 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
 #pragma unroll
           for (int blk = 0; blk < 2; ++blk) {
             if (co0 + 16 * blk >= a.co) break;
-            uint4* o = reinterpret_cast<uint4*>(
-                out + ((((int64_t)(co0 / 16 + blk) * a.oh + oh) * a.ow + ow) << 4));
+            const int64_t at = (((int64_t)(co0 / 16 + blk) * a.oh + oh) * a.ow + ow) << 4;
+            if (kResidual) {  // the reference's separate fp16 add: fp16(float(res) + float(y))
+              const uint4* rp = reinterpret_cast<const uint4*>(a.res + img * a.res_bs + at);
+              const uint4 q0 = rp[0], q1 = rp[1];
+              const uint32_t rv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float2 y2 = __half22float2(bits_h2(packed[8 * blk + e]));
+                const float2 r2 = __half22float2(bits_h2(rv[e]));
+                packed[8 * blk + e] = h2_bits(__floats2half2_rn(__fadd_rn(r2.x, y2.x), __fadd_rn(r2.y, y2.y)));
+              }
+            }
+            uint4* o = reinterpret_cast<uint4*>(out + at);
             o[0] = make_uint4(packed[8 * blk], packed[8 * blk + 1], packed[8 * blk + 2], packed[8 * blk + 3]);
             o[1] = make_uint4(packed[8 * blk + 4], packed[8 * blk + 5], packed[8 * blk + 6], packed[8 * blk + 7]);
           }
@@ -301,13 +315,12 @@ int gcd_int(int x, int y) {
 
 using namespace ttn;
 
-extern "C" {
+namespace {
 
-ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int64_t h, int64_t w,
-                                  int64_t x_batch_stride, const void* packed_weights, const void* bias,
-                                  int64_t co, int32_t kernel, int32_t stride, uint32_t flags, void* out,
-                                  int64_t out_batch_stride, ttn_stream stream) {
-  const char* name = "ttn_conv2d_nc1hwc0_f16";
+ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c1, int64_t h, int64_t w,
+                       int64_t x_batch_stride, const void* packed_weights, const void* bias, int64_t co,
+                       int32_t kernel, int32_t stride, uint32_t flags, const void* residual,
+                       int64_t residual_batch_stride, void* out, int64_t out_batch_stride, ttn_stream stream) {
   if (flags & ~(TTN_CONV_SILU | TTN_CONV_NCHW)) return fail(TTN_INVALID_ARG, "%s: unknown flags %u", name, flags);
   if (batch < 0 || c1 <= 0 || h <= 0 || w <= 0 || co <= 0)
     return fail(TTN_INVALID_ARG, "%s: sizes must be positive (batch >= 0)", name);
@@ -330,13 +343,20 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
     return fail(TTN_INVALID_ARG, "%s: output images overlap", name);
   if (c1 > 65535 || h > 65535 || w > 65535 || co > 65536 || batch > INT32_MAX)
     return fail(TTN_UNSUPPORTED, "%s: shape beyond the supported range", name);
+  if (residual) {
+    if (nchw) return fail(TTN_UNSUPPORTED, "%s: the residual needs NC1HWC0 output", name);
+    if (((uintptr_t)residual & 15u) || residual_batch_stride % 8)
+      return fail(TTN_INVALID_ARG, "%s: 16-byte aligned residual, batch stride a multiple of 8", name);
+  }
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return fail(TTN_CUDA_ERROR, "%s: cuTensorMapEncodeTiled is not available", name);
 
   ConvArgs a;
   a.bias = (const uint16_t*)bias;
+  a.res = (const uint16_t*)residual;
   a.out = (uint16_t*)out;
   a.out_bs = out_batch_stride;
+  a.res_bs = batch > 1 ? residual_batch_stride : 0;
   a.c1 = (int)c1, a.oh = (int)oh, a.ow = (int)ow, a.co = (int)co;
   a.kernel = kernel, a.stride = stride, a.pad = pad;
   // halo tiles are 8 pixels wide; where the plain path gets 16-pixel-wide tiles sharing their weight
@@ -396,16 +416,43 @@ ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int6
       return fail(TTN_UNSUPPORTED, "%s: weight tensor map: cuTensorMapEncodeTiled %d", name, (int)r);
   }
   const size_t stage = a.stage_bytes;
+  const void* kernel_fn = residual ? (const void*)conv_tc<true> : (const void*)conv_tc<false>;
   cudaFuncAttributes attr;
-  TTN_TRY(cuda_check(cudaFuncGetAttributes(&attr, (const void*)conv_tc), "cudaFuncGetAttributes"));
+  TTN_TRY(cuda_check(cudaFuncGetAttributes(&attr, kernel_fn), "cudaFuncGetAttributes"));
   const int64_t budget = (int64_t)max_dynamic_smem() - (int64_t)attr.sharedSizeBytes - 1024;  // 1 KB: alignment
   a.stages = (int)(budget / (int64_t)stage < kConvMaxStages ? budget / (int64_t)stage : kConvMaxStages);
   if (a.stages < 2) return fail(TTN_UNSUPPORTED, "%s: a ring stage of %zu bytes does not fit twice", name, stage);
   const size_t smem = stage * a.stages + 1024;
-  TTN_TRY(ensure_dynamic_smem((const void*)conv_tc, (int)smem));
+  TTN_TRY(ensure_dynamic_smem(kernel_fn, (int)smem));
   const int64_t grid = a.tiles < sm_count() ? a.tiles : sm_count();
-  conv_tc<<<(unsigned)grid, kConvThreads, smem, (cudaStream_t)stream>>>(a, maps);
+  if (residual)
+    conv_tc<true><<<(unsigned)grid, kConvThreads, smem, (cudaStream_t)stream>>>(a, maps);
+  else
+    conv_tc<false><<<(unsigned)grid, kConvThreads, smem, (cudaStream_t)stream>>>(a, maps);
   return launch_check(name);
+}
+
+}  // namespace
+
+extern "C" {
+
+ttn_status ttn_conv2d_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int64_t h, int64_t w,
+                                  int64_t x_batch_stride, const void* packed_weights, const void* bias,
+                                  int64_t co, int32_t kernel, int32_t stride, uint32_t flags, void* out,
+                                  int64_t out_batch_stride, ttn_stream stream) {
+  return conv_launch("ttn_conv2d_nc1hwc0_f16", x, batch, c1, h, w, x_batch_stride, packed_weights, bias, co,
+                     kernel, stride, flags, nullptr, 0, out, out_batch_stride, stream);
+}
+
+ttn_status ttn_conv2d_residual_nc1hwc0_f16(const void* x, int64_t batch, int64_t c1, int64_t h, int64_t w,
+                                           int64_t x_batch_stride, const void* packed_weights, const void* bias,
+                                           int64_t co, int32_t kernel, int32_t stride, uint32_t flags,
+                                           const void* residual, int64_t residual_batch_stride, void* out,
+                                           int64_t out_batch_stride, ttn_stream stream) {
+  const char* name = "ttn_conv2d_residual_nc1hwc0_f16";
+  if (!residual) return fail(TTN_INVALID_ARG, "%s: null residual", name);
+  return conv_launch(name, x, batch, c1, h, w, x_batch_stride, packed_weights, bias, co, kernel, stride, flags,
+                     residual, residual_batch_stride, out, out_batch_stride, stream);
 }
 
 ttn_status ttn_conv2d_pack_weights_f16(const void* weights, int64_t co, int64_t ci, int32_t kernel, void* packed,

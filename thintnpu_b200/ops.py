@@ -408,12 +408,15 @@ def conv2d_pack_weights(w: torch.Tensor) -> torch.Tensor:
 
 def conv2d(x: torch.Tensor, packed: torch.Tensor, bias: Optional[torch.Tensor], co: int, kernel: int,
            stride: int = 1, silu: bool = True, nchw: bool = False,
-           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+           out: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """The reference's fused convolution (thin_native_flow::conv, conv_flow.cpp:594-646) on
     the tensor cores: x NC1HWC0 fp16 [B, C1, H, W, 16] (images may be strided), packed
     weights from ``conv2d_pack_weights``, bias fp16 [co] or None; returns (or fills)
     NC1HWC0 [B, co/16, OH, OW, 16], or NCHW [B, co, OH, OW] with ``nchw``.  ``out`` may
-    be a batch-strided view, e.g. a channel slice of a concat buffer."""
+    be a batch-strided view, e.g. a channel slice of a concat buffer.  ``residual``
+    (NC1HWC0, the output's shape, dense images; may be ``out`` itself) is added after
+    the epilogue as the reference's residual bottleneck does (blocked_c2f.py:20-24):
+    fp16(residual + y), bit-identical to the conv followed by the fp16 add."""
     _cuda(x, "conv2d")
     _require(x.dtype == torch.float16 and x.dim() == 5 and x.size(4) == 16 and x[0].is_contiguous(),
              "conv2d: x must be fp16 NC1HWC0 [B, C1, H, W, 16] with dense images")
@@ -432,9 +435,19 @@ def conv2d(x: torch.Tensor, packed: torch.Tensor, bias: Optional[torch.Tensor], 
     _require(tuple(out.shape) == shape and out.dtype == torch.float16 and out[0].is_contiguous(),
              f"conv2d: out must be fp16 {shape} with dense images")
     flags = (_lib.CONV_SILU if silu else 0) | (_lib.CONV_NCHW if nchw else 0)
-    call("ttn_conv2d_nc1hwc0_f16", x.data_ptr(), b, c1, h, w, x.stride(0) if b > 1 else c1 * h * w * 16,
-         packed.data_ptr(), None if bias is None else bias.data_ptr(), co, kernel, stride, flags, out.data_ptr(),
-         out.stride(0) if b > 1 else out[0].numel(), stream())
+    x_bs, out_bs = x.stride(0) if b > 1 else c1 * h * w * 16, out.stride(0) if b > 1 else out[0].numel()
+    bias_ptr = None if bias is None else bias.data_ptr()
+    if residual is None:
+        call("ttn_conv2d_nc1hwc0_f16", x.data_ptr(), b, c1, h, w, x_bs, packed.data_ptr(), bias_ptr, co, kernel,
+             stride, flags, out.data_ptr(), out_bs, stream())
+        return out
+    _cuda(residual, "conv2d")
+    _require(not nchw, "conv2d: the residual needs NC1HWC0 output")
+    _require(tuple(residual.shape) == shape and residual.dtype == torch.float16 and residual[0].is_contiguous(),
+             f"conv2d: residual must be fp16 {shape} with dense images")
+    call("ttn_conv2d_residual_nc1hwc0_f16", x.data_ptr(), b, c1, h, w, x_bs, packed.data_ptr(), bias_ptr, co,
+         kernel, stride, flags, residual.data_ptr(), residual.stride(0) if b > 1 else residual[0].numel(),
+         out.data_ptr(), out_bs, stream())
     return out
 
 

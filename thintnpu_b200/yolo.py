@@ -431,3 +431,60 @@ class OpPass:
         """Kernels one pass launches: one per step, two for the decode (the box
         reduction and the class-row sigmoid, on forked branches)."""
         return sum(2 if step.op == "decode" else 1 for step in self.steps)
+
+
+class C2fRegion:
+    """The reference's blocked C2f region (BlockedC2f, blocked_c2f.py:13-24 and
+    :83-88; there pinned to YOLOv8s model.6, 256 -> 256 channels at 40x40 with two
+    residual bottlenecks) on the tensor cores, with no separate add, cat or unpack pass:
+
+    * cv1 (1x1, c_in -> 2c) writes straight into the concat buffer, whose first two
+      c-channel blocks are ``chunk(2, 1)``;
+    * bottleneck i runs cv1 (3x3) into a scratch tensor and cv2 (3x3) with the
+      residual ``y[-1]`` fused into its epilogue (``y.append(y[-1] + value)``),
+      writing its own slice of the concat buffer;
+    * cv2 (1x1, (2 + n) c -> c_out) reads the whole buffer and writes NCHW (the
+      reference's ``unpack``).
+
+    Every conv is conv + bias + SiLU in FP32 with one fp16 rounding, and the residual
+    is fp16(y[-1] + value), so the region equals the reference's op sequence on the
+    same weights.  Each conv is given as (OIHW fp16 weight, fp16 bias) on the GPU;
+    ``c`` and ``c_out`` must be multiples of 16."""
+
+    def __init__(self, cv1, bottlenecks, cv2, shortcut: bool = True):
+        w1, b1 = cv1
+        wo, bo = cv2
+        _check = ops._require
+        _check(w1.dim() == 4 and w1.shape[2:] == (1, 1) and w1.shape[0] % 32 == 0,
+               "C2fRegion: cv1 must be 1x1 with 2c outputs, c a multiple of 16")
+        self.c_in, self.c = int(w1.shape[1]), int(w1.shape[0]) // 2
+        self.n = len(bottlenecks)
+        _check(wo.dim() == 4 and wo.shape[2:] == (1, 1) and wo.shape[1] == (2 + self.n) * self.c
+               and wo.shape[0] % 16 == 0, "C2fRegion: cv2 must be 1x1 from (2 + n) c channels, c_out % 16 == 0")
+        self.c_out = int(wo.shape[0])
+        for wa, _, wb, _ in ((a[0], a[1], b[0], b[1]) for a, b in bottlenecks):
+            _check(tuple(wa.shape) == (self.c, self.c, 3, 3) and tuple(wb.shape) == (self.c, self.c, 3, 3),
+                   "C2fRegion: bottleneck convs must be 3x3 c -> c")
+        self.shortcut = shortcut
+        self.cv1 = (ops.conv2d_pack_weights(w1), b1)
+        self.m = [(ops.conv2d_pack_weights(a[0]), a[1], ops.conv2d_pack_weights(b[0]), b[1])
+                  for a, b in bottlenecks]
+        self.cv2 = (ops.conv2d_pack_weights(wo), bo)
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x: NCHW fp16 [B, c_in, H, W] on the GPU -> NCHW fp16 [B, c_out, H, W]."""
+        ops._require(x.dim() == 4 and x.size(1) == self.c_in and x.dtype == torch.float16,
+                     f"C2fRegion: expected fp16 NCHW input with {self.c_in} channels")
+        b, _, h, w = x.shape
+        cb = self.c // C0
+        xb = ops.pack(x)
+        cat = torch.empty((b, (2 + self.n) * cb, h, w, C0), dtype=torch.float16, device=x.device)
+        ops.conv2d(xb, self.cv1[0], self.cv1[1], 2 * self.c, 1, out=cat[:, : 2 * cb])
+        scratch = torch.empty((b, cb, h, w, C0), dtype=torch.float16, device=x.device)
+        prev = cat[:, cb: 2 * cb]
+        for i, (pa, ba, pb, bb) in enumerate(self.m):
+            ops.conv2d(prev, pa, ba, self.c, 3, out=scratch)
+            dst = cat[:, (2 + i) * cb: (3 + i) * cb]
+            ops.conv2d(scratch, pb, bb, self.c, 3, out=dst, residual=prev if self.shortcut else None)
+            prev = dst
+        return ops.conv2d(cat, self.cv2[0], self.cv2[1], self.c_out, 1, nchw=True, out=out)
