@@ -43,8 +43,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-variants", action="store_true")
-    p.add_argument("--sweep", choices=("silu", "sigmoid"),
-                   help="print fp16 unary bandwidth by tensor size (one GPU) and exit")
+    p.add_argument("--sweep", choices=("silu", "sigmoid", "c2f"),
+                   help="print fp16 unary bandwidth by tensor size, or the C2f region fused vs op by op "
+                        "(one GPU), and exit")
     p.add_argument("--config", type=int, default=4, choices=(1, 2, 3, 4, 5, 6, 7, 8),
                    help="BASELINE config; 4 (the op pass) is the headline workload; 6 = fused C2PSA attention; 7 = YOLOv8s conv pass; 8 = YOLO11s depthwise convs")
     return p.parse_args()
@@ -191,7 +192,10 @@ def main():
     args = parse()
     if args.sweep:
         from thintnpu_b200 import perf
-        print(json.dumps({"sweep": args.sweep, "unit": "us / GB/s", **perf.unary_sweep(args.sweep)}))
+        if args.sweep == "c2f":
+            print(json.dumps({"sweep": "c2f", "unit": "us", **perf.c2f_sweep()}))
+        else:
+            print(json.dumps({"sweep": args.sweep, "unit": "us / GB/s", **perf.unary_sweep(args.sweep)}))
         return
     if args.config != 4:
         from thintnpu_b200 import perf

@@ -311,6 +311,49 @@ def unary_sweep(op: str = "silu", sizes_m=(13, 26, 52, 105, 210, 420, 839), reps
     return out
 
 
+def c2f_sweep(batch: int = 32, reps: int = 20) -> dict:
+    """YOLOv8s model.6's C2f region (256 -> 256 channels at 40x40, two residual
+    bottlenecks; blocked_c2f.py:13-24) fused (``yolo.C2fRegion``) against the same
+    op sequence run op by op (pack, conv, chunk, conv, conv, add, cat, conv, unpack),
+    seeded random weights; median of ``reps`` CUDA-event timings after 3 warm-ups."""
+    import thintnpu_b200
+    from .yolo import C2fRegion
+    thintnpu_b200.load()
+    device = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator().manual_seed(1)
+
+    def conv(co, ci, k):
+        return ((torch.randn(co, ci, k, k, generator=g) * (1.0 / (ci * k * k) ** 0.5)).half().to(device),
+                (torch.randn(co, generator=g) * 0.1).half().to(device))
+    cv1, m, cv2 = conv(256, 256, 1), [(conv(128, 128, 3), conv(128, 128, 3)) for _ in range(2)], conv(256, 512, 1)
+    region = C2fRegion(cv1, m, cv2)
+    x = torch.randn(batch, 256, 40, 40, generator=g).half().to(device)
+    packed = {id(w): ops.conv2d_pack_weights(w) for w in [cv1[0], cv2[0]] + [t[0] for pair in m for t in pair]}
+
+    def op_by_op():
+        c = lambda t, wb, k, nchw=False: ops.conv2d(t, packed[id(wb[0])], wb[1], wb[0].shape[0], k, nchw=nchw)
+        y = list(c(ops.pack(x), cv1, 1).chunk(2, 1))
+        for a, b in m:
+            prev = y[-1].contiguous()
+            y.append(ops.add(prev, c(c(prev, a, 3), b, 3)))
+        return ops.unpack(c(ops.cat([t.contiguous() for t in y], 1), cv2, 1))
+
+    out = {"batch": batch}
+    for name, fn in (("fused_region", lambda: region(x)), ("op_by_op", op_by_op)):
+        for _ in range(3):
+            fn()
+        times = []
+        for _ in range(reps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize(device)
+            times.append(s.elapsed_time(e))
+        out[name] = round(sorted(times)[len(times) // 2] * 1000, 1)
+    return out
+
+
 def run_config(args):
     import torch.distributed as dist
     cfg = CONFIGS[args.config]()
