@@ -71,3 +71,30 @@ def test_gpu_entry_points_refuse_cpu_tensors():
     q = torch.zeros(1, 1, 32, 64, dtype=torch.float16)
     with pytest.raises((RuntimeError, ValueError, TypeError)):
         ttn.attention(q, q, torch.zeros(1, 1, 64, 64, dtype=torch.float16), 1.0)
+
+
+def _c2f_parts(c_in=64, c=32, n=1, c_out=64, k_cv1=1, k_m=3, cv2_in=None):
+    conv = lambda co, ci, k: (torch.zeros(co, ci, k, k, dtype=torch.float16), torch.zeros(co, dtype=torch.float16))
+    return (conv(2 * c, c_in, k_cv1), [(conv(c, c, k_m), conv(c, c, k_m)) for _ in range(n)],
+            conv(c_out, (2 + n) * c if cv2_in is None else cv2_in, 1))
+
+
+@pytest.mark.parametrize("kwargs,match", [
+    (dict(k_cv1=3), "cv1 must be 1x1"),
+    (dict(c=24), "cv1 must be 1x1 with 2c outputs"),
+    (dict(cv2_in=64), "cv2 must be 1x1 from"),
+    (dict(c_out=40), "c_out % 16"),
+    (dict(k_m=1), "bottleneck convs must be 3x3"),
+])
+def test_c2f_region_checks_its_weights(kwargs, match):
+    """The region (blocked_c2f.py:28-68 checks the module's exact shapes) refuses
+    malformed weights before any GPU work."""
+    from thintnpu_b200.yolo import C2fRegion
+    with pytest.raises(RuntimeError, match=match):
+        C2fRegion(*_c2f_parts(**kwargs))
+
+
+def test_c2f_region_needs_cuda_weights():
+    from thintnpu_b200.yolo import C2fRegion
+    with pytest.raises(RuntimeError, match="CUDA"):
+        C2fRegion(*_c2f_parts())
