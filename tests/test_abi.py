@@ -87,3 +87,29 @@ def test_workspace_size_is_positive_and_monotone():
     assert 0 < agnostic <= small < big
     assert small % 256 == 0
     assert lib.ttn_select_workspace_size(1, 8400, 80, 0, 0) >= 8400 * 4
+
+
+def test_conv_and_depthwise_argument_errors_need_no_gpu():
+    """The conv entry points check flags, shapes, alignment and the residual's form
+    before any CUDA call (fake, aligned device addresses are never dereferenced)."""
+    from thintnpu_b200 import _lib
+    lib = _lib.lib()
+    X, W, O, R = 1 << 20, 2 << 20, 3 << 20, 4 << 20  # 16-byte aligned fake addresses
+    conv = lambda flags=1, co=64, k=3, s=1, x=X: lib.ttn_conv2d_nc1hwc0_f16(
+        x, 1, 4, 8, 8, 4 * 8 * 8 * 16, W, None, co, k, s, flags, O, co * 64, None)
+    assert conv(flags=8) == 1 and b"unknown flags" in lib.ttn_last_error()
+    assert conv(k=5) == 2 and b"3x3" in lib.ttn_last_error()
+    assert conv(co=40) == 2 and b"co % 16" in lib.ttn_last_error()
+    assert conv(x=X + 2) == 1 and b"aligned" in lib.ttn_last_error()
+    res = lambda flags=1, r=R, rbs=64 * 64: lib.ttn_conv2d_residual_nc1hwc0_f16(
+        X, 1, 4, 8, 8, 4 * 8 * 8 * 16, W, None, 64, 3, 1, flags, r, rbs, O, 64 * 64, None)
+    assert res(r=None) == 1 and b"null residual" in lib.ttn_last_error()
+    assert res(flags=3) == 2 and b"NC1HWC0" in lib.ttn_last_error()
+    assert res(r=R + 8) == 1 and b"residual" in lib.ttn_last_error()
+    assert res(rbs=12) == 1 and b"residual" in lib.ttn_last_error()
+    dw = lambda k=3, s=1, flags=1, x=X: lib.ttn_depthwise_nc1hwc0_f16(
+        x, 1, 4, 8, 8, 4 * 8 * 8 * 16, W, None, k, s, flags, O, 4 * 8 * 8 * 16, None)
+    assert dw(k=4) == 2 and b"odd kernel" in lib.ttn_last_error()
+    assert dw(s=3) == 2
+    assert dw(flags=2) == 1 and b"unknown flags" in lib.ttn_last_error()
+    assert dw(x=X + 8) == 1 and b"aligned" in lib.ttn_last_error()
