@@ -226,14 +226,22 @@ __global__ void __launch_bounds__(kThreads) unary_f16_dense(const uint16_t* x, u
   if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = unary_h<K>(xt[threadIdx.x]);
 }
 
-// Dense fp16, 16-byte aligned, table core: each block (one per SM, 1024
-// threads) copies the 128 KB table of the op into shared memory, then maps
-// 16-byte vectors on a grid-stride loop, four independent vectors per thread in
-// flight; the first four are requested before the table copy to overlap it.  One shared-memory read per element and no transcendental work: the
-// kernel is bound by HBM.  x may equal y.
-constexpr int kLutThreads = 1024;
+// Table core for dense fp16 and for two-level row families: one block per SM
+// (768 threads) copies the op's 128 KB table into shared memory, then maps
+// 16-byte vectors with one shared-memory read per element and no
+// transcendental work.  The loads go through a per-thread ring of kLutSlots
+// shared-memory slots filled by cp.async, so kLutSlots - 1 vectors per thread
+// (48 KB per SM) are always in flight while one is mapped; a thread only reads
+// back its own slots, so the ring needs no block barrier.  The table copy is
+// the first cp.async group and overlaps the first loads.  Vector g of the
+// launch is the thread's (g - first) / stride-th; with kRows its (row, column)
+// and the row's (i1, i2) come from multiply-high divisions, else it sits at
+// element 8 g.  Fewer than 2^31 vectors per launch; x may equal y.
+constexpr int kLutThreads = 768;
+constexpr int kLutSlots = 5;
 constexpr int kLutBytes = 65536 * 2;
-constexpr int64_t kLutMinVecs = (int64_t)4 << 20;  // below ~34M elements the table copy does not pay
+constexpr int kLutSmem = kLutBytes + kLutSlots * kLutThreads * 16;
+constexpr int64_t kLutMinVecs = (int64_t)1 << 21;  // below ~17M elements the table copy does not pay
 
 __device__ __forceinline__ uint32_t lut_word(const uint16_t* lut, uint32_t w) {
   return (uint32_t)lut[w & 0xffffu] | ((uint32_t)lut[w >> 16] << 16);
@@ -242,75 +250,74 @@ __device__ __forceinline__ uint4 lut_vec(const uint16_t* lut, uint4 v) {
   return make_uint4(lut_word(lut, v.x), lut_word(lut, v.y), lut_word(lut, v.z), lut_word(lut, v.w));
 }
 
-__global__ void __launch_bounds__(kLutThreads) unary_f16_lut(const uint16_t* table, const uint16_t* x,
-                                                             uint16_t* y, int64_t nvec, const uint16_t* xt,
-                                                             uint16_t* yt, int tail) {
-  extern __shared__ __align__(16) uint16_t lut[];
-  const uint4* xs = reinterpret_cast<const uint4*>(x);
-  uint4* ys = reinterpret_cast<uint4*>(y);
-  const int64_t stride = (int64_t)gridDim.x * kLutThreads;
-  int64_t i = (int64_t)blockIdx.x * kLutThreads + threadIdx.x;
-  uint4 cur[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) cur[k] = i + k * stride < nvec ? xs[i + k * stride] : make_uint4(0, 0, 0, 0);
+// Element offsets of x and y for vector g: dense (kRows false) or a row family
+// [n1][n2][vpr vectors] with element strides xs1/xs2 and ys1/ys2.
+struct LutRows {
+  int64_t xs1, xs2, ys1, ys2;
+  FastDiv vpr, n2;
+};
+
+template <bool kRows>
+__device__ __forceinline__ int64_t lut_offset(const LutRows& r, uint32_t g, bool of_y) {
+  if constexpr (!kRows) {
+    return (int64_t)g * 8;
+  } else {
+    const uint32_t row = r.vpr.div(g), col = g - row * r.vpr.d;
+    const uint32_t i1 = r.n2.div(row), i2 = row - i1 * r.n2.d;
+    return of_y ? (int64_t)i1 * r.ys1 + (int64_t)i2 * r.ys2 + (int64_t)col * 8
+                : (int64_t)i1 * r.xs1 + (int64_t)i2 * r.xs2 + (int64_t)col * 8;
+  }
+}
+
+template <bool kRows>
+__global__ void __launch_bounds__(kLutThreads, 1) unary_f16_lut(const uint16_t* table, const uint16_t* x,
+                                                                uint16_t* y, LutRows rows, uint32_t total,
+                                                                const uint16_t* xt, uint16_t* yt, int tail) {
+  extern __shared__ __align__(16) uint8_t lut_smem[];
+  uint16_t* lut = reinterpret_cast<uint16_t*>(lut_smem);
+  uint4* ring = reinterpret_cast<uint4*>(lut_smem + kLutBytes) + threadIdx.x;
+  const uint32_t stride = gridDim.x * kLutThreads;  // total < 2^31: g + kLutSlots * stride fits
+  const uint32_t first = blockIdx.x * kLutThreads + threadIdx.x;
   {
     const uint4* src = reinterpret_cast<const uint4*>(table);
     uint4* dst = reinterpret_cast<uint4*>(lut);
-    for (int t = threadIdx.x; t < kLutBytes / 16; t += kLutThreads) dst[t] = src[t];
+    for (int t = threadIdx.x; t < kLutBytes / 16; t += kLutThreads) cp_async16(dst + t, src + t);
+    cp_async_commit();
   }
-  __syncthreads();
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
-    if (i + k * stride < nvec) ys[i + k * stride] = lut_vec(lut, cur[k]);
-  for (i += 4 * stride; i + 3 * stride < nvec; i += 4 * stride) {
-    const uint4 v0 = xs[i], v1 = xs[i + stride], v2 = xs[i + 2 * stride], v3 = xs[i + 3 * stride];
-    ys[i] = lut_vec(lut, v0);
-    ys[i + stride] = lut_vec(lut, v1);
-    ys[i + 2 * stride] = lut_vec(lut, v2);
-    ys[i + 3 * stride] = lut_vec(lut, v3);
+  for (int k = 0; k < kLutSlots - 1; ++k) {
+    const uint32_t g = first + k * stride;
+    if (g < total) cp_async16(ring + k * kLutThreads, x + lut_offset<kRows>(rows, g, false));
+    cp_async_commit();
   }
-  for (; i < nvec; i += stride) ys[i] = lut_vec(lut, xs[i]);
+  cp_async_wait<kLutSlots - 1>();  // the table group has landed (for this thread's part)
+  __syncthreads();                 // ... and for every thread's part
+  int slot = 0;
+  for (uint32_t g = first; g < total; g += stride) {
+    const uint32_t ahead = g + (kLutSlots - 1) * stride;
+    const int refill = slot == 0 ? kLutSlots - 1 : slot - 1;  // the slot mapped last iteration
+    if (ahead < total) cp_async16(ring + refill * kLutThreads, x + lut_offset<kRows>(rows, ahead, false));
+    cp_async_commit();
+    cp_async_wait<kLutSlots - 1>();  // the group that filled `slot`
+    const uint4 v = ring[slot * kLutThreads];
+    *reinterpret_cast<uint4*>(y + lut_offset<kRows>(rows, g, true)) = lut_vec(lut, v);
+    slot = slot == kLutSlots - 1 ? 0 : slot + 1;
+  }
+  cp_async_wait<0>();
   if (blockIdx.x == 0 && (int)threadIdx.x < tail) yt[threadIdx.x] = lut[xt[threadIdx.x]];
 }
 
-// Table core over a two-level family of rows (see unary_rows2_f16): the flat
-// vector index g splits into (row, column) and row into (i1, i2) with
-// multiply-high divisions; four independent vectors per thread in flight.
-__global__ void __launch_bounds__(kLutThreads) unary_f16_lut2d(const uint16_t* table, const uint16_t* x,
-                                                               int64_t xs1, int64_t xs2, uint16_t* y,
-                                                               int64_t ys1, int64_t ys2, FastDiv vpr,
-                                                               FastDiv n2, uint32_t total) {
-  extern __shared__ __align__(16) uint16_t lut[];
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(table);
-    uint4* dst = reinterpret_cast<uint4*>(lut);
-    for (int t = threadIdx.x; t < kLutBytes / 16; t += kLutThreads) dst[t] = src[t];
-  }
-  __syncthreads();
-  auto locate = [&](uint32_t gi, int64_t& ox, int64_t& oy) {
-    const uint32_t row = vpr.div(gi), col = gi - row * vpr.d;
-    const uint32_t i1 = n2.div(row), i2 = row - i1 * n2.d;
-    ox = (int64_t)i1 * xs1 + (int64_t)i2 * xs2 + (int64_t)col * 8;
-    oy = (int64_t)i1 * ys1 + (int64_t)i2 * ys2 + (int64_t)col * 8;
-  };
-  const uint32_t stride = gridDim.x * kLutThreads;  // total < 2^31, so g + 3 * stride fits
-  uint32_t g = blockIdx.x * kLutThreads + threadIdx.x;
-  for (; g + 3 * stride < total; g += 4 * stride) {
-    int64_t ox[4], oy[4];
-    uint4 v[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      locate(g + k * stride, ox[k], oy[k]);
-      v[k] = *reinterpret_cast<const uint4*>(x + ox[k]);
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(y + oy[k]) = lut_vec(lut, v[k]);
-  }
-  for (; g < total; g += stride) {
-    int64_t ox, oy;
-    locate(g, ox, oy);
-    *reinterpret_cast<uint4*>(y + oy) = lut_vec(lut, *reinterpret_cast<const uint4*>(x + ox));
-  }
+// Launches the table kernel over `total` vectors (< 2^31) on the current device.
+template <bool kRows>
+ttn_status launch_lut(int kind, const uint16_t* x, uint16_t* y, const LutRows& rows, int64_t total,
+                      const uint16_t* xt, uint16_t* yt, int tail, cudaStream_t s, const char* name) {
+  const uint16_t* table = nullptr;
+  TTN_TRY(unary_table(kind, s, &table));
+  TTN_TRY(ensure_dynamic_smem((const void*)unary_f16_lut<kRows>, kLutSmem));
+  const int64_t want = (total + 4 * kLutThreads - 1) / (4 * kLutThreads);
+  const unsigned grid = (unsigned)(want < sm_count() ? (want < 1 ? 1 : want) : sm_count());
+  unary_f16_lut<kRows><<<grid, kLutThreads, kLutSmem, s>>>(table, x, y, rows, (uint32_t)total, xt, yt, tail);
+  return launch_check(name);
 }
 
 template <int K>
@@ -318,15 +325,8 @@ ttn_status rows2(const uint16_t* x, int64_t xs1, int64_t xs2, uint16_t* y, int64
                  int64_t n1, int64_t n2, int64_t ncols, cudaStream_t s) {
   const int64_t vpr = ncols / 8, total = n1 * n2 * vpr;
   if (total >= kLutMinVecs && total < ((int64_t)1 << 31)) {
-    const uint16_t* table = nullptr;
-    TTN_TRY(unary_table(K, s, &table));
-    TTN_TRY(ensure_dynamic_smem((const void*)unary_f16_lut2d, kLutBytes));
-    int64_t want = (total + 4 * kLutThreads - 1) / (4 * kLutThreads);
-    unsigned grid = (unsigned)(want < sm_count() ? want : sm_count());
-    unary_f16_lut2d<<<grid, kLutThreads, kLutBytes, s>>>(table, x, xs1, xs2, y, ys1, ys2,
-                                                         FastDiv((uint32_t)vpr), FastDiv((uint32_t)n2),
-                                                         (uint32_t)total);
-    return launch_check("unary_rows2_f16");
+    LutRows rows{xs1, xs2, ys1, ys2, FastDiv((uint32_t)vpr), FastDiv((uint32_t)n2)};
+    return launch_lut<true>(K, x, y, rows, total, nullptr, nullptr, 0, s, "unary_rows2_f16");
   }
   // arithmetic rows kernel; its queue holds 32-bit element offsets from y, so
   // each launch covers a slice of i1 whose y extent stays below 2^32
@@ -626,15 +626,10 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
       int64_t nvec = total_vec - v0 < chunk ? total_vec - v0 : chunk;
       bool last = v0 + chunk >= total_vec;
       if (nvec >= kLutMinVecs) {
-        const uint16_t* table = nullptr;
-        TTN_TRY(unary_table(K, s, &table));
-        TTN_TRY(ensure_dynamic_smem((const void*)unary_f16_lut, kLutBytes));
-        int64_t want = (nvec + 4 * kLutThreads - 1) / (4 * kLutThreads);
-        unsigned grid = (unsigned)(want < sm_count() ? want : sm_count());
-        unary_f16_lut<<<grid, kLutThreads, kLutBytes, s>>>(
-            table, (const uint16_t*)x->data + v0 * 8, (uint16_t*)y->data + v0 * 8, nvec,
-            (const uint16_t*)x->data + total_vec * 8, (uint16_t*)y->data + total_vec * 8,
-            last ? tail : 0);
+        const LutRows dense_rows{0, 0, 0, 0, FastDiv(1), FastDiv(1)};
+        TTN_TRY(launch_lut<false>(K, (const uint16_t*)x->data + v0 * 8, (uint16_t*)y->data + v0 * 8,
+                                  dense_rows, nvec, (const uint16_t*)x->data + total_vec * 8,
+                                  (uint16_t*)y->data + total_vec * 8, last ? tail : 0, s, name));
       } else {
         unsigned grid = resident_grid(unary_f16_dense<K>, kThreads, 0, nvec ? nvec : 1,
                                       (int64_t)kThreads * kVec);
