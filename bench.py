@@ -3,19 +3,30 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ttn|reference]
 
 One process per GPU (torchrun for N > 1).  Each rank owns a fixed shard of
-``--batch`` images (weak scaling: images are independent, nothing is
-exchanged on the data path; a tiny all-reduce only takes the max time).  A
-step is one CUDA-graph replay of the whole op pass over the rank's batch with
-all inputs resident in HBM (inputs are ~14 GB per step, far above the 126 MB
-L2, so no flush is needed).  ``e2e`` times the same pass through the public
-API with the inputs copied from pinned host memory and the decoded output read
-back every step.  ``--impl reference`` times the CPU-eager pass (the oracle)
-on the host cores instead.  Rank 0 prints one JSON line.
+``--batch`` images (weak scaling: images are independent, nothing is exchanged
+on the data path); the control plane -- barriers, the max over ranks of the
+elapsed time, and host heartbeats between steps -- runs on a gloo group, so no
+NCCL communicator is created.  A step is one CUDA-graph replay of the whole op
+pass over the rank's batch with every input resident in HBM (inputs are ~14 GB
+per step, far above the 126 MB L2, so no flush is needed).  The timed pass is
+the zero-copy plan (every concat filled by its producers, bit-identical to the
+plain pass, which is reported under ``variants``).
+
+Also reported: ``roofline`` (the SiLU kernel, the pass's dominant kernel),
+``sustained`` (the same pass for at least 2 s with its own clock record),
+``variants`` (plain pass; config 3 at B=64 and config 5 at N=512, split over the
+ranks), ``e2e`` (the pass through the public API with the inputs copied from
+pinned host memory and the decoded output read back every step, double
+buffered, beside the measured host-to-device copy peak) and, on rank 0 at N=1,
+``cpu_baseline`` (the CPU-eager pass, run in a child process with the same
+protocol as ``--impl reference``).  ``--impl reference`` times the CPU-eager
+pass (the oracle) on the host cores.  Rank 0 prints one JSON line.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -28,7 +39,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "non-conv op pass images/s at 640² fp16; achieved HBM GB/s vs ~8 TB/s peak"
-WORKLOAD = "yolov8s-640 non-conv op pass (BASELINE config 4): 57 SiLU, 6 residual adds, 12 C2f/neck concats, SPPF, 2 upsamples, Detect NCHW restore, DFL decode"
+WORKLOAD = ("yolov8s-640 non-conv op pass (BASELINE config 4): 57 SiLU, 6 residual adds, 12 C2f/neck concats, "
+            "SPPF, 2 upsamples, Detect NCHW restore, DFL decode")
+CPU_IMAGES_PER_STEP = 8
 
 
 def parse():
@@ -39,7 +52,11 @@ def parse():
     p.add_argument("--batch", type=int, default=256, help="images per GPU per step")
     p.add_argument("--imgsz", type=int, default=640)
     p.add_argument("--impl", choices=("ttn", "reference"), default="ttn")
-    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--cpu-threads", type=int, default=0, help="--impl reference: host threads (0 = all)")
+    p.add_argument("--cpu-seconds", type=float, default=0.0,
+                   help="--impl reference: keep sampling until this much CPU time has been timed")
+    p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--sustained-s", type=float, default=2.0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-variants", action="store_true")
@@ -47,69 +64,72 @@ def parse():
                    help="print fp16 unary bandwidth by tensor size, or the C2f region fused vs op by op "
                         "(one GPU), and exit")
     p.add_argument("--config", type=int, default=4, choices=(1, 2, 3, 4, 5, 6, 7, 8),
-                   help="BASELINE config; 4 (the op pass) is the headline workload; 6 = fused C2PSA attention; 7 = YOLOv8s conv pass; 8 = YOLO11s depthwise convs")
+                   help="BASELINE config; 4 (the op pass) is the headline workload; 6 = fused C2PSA attention; "
+                        "7 = YOLOv8s conv pass; 8 = YOLO11s depthwise convs")
     return p.parse_args()
 
 
-def peaks():
-    path = ROOT / "MEASURED_PEAKS.json"
-    if path.exists():
-        data = json.loads(path.read_text())
-        return float(data["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
-
-
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock, power and clock-event reasons of one GPU, polled through NVML
+    every `period_s` in a thread while a timed region runs (read-only queries)."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, torch_index: int, period_s: float = 0.01):
+        self.period = period_s
         self.rows = []
-        self.proc = None
+        self.handle = None
+        self.stop_flag = threading.Event()
         self.thread = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            try:  # the same physical GPU as torch's device index (orders can differ)
+                props = torch.cuda.get_device_properties(torch_index)
+                bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+                index = int(visible.split(",")[torch_index]) if visible else torch_index
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: report the absence
+            self.handle = None
+
+    def _poll(self):
+        n = self.nvml
+        while not self.stop_flag.is_set():
+            try:
+                self.rows.append((n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM),
+                                  n.nvmlDeviceGetCurrentClocksEventReasons(self.handle),
+                                  n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0))
+            except Exception:
+                pass
+            self.stop_flag.wait(self.period)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, FileNotFoundError):
-            self.proc = None
-            return
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
+        if self.handle is not None:
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+        return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
-
-    def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        if self.thread:
-            self.thread.join(timeout=2)
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+    def stop(self) -> dict:
+        if self.handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["NVML unavailable"], "samples": 0}
+        self.stop_flag.set()
+        self.thread.join(timeout=2)
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({name for r in self.rows for name, bit in self.REASONS.items() if r[1] & bit})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "sm_mhz_min": min(sm) if sm else None, "reasons": reasons, "samples": len(self.rows),
+                "power_w_max": max(r[2] for r in self.rows) if self.rows else None,
+                "source": f"NVML every {self.period * 1000:.0f} ms"}
 
 
 def cpu_model() -> str:
-    """The host CPU's model name (from /proc/cpuinfo), or "unknown"."""
     try:
         for line in open("/proc/cpuinfo"):
             if line.startswith("model name"):
@@ -119,106 +139,102 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def cpu_pass_rate(imgsz: int, budget_s: float = 12.0, one_thread_s: float = 5.0):
-    """CPU-eager op pass (the oracle) on the host cores: images/s over a bounded
-    sample with every core, plus a shorter sample on one thread."""
-    import torch
-    from oracle import yolo as oyolo
-    from thintnpu_b200 import yolo
-
-    plan = yolo.yolov8s_plan(imgsz)
-    batch = 2
-    inputs = yolo.synthetic_inputs(plan, batch, "cpu", seed=4)
-
-    def rate(threads: int, budget: float):
-        torch.set_num_threads(threads)
-        with torch.inference_mode():
-            oyolo.run_pass(plan, inputs)  # warm-up
-            done, start = 0, time.perf_counter()
-            while True:
-                oyolo.run_pass(plan, inputs)
-                done += batch
-                elapsed = time.perf_counter() - start
-                if elapsed >= budget:
-                    return done, elapsed
-
-    cores = os.cpu_count() or 1
-    done, elapsed = rate(cores, budget_s)
-    done1, elapsed1 = rate(1, one_thread_s)
-    torch.set_num_threads(cores)
-    return {"value": done / elapsed, "unit": "images/s", "cores": cores, "kind": "port",
-            "sample": f"{done} images ({batch} per pass) of the same {imgsz} op pass, PyTorch CPU eager, "
-                      f"{elapsed:.1f} s",
-            "one_thread": {"value": done1 / elapsed1, "unit": "images/s",
-                           "sample": f"{done1} images, {elapsed1:.1f} s"},
-            "cpu_model": cpu_model()}
-
-
 def run_reference(args):
-    """--impl reference: the CPU-eager pass on the host cores (rank 0 only)."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    """--impl reference: the CPU-eager op pass (oracle) on the host cores, rank 0
+    only.  A step is CPU_IMAGES_PER_STEP images; W warm-up steps, then at least K
+    timed steps (more while --cpu-seconds of timed CPU work is not reached);
+    value = images per step / median step time."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return
     import torch
     from oracle import yolo as oyolo
     from thintnpu_b200 import yolo
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    threads = args.cpu_threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
     plan = yolo.yolov8s_plan(args.imgsz)
-    batch = 2
+    batch = CPU_IMAGES_PER_STEP
     inputs = yolo.synthetic_inputs(plan, batch, "cpu", seed=4)
     times = []
     with torch.inference_mode():
-        for i in range(args.warmup + args.steps):
+        for _ in range(args.warmup):
+            oyolo.run_pass(plan, inputs)
+        while len(times) < args.steps or sum(times) < args.cpu_seconds:
             start = time.perf_counter()
             oyolo.run_pass(plan, inputs)
-            if i >= args.warmup:
-                times.append(time.perf_counter() - start)
-    total = sum(times)
-    value = batch * len(times) / total
+            times.append(time.perf_counter() - start)
+    med = statistics.median(times)
+    value = batch / med
+    sample = (f"{batch * len(times)} images: {len(times)} steps of {batch} images of the same {args.imgsz} op pass "
+              f"(PyTorch CPU eager, with its 12 concat copies), median step after {args.warmup} warm-ups, "
+              f"{sum(times):.1f} s timed")
     line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000 * total / len(times), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": 1000 * med, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic", "impl": "reference",
             "config": {"workload": WORKLOAD, "batch_per_step": batch, "imgsz": args.imgsz,
-                       "sample": "bounded CPU sample: 2 images per step"},
-            "cpu_baseline": {"value": value, "unit": "images/s", "cores": torch.get_num_threads(),
-                             "kind": "port",
-                             "sample": f"{batch * len(times)} images, PyTorch CPU eager op pass (oracle)"},
+                       "sample": f"bounded CPU sample: {batch} images per step"},
+            "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port",
+                             "sample": sample, "cpu_model": cpu_model()},
             "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(imgsz: int) -> dict:
+    """The reference arm's measurement, run in a child process on this host: all
+    host threads for at least 10 s of timed CPU work, plus a one-thread sample."""
+    def child(threads: int, seconds: float):
+        cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "11", "--warmup", "3",
+               "--imgsz", str(imgsz), "--cpu-threads", str(threads), "--cpu-seconds", str(seconds)]
+        env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+        done = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=600)
+        lines = [ln for ln in done.stdout.splitlines() if ln.startswith("{")]
+        if done.returncode or not lines:
+            raise RuntimeError(f"CPU baseline child failed: {done.stderr[-500:]}")
+        return json.loads(lines[-1])["cpu_baseline"]
+
+    every = child(os.cpu_count() or 1, 10.0)
+    one = child(1, 3.0)
+    every["one_thread"] = {"value": one["value"], "unit": "images/s", "sample": one["sample"]}
+    every["protocol"] = "child process of bench.py --impl reference: 3 warm-ups, median of >= 11 steps"
+    return every
 
 
 def main():
     args = parse()
     if args.sweep:
-        from thintnpu_b200 import perf
+        import bench_configs
         if args.sweep == "c2f":
-            print(json.dumps({"sweep": "c2f", "unit": "us", **perf.c2f_sweep()}))
+            print(json.dumps({"sweep": "c2f", "unit": "us", **bench_configs.c2f_sweep()}))
         else:
-            print(json.dumps({"sweep": args.sweep, "unit": "us / GB/s", **perf.unary_sweep(args.sweep)}))
+            print(json.dumps({"sweep": args.sweep, "unit": "us / GB/s", **bench_configs.unary_sweep(args.sweep)}))
         return
     if args.config != 4:
-        from thintnpu_b200 import perf
-        perf.run_config(args)
+        import bench_configs
+        bench_configs.run_config(args)
         return
     if args.impl == "reference":
         run_reference(args)
         return
+    run_pass(args)
+
+
+def run_pass(args):
     import torch
     import torch.distributed as dist
 
-    from thintnpu_b200 import shard
-    rank, world, local = shard.init("nccl", timeout_s=600)
+    import bench_configs
+    import thintnpu_b200
+    from thintnpu_b200 import shard, yolo
+
+    rank, world, local = shard.init("gloo", timeout_s=600)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-
-    import thintnpu_b200
     thintnpu_b200.load()  # fails loudly without libttn.so
-    from thintnpu_b200 import yolo
+    heartbeat = shard.Heartbeat(dist.distributed_c10d._get_default_store(), rank, world) if world > 1 else None
 
     plan = yolo.yolov8s_plan(args.imgsz)
     per_image = plan.bytes_per_image()
-    bytes_per_image = sum(per_image.values())
+    bytes_per_image = sum(per_image.values()) - per_image.get("cat", 0)  # zero-copy plan: no concat copies
 
     def barrier():
         torch.cuda.synchronize(device)
@@ -226,12 +242,12 @@ def main():
             dist.barrier()
 
     def max_over_ranks(value: float) -> float:
-        return shard.max_over_ranks(value, device)
+        return shard.max_over_ranks(value)
 
     # --- inputs resident in HBM; rank r owns images shard_range(world*B, world, r)
     images_mine = shard.shard_range(world * args.batch, world, rank)
     inputs = yolo.synthetic_inputs(plan, len(images_mine), device, seed=4 + images_mine.start)
-    op_pass = yolo.OpPass(plan, inputs)
+    op_pass = yolo.OpPass(plan, inputs, concat_in_place=True)
     op_pass.capture(warmup=2)
     stream = torch.cuda.current_stream(device)
 
@@ -239,7 +255,7 @@ def main():
     kinds = {}
     for _ in range(2):
         events = []
-        for step in plan.steps:
+        for step in op_pass.steps:
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
             op_pass.run_step(step)
@@ -252,84 +268,101 @@ def main():
         k["bytes"] += plan.step_bytes(step) * args.batch
         k["launches"] += 1
 
-    # --- timed region: K graph replays
+    # --- timed region: exactly K graph replays, heartbeats between steps
     for _ in range(args.warmup):
         op_pass.replay()
     barrier()
-    clocks = ClockSampler(local) if local == 0 or world == 1 else None
-    if clocks:
-        clocks.start()
+    clocks = ClockSampler(local).start()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        if heartbeat:
+            heartbeat.beat(i)
+            heartbeat.check(i, wait_s=60)
         op_pass.replay()
     end.record(stream)
     barrier()
-    clock_info = clocks.stop() if clocks else None
+    clock_info = clocks.stop()
     elapsed_ms = max_over_ranks(start.elapsed_time(end))
     images = world * args.batch * args.steps
     value = images / (elapsed_ms / 1000.0)
 
-    # --- variant: zero-copy concat plan (producers write into concat slices)
+    # --- sustained: the same replays for >= --sustained-s, with their own clock record
+    sustained = None
+    if args.sustained_s > 0:
+        reps = max(args.steps, math.ceil(args.sustained_s / (elapsed_ms / args.steps / 1000.0)))
+        reps = int(max_over_ranks(reps))
+        barrier()
+        sclocks = ClockSampler(local, period_s=0.05).start()
+        ss, se = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ss.record(stream)
+        for _ in range(reps):
+            op_pass.replay()
+        se.record(stream)
+        barrier()
+        sinfo = sclocks.stop()
+        sms = max_over_ranks(ss.elapsed_time(se))
+        sustained = {"value": world * args.batch * reps / (sms / 1000.0), "unit": "images/s", "steps": reps,
+                     "ms_per_step": sms / reps, "timed_s": sms / 1000.0, "clocks": sinfo}
+
+    # --- variants: the plain pass (concat copies kept); configs 3 and 5 split over the ranks
     variants = {}
     if not args.no_variants:
-        zc = yolo.OpPass(plan, inputs, concat_in_place=True)
-        zc.capture(warmup=2)
-        for _ in range(args.warmup):
-            zc.replay()
-        barrier()
-        zs, ze = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        zs.record(stream)
-        for _ in range(args.steps):
-            zc.replay()
-        ze.record(stream)
-        barrier()
-        zms = max_over_ranks(zs.elapsed_time(ze))
-        zbytes = bytes_per_image - per_image.get("cat", 0)
-        variants["concat_in_place"] = {
-            "value": images / (zms / 1000.0), "unit": "images/s", "ms_per_step": zms / args.steps,
-            "gpu_launches": zc.launches_per_pass() * args.steps,
-            "algorithmic_bytes_per_image": zbytes,
-            "achieved_hbm_gbs_pass": zbytes * images / world / (zms / 1000.0) / 1e9,
-            "note": "same outputs bit for bit; the 12 concat copies are elided by placing each "
-                    "producer's output in its concat slice"}
-        zc.graph = None
-        del zc
+        plain = yolo.OpPass(plan, inputs)
+        plain.capture(warmup=2)
+        pms = bench_configs.device_time(plain.replay, args.steps, args.warmup, device, barrier, max_over_ranks)
+        pbytes = sum(per_image.values())
+        variants["plain_pass"] = {
+            "value": images / (pms / 1000.0), "unit": "images/s", "ms_per_step": pms / args.steps,
+            "gpu_launches": plain.launches_per_pass() * args.steps, "algorithmic_bytes_per_image": pbytes,
+            "achieved_hbm_gbs_pass": pbytes * args.batch * args.steps / (pms / 1000.0) / 1e9,
+            "note": "the same pass with the 12 concat copies run as kernels (outputs bit-identical)"}
+        plain.graph = None
+        del plain
+        torch.cuda.empty_cache()
+        for key, cfg, total, seed in (("config3_b64", bench_configs.Config3(), 64, 30),
+                                      ("config5_n512", bench_configs.Config5(), 512, 50)):
+            variants[key] = bench_configs.measure_config(cfg, total, args.steps, args.warmup, device, rank, world,
+                                                         barrier, max_over_ranks, seed)
+            del cfg
+            torch.cuda.empty_cache()
 
     # --- e2e: public API with host buffers (H2D inputs + D2H output every step)
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, plan, op_pass, device, stream, world, barrier, max_over_ranks)
+        e2e = run_e2e(args, plan, op_pass, inputs, device, world, barrier, max_over_ranks)
 
-    peak, peak_kind = peaks()
+    peak, peak_kind = bench_configs.hbm_peak()
     silu = kinds["silu"]
     achieved = silu["bytes"] / (silu["ms"] / 1000.0) / 1e9
-    traffic = silu_traffic_per_launch(plan, args.batch)
     line = {
         "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "batch_per_gpu": args.batch, "imgsz": args.imgsz,
-                   "parallelism": f"image-sharded x{world}, no data-path collective",
+                   "parallelism": f"image-sharded x{world}, no data-path collective (gloo control plane)",
                    "l2": "inputs larger than L2 (no flush needed)",
-                   "algorithmic_bytes_per_image": bytes_per_image, "replay": "one CUDA graph per step"},
-        "achieved_hbm_gbs_pass": bytes_per_image * value / world / 1e9,
+                   "algorithmic_bytes_per_image": bytes_per_image, "replay": "one CUDA graph per step",
+                   "concat": "zero-copy: every concat buffer filled in place by its producers (no copy kernels)"},
+        "achieved_hbm_gbs_pass": bytes_per_image * args.batch * args.steps / (elapsed_ms / 1000.0) / 1e9,
         "roofline": {"kernel": "silu (ttn_silu, 57 launches per pass)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-                     "traffic": traffic,
+                     "traffic": silu_traffic_per_launch(plan, args.batch),
                      "how": "algorithmic bytes (read+write, 4 B/element) of all SiLU launches of one "
                             "pass / their summed CUDA-event durations"},
         "kernels": {k: {"ms_per_pass": v["ms"], "launches": v["launches"],
-                        "gbs": v["bytes"] / (v["ms"] / 1000.0) / 1e9 if v["ms"] else None}
+                        "gbs": v["bytes"] / (v["ms"] / 1000.0) / 1e9 if v["ms"] else None,
+                        "frac": v["bytes"] / (v["ms"] / 1000.0) / 1e9 / peak if v["ms"] else None}
                     for k, v in kinds.items()},
         "gpu_launches": op_pass.launches_per_pass() * args.steps,
         "clocks": clock_info,
+        "sustained": sustained,
         "e2e": e2e,
         "variants": variants,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_pass_rate(args.imgsz)
+        line["cpu_baseline"] = cpu_baseline(args.imgsz)
     if rank == 0:
         print(json.dumps(line), flush=True)
     op_pass.graph = None
@@ -339,67 +372,129 @@ def main():
 
 
 def silu_traffic_per_launch(plan, batch):
-    """DRAM bytes of the average SiLU launch, scaled from the committed ncu capture
-    (profiles/silu_f16.md: `dram_bytes_per_element: X`), else None."""
-    path = ROOT / "profiles" / "silu_f16.md"
+    """DRAM bytes of the average SiLU launch of the pass, scaled from the
+    committed ncu capture's bytes per element (profiles/silu_f16.json)."""
+    path = ROOT / "profiles" / "silu_f16.json"
     if not path.exists():
         return None
-    for line in path.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_element:"):
-            per_element = float(line.split(":", 1)[1])
-            elements = sum(plan.elements(s.inputs[0].name) for s in plan.steps if s.op == "silu")
-            launches = sum(1 for s in plan.steps if s.op == "silu")
-            return per_element * elements * batch / launches
-    return None
+    per_element = float(json.loads(path.read_text())["dram_bytes_per_element"])
+    silu_steps = [s for s in plan.steps if s.op == "silu"]
+    elements = sum(plan.elements(s.inputs[0].name) for s in silu_steps)
+    return per_element * elements * batch / len(silu_steps)
 
 
-def run_e2e(args, plan, op_pass, device, stream, world, barrier, max_over_ranks):
-    """Same pass through the public API with host buffers: every step copies all of
-    the step's conv outputs host->device from pinned memory, replays the pass and
-    reads the decoded output back.  The pinned source is one pool per rank of at
-    most a quarter of the free host RAM split over the local ranks; inputs larger
-    than the pool are copied from it chunk by chunk, so the bytes crossing PCIe
-    per step are always the full input set."""
+def run_e2e(args, plan, op_pass, inputs, device, world, barrier, max_over_ranks):
+    """The pass through the public API with host buffers, double buffered: every
+    step copies all of the step's conv outputs host->device from pinned memory
+    (copy stream), replays the pass on them (compute stream) and reads the decoded
+    output back (a second copy stream).  Step i+1's inputs go into the other of
+    two device input sets while step i runs.  The pinned source is one pool per
+    rank of at most a quarter of the free host RAM split over the local ranks;
+    inputs larger than the pool are copied from it chunk by chunk, so the bytes
+    crossing PCIe per step are always the full input set.  Before the timed steps,
+    every rank copies 4 GiB from the pool at once (256 MiB copies) to measure the
+    concurrent host-to-device copy peak."""
     import psutil
     import torch
+
+    from thintnpu_b200 import yolo
     names = plan.conv_inputs
-    step_bytes = sum(op_pass.buffers[n].numel() * 2 for n in names)
+    step_bytes = sum(inputs[n].numel() * 2 for n in names)
     local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     budget = int(0.25 * psutil.virtual_memory().available / local_ranks)
-    pool_elems = max(1 << 20, min(step_bytes, budget) // 2)
+    pool_elems = max(1 << 28, min(step_bytes, budget) // 2)
     pool = torch.empty(pool_elems, dtype=torch.float16, pin_memory=True)
-    pool.copy_(op_pass.buffers[names[0]].reshape(-1)[:pool_elems]
-               if op_pass.buffers[names[0]].numel() >= pool_elems else
-               torch.randn(pool_elems, dtype=torch.float32).half())
-    result = torch.empty(op_pass.output.shape, dtype=torch.float16, pin_memory=True)
+    filled = 0
+    for n in names:  # the pool holds real conv outputs
+        take = min(inputs[n].numel(), pool_elems - filled)
+        pool[filled:filled + take].copy_(inputs[n].reshape(-1)[:take])
+        filled += take
+        if filled == pool_elems:
+            break
+    second = {n: torch.empty_like(t) for n, t in inputs.items()}
+    passes = [op_pass, yolo.OpPass(plan, second, concat_in_place=True)]
+    passes[1].capture(warmup=1)
+    results = [torch.empty(p.output.shape, dtype=torch.float16, pin_memory=True) for p in passes]
+    compute = torch.cuda.current_stream(device)
+    h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
 
-    def step():
-        offset = 0
-        for n in names:  # H2D of this step's inputs
-            dst = op_pass.buffers[n].reshape(-1)
-            done = 0
-            while done < dst.numel():
-                take = min(dst.numel() - done, pool_elems - offset)
-                dst[done:done + take].copy_(pool[offset:offset + take], non_blocking=True)
-                done += take
-                offset = (offset + take) % pool_elems
-        op_pass.replay()
-        result.copy_(op_pass.output, non_blocking=True)  # D2H of the step's result
-
-    step()
+    # concurrent host->device copy peak (all ranks at once)
+    dst = inputs[names[0]].reshape(-1)
+    chunk = min(1 << 27, pool_elems, dst.numel())
+    total = 0
     barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.e2e_steps):
-        step()
-    end.record(stream)
+    ps, pe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ps.record(h2d)
+    with torch.cuda.stream(h2d):
+        while total < (4 << 30):
+            dst[:chunk].copy_(pool[:chunk], non_blocking=True)
+            total += 2 * chunk
+    pe.record(h2d)
+    barrier()
+    peak_ms = max_over_ranks(ps.elapsed_time(pe))
+    h2d_peak = world * total / (peak_ms / 1000.0) / 1e9
+
+    offset = [0]
+
+    def upload(p):
+        """H2D of one step's inputs into pass p's input set, on the copy stream."""
+        for n in names:
+            t = p.buffers[n].reshape(-1)
+            done = 0
+            while done < t.numel():
+                take = min(t.numel() - done, pool_elems - offset[0])
+                t[done:done + take].copy_(pool[offset[0]:offset[0] + take], non_blocking=True)
+                done += take
+                offset[0] = (offset[0] + take) % pool_elems
+
+    def run(steps: int) -> float:
+        uploaded = [torch.cuda.Event() for _ in passes]
+        replayed = [torch.cuda.Event() for _ in passes]
+        read = [torch.cuda.Event() for _ in passes]
+        for e in replayed + read:
+            e.record(compute)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(compute)
+        h2d.wait_event(start)
+        for i in range(steps + 1):
+            if i < steps:  # inputs of step i: wait until step i-2 has finished reading this set
+                j = i % 2
+                h2d.wait_event(replayed[j])
+                with torch.cuda.stream(h2d):
+                    upload(passes[j])
+                uploaded[j].record(h2d)
+            if i > 0:  # replay step i-1 (its inputs landed, its output buffer was read back)
+                j = (i - 1) % 2
+                compute.wait_event(uploaded[j])
+                compute.wait_event(read[j])
+                passes[j].replay()
+                replayed[j].record(compute)
+                d2h.wait_event(replayed[j])
+                with torch.cuda.stream(d2h):
+                    results[j].copy_(passes[j].output, non_blocking=True)
+                read[j].record(d2h)
+        for e in read:
+            compute.wait_event(e)
+        end.record(compute)
+        return start, end
+
+    run(1)
+    barrier()
+    start, end = run(args.e2e_steps)
     barrier()
     ms = max_over_ranks(start.elapsed_time(end))
     value = world * args.batch * args.e2e_steps / (ms / 1000.0)
-    return {"value": value, "unit": "images/s", "h2d_bytes_per_step": step_bytes,
-            "d2h_bytes_per_step": result.numel() * 2, "steps": args.e2e_steps,
-            "pinned_pool_bytes": pool_elems * 2,
-            "path": "pinned host pool -> cudaMemcpyAsync per conv output -> graph replay -> pinned host"}
+    out = {"value": value, "unit": "images/s", "h2d_bytes_per_step": step_bytes,
+           "d2h_bytes_per_step": results[0].numel() * 2, "steps": args.e2e_steps,
+           "h2d_gbs": world * step_bytes * args.e2e_steps / (ms / 1000.0) / 1e9,
+           "h2d_peak_gbs": h2d_peak,
+           "pinned_pool_bytes": pool_elems * 2,
+           "path": "pinned host pool -> cudaMemcpyAsync per conv output (copy stream) -> graph replay "
+                   "(compute stream, two input sets) -> pinned host (second copy stream)"}
+    out["h2d_frac_of_peak"] = out["h2d_gbs"] / h2d_peak
+    for p in passes[1:]:
+        p.graph = None
+    return out
 
 
 if __name__ == "__main__":

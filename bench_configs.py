@@ -1,47 +1,121 @@
-"""Per-config measurements for BASELINE configs 1, 2, 3 and 5, and 6 = the fused
-C2PSA attention built on config 3's softmax (``bench.py --config N``).
+"""Workloads and measurement helpers of ``bench.py``.
 
-Each config is one kernel family on its own batch, inputs resident in HBM
-(every batch is far above the 126 MB L2), timed with CUDA events on the
-launching stream over K steps after W warm-ups, max over ranks.  The printed
-JSON line has the bench.py keys: value (images/s over all GPUs), roofline
-(algorithmic bytes per step / step time vs the measured HBM copy peak), e2e
-(host buffers copied in and results read back every step) and, on rank 0 at
-N=1, the CPU-eager baseline on a bounded sample.
+Each config is one kernel family on its own batch of seeded synthetic data,
+inputs resident in HBM (every batch is far above the 126 MB L2, so no flush is
+needed between steps), timed with CUDA events on the launching stream over K
+steps after W warm-ups, max over ranks.  The same config objects are what the
+GPU parity tests run (tests/test_bench_configs_gpu.py), so the timed
+configuration is the tested one.
+
+CPU legs (``cpu_step``) run the oracle -- PyTorch CPU eager, or the numpy
+selection restatement -- and are only used for the reported CPU baseline; they
+follow one protocol (``cpu_rate``): 3 warm-ups, then the median of at least 11
+timed samples.
+
+Multi-GPU: ranks shard images (no data-path collective) and the control plane
+(barrier, max over ranks) is a gloo group, so no NCCL communicator exists.
 """
 from __future__ import annotations
 
 import json
 import os
+import statistics
 import time
 from pathlib import Path
 
 import torch
 
-from . import ops
+import thintnpu_b200
+from thintnpu_b200 import ops, shard
 
-ROOT = Path(__file__).resolve().parent.parent
+ROOT = Path(__file__).resolve().parent
 METRIC = "non-conv op pass images/s at 640² fp16; achieved HBM GB/s vs ~8 TB/s peak"
 
 
-def _peak():
+def hbm_peak():
+    """Measured HBM copy peak of this pool (GB/s) and its kind."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
 
 
-def _tensor_peak():
+def tensor_peak():
+    """Measured dense bf16 GEMM peak (TFLOP/s, burst) and its kind."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         return float(json.loads(path.read_text())["bf16_tflops"]), "measured (burst)"
     return 1590.0, "fallback"
 
 
-def _gen(shape, seed, device, mean=0.0, std=1.0):
+def gen(shape, seed, device, mean=0.0, std=1.0):
+    """Seeded N(mean, std) fp16: drawn in FP32 with the device's own generator
+    (Philox on CUDA), then rounded to fp16."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std + mean).half()
+
+
+def config5_logits(n: int, seed: int = 5, device="cpu", anchors: int = 8400, nc: int = 80) -> torch.Tensor:
+    """BASELINE config 5 input: logits [n, 4 + nc, anchors] fp16, channel-planar
+    (selection reads the [n, anchors, 4 + nc] transposed view).  Class logits
+    ~ N(-4, 2), box rows ~ U(0, 640); per image ~1% of anchors copy another
+    anchor's whole class row (exact ties), 0.5% of anchors hold one value across
+    all classes, and 8 NaNs (both signs, quiet and signalling payloads) at
+    distinct anchors.  The bulk is drawn on `device`; the tie and NaN positions
+    come from a seeded CPU generator (distinct targets, so the scatters are
+    deterministic)."""
+    device = torch.device(device)
+    x = gen((n, 4 + nc, anchors), seed, device, mean=-4.0, std=2.0)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 1)
+    x[:, :4] = (torch.rand((n, 4, anchors), generator=g, device=device) * 640).half()
+    if n == 0 or anchors == 0:
+        return x
+    c = torch.Generator().manual_seed(seed + 2)
+    ties, flat, nans = max(1, anchors // 100), max(1, anchors // 200), min(8, anchors)
+    perm = torch.stack([torch.randperm(anchors, generator=c) for _ in range(n)])  # [n, anchors]
+    dst = perm[:, :ties]
+    src = torch.randint(0, anchors, (n, ties), generator=c)
+    rows = perm[:, ties:ties + flat] if ties + flat <= anchors else perm[:, :flat]
+    nan_at = perm[:, -nans:]
+    nan_cls = torch.randint(0, nc, (n, nans), generator=c)
+    b = torch.arange(n, device=device)[:, None]
+    dst, src, rows, nan_at, nan_cls = (t.to(device) for t in (dst, src, rows, nan_at, nan_cls))
+    view = x.transpose(1, 2)  # [n, anchors, 4 + nc], shares storage with x
+    view[b, dst, 4:] = view[b, src, 4:]
+    view[b, rows, 4:] = view[b, rows, 4:5]
+    payload = torch.tensor([0x7E00, 0xFE00, 0x7C01, 0xFD23, 0x7E01, 0xFFFF, 0x7D00, 0xFC02],
+                           dtype=torch.int32).to(torch.int16)[:nans]
+    x.view(torch.int16)[b, 4 + nan_cls, nan_at] = payload.to(device).expand(n, nans)
+    return x
+
+
+def cpu_rate(fn, images_per_call: int, warmup: int = 3, samples: int = 11) -> dict:
+    """CPU baseline protocol: `warmup` untimed calls, then the median of `samples`
+    timed calls (time.perf_counter) under inference_mode; images/s from the median."""
+    with torch.inference_mode():
+        for _ in range(warmup):
+            fn()
+        times = []
+        for _ in range(samples):
+            t = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t)
+    med = statistics.median(times)
+    return {"value": images_per_call / med, "median_s": med, "samples": samples, "warmup": warmup,
+            "total_s": sum(times)}
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), or "unknown"."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 class Config1:
@@ -49,11 +123,12 @@ class Config1:
     name = "config 1: fused SiLU(x+b)+r, NC1HWC0 [B,8,80,80,16] fp16"
     batch, cpu_batch = 256, 4
     bytes_per_image = 3 * 2 * 819200  # x, r read and y written once; the 256-byte bias is per launch
+    launches = 1
 
     def setup(self, batch, device, seed):
-        self.x = _gen((batch, 8, 80, 80, 16), seed, device)
-        self.r = _gen((batch, 8, 80, 80, 16), seed + 1, device)
-        self.b = _gen((128,), seed + 2, device, std=0.1)
+        self.x = gen((batch, 8, 80, 80, 16), seed, device)
+        self.r = gen((batch, 8, 80, 80, 16), seed + 1, device)
+        self.b = gen((128,), seed + 2, device, std=0.1)
         self.y = torch.empty_like(self.x)
         return [self.x, self.r], [self.y]
 
@@ -76,10 +151,11 @@ class Config2:
     batch, cpu_batch = 256, 2
     shapes, strides = [(80, 80), (40, 40), (20, 20)], [8.0, 16.0, 32.0]
     bytes_per_image = 2 * (64 + 80) * 8400 + 2 * 84 * 8400
+    launches = 2
 
     def setup(self, batch, device, seed):
-        self.box = _gen((batch, 64, 8400), seed, device, std=2.0)
-        self.cls = _gen((batch, 80, 8400), seed + 1, device, std=3.0)
+        self.box = gen((batch, 64, 8400), seed, device, std=2.0)
+        self.cls = gen((batch, 80, 8400), seed + 1, device, std=3.0)
         self.out = torch.empty((batch, 84, 8400), dtype=torch.float16, device=device)
         return [self.box, self.cls], [self.out]
 
@@ -101,9 +177,10 @@ class Config3:
     batch, cpu_batch = 256, 4
     scale = 32 ** -0.5
     bytes_per_image = 2 * 2 * 4 * 400 * 400
+    launches = 1
 
     def setup(self, batch, device, seed):
-        self.x = _gen((batch, 4, 400, 400), seed, device)
+        self.x = gen((batch, 4, 400, 400), seed, device)
         self.y = torch.empty_like(self.x)
         return [self.x], [self.y]
 
@@ -118,36 +195,46 @@ class Config3:
 
 
 class Config5:
-    """YOLO26 selection: logits [N, 84, 8400] (transposed view), fp16 sigmoid fused,
-    class max, stable top-300 anchors, stable top-300 pairs, packed [N, 300, 6]."""
-    name = "config 5: YOLO26 NMS-free selection, [N,8400,84] logits view, K=300, class-aware"
+    """YOLO26 selection: logits [N, 84, 8400] (transposed view, ties and NaNs as
+    the config describes), fp16 sigmoid fused, class max, stable top-k anchors,
+    stable top-k pairs (class-aware) or argmax labels (agnostic), packed [N, k, 6]."""
     batch, cpu_batch = 512, 4
-    k = 300
     bytes_per_image = 2 * 80 * 8400 + 2 * 4 * 300 + 24 * 300
+    launches = 3
+
+    def __init__(self, k: int = 300, agnostic: bool = False, nan_last: bool = False):
+        self.k, self.agnostic, self.nan_last = k, agnostic, nan_last
+        self.name = (f"config 5: YOLO26 NMS-free selection, [N,8400,84] logits view with ties and NaNs, "
+                     f"K={k}, {'agnostic' if agnostic else 'class-aware'}, NaN {'last' if nan_last else 'first'}")
+        self.bytes_per_image = 2 * 80 * 8400 + 2 * 4 * k + 24 * k
 
     def setup(self, batch, device, seed):
-        x = _gen((batch, 84, 8400), seed, device, mean=-4.0, std=2.0)
-        x[:, :4] = (torch.rand((batch, 4, 8400), device=device) * 640).half()
-        self.base = x
-        self.decoded = x.transpose(1, 2)
-        self.ws = torch.empty(ops.workspace_size(batch, 8400, 80, self.k, 4), dtype=torch.uint8, device=device)
-        self.out = torch.empty((batch, self.k, 6), dtype=torch.float32, device=device)
+        return self.bind(config5_logits(batch, seed, device))
+
+    def bind(self, logits):
+        """Select from these logits [N, 84, 8400] (fp16, on the GPU) from now on."""
+        batch = logits.size(0)
+        self.base = logits
+        self.decoded = logits.transpose(1, 2)
+        flags = (1 if self.agnostic else 0) | (2 if self.nan_last else 0) | 4
+        self.ws = torch.empty(ops.workspace_size(batch, 8400, 80, self.k, flags), dtype=torch.uint8,
+                              device=logits.device)
+        self.out = torch.empty((batch, self.k, 6), dtype=torch.float32, device=logits.device)
         return [self.base], [self.out]
 
     def step(self):
-        ops.detection_select(self.decoded, self.k, False, apply_sigmoid=True, workspace=self.ws,
-                             out=self.out)
+        ops.detection_select(self.decoded, self.k, self.agnostic, nan_last=self.nan_last, apply_sigmoid=True,
+                             workspace=self.ws, out=self.out)
 
     def cpu_step(self, batch):
         import numpy as np
         from oracle import select as osel
-        if not hasattr(self, "cbits"):
-            g = torch.Generator().manual_seed(5)
-            x = (torch.randn(batch, 84, 8400, generator=g) * 2 - 4).half()
-            self.cx = x.transpose(1, 2)
+        if not hasattr(self, "cx"):
+            self.cx = config5_logits(batch, 5, "cpu").transpose(1, 2)
         s = self.cx.clone()
         s[..., 4:] = torch.sigmoid(s[..., 4:])
-        osel.select(s.contiguous().view(torch.int16).numpy().view(np.uint16), self.k)
+        osel.select(s.contiguous().view(torch.int16).numpy().view(np.uint16), self.k, self.agnostic,
+                    self.nan_last)
 
 
 class Config6:
@@ -159,12 +246,13 @@ class Config6:
     scale = 32 ** -0.5
     bytes_per_image = 2 * heads * (2 * kd + hd) * n + 2 * heads * hd * n  # qkv read, out written
     flops_per_image = heads * (2 * n * n * kd + 2 * n * n * hd)
+    launches = 1
 
     def _split(self, qkv):
         return qkv.view(qkv.shape[0], self.heads, 2 * self.kd + self.hd, self.n).split([self.kd, self.kd, self.hd], 2)
 
     def setup(self, batch, device, seed):
-        self.qkv = _gen((batch, self.heads * (2 * self.kd + self.hd), self.n), seed, device)
+        self.qkv = gen((batch, self.heads * (2 * self.kd + self.hd), self.n), seed, device)
         self.q, self.k, self.v = self._split(self.qkv)
         self.out = torch.empty((batch, self.heads, self.hd, self.n), dtype=torch.float16, device=device)
         return [self.qkv], [self.out]
@@ -189,8 +277,9 @@ class Config7:
     bound = "tensor"
 
     def __init__(self):
-        from . import yolo
+        from thintnpu_b200 import yolo
         self.specs = yolo.yolov8s_convs(640)
+        self.launches = len(self.specs)
         self.flops_per_image = sum(sp.flops for sp in self.specs)
         self.bytes_per_image = sum(2 * 16 * ((sp.cin + 15) // 16) * sp.h * sp.w + 2 * sp.cout * sp.out_hw[0] *
                                    sp.out_hw[1] for sp in self.specs)
@@ -243,7 +332,7 @@ class Config8:
     batch, cpu_batch = 64, 2
     shapes = [(128, 80), (128, 80), (256, 40), (128, 40), (512, 20), (128, 20)]
     bytes_per_image = sum(2 * 2 * c * hw * hw for c, hw in shapes)  # read once, written once
-    specs = shapes
+    launches = len(shapes)
 
     def _layer(self, c, hw, batch, seed, device):
         g = torch.Generator().manual_seed(seed)
@@ -282,18 +371,53 @@ class Config8:
 CONFIGS = {1: Config1, 2: Config2, 3: Config3, 5: Config5, 6: Config6, 7: Config7, 8: Config8}
 
 
+def device_time(step, steps: int, warmup: int, device, barrier, max_over_ranks) -> float:
+    """Milliseconds of `steps` calls of `step` after `warmup` untimed ones: CUDA
+    events on the current stream, a barrier and synchronize on both sides, max
+    over ranks."""
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        step()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    barrier()
+    return max_over_ranks(start.elapsed_time(end))
+
+
+def measure_config(cfg, images_total: int, steps: int, warmup: int, device, rank: int, world: int,
+                   barrier, max_over_ranks, seed: int) -> dict:
+    """One device-timed line for a config with `images_total` images split over the
+    ranks (strong scaling: shard_range), roofline against the measured peak."""
+    mine = len(shard.shard_range(images_total, world, rank))
+    cfg.setup(max(mine, 1), device, seed=seed + rank)
+    ms = device_time(cfg.step, steps, warmup, device, barrier, max_over_ranks)
+    value = images_total * steps / (ms / 1000.0)
+    peak, kind = hbm_peak()
+    per_gpu_images = -(-images_total // world)
+    achieved = cfg.bytes_per_image * per_gpu_images * steps / (ms / 1000.0) / 1e9
+    return {"value": value, "unit": "images/s", "images_total": images_total, "images_per_gpu": per_gpu_images,
+            "scaling": "strong", "ms_per_step": ms / steps, "steps": steps, "workload": cfg.name,
+            "gpu_launches": cfg.launches * steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": f"{kind} hbm_gbs",
+                         "how": "algorithmic bytes of the busiest rank's images per step / step time"}}
+
+
 def unary_sweep(op: str = "silu", sizes_m=(13, 26, 52, 105, 210, 420, 839), reps: int = 10) -> dict:
     """In-place fp16 SiLU/sigmoid bandwidth by tensor size (4 algorithmic bytes per
     element): N(0,1) inputs, 3 warm-ups, then the median of `reps` launches each
     timed with CUDA events after flushing L2 with a 256 MB write."""
-    import thintnpu_b200
     thintnpu_b200.load()
     device = torch.device("cuda", torch.cuda.current_device())
     fn = ops.silu_ if op == "silu" else (lambda t: ops.sigmoid(t, out=t))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     out = {}
     for m in sizes_m:
-        x = _gen((m * 1000 * 1000,), m, device)
+        x = gen((m * 1000 * 1000,), m, device)
         for _ in range(3):
             fn(x)
         times = []
@@ -316,8 +440,7 @@ def c2f_sweep(batch: int = 32, reps: int = 20) -> dict:
     bottlenecks; blocked_c2f.py:13-24) fused (``yolo.C2fRegion``) against the same
     op sequence run op by op (pack, conv, chunk, conv, conv, add, cat, conv, unpack),
     seeded random weights; median of ``reps`` CUDA-event timings after 3 warm-ups."""
-    import thintnpu_b200
-    from .yolo import C2fRegion
+    from thintnpu_b200.yolo import C2fRegion
     thintnpu_b200.load()
     device = torch.device("cuda", torch.cuda.current_device())
     g = torch.Generator().manual_seed(1)
@@ -354,45 +477,9 @@ def c2f_sweep(batch: int = 32, reps: int = 20) -> dict:
     return out
 
 
-def run_config(args):
+def _control_plane(world: int, device):
+    """Barrier and max-over-ranks on a gloo group (host tensors; no NCCL)."""
     import torch.distributed as dist
-    cfg = CONFIGS[args.config]()
-    if args.impl == "reference":
-        if int(os.environ.get("RANK", "0")) != 0:
-            return
-        torch.set_num_threads(os.cpu_count() or 1)
-        with torch.inference_mode():
-            cfg.cpu_step(cfg.cpu_batch)
-            times = []
-            for _ in range(args.steps):
-                t = time.perf_counter()
-                cfg.cpu_step(cfg.cpu_batch)
-                times.append(time.perf_counter() - t)
-        value = cfg.cpu_batch * len(times) / sum(times)
-        print(json.dumps({"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
-                          "steps": args.steps, "warmup": args.warmup, "impl": "reference",
-                          "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
-                          "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-                          "config": {"workload": cfg.name, "batch_per_step": cfg.cpu_batch},
-                          "cpu_baseline": {"value": value, "unit": "images/s",
-                                           "cores": torch.get_num_threads(), "kind": "port",
-                                           "sample": f"{cfg.cpu_batch} images per step, PyTorch CPU eager"},
-                          "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0,
-                                  "d2h_bytes_per_step": 0}}), flush=True)
-        return
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
-    import thintnpu_b200
-    thintnpu_b200.load()
-    batch = args.batch if args.batch != 256 else cfg.batch
-    inputs, outputs = cfg.setup(batch, device, seed=10 * args.config + 1000 * rank)
-    stream = torch.cuda.current_stream(device)
 
     def barrier():
         torch.cuda.synchronize(device)
@@ -400,31 +487,51 @@ def run_config(args):
             dist.barrier()
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(v)
 
-    for _ in range(args.warmup):
-        cfg.step()
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.steps):
-        cfg.step()
-    end.record(stream)
-    barrier()
-    ms = max_over_ranks(start.elapsed_time(end))
+    return barrier, max_over_ranks
+
+
+def run_config(args):
+    """``bench.py --config N``: one JSON line for config N on the ranks of this job."""
+    cfg = CONFIGS[args.config]()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        cfg.cpu_step(cfg.cpu_batch)  # builds the inputs
+        rate = cpu_rate(lambda: cfg.cpu_step(cfg.cpu_batch), cfg.cpu_batch, warmup=args.warmup,
+                        samples=max(args.steps, 11))
+        value = rate["value"]
+        print(json.dumps({"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
+                          "steps": args.steps, "warmup": args.warmup, "impl": "reference",
+                          "ms_per_step": 1000 * rate["median_s"], "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                          "config": {"workload": cfg.name, "batch_per_step": cfg.cpu_batch},
+                          "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port",
+                                           "sample": f"{cfg.cpu_batch} images per step, PyTorch CPU eager, "
+                                                     f"median of {rate['samples']} after {rate['warmup']} warm-ups"},
+                          "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    rank, world, local = shard.init("gloo", timeout_s=600)
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    thintnpu_b200.load()
+    barrier, max_over_ranks = _control_plane(world, device)
+    batch = args.batch if args.batch != 256 else cfg.batch
+    inputs, outputs = cfg.setup(batch, device, seed=10 * args.config + 1000 * rank)
+    ms = device_time(cfg.step, args.steps, args.warmup, device, barrier, max_over_ranks)
     images = world * batch * args.steps
     value = images / (ms / 1000.0)
-    peak, kind = _peak()
-    achieved = cfg.bytes_per_image * batch * args.steps / (ms / 1000.0) / 1e9 / 1.0
-    per_gpu = achieved / world
     tensor = getattr(cfg, "bound", "hbm") == "tensor"
     if tensor:  # TFLOP/s per GPU against the measured dense bf16/fp16 GEMM peak (burst)
-        per_gpu = cfg.flops_per_image * batch * args.steps / (ms / 1000.0) / 1e12 / world
-        peak, kind = _tensor_peak()
+        per_gpu = cfg.flops_per_image * batch * args.steps / (ms / 1000.0) / 1e12
+        peak, kind = tensor_peak()
+    else:
+        per_gpu = cfg.bytes_per_image * batch * args.steps / (ms / 1000.0) / 1e9
+        peak, kind = hbm_peak()
     # e2e: host copies of the inputs in, results out, every step
     host_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in inputs]
     host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outputs]
@@ -438,16 +545,8 @@ def run_config(args):
         for h, t in zip(host_out, outputs):
             h.copy_(t, non_blocking=True)
 
-    e2e_step()
-    barrier()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record(stream)
-    for _ in range(max(2, args.steps // 4)):
-        e2e_step()
-    e2.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2))
-    e2e_steps = max(2, args.steps // 4)
+    e2e_steps = max(10, args.steps // 4)
+    e2e_ms = device_time(e2e_step, e2e_steps, 1, device, barrier, max_over_ranks)
     line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
@@ -458,23 +557,22 @@ def run_config(args):
             "roofline": {"bound": "tensor" if tensor else "hbm", "achieved": per_gpu, "peak": peak,
                          "unit": "TFLOP/s" if tensor else "GB/s", "frac": per_gpu / peak, "peak_kind": kind,
                          "traffic": None},
-            "gpu_launches": args.steps * (4 if args.config == 5 else len(getattr(cfg, "specs", [0]))),
-            "e2e": {"value": world * batch * e2e_steps / (e2e_ms / 1000.0), "unit": "images/s",
+            "gpu_launches": args.steps * cfg.launches,
+            "e2e": {"value": world * batch * e2e_steps / (e2e_ms / 1000.0), "unit": "images/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in inputs),
                     "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in outputs)}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        torch.set_num_threads(os.cpu_count() or 1)
-        with torch.inference_mode():
-            cfg.cpu_step(cfg.cpu_batch)
-            done, t0 = 0, time.perf_counter()
-            while time.perf_counter() - t0 < 10.0:
-                cfg.cpu_step(cfg.cpu_batch)
-                done += cfg.cpu_batch
-            el = time.perf_counter() - t0
-        line["cpu_baseline"] = {"value": done / el, "unit": "images/s", "cores": torch.get_num_threads(),
-                                "kind": "port", "sample": f"{done} images, PyTorch CPU eager, {el:.1f} s"}
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        cfg.cpu_step(cfg.cpu_batch)
+        rate = cpu_rate(lambda: cfg.cpu_step(cfg.cpu_batch), cfg.cpu_batch)
+        line["cpu_baseline"] = {"value": rate["value"], "unit": "images/s", "cores": threads, "kind": "port",
+                                "sample": f"{cfg.cpu_batch} images per call, PyTorch CPU eager, median of "
+                                          f"{rate['samples']} after {rate['warmup']} warm-ups",
+                                "cpu_model": cpu_model()}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
