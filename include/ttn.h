@@ -286,6 +286,18 @@ ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs,
                               const int64_t* widths, const float* strides, int32_t xywh,
                               void* out, ttn_stream stream);
 
+/* ttn_dfl_decode_f16 that also writes the DFL distances it decoded from:
+ * distances fp16 [n, 4, a] contiguous (left, top, right, bottom per anchor, each
+ * the fp16-rounded expectation of its 16-bin softmax), or NULL to skip.  The
+ * reference's chain has this tensor as the output of its DFL (the 1x1 conv with
+ * arange(16) weights, whole_blocked.py:138) before the anchor arithmetic of
+ * :139-146; tests use it to check the two halves of the decode separately. */
+ttn_status ttn_dfl_decode_trace_f16(const void* box, int64_t box_bs, int64_t box_cs,
+                                    const void* cls, int64_t cls_bs, int64_t cls_cs, int64_t n,
+                                    int64_t nc, int32_t levels, const int64_t* heights,
+                                    const int64_t* widths, const float* strides, int32_t xywh,
+                                    void* out, void* distances, ttn_stream stream);
+
 /* ------------------------------------------------------- selection (a10) */
 
 /* Flags for ttn_select_f16. */
@@ -326,8 +338,12 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
  * lives in an 8 MiB array compiled into the library (held by every GPU that
  * loads it until exit); requests needing more (ttn_select_workspace_size) fail
  * with TTN_UNSUPPORTED.  All calls share that array: calls whose kernels overlap
- * on the GPU race, calls on one stream are safe.  The first call on a device
- * resolves the array's address and should come before any stream capture.
+ * on the GPU race, calls on one stream are safe.  The array's address belongs to
+ * the calling thread's current CUDA context and is looked up on every call made
+ * outside stream capture (so contexts the host creates itself, or re-creates
+ * with cudaDeviceReset, each get theirs); a call under stream capture uses the
+ * address found by an earlier call in the same context, and is rejected with
+ * TTN_INVALID_ARG when there was none.
  * This entry point has no counterpart in the reference. */
 ttn_status ttn_select_f16_static(const ttn_tensor* decoded, int64_t max_det, uint32_t flags,
                                  float* out, const ttn_select_trace* trace, ttn_stream stream);

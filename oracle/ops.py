@@ -126,10 +126,27 @@ def dfl(box: torch.Tensor) -> torch.Tensor:
     return F.conv2d(prob, weight).view(b, 4, a)
 
 
-def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes, strides, xywh: bool = True) -> torch.Tensor:
-    """anchorfree_predictions (whole_blocked.py:118-146) on CPU fp16 eager."""
+def dfl_sequential(box: torch.Tensor) -> torch.Tensor:
+    """The DFL expectation in the reference's order, written out: fp16 softmax
+    probabilities over the 16 bins (CPU eager), then sum_{i=1..15} p_i * i
+    accumulated in FP32 from bin 1 upwards and rounded once to fp16 -- the 1x1
+    conv with arange(16) weights of whole_blocked.py:138 (each product p_i * i of
+    an fp16 value and a 4-bit integer is exact in FP32, so only the additions
+    round).  CPU eager's fp16 conv gives the same bits (tests/test_oracle.py)."""
+    b, _, a = box.shape
+    prob = box.view(b, 4, 16, a).transpose(2, 1).softmax(1).float()  # [b, 16, 4, a]
+    acc = torch.zeros(b, 4, a)
+    for i in range(1, 16):
+        acc = acc + prob[:, i] * float(i)
+    return acc.half()
+
+
+def decode_from_distances(distance: torch.Tensor, cls: torch.Tensor, shapes, strides,
+                          xywh: bool = True) -> torch.Tensor:
+    """The decode after the DFL (whole_blocked.py:139-146) on CPU fp16 eager:
+    lower = anchors - lt, upper = anchors + rb, xywh ((l+u)/2, u-l) or xyxy,
+    times the level stride, then cat with sigmoid(cls)."""
     anchors, stride_row = make_anchors(shapes, strides)
-    distance = dfl(box)
     left_top, right_bottom = distance.split((2, 2), dim=1)
     lower, upper = anchors.unsqueeze(0) - left_top, anchors.unsqueeze(0) + right_bottom
     if xywh:
@@ -137,6 +154,11 @@ def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes, strides, xywh: bool
     else:
         boxes = torch.cat((lower, upper), 1) * stride_row
     return torch.cat((boxes, cls.sigmoid()), 1)
+
+
+def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes, strides, xywh: bool = True) -> torch.Tensor:
+    """anchorfree_predictions (whole_blocked.py:118-146) on CPU fp16 eager."""
+    return decode_from_distances(dfl(box), cls, shapes, strides, xywh)
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,

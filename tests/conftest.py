@@ -49,6 +49,32 @@ def ulp_diff(a: torch.Tensor, b: torch.Tensor) -> np.ndarray:
     return d
 
 
+def ulp16(t: torch.Tensor) -> torch.Tensor:
+    """Spacing of fp16 values at |t| (2^-24 in the subnormal range), as FP32."""
+    a = t.float().abs()
+    e = torch.floor(torch.log2(torch.clamp(a, min=2.0 ** -14)))
+    return torch.pow(2.0, e - 10)
+
+
+def check_bias_silu_residual(got, x, bias, residual, want):
+    """Gate of the fused y = fp16(SiLU(x + b) + r) against CPU
+    eager: |y - y_cpu| <= 2 fp16 ulp of y_cpu + 2^-18 |s| with s = SiLU(x + b) in
+    FP32, and at least 99% of outputs bit-equal.  The second term is the FP32
+    evaluation error of the SiLU value (CPU eager's own fp32 SiLU is not the
+    correctly rounded formula: its exp is a low-accuracy polynomial), which the
+    residual add passes on unscaled and which is many fp16 ulps of y wherever
+    s + r nearly cancels.  Returns the bit-equal fraction."""
+    got = got.detach().cpu()
+    b = bias.float().view(1, x.size(1), 1, 1, 16)
+    s = torch.nn.functional.silu(x.float() + b)
+    err = (got.float() - want.float()).abs()
+    bound = 2 * ulp16(want) + 2.0 ** -18 * s.abs()
+    assert bool(torch.all(err <= bound)), float((err - bound).max())
+    exact = float((got.view(torch.int16) == want.view(torch.int16)).float().mean())
+    assert exact >= 0.99, exact
+    return exact
+
+
 def assert_bits_equal(a: torch.Tensor, b: torch.Tensor, what: str = "") -> None:
     assert a.shape == b.shape and a.dtype == b.dtype, (what, a.shape, b.shape, a.dtype, b.dtype)
     x = a.detach().cpu().contiguous().reshape(-1).view(torch.uint8)

@@ -11,7 +11,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from conftest import assert_bits_equal, half_bits, ulp_diff
+from conftest import assert_bits_equal, check_bias_silu_residual, half_bits, ulp_diff
 from oracle import ops as oops
 
 pytestmark = pytest.mark.gpu
@@ -159,10 +159,7 @@ def test_config1_bias_silu_residual(device):
     r = oops.to_blocked(torch.randn(1, 128, 80, 80, generator=g).half())
     b = (torch.randn(128, generator=g) * 0.1).half()
     got = ttn.bias_silu_residual(x.to(device), b.to(device), r.to(device))
-    want = oops.bias_silu_residual(x, b, r)
-    d = ulp_diff(got, want)
-    assert d.max() <= 2, d.max()
-    assert (d == 0).mean() > 0.99
+    check_bias_silu_residual(got, x, b, r, oops.bias_silu_residual(x, b, r))
 
 
 @pytest.mark.parametrize("dtype", [torch.float32])

@@ -93,3 +93,29 @@ def test_dfl_decode_oracle_shapes_and_anchor_points():
     # uniform bins -> distance 7.5 per side: w = h = 15 * stride, centre = anchor * stride
     assert float(out[0, 2, 0]) == 15 * 8 and float(out[0, 0, 0]) == 0.5 * 8
     assert torch.all(out[0, 4:] == 0.5)
+
+
+@pytest.mark.parametrize("scale", [0.5, 2.0, 6.0])
+def test_dfl_sequential_order_equals_cpu_conv(scale):
+    """The reference-order restatement of the DFL expectation (sequential FP32 sum
+    of p_i * i) gives the same bits as CPU eager's fp16 1x1 arange conv, so the
+    CPU chain's expectation order is the reference's; also for the special rows
+    of verify_dfl_softmax.py (NaN, -inf, zeros, large shifts)."""
+    g = torch.Generator().manual_seed(int(scale * 10))
+    box = (torch.randn(3, 64, 2100, generator=g) * scale).half()
+    box[0, 5, 7] = float("nan")
+    box[1, 16:32, 9] = float("-inf")
+    box[1, 32:48, 11] = 0
+    box[2, :, 13] = 6000
+    assert torch.equal(oops.dfl_sequential(box).view(torch.int16), oops.dfl(box).view(torch.int16))
+
+
+def test_decode_is_distances_then_anchor_arithmetic():
+    g = torch.Generator().manual_seed(3)
+    shapes, strides = [(8, 8), (4, 4), (2, 2)], [8.0, 16.0, 32.0]
+    box = (torch.randn(2, 64, 84, generator=g) * 2).half()
+    cls = (torch.randn(2, 5, 84, generator=g) * 3).half()
+    for xywh in (True, False):
+        whole = oops.dfl_decode(box, cls, shapes, strides, xywh)
+        parts = oops.decode_from_distances(oops.dfl_sequential(box), cls, shapes, strides, xywh)
+        assert torch.equal(whole.view(torch.int16), parts.view(torch.int16))

@@ -29,8 +29,7 @@ def test_yolov8s_pass_matches_cpu_eager(device, batch):
         if step.output is not None:
             assert_bits_equal(gpu.buffers[step.output], buffers[step.output], f"{step.op} {step.output}")
     assert_bits_equal(gpu.head, head, "head")
-    _, stride_row = oops.make_anchors(plan.levels, plan.strides)
-    _check_decode(out, want, stride_row, plan.nc)
+    _check_decode(out, want, plan.levels, plan.strides)
 
 
 def test_yolov8s_pass_graph_replay_equals_eager(device):
@@ -55,8 +54,7 @@ def test_smaller_resolution_pass(device):
     out = gpu.run()
     want, buffers, head = oyolo.run_pass(plan, inputs, keep=True)
     assert_bits_equal(gpu.head, head, "head")
-    _, stride_row = oops.make_anchors(plan.levels, plan.strides)
-    _check_decode(out, want, stride_row, plan.nc)
+    _check_decode(out, want, plan.levels, plan.strides)
 
 
 @pytest.mark.parametrize("batch", [1, 3])

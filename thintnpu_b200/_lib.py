@@ -30,7 +30,7 @@ EXPORTS = (
     "ttn_bias_silu_residual_nc1hwc0_f16",
     "ttn_copy", "ttn_cat", "ttn_nc1hwc0_to_nchw_f16", "ttn_nchw_to_nc1hwc0_f16",
     "ttn_upsample2x", "ttn_upsample2x_nc1hwc0_f16", "ttn_maxpool", "ttn_sppf_f16",
-    "ttn_softmax", "ttn_dfl_decode_f16", "ttn_attention_f16", "ttn_attention_fault_f16",
+    "ttn_softmax", "ttn_dfl_decode_f16", "ttn_dfl_decode_trace_f16", "ttn_attention_f16", "ttn_attention_fault_f16",
     "ttn_conv2d_nc1hwc0_f16", "ttn_conv2d_residual_nc1hwc0_f16", "ttn_conv2d_pack_weights_f16",
     "ttn_conv2d_fault_f16", "ttn_depthwise_nc1hwc0_f16",
     "ttn_select_workspace_size", "ttn_select_f16", "ttn_select_f16_static",
@@ -94,6 +94,9 @@ _SIGNATURES = {
     "ttn_dfl_decode_f16": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I32,
                                           ctypes.POINTER(_I64), ctypes.POINTER(_I64),
                                           ctypes.POINTER(ctypes.c_float), _I32, _P, _P]),
+    "ttn_dfl_decode_trace_f16": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I32,
+                                                ctypes.POINTER(_I64), ctypes.POINTER(_I64),
+                                                ctypes.POINTER(ctypes.c_float), _I32, _P, _P, _P]),
     "ttn_attention_f16": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, ctypes.POINTER(_I64),
                                          ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
                                          ctypes.c_float, ctypes.c_uint32, _P]),

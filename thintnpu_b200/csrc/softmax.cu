@@ -381,7 +381,7 @@ template <int APT>
 __global__ void __launch_bounds__(128) dfl_decode(const __half* box, int64_t box_bs, int64_t box_cs,
                                                   const __half* cls, int64_t cls_bs, int64_t cls_cs,
                                                   int64_t n, int64_t nc, int64_t anchors, Levels lv,
-                                                  bool xywh, __half* out) {
+                                                  bool xywh, __half* out, __half* dist_out) {
   const int64_t groups = (anchors + APT - 1) / APT;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n * groups; t += stride) {
@@ -414,6 +414,10 @@ __global__ void __launch_bounds__(128) dfl_decode(const __half* box, int64_t box
       if (a >= anchors) {
         res[0][k] = res[1][k] = res[2][k] = res[3][k] = 0.0f;
         continue;
+      }
+      if (dist_out) {
+#pragma unroll
+        for (int sd = 0; sd < 4; ++sd) dist_out[(b * 4 + sd) * anchors + a] = __float2half_rn(dist[sd][k]);
       }
       int l = 0;
       while (l + 1 < lv.count && a >= lv.start[l + 1]) ++l;
@@ -505,7 +509,7 @@ constexpr int kTileA = 128;
 
 __global__ void __launch_bounds__(256) dfl_box_tiled(const __half* box, int64_t box_bs, int64_t box_cs,
                                                      int n, int anchors, Levels lv, bool xywh,
-                                                     __half* out, int64_t out_bs) {
+                                                     __half* out, int64_t out_bs, __half* dist_out) {
   __shared__ __align__(16) uint16_t in_box[2][64][kTileA];
   __shared__ float dist[4][kTileA];
   __shared__ __align__(16) uint16_t out_box[4][kTileA];
@@ -545,6 +549,11 @@ __global__ void __launch_bounds__(256) dfl_box_tiled(const __half* box, int64_t 
     __syncthreads();
     if (tid < kTileA) {  // box decode: thread -> anchor
       const int a = tid, idx = a0 + a;
+      if (dist_out && idx < anchors) {  // trace: the four DFL distances of this anchor
+#pragma unroll
+        for (int side = 0; side < 4; ++side)
+          dist_out[((int64_t)b * 4 + side) * anchors + idx] = __float2half_rn(dist[side][a]);
+      }
       int lstart = 0, lwidth = (int)lv.width[0];
       float lstride = lv.stride[0];
 #pragma unroll
@@ -704,11 +713,12 @@ ttn_status ttn_softmax(const ttn_tensor* x, int32_t dim, float scale, const ttn_
   return launch_softmax<float, float>(x, y, dim, scale, s);
 }
 
-ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs, const void* cls,
-                              int64_t cls_bs, int64_t cls_cs, int64_t n, int64_t nc,
-                              int32_t levels, const int64_t* heights, const int64_t* widths,
-                              const float* strides, int32_t xywh, void* out, ttn_stream stream) {
-  const char* name = "ttn_dfl_decode_f16";
+ttn_status ttn_dfl_decode_trace_f16(const void* box, int64_t box_bs, int64_t box_cs, const void* cls,
+                                    int64_t cls_bs, int64_t cls_cs, int64_t n, int64_t nc,
+                                    int32_t levels, const int64_t* heights, const int64_t* widths,
+                                    const float* strides, int32_t xywh, void* out, void* distances,
+                                    ttn_stream stream) {
+  const char* name = distances ? "ttn_dfl_decode_trace_f16" : "ttn_dfl_decode_f16";
   if (n < 0 || nc < 0) return fail(TTN_INVALID_ARG, "%s: negative size", name);
   if (levels < 1 || levels > kMaxLevels || !heights || !widths || !strides)
     return fail(TTN_INVALID_ARG, "%s: 1..%d levels with heights/widths/strides", name, kMaxLevels);
@@ -747,7 +757,7 @@ ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs, c
                                          nc, anchors, aux)
                        : TTN_OK;
     dfl_box_tiled<<<grid, 256, 0, s>>>((const __half*)box, box_bs, box_cs, (int)n, (int)anchors, lv,
-                                       xywh != 0, (__half*)out, (4 + nc) * anchors);
+                                       xywh != 0, (__half*)out, (4 + nc) * anchors, (__half*)distances);
     ttn_status launched = launch_check(name);
     ttn_status joined = nc ? branch_join(s) : TTN_OK;
     return st != TTN_OK ? st : launched != TTN_OK ? launched : joined;
@@ -756,14 +766,22 @@ ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs, c
     int64_t work = n * (anchors / 2);
     dfl_decode<2><<<grid_for(work, 128, 16), 128, 0, s>>>(
         (const __half*)box, box_bs, box_cs, (const __half*)cls, cls_bs, cls_cs, n, nc, anchors, lv,
-        xywh != 0, (__half*)out);
+        xywh != 0, (__half*)out, (__half*)distances);
   } else {
     int64_t work = n * anchors;
     dfl_decode<1><<<grid_for(work, 128, 16), 128, 0, s>>>(
         (const __half*)box, box_bs, box_cs, (const __half*)cls, cls_bs, cls_cs, n, nc, anchors, lv,
-        xywh != 0, (__half*)out);
+        xywh != 0, (__half*)out, (__half*)distances);
   }
   return launch_check(name);
+}
+
+ttn_status ttn_dfl_decode_f16(const void* box, int64_t box_bs, int64_t box_cs, const void* cls,
+                              int64_t cls_bs, int64_t cls_cs, int64_t n, int64_t nc,
+                              int32_t levels, const int64_t* heights, const int64_t* widths,
+                              const float* strides, int32_t xywh, void* out, ttn_stream stream) {
+  return ttn_dfl_decode_trace_f16(box, box_bs, box_cs, cls, cls_bs, cls_cs, n, nc, levels, heights, widths,
+                                  strides, xywh, out, nullptr, stream);
 }
 
 }  // extern "C"

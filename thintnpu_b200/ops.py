@@ -494,12 +494,14 @@ def conv2d_fault() -> int:
 
 def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes: Sequence[tuple],
                strides: Sequence[float], xywh: bool = True,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None, distances: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Detect decode: DFL(16) softmax + expectation, anchor decode, sigmoid(cls).
 
     box [n, 64, a] and cls [n, nc, a] fp16 logits (any batch/channel strides,
     unit anchor stride); shapes = [(h, w)] per level; strides per level.
-    Returns [n, 4+nc, a] = cat(boxes*stride, sigmoid(cls)) (whole_blocked.py:118-146)."""
+    Returns [n, 4+nc, a] = cat(boxes*stride, sigmoid(cls)) (whole_blocked.py:118-146).
+    ``distances`` (fp16 [n, 4, a], contiguous) also receives the DFL expectations
+    the boxes were decoded from (the trace entry point)."""
     for t, name in ((box, "box"), (cls, "cls")):
         _cuda(t, "dfl_decode")
         _require(t.dtype == torch.float16 and t.dim() == 3 and t.stride(2) == 1,
@@ -516,9 +518,17 @@ def dfl_decode(box: torch.Tensor, cls: torch.Tensor, shapes: Sequence[tuple],
     strides_c = (ctypes.c_float * levels)(*[float(s) for s in strides])
     y = torch.empty((n, 4 + nc, a), dtype=torch.float16, device=box.device) if out is None else out
     _require(y.is_contiguous() and tuple(y.shape) == (n, 4 + nc, a), "dfl_decode: bad out")
-    call("ttn_dfl_decode_f16", box.data_ptr(), box.stride(0), box.stride(1), cls.data_ptr(),
+    if distances is None:
+        call("ttn_dfl_decode_f16", box.data_ptr(), box.stride(0), box.stride(1), cls.data_ptr(),
+             cls.stride(0), cls.stride(1), n, nc, levels, heights, widths, strides_c, int(bool(xywh)),
+             y.data_ptr(), stream())
+        return y
+    _cuda(distances, "dfl_decode")
+    _require(distances.dtype == torch.float16 and distances.is_contiguous() and tuple(distances.shape) == (n, 4, a),
+             "dfl_decode: distances must be contiguous fp16 [n, 4, anchors]")
+    call("ttn_dfl_decode_trace_f16", box.data_ptr(), box.stride(0), box.stride(1), cls.data_ptr(),
          cls.stride(0), cls.stride(1), n, nc, levels, heights, widths, strides_c, int(bool(xywh)),
-         y.data_ptr(), stream())
+         y.data_ptr(), distances.data_ptr(), stream())
     return y
 
 
