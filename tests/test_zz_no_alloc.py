@@ -6,11 +6,20 @@ start-up -- use this entry point; its scratch is an array compiled into the
 library.  Through the C ABI, two calls in a row must give exactly (bit for bit,
 the selection tolerance) what ttn_select_f16 gives with a caller-owned
 workspace; the second call runs on the scratch the first one left behind.
+The large-k path (max_det 8400 over 8400 anchors: the 65,536-bin histogram and
+the counting-sort scratch) is rerun on the array a previous call left dirty.
+A first call under stream capture in a context must be refused (the address
+lookup happens outside capture); that runs in a fresh child process, whose
+context has never called the entry point.
 This file is collected last so a stop-at-first-failure run has already run
 every other test; it also passes alone in a fresh process."""
 from __future__ import annotations
 
 import ctypes
+import subprocess
+import sys
+import textwrap
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -70,3 +79,49 @@ def test_static_scratch_rejects_oversized_batch(device):
     status = lib.ttn_select_f16_static(ctypes.byref(d), 300, 0, out.data_ptr(), None, stream())
     assert status == 2  # TTN_UNSUPPORTED
     assert b"static scratch holds" in lib.ttn_last_error()
+
+
+@pytest.mark.parametrize("flags", [0, 4])
+def test_static_scratch_large_k_twice(device, flags):
+    """Class-aware, max_det = anchors = 8400 (7.2 MB of scratch): two calls in a
+    row, each after a different-sized call dirtied the array, equal the
+    workspace entry point bit for bit."""
+    from thintnpu_b200 import _lib
+    lib = _lib.lib()
+    assert lib.ttn_select_workspace_size(1, 8400, 80, 8400, flags) <= 8 << 20
+    for call, seed in enumerate((41, 42)):
+        _run(lib, "ttn_select_f16_static", _logits(2, seed + 10).to(device).transpose(1, 2), 300, flags, True)
+        decoded = _logits(1, seed).to(device).transpose(1, 2)
+        want = _run(lib, "ttn_select_f16", decoded, 8400, flags, use_static=False)
+        got = _run(lib, "ttn_select_f16_static", decoded, 8400, flags, use_static=True)
+        assert np.array_equal(got, want), f"call {call + 1} differs"
+
+
+_CAPTURE_CHILD = textwrap.dedent("""
+    import ctypes, sys
+    import torch
+    sys.path.insert(0, sys.argv[1])
+    from thintnpu_b200 import _lib
+    from thintnpu_b200.ops import desc, stream
+    lib = _lib.lib()
+    x = torch.zeros(1, 84, 8400, dtype=torch.float16, device="cuda").transpose(1, 2)
+    out = torch.empty(1, 300, 6, dtype=torch.float32, device="cuda")
+    d = desc(x)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        status = lib.ttn_select_f16_static(ctypes.byref(d), 300, 0, out.data_ptr(), None, stream())
+        message = lib.ttn_last_error().decode()
+    after = lib.ttn_select_f16_static(ctypes.byref(d), 300, 0, out.data_ptr(), None, stream())
+    torch.cuda.synchronize()
+    print(status, after, message)
+""")
+
+
+def test_static_scratch_first_call_under_capture_is_refused(device):
+    root = Path(__file__).resolve().parent.parent
+    done = subprocess.run([sys.executable, "-c", _CAPTURE_CHILD, str(root)], capture_output=True, text=True,
+                          timeout=300)
+    assert done.returncode == 0, done.stderr[-2000:]
+    status, after, message = done.stdout.strip().splitlines()[-1].split(" ", 2)
+    assert status == "1" and "outside capture" in message, done.stdout  # TTN_INVALID_ARG
+    assert after == "0", done.stdout  # a call outside capture then succeeds

@@ -18,11 +18,19 @@
 //    on one stream are ordered and safe;
 //  * the array keeps the previous call's contents: the selection kernels write
 //    every scratch word they read, so nothing has to start at zero;
-//  * the first call on a device resolves the array's device address with
-//    cudaGetSymbolAddress (once per device, with that device current), so make
-//    that first call before any stream capture.
+//  * the array's device address belongs to the CUDA context current on the
+//    calling thread (the device's primary context, or a context the host made
+//    with the driver API).  Outside stream capture every call looks it up afresh
+//    with cudaGetSymbolAddress (a host-side lookup that allocates nothing), so a
+//    context created later, or re-created by cudaDeviceReset, gets its own
+//    address; the lookup is remembered per context.  Under stream capture no
+//    lookup is made: the address remembered for the current context is used,
+//    and if there is none (no call yet outside capture in this context) the call
+//    is rejected with TTN_INVALID_ARG -- make one call outside capture first.
 // The entry point itself calls no cudaMalloc, cudaFree or other allocating
 // routine.
+#include <cuda.h>  // CUcontext / CUresult types; the driver call is reached through the runtime
+
 #include <mutex>
 
 #include "common.cuh"
@@ -36,21 +44,58 @@ constexpr size_t kStaticScratchBytes = (size_t)8 << 20;
 // kernels must be given the address from cudaGetSymbolAddress.
 __device__ __align__(256) unsigned char g_select_scratch[kStaticScratchBytes];
 
-ttn_status scratch_address(void** out) {
+// The calling thread's current context (NULL when none is bound yet), through
+// the driver's cuCtxGetCurrent as the runtime exposes it (no libcuda link).
+ttn_status current_context(CUcontext* ctx) {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  static GetCurrent get_current = nullptr;
+  static std::once_flag once;
+  static cudaError_t lookup = cudaSuccess;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult found = cudaDriverEntryPointSymbolNotFound;
+    lookup = cudaGetDriverEntryPoint("cuCtxGetCurrent", (void**)&get_current, cudaEnableDefault, &found);
+    if (lookup == cudaSuccess && found != cudaDriverEntryPointSuccess) lookup = cudaErrorNotSupported;
+  });
+  TTN_TRY(cuda_check(lookup, "ttn_select_f16_static: cuCtxGetCurrent entry point"));
+  if (get_current(ctx) != CUDA_SUCCESS)
+    return fail(TTN_CUDA_ERROR, "ttn_select_f16_static: cuCtxGetCurrent failed");
+  return TTN_OK;
+}
+
+ttn_status scratch_address(cudaStream_t stream, void** out) {
   static std::mutex mutex;
-  static void* address[64] = {nullptr};
-  int device = 0;
-  TTN_TRY(cuda_check(cudaGetDevice(&device), "ttn_select_f16_static: cudaGetDevice"));
-  if (device < 0 || device >= 64)
-    return fail(TTN_UNSUPPORTED, "ttn_select_f16_static: device index %d out of range", device);
+  static CUcontext contexts[64] = {nullptr};
+  static void* addresses[64] = {nullptr};
+  static int used = 0;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  TTN_TRY(cuda_check(cudaStreamIsCapturing(stream, &capture), "ttn_select_f16_static: cudaStreamIsCapturing"));
+  CUcontext ctx = nullptr;
+  TTN_TRY(current_context(&ctx));
   std::lock_guard<std::mutex> lock(mutex);
-  if (!address[device]) {
-    void* p = nullptr;
-    TTN_TRY(cuda_check(cudaGetSymbolAddress(&p, g_select_scratch),
-                       "ttn_select_f16_static: cudaGetSymbolAddress"));
-    address[device] = p;
+  int slot = -1;
+  for (int i = 0; i < used; ++i)
+    if (ctx && contexts[i] == ctx) slot = i;
+  if (capture != cudaStreamCaptureStatusNone) {
+    if (slot < 0)
+      return fail(TTN_INVALID_ARG,
+                  "ttn_select_f16_static: first call in this CUDA context made during stream capture; "
+                  "make one call outside capture first (it resolves the scratch address)");
+    *out = addresses[slot];
+    return TTN_OK;
   }
-  *out = address[device];
+  void* p = nullptr;
+  TTN_TRY(cuda_check(cudaGetSymbolAddress(&p, g_select_scratch), "ttn_select_f16_static: cudaGetSymbolAddress"));
+  if (!ctx) TTN_TRY(current_context(&ctx));  // the lookup bound the device's primary context
+  if (slot < 0) {
+    for (int i = 0; i < used; ++i)
+      if (contexts[i] == ctx) slot = i;
+  }
+  if (slot < 0) {
+    slot = used < 64 ? used++ : 63;  // beyond 64 contexts the last entry is reused
+    contexts[slot] = ctx;
+  }
+  addresses[slot] = p;
+  *out = p;
   return TTN_OK;
 }
 
@@ -76,6 +121,6 @@ extern "C" ttn_status ttn_select_f16_static(const ttn_tensor* decoded, int64_t m
                 "(split the batch, or call ttn_select_f16 with your own workspace)",
                 name, need, kStaticScratchBytes);
   void* scratch = nullptr;
-  TTN_TRY(scratch_address(&scratch));
+  TTN_TRY(scratch_address((cudaStream_t)stream, &scratch));
   return ttn_select_f16(decoded, max_det, flags, scratch, kStaticScratchBytes, out, trace, stream);
 }
