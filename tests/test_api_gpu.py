@@ -152,7 +152,7 @@ def test_aten_routing_matches_cpu_and_routes(device):
 def test_frozen_graph_region_contract(device):
     from thintnpu_b200.aten import aten_routing
     from thintnpu_b200.graph import FrozenGraph, RegionContract
-    conv = torch.nn.Conv2d(16, 16, 1).half().to(device).requires_grad_(False)
+    conv = torch.nn.Conv2d(16, 16, 1).half().to(device).requires_grad_(False).eval()
 
     def forward(x):
         return torch.sigmoid(x) + x
@@ -163,11 +163,58 @@ def test_frozen_graph_region_contract(device):
         frozen = FrozenGraph(pilot, forward, x)
         out = frozen.replay().clone()
         assert_bits_equal(out, forward(x))
+        assert_bits_equal(frozen(x * 2).clone(), forward(x * 2))
         with torch.no_grad():
             conv.weight.add_(1)
-        with pytest.raises(RuntimeError, match="changed"):
+        with pytest.raises(ValueError, match="version or gradient mode changed"):
             frozen.replay()
         frozen.close()
+
+
+def _contract_breakers():
+    """(description, mutation, expected message) for RegionContract.validate."""
+    def replace_weight(m):
+        m.weight = torch.nn.Parameter(m.weight.detach().clone(), requires_grad=False)
+
+    def hook(m):
+        m.register_forward_hook(lambda *a: None)
+
+    def rebind(m):
+        m.forward = lambda x: x
+
+    def add_child(m):
+        m.extra = torch.nn.Identity()
+
+    return [("in-place update", lambda m: m.weight.mul_(1), "version or gradient mode changed"),
+            ("replaced parameter", replace_weight, "identity changed"),
+            ("stride", lambda m: setattr(m, "stride", (2, 2)), "operator configuration changed"),
+            ("training mode", lambda m: m.train(), "inference-only"),
+            ("forward hook", hook, "hooks changed"),
+            ("rebound forward", rebind, "forward changed"),
+            ("new child", add_child, "children changed")]
+
+
+@pytest.mark.parametrize("case", range(7))
+def test_region_contract_detects_each_change(device, case):
+    from thintnpu_b200.graph import RegionContract
+    name, mutate, message = _contract_breakers()[case]
+    conv = torch.nn.Conv2d(16, 16, 3, padding=1).half().to(device).requires_grad_(False).eval()
+    pilot = RegionContract([torch.nn.Sequential(conv).eval()])
+    pilot.validate()
+    with torch.no_grad():
+        mutate(conv)
+    with pytest.raises(ValueError, match=message):
+        pilot.validate()
+
+
+def test_region_contract_rejects_unprepared_parameters(device):
+    from thintnpu_b200.graph import RegionContract
+    with pytest.raises(ValueError, match="FP16 CUDA inference"):
+        RegionContract([torch.nn.Conv2d(16, 16, 1).half().to(device)])  # requires_grad
+    with torch.inference_mode():
+        inference = torch.nn.Conv2d(16, 16, 1).half().to(device)
+    with pytest.raises(ValueError, match="no_grad"):
+        RegionContract([inference])
 
 
 def test_bias_silu_residual_via_torch_ops(device):
