@@ -176,3 +176,64 @@ def test_c2f_region_equals_reference_op_sequence(device, b, c_in, c, n, c_out, h
     cpu = ccv(torch.cat(ys, 1), cv2).float()
     diff = (got.cpu().float() - cpu).norm() / cpu.norm()
     assert diff < 2e-3, float(diff)
+
+
+@pytest.mark.parametrize("ci,co,k,stride,bias", [(32, 64, 3, 2, True), (64, 80, 1, 1, False), (3, 32, 3, 2, True),
+                                                  (128, 128, 3, 1, True)])
+def test_aten_convolution_routing(device, ci, co, k, stride, bias):
+    """aten::convolution (aten_adapter.cpp:106-112) routed to the tensor-core conv:
+    F.conv2d / nn.Conv2d on fp16 CUDA tensors inside aten_routing(), NCHW in and out,
+    no activation; the packed weight is reused while the weight is unchanged."""
+    from thintnpu_b200 import aten
+    x, wt, bs = _case(2, ci, co, 20, 24, k, 7 + ci, bias)
+    conv = torch.nn.Conv2d(ci, co, k, stride, (k - 1) // 2, bias=bias).half().to(device).requires_grad_(False)
+    with torch.no_grad():
+        conv.weight.copy_(wt)
+        if bias:
+            conv.bias.copy_(bs)
+    before = aten.ROUTED.get("aten::convolution", 0)
+    with torch.inference_mode(), aten.aten_routing():
+        got = conv(x.to(device))
+        again = conv(x.to(device))
+    assert aten.ROUTED["aten::convolution"] == before + 2
+    assert torch.equal(got, again)
+    _check(got, x, wt, bs, stride, silu=False)
+
+
+def test_aten_convolution_rejects_unsupported(device):
+    from thintnpu_b200 import aten
+    x = torch.randn(1, 16, 8, 8, device=device).half()
+    w = torch.randn(16, 16, 3, 3, device=device).half()
+    with torch.inference_mode(), aten.aten_routing():
+        with pytest.raises(RuntimeError, match="transposed/groups"):
+            F.conv2d(x, w[:, :8], None, 1, 1, 1, 2)
+        with pytest.raises(RuntimeError, match="dilation"):
+            F.conv2d(x, w, None, 1, 2, 2)
+        with pytest.raises(RuntimeError, match="k1/p0 stride 1 or k3/p1"):
+            F.conv2d(x, torch.randn(16, 16, 5, 5, device=device).half(), None, 1, 2)
+        y = F.conv2d(x.float(), w.float(), None, 1, 1)  # fp32 stays with PyTorch
+    assert y.dtype == torch.float32
+
+
+def test_torch_ops_conv_schemas(device):
+    """thin_native_flow::conv / depthwise / pack_input and thin_blocked::conv
+    (conv_flow.cpp:630-646, depthwise_flow.cpp:225-233, conv_blocked.cpp:198-210)."""
+    import thintnpu_b200 as ttn
+    from thintnpu_b200 import library  # noqa: F401
+    nf, bl = torch.ops.thin_native_flow, torch.ops.thin_blocked
+    x, wt, bs = _case(1, 64, 128, 16, 16, 3, 11)
+    xb = nf.pack_input(x.to(device))
+    assert torch.equal(xb.cpu(), oops.pack_padded(x))
+    packed = ttn.conv2d_pack_weights(wt.to(device))
+    y = nf.conv(xb, packed, bs.to(device), 128, 3, 1)
+    _check(oops.from_blocked(y.cpu()), x, wt, bs, 1, True)
+    y_nchw = nf.conv(xb, packed, bs.to(device), 128, 3, 2, False, True)
+    _check(y_nchw, x, wt, bs, 2, False)
+    y_blocked = bl.conv(xb, packed, bs.to(device), 128, 3, 1, False, True)
+    assert torch.equal(y_blocked, y)
+    with pytest.raises(RuntimeError, match="FP16 output"):
+        bl.conv(xb, packed, bs.to(device), 128, 3, 1, True, True)
+    xd = torch.randn(1, 4, 16, 16, 16, generator=torch.Generator().manual_seed(3)).half()
+    wd = (torch.randn(64, 1, 3, 3, generator=torch.Generator().manual_seed(4)) / 3).half()
+    got = nf.depthwise(xd.to(device), ttn.depthwise_pack_weights(wd.to(device)), None, 3, 1, False)
+    assert torch.equal(got.cpu().view(torch.int16), oops.depthwise(xd, wd, None, 3, 1, False).view(torch.int16))

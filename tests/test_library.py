@@ -12,9 +12,10 @@ def test_schemas_and_dispatch_keys():
         for key in ("CUDA", "AutogradCUDA", "Meta"):
             assert torch._C._dispatch_has_kernel_for_dispatch_key("thin_backend::" + op, key), (op, key)
     for op in ("maxpool", "upsample", "detection_select", "detection_select_trace", "silu_", "sppf",
-               "softmax", "dfl_decode", "bias_silu_residual"):
-        assert torch._C._dispatch_has_kernel_for_dispatch_key("thin_native_flow::" + op, "CUDA"), op
-    for op in ("pack", "unpack"):
+               "softmax", "dfl_decode", "bias_silu_residual", "conv", "depthwise", "pack_input"):
+        for key in ("CUDA", "AutogradCUDA", "Meta"):
+            assert torch._C._dispatch_has_kernel_for_dispatch_key("thin_native_flow::" + op, key), (op, key)
+    for op in ("pack", "unpack", "conv"):
         assert torch._C._dispatch_has_kernel_for_dispatch_key("thin_blocked::" + op, "Meta"), op
 
 
@@ -36,20 +37,34 @@ def test_meta_shapes():
     dec = torch.ops.thin_native_flow.dfl_decode(meta(2, 64, 8400), meta(2, 80, 8400), [80, 40, 20],
                                                 [80, 40, 20], [8.0, 16.0, 32.0])
     assert dec.shape == (2, 84, 8400)
+    nf, bl = torch.ops.thin_native_flow, torch.ops.thin_blocked
+    x = meta(2, 8, 40, 40, 16)
+    assert nf.conv(x, meta(8, 9, 128, 16), meta(128), 128, 3, 2).shape == (2, 8, 20, 20, 16)
+    assert nf.conv(x, meta(8, 1, 128, 16), None, 80, 1, 1, False, True).shape == (2, 80, 40, 40)
+    assert nf.depthwise(x, meta(8, 3, 3, 16), meta(128), 3, 1).shape == (2, 8, 40, 40, 16)
+    assert nf.depthwise(x, meta(8, 5, 5, 16), None, 5, 2).shape == (2, 8, 20, 20, 16)
+    assert bl.conv(x, meta(8, 1, 256, 16), meta(256), 256, 1, 1, False, True).shape == (2, 16, 40, 40, 16)
+    assert nf.pack_input(meta(1, 3, 64, 64)).shape == (1, 1, 64, 64, 16)
 
 
 def test_import_thin_backend_registers_and_routes():
-    """``import thin_backend`` works like the reference's import side effect."""
+    """``import thin_backend`` registers the namespaces and loads the library like the
+    reference's import; ATen routing stays off unless THIN_BACKEND_ATEN=1."""
     import subprocess
     import sys
     code = ("import torch, thin_backend\n"
             "from thintnpu_b200 import aten\n"
             "assert thin_backend.device == 'cuda'\n"
-            "assert aten._GLOBAL is not None\n"
+            "import os\n"
+            "assert (aten._GLOBAL is not None) == (os.environ.get('THIN_BACKEND_ATEN') == '1')\n"
             "assert torch._C._dispatch_has_kernel_for_dispatch_key('thin_native_flow::detection_select', 'CUDA')\n"
             "from thin_backend.graph import CapturedForward\n"
             "from thin_backend.blocked_graph import FrozenGraph\n"
             "print('ok')\n")
+    import os
     from conftest import ROOT
-    done = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
-    assert done.returncode == 0 and "ok" in done.stdout, done.stderr
+    for flag in ("0", "1"):
+        env = dict(os.environ, THIN_BACKEND_ATEN=flag)
+        done = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300,
+                              env=env)
+        assert done.returncode == 0 and "ok" in done.stdout, done.stderr

@@ -2,12 +2,16 @@
 
 The reference overrides these ATen ops for its PrivateUse1 device
 (aten_adapter.cpp:106-112, ops.cpp:513-524, softmax_host.cpp:90-92,
-backend.cpp:357-361).  On CUDA the same routing is a dispatch mode, active
-inside ``with aten_routing():`` (or globally after ``enable_aten_routing()``):
+backend.cpp:357-361).  On CUDA tensors, which PyTorch's own kernels also serve,
+the routing is opt-in: a dispatch mode, active inside ``with aten_routing():``
+or after ``enable_aten_routing()`` (``import thin_backend`` turns it on only
+when ``THIN_BACKEND_ATEN=1``), so code that does not ask for it pays nothing:
 
     silu, silu_, sigmoid, add/sub/mul/div.Tensor (and .Scalar), cat, _softmax,
     max_pool2d and max_pool2d_with_indices (k5/s1/p2 only; indices are a zero
-    placeholder), upsample_nearest2d (2x only), copy_ (device to device, same dtype)
+    placeholder), upsample_nearest2d (2x only), copy_ (device to device, same
+    dtype), convolution (fp16, k1/p0 stride 1 or k3/p1 stride 1/2, groups 1: the
+    tensor-core conv of ttn_conv2d_nc1hwc0_f16 with NCHW output)
 
 for float16/float32 CUDA tensors.  Calls with unsupported arguments raise, as
 the reference's TORCH_CHECKs do; other dtypes, devices and ops are left to
@@ -191,6 +195,59 @@ def _h_upsample_vec(args, kwargs):
     return _upsample(x, list(output_size))
 
 
+_PACKED_WEIGHTS: Dict[tuple, torch.Tensor] = {}
+
+
+def _packed_weight(w: torch.Tensor) -> torch.Tensor:
+    """The prepared conv layout of an OIHW weight, built once per (storage,
+    version, shape) and kept while that weight is unchanged."""
+    try:
+        version = w._version
+    except RuntimeError:  # an inference tensor has no version counter: pack every call
+        return ops.conv2d_pack_weights(ops.contiguous(w))
+    key = (w.data_ptr(), version, tuple(w.shape), tuple(w.stride()))
+    packed = _PACKED_WEIGHTS.get(key)
+    if packed is None:
+        if len(_PACKED_WEIGHTS) > 256:
+            _PACKED_WEIGHTS.clear()
+        packed = _PACKED_WEIGHTS[key] = ops.conv2d_pack_weights(ops.contiguous(w))
+    return packed
+
+
+def _h_convolution(args, kwargs):
+    names = ("input", "weight", "bias", "stride", "padding", "dilation", "transposed", "output_padding", "groups")
+    a = dict(zip(names, args), **kwargs)
+    x, w, bias = a["input"], a["weight"], a.get("bias")
+    if not (_ours(x, w) and x.dtype == torch.float16 and w.dtype == torch.float16):
+        return NotImplemented
+    if bias is not None and not (_ours(bias) and bias.dtype == torch.float16):
+        return NotImplemented
+    if a["transposed"] or a["groups"] != 1:
+        raise RuntimeError("thin aten convolution: transposed/groups are unsupported")
+    if x.dim() != 4 or w.dim() != 4:
+        raise RuntimeError("thin aten convolution requires 2D NCHW/OIHW")
+    s, p = _square(a["stride"], "stride"), _square(a["padding"], "padding")
+    if _square(a["dilation"], "dilation") != 1 or any(v != 0 for v in a["output_padding"]):
+        raise RuntimeError("thin aten convolution requires dilation=1 and output_padding=0")
+    k = w.size(2)
+    if not ((k == 1 and p == 0 and s == 1) or (k == 3 and w.size(3) == 3 and p == 1 and s in (1, 2))):
+        raise RuntimeError("thin aten convolution supports only k1/p0 stride 1 or k3/p1 stride 1/2")
+    _trace("aten::convolution", "ttn_conv2d_nc1hwc0_f16 (NCHW output)")
+    co = w.size(0)
+    return ops.conv2d(ops.pack(x), _packed_weight(w), None if bias is None else ops.contiguous(bias), co, k, s,
+                      silu=False, nchw=True)
+
+
+def _h_conv2d(args, kwargs):
+    """aten::conv2d (what nn.Conv2d / F.conv2d reach first): the convolution above."""
+    names = ("input", "weight", "bias", "stride", "padding", "dilation", "groups")
+    a = dict(zip(names, args), **kwargs)
+    pair = lambda v, d: list(v) if isinstance(v, (list, tuple)) else [v if v is not None else d]
+    return _h_convolution((a["input"], a["weight"], a.get("bias"), pair(a.get("stride", 1), 1),
+                           pair(a.get("padding", 0), 0), pair(a.get("dilation", 1), 1), False, [0, 0],
+                           a.get("groups", 1)), {})
+
+
 def _h_copy(args, kwargs):
     dst, src = args[0], args[1]
     if not (_ours(dst, src) and dst.dtype == src.dtype and dst.shape == src.shape and dst.device == src.device):
@@ -219,6 +276,8 @@ _HANDLERS = {
     aten.upsample_nearest2d.default: _h_upsample,
     aten.upsample_nearest2d.vec: _h_upsample_vec,
     aten.copy_.default: _h_copy,
+    aten.convolution.default: _h_convolution,
+    aten.conv2d.default: _h_conv2d,
 }
 
 

@@ -4,10 +4,11 @@ Namespaces and schemas follow the reference (backend.cpp:321-356,
 flow_ops.cpp:255-266, selection_flow.cpp:503-514, conv_blocked.cpp:199-206):
 
 * ``thin_backend::{add, sigmoid, maxpool2d, upsample_nearest2d}``
-* ``thin_native_flow::{maxpool, upsample, detection_select, detection_select_trace}``
-  plus the fused ops of this build: ``silu_``, ``sppf``, ``softmax``,
-  ``dfl_decode``, ``bias_silu_residual``
-* ``thin_blocked::{pack, unpack}``
+* ``thin_native_flow::{maxpool, upsample, detection_select, detection_select_trace}``,
+  the convolutions ``conv`` (conv_flow.cpp:630-646), ``depthwise``
+  (depthwise_flow.cpp:225-233) and ``pack_input``, plus the fused ops of this
+  build: ``silu_``, ``sppf``, ``softmax``, ``dfl_decode``, ``bias_silu_residual``
+* ``thin_blocked::{pack, unpack, conv}`` (conv_blocked.cpp:198-210)
 
 Each op has a CUDA kernel (libttn through ``thintnpu_b200.ops``), a Meta kernel
 for shape inference, and an Autograd fallthrough (the ops are inference-only and
@@ -168,6 +169,46 @@ def _bsr_meta(x, bias, residual):
     return torch.empty_like(x)
 
 
+def _conv_out_shape(x, co, kernel, stride, nchw):
+    n, _, h, w, _ = x.shape
+    pad = (kernel - 1) // 2
+    oh, ow = (h + 2 * pad - kernel) // stride + 1, (w + 2 * pad - kernel) // stride + 1
+    return (n, co, oh, ow) if nchw else (n, co // 16, oh, ow, 16)
+
+
+def _conv_cuda(x, packed, bias, co, kernel, stride, fused=True, nchw_output=False):
+    return ops.conv2d(x, packed, bias, co, kernel, stride, silu=fused, nchw=nchw_output)
+
+
+def _conv_meta(x, packed, bias, co, kernel, stride, fused=True, nchw_output=False):
+    _blocked_meta(x)
+    _require((kernel == 1 and stride == 1) or (kernel in (3, 6) and stride in (1, 2)),
+             "expected point stride1 or spatial stride1/2")
+    _require(co > 0 and (nchw_output or co % 16 == 0), "blocked outputs require aligned channels")
+    return x.new_empty(_conv_out_shape(x, co, kernel, stride, nchw_output))
+
+
+def _depthwise_cuda(x, packed, bias, kernel, stride, fused=True):
+    return ops.depthwise(x, packed, bias, kernel, stride, silu=fused)
+
+
+def _depthwise_meta(x, packed, bias, kernel, stride, fused=True):
+    _blocked_meta(x)
+    n, c1, h, w, _ = x.shape
+    pad = kernel // 2
+    return x.new_empty((n, c1, (h + 2 * pad - kernel) // stride + 1, (w + 2 * pad - kernel) // stride + 1, 16))
+
+
+def _blocked_conv_cuda(x, packed, bias, co, kernel, stride, fp32_output=False, fused=False):
+    _require(not fp32_output, "blocked C2f requires FP16 output and fused FP32 SiLU")
+    return ops.conv2d(x, packed, bias, co, kernel, stride, silu=fused)
+
+
+def _blocked_conv_meta(x, packed, bias, co, kernel, stride, fp32_output=False, fused=False):
+    _require(not fp32_output, "blocked C2f requires FP16 output and fused FP32 SiLU")
+    return _conv_meta(x, packed, bias, co, kernel, stride)
+
+
 # --------------------------------------------------------------- thin_blocked
 
 def _pack_cuda(x):
@@ -215,9 +256,16 @@ def register() -> None:
                   "bool xywh=True) -> Tensor", _decode_cuda, _decode_meta)
     _register(nf, "bias_silu_residual(Tensor x, Tensor bias, Tensor residual) -> Tensor", _bsr_cuda,
               _bsr_meta)
+    _register(nf, "conv(Tensor x, Tensor packed, Tensor? bias, int co, int kernel, int stride, bool fused=True, "
+                  "bool nchw_output=False) -> Tensor", _conv_cuda, _conv_meta)
+    _register(nf, "depthwise(Tensor x, Tensor packed, Tensor? bias, int kernel, int stride, bool fused=True) -> Tensor",
+              _depthwise_cuda, _depthwise_meta)
+    _register(nf, "pack_input(Tensor x) -> Tensor", _pack_cuda, _pack_meta)
     bl = _lib("thin_blocked")
     _register(bl, "pack(Tensor x) -> Tensor", _pack_cuda, _pack_meta)
     _register(bl, "unpack(Tensor x) -> Tensor", _unpack_cuda, _unpack_meta)
+    _register(bl, "conv(Tensor x, Tensor packed, Tensor? bias, int co, int kernel, int stride, "
+                  "bool fp32_output=False, bool fused=False) -> Tensor", _blocked_conv_cuda, _blocked_conv_meta)
 
 
 register()
