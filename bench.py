@@ -277,8 +277,7 @@ def run_pass(args):
     start.record(stream)
     for i in range(args.steps):
         if heartbeat:
-            heartbeat.beat(i)
-            heartbeat.check(i, wait_s=60)
+            heartbeat.step(i)
         op_pass.replay()
     end.record(stream)
     barrier()

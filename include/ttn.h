@@ -273,6 +273,14 @@ ttn_status ttn_conv2d_pack_weights_f16(const void* weights, int64_t co, int64_t 
  * accumulator); its output is then incomplete.  Synchronous. */
 ttn_status ttn_conv2d_fault_f16(uint32_t* fault);
 
+/* Test hook for the bounded waits above: the next ttn_conv2d_* launch (from any
+ * thread) issues no input copy, so its MMA and epilogue roles wait on barriers
+ * that nothing signals; each gives up after its 200 ms limit, sets its bit in the
+ * fault word (1 = copy, 4 = accumulator) and the kernel frees its tensor memory
+ * and returns with nothing in flight.  The output of that launch is not written.
+ * The reference has no counterpart (its kernels do not wait on device flags). */
+void ttn_conv2d_test_withhold_copies(void);
+
 /* Fused Detect decode (v8 DFL / v26).  box: fp16 [n, 4*16, a] logits (element
  * (b, s*16+i, j) at box[b*box_bs + (s*16+i)*box_cs + j]); cls: fp16 [n, nc, a]
  * logits with its own strides.  Anchors come from `levels` feature maps of

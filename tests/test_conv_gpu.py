@@ -237,3 +237,33 @@ def test_torch_ops_conv_schemas(device):
     wd = (torch.randn(64, 1, 3, 3, generator=torch.Generator().manual_seed(4)) / 3).half()
     got = nf.depthwise(xd.to(device), ttn.depthwise_pack_weights(wd.to(device)), None, 3, 1, False)
     assert torch.equal(got.cpu().view(torch.int16), oops.depthwise(xd, wd, None, 3, 1, False).view(torch.int16))
+
+
+def test_bounded_wait_runs_out_and_is_reported(device):
+    """Failure detection on the GPU without a fault: with the test hook armed, the
+    next conv launch issues no input copy, so its MMA role (waiting for a ring stage)
+    and its epilogue (waiting for an accumulator) wait on barriers that nothing
+    signals.  Each gives up at its 200 ms limit, the fault word reports 1 | 4, the
+    kernel frees its tensor memory with nothing in flight, the context stays usable,
+    and the next call is correct."""
+    import time
+
+    import thintnpu_b200 as ttn
+    from thintnpu_b200 import _lib
+    x, wt, bs = _case(1, 32, 64, 8, 16, 3, 5)
+    xd = oops.pack_padded(x).to(device)
+    packed = ttn.conv2d_pack_weights(wt.to(device))
+    b = bs.to(device)
+    torch.cuda.synchronize()
+    assert ttn.ops.conv2d_fault() == 0
+    _lib.lib().ttn_conv2d_test_withhold_copies()
+    start = time.perf_counter()
+    ttn.conv2d(xd, packed, b, 64, 3, 1)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - start >= 0.15
+    assert ttn.ops.conv2d_fault() == 5
+    assert ttn.ops.conv2d_fault() == 0  # reading clears it
+    out = ttn.conv2d(xd, packed, b, 64, 3, 1)
+    torch.cuda.synchronize()
+    assert ttn.ops.conv2d_fault() == 0
+    _check(oops.from_blocked(out.cpu()), x, wt, bs, 1, True)

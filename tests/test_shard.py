@@ -53,6 +53,29 @@ def _worker(rank, world, port, mode, results):
                 results[rank] = "missed"
             except shard.PeerFailure as err:
                 results[rank] = f"detected: {err}"
+        elif mode == "runner":  # the bench runner's per-step calls; rank 1 fails after step 2
+            for i in range(10):
+                if rank == 1 and i == 3:
+                    hb.fail("injected failure after step 2")
+                    results[rank] = "failed"
+                    return
+                try:
+                    hb.step(i, every=4, wait_s=10.0)
+                except shard.PeerFailure as err:
+                    results[rank] = f"detected at step {i}: {err}"
+                    return
+            results[rank] = "missed"
+        elif mode == "runner_stall":  # rank 1 stops beating after step 2 without a word
+            for i in range(10):
+                if rank == 1 and i == 3:
+                    results[rank] = "stalled"
+                    return
+                try:
+                    hb.step(i, every=4, wait_s=1.0)
+                except shard.PeerFailure as err:
+                    results[rank] = f"detected at step {i}: {err}"
+                    return
+            results[rank] = "missed"
         elif mode == "stall":
             hb.beat(0)
             hb.check(0)
@@ -100,3 +123,16 @@ def test_stalled_rank_is_detected_by_peer():
     results = _run("stall")
     assert results[1] == "stalled"
     assert results[0].startswith("detected") and "did not reach step 1" in results[0]
+
+
+def test_runner_heartbeat_detects_failure_within_a_step():
+    results = _run("runner")
+    assert results[1] == "failed"
+    assert results[0].startswith("detected at step") and "injected failure" in results[0]
+    assert int(results[0].split()[3].rstrip(":")) <= 4
+
+
+def test_runner_heartbeat_detects_silent_stall_at_the_next_progress_check():
+    results = _run("runner_stall")
+    assert results[1] == "stalled"
+    assert results[0] == "detected at step 4: ranks [1] did not reach step 4 within 1.0 s"

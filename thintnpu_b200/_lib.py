@@ -32,7 +32,7 @@ EXPORTS = (
     "ttn_upsample2x", "ttn_upsample2x_nc1hwc0_f16", "ttn_maxpool", "ttn_sppf_f16",
     "ttn_softmax", "ttn_dfl_decode_f16", "ttn_dfl_decode_trace_f16", "ttn_attention_f16", "ttn_attention_fault_f16",
     "ttn_conv2d_nc1hwc0_f16", "ttn_conv2d_residual_nc1hwc0_f16", "ttn_conv2d_pack_weights_f16",
-    "ttn_conv2d_fault_f16", "ttn_depthwise_nc1hwc0_f16",
+    "ttn_conv2d_fault_f16", "ttn_conv2d_test_withhold_copies", "ttn_depthwise_nc1hwc0_f16",
     "ttn_select_workspace_size", "ttn_select_f16", "ttn_select_f16_static",
 )
 
@@ -107,6 +107,7 @@ _SIGNATURES = {
                                                        ctypes.c_uint32, _P, _I64, _P, _I64, _P]),
     "ttn_conv2d_pack_weights_f16": (ctypes.c_int, [_P, _I64, _I64, _I32, _P, _P]),
     "ttn_conv2d_fault_f16": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+    "ttn_conv2d_test_withhold_copies": (None, []),
     "ttn_depthwise_nc1hwc0_f16": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I32, _I32,
                                                  ctypes.c_uint32, _P, _I64, _P]),
     "ttn_select_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, ctypes.c_uint32]),

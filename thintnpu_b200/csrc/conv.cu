@@ -33,6 +33,8 @@
 // Every wait is bounded (200 ms of wall time); a role that gives up records the
 // reason in a device word (ttn_conv2d_fault_f16: 1 = copy, 2 = stage, 4 =
 // accumulator), stops, and the CTA drains its copies and frees its TMEM.
+#include <atomic>
+
 #include "tcgen05.cuh"
 
 namespace ttn {
@@ -51,6 +53,10 @@ constexpr int kConvThreads = 64 + 32 * kConvEpiWarps;
 
 __device__ uint32_t g_conv_fault;
 
+// Test hook (ttn_conv2d_test_withhold_copies): the next convolution launch issues
+// no input copy.
+std::atomic<bool> g_withhold_next_conv{false};
+
 struct ConvArgs {
   const uint16_t* bias;  // fp16 [co] or null
   const uint16_t* res;   // NC1HWC0 residual of the output's shape, or null
@@ -68,6 +74,7 @@ struct ConvArgs {
   int sub;               // pixel sub-tiles per tile (2 when tile_n <= 128: they share each weight stage)
   int halo;              // 3x3 stride 1: one halo box per channel block, the taps as shifted descriptors
   int steps;             // ring stages per tile
+  int withhold;          // test hook: the producer issues no copy, so every other role's first wait runs out
   uint32_t a_box, a_bytes, b_off, b_bytes, stage_bytes;  // shared-memory layout of one stage
 };
 struct ConvMaps {
@@ -126,7 +133,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
     uint32_t fills[kConvMaxStages] = {0, 0, 0, 0, 0, 0, 0, 0};
     int s = 0;
     uint32_t phase = 0;
-    bool ok = true;
+    bool ok = !a.withhold;
     for (int j = 0; j < count && ok; ++j) {
       int img, oh0, ow0, n0;
       tile_coords(j, img, oh0, ow0, n0);
@@ -389,6 +396,7 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
   a.tiles = batch * a.tiles_h * a.tiles_w * a.co_tiles;
   a.silu = (flags & TTN_CONV_SILU) ? 1 : 0;
   a.nchw = nchw ? 1 : 0;
+  a.withhold = g_withhold_next_conv.exchange(false) ? 1 : 0;
 
   ConvMaps maps;
   {  // input: (16 channels, w, h, c1, image), boxes of 16 x (wt, ht) pixels at the conv stride x blocks
@@ -469,6 +477,8 @@ ttn_status ttn_conv2d_pack_weights_f16(const void* weights, int64_t co, int64_t 
       (const uint16_t*)weights, (uint16_t*)packed, (int)co, (int)ci, (int)taps, (int)co_pad, total);
   return launch_check(name);
 }
+
+void ttn_conv2d_test_withhold_copies(void) { g_withhold_next_conv.store(true); }
 
 ttn_status ttn_conv2d_fault_f16(uint32_t* fault) {
   if (!fault) return fail(TTN_INVALID_ARG, "ttn_conv2d_fault_f16: null output");

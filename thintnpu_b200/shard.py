@@ -77,6 +77,21 @@ class Heartbeat:
     def fail(self, reason: str) -> None:
         self.store.set("hb/failed", f"{self.rank}: {reason}")
 
+    def check_failed(self) -> None:
+        """One store round trip: raise PeerFailure if a peer published a failure."""
+        if self.store.check(["hb/failed"]):
+            raise PeerFailure(self.store.get("hb/failed").decode())
+
+    def step(self, step: int, every: int = 8, wait_s: float = 60.0) -> None:
+        """Between steps of a runner: beat `step`, check for a published failure,
+        and every `every` steps also wait (up to wait_s) until every rank has
+        reached `step`, so no rank runs more than `every` steps ahead of a stopped one."""
+        self.beat(step)
+        if step % every == 0:
+            self.check(step, wait_s)
+        else:
+            self.check_failed()
+
     def check(self, step: int, wait_s: float = 5.0) -> None:
         deadline = time.monotonic() + wait_s
         while True:
