@@ -186,6 +186,21 @@ def test_sppf(device, n, c1, hw):
     assert_bits_equal(ttn.sppf(x.to(device), 5), oops.sppf(x, 5))
 
 
+@pytest.mark.parametrize("n,c1,h,w", [(2, 3, 13, 7), (1, 2, 5, 22), (1, 1, 1, 9), (2, 1, 3, 1), (1, 2, 21, 18),
+                                      (3, 5, 4, 4), (1, 1, 30, 31)])
+def test_sppf_rectangular_planes(device, n, c1, h, w):
+    """Rows and columns that are not multiples of the kernel's four-output runs."""
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(h * 100 + w)
+    x = torch.randn(n, c1, h, w, 16, generator=g).half()
+    assert_bits_equal(ttn.sppf(x.to(device), 5), oops.sppf(x, 5))
+    special = x.clone()
+    bits = special.view(torch.int16)
+    bits[0, 0, h // 2, w // 2, 3] = 0x7E05
+    bits[-1, -1].masked_fill_(torch.rand(h, w, 16, generator=g) < 0.3, -0x8000)
+    assert_bits_equal(ttn.sppf(special.to(device), 5), oops.sppf(special, 5))
+
+
 @pytest.mark.parametrize("hw", [20, 7])
 def test_sppf_nan_and_negative_zero_planes(device, hw):
     """Planes holding NaN (with payloads) or -0 take the exact per-lane CPU rule."""

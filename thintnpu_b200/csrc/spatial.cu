@@ -472,6 +472,170 @@ __global__ void __launch_bounds__(256) sppf_planes_small(const uint16_t* x, uint
   }
 }
 
+// SPPF with a 5x5 window (radius 2), the YOLO case, in runs of four outputs:
+// each thread of the horizontal pass takes a run of four output pixels of one row
+// (and one half of the 16 channel lanes), loads the eight-pixel window once and
+// shares the partial maxima between the four outputs; the vertical pass does the
+// same along a column.  So a pool stage costs two shared-memory loads and one
+// store per output vector and pass, instead of five loads.  Planes whose width
+// and height are rounded up to multiples of 4 sit in shared memory with a 2-pixel
+// -inf border (padded columns and rows past the image stay -inf).  Planes with a
+// NaN or -0 take the CPU's exact per-lane rule over the same windows.
+__device__ __forceinline__ void run_max4(const uint4 (&x)[8], uint4 (&y)[4]) {
+  const uint4 c34 = hmax4(x[3], x[4]), a12 = hmax4(x[1], x[2]), b56 = hmax4(x[5], x[6]);
+  y[0] = hmax4(hmax4(x[0], a12), c34);
+  y[1] = hmax4(a12, hmax4(c34, x[5]));
+  y[2] = hmax4(hmax4(x[2], c34), b56);
+  y[3] = hmax4(c34, hmax4(b56, x[7]));
+}
+
+// A whole plane under the CPU's exact per-lane rule (planes holding NaN or -0;
+// the CTA branches here together): three chained 5x5 pools, each a horizontal
+// pass cur -> tmp and a vertical pass tmp -> cur and the stage's output slice,
+// every window folded in index order (first maximum, last NaN, NaN quieted on
+// the vertical pass).  Out of line so the fast path's registers stay its own.
+__device__ __noinline__ void sppf_plane_exact(uint4* cur, uint4* tmp, int pw, int h, int w, uint4* const* dst) {
+  auto at = [&](int prow, int pcol, int hf) { return (prow * pw + (pcol ^ ((pcol >> 2) & 3))) * 2 + hf; };
+  const int plane_vec = h * w * 2;
+  for (int stage = 0; stage < 3; ++stage) {
+    for (int pass = 0; pass < 2; ++pass) {
+      for (int v = threadIdx.x; v < plane_vec; v += blockDim.x) {
+        const int pix = v >> 1, row = pix / w, col = pix - row * w, hf = v & 1;
+        uint16_t best[8];
+        float bv[8];
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+          best[l] = 0xfc00u;
+          bv[l] = -INFINITY;
+        }
+        for (int t = -2; t <= 2; ++t) {
+          const uint4 q = pass == 0 ? cur[at(row + 2, col + 2 + t, hf)] : tmp[at(row + 2 + t, col + 2, hf)];
+          const uint16_t* e = reinterpret_cast<const uint16_t*>(&q);
+#pragma unroll
+          for (int l = 0; l < 8; ++l) pool_update(best[l], bv[l], e[l]);
+        }
+        if (pass == 1) {
+#pragma unroll
+          for (int l = 0; l < 8; ++l) best[l] = PoolBits<uint16_t>::finish(best[l]);
+        }
+        const uint4 m = *reinterpret_cast<uint4*>(best);
+        if (pass == 0) {
+          tmp[at(row + 2, col + 2, hf)] = m;
+        } else {
+          dst[stage][v] = m;
+          if (stage < 2) cur[at(row + 2, col + 2, hf)] = m;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Each thread takes at most IPT runs per pass; every plane has the same
+// geometry, so the runs' shared-memory bases and swizzle terms are computed once
+// per kernel.
+template <int IPT>
+__global__ void __launch_bounds__(256, 4) sppf_runs(const uint16_t* x, uint16_t* out, int64_t n, int64_t c1, int h,
+                                                 int w, FastDiv wdiv) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int w4 = (w + 3) & ~3, h4 = (h + 3) & ~3;
+  const int pw = w4 + 4, ph = h4 + 4;  // padded plane, in pixels
+  const int padded_vec = ph * pw * 2;
+  uint4* cur = reinterpret_cast<uint4*>(smem_raw);  // the plane being pooled
+  uint4* tmp = cur + padded_vec;                     // the horizontal-pass scratch
+  // Vector of (padded row, padded column, half): the column is XOR-swizzled inside
+  // its aligned block of four by the block index, so the lanes of a horizontal run
+  // pass (runs four pixels apart) spread over all eight 16-byte bank groups.
+  auto at = [&](int prow, int pcol, int hf) { return (prow * pw + (pcol ^ ((pcol >> 2) & 3))) * 2 + hf; };
+  const int plane_vec = h * w * 2;
+  const int runs_w = w4 / 4, runs_h = h4 / 4;
+  const int h_items = h * runs_w * 2, v_items = w * runs_h * 2;
+  // horizontal run i: window vectors k < 4 at hb + 2 (k ^ s1), k >= 4 at hb + 8 + 2 ((k - 4) ^ s2);
+  // output k (k < hvalid) at column 4q + k + 2 (k < 2 in block q, else block q + 1)
+  int hb[IPT], hs[IPT], hvalid[IPT], vb[IPT], vvalid[IPT], vout[IPT];
+#pragma unroll
+  for (int i = 0; i < IPT; ++i) {
+    const int e = threadIdx.x + i * 256;
+    hvalid[i] = vvalid[i] = 0;
+    hb[i] = hs[i] = vb[i] = vout[i] = 0;
+    if (e < h_items) {
+      const int hf = e & 1, t = e >> 1, q = t % runs_w, row = t / runs_w;
+      hb[i] = ((row + 2) * pw + 4 * q) * 2 + hf;
+      hs[i] = (q & 3) | (((q + 1) & 3) << 2);
+      hvalid[i] = w - 4 * q < 4 ? w - 4 * q : 4;
+    }
+    if (e < v_items) {
+      const int hf = e & 1, t = e >> 1, col = t % w, q = t / w;
+      vb[i] = at(4 * q, col + 2, hf);
+      vout[i] = ((4 * q) * w + col) * 2 + hf;
+      vvalid[i] = h - 4 * q < 4 ? h - 4 * q : 4;
+    }
+  }
+  const int row_step = 2 * pw;
+  const uint4 ninf = make_uint4(0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u);
+  for (int v = threadIdx.x; v < 2 * padded_vec; v += blockDim.x) cur[v] = ninf;
+  __syncthreads();
+#pragma unroll 1
+  for (int64_t job = blockIdx.x; job < n * c1; job += gridDim.x) {
+    const int64_t b = job / c1, cb = job - b * c1;
+    const uint4* src = reinterpret_cast<const uint4*>(x + job * (int64_t)plane_vec * 8);
+    uint4* dst0 = reinterpret_cast<uint4*>(out + ((b * 4 * c1) + cb) * (int64_t)plane_vec * 8);
+    bool special = false;
+    for (int v = threadIdx.x; v < plane_vec; v += blockDim.x) {  // slice 0 of the concat: the plane itself
+      const uint4 q = src[v];
+      dst0[v] = q;
+      const int pix = v >> 1, row = (int)wdiv.div((uint32_t)pix), col = pix - row * w;
+      cur[at(row + 2, col + 2, v & 1)] = q;
+      special |= special_word(q.x) | special_word(q.y) | special_word(q.z) | special_word(q.w);
+    }
+    special = __syncthreads_or(special);
+    uint4* const slices[3] = {
+        reinterpret_cast<uint4*>(out + ((b * 4 * c1) + c1 + cb) * (int64_t)plane_vec * 8),
+        reinterpret_cast<uint4*>(out + ((b * 4 * c1) + 2 * c1 + cb) * (int64_t)plane_vec * 8),
+        reinterpret_cast<uint4*>(out + ((b * 4 * c1) + 3 * c1 + cb) * (int64_t)plane_vec * 8)};
+    if (special) {
+      sppf_plane_exact(cur, tmp, pw, h, w, slices);
+    } else {
+#pragma unroll 1
+      for (int stage = 1; stage <= 3; ++stage) {
+#pragma unroll
+        for (int i = 0; i < IPT; ++i) {  // horizontal runs: cur -> tmp
+          if (!hvalid[i]) continue;
+          const int s1 = hs[i] & 3, s2 = hs[i] >> 2, base = hb[i];
+          uint4 xs[8], ys[4];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) xs[k] = cur[base + (k < 4 ? 2 * (k ^ s1) : 8 + 2 * ((k - 4) ^ s2))];
+          run_max4(xs, ys);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (k < hvalid[i]) tmp[base + (k < 2 ? 2 * ((k + 2) ^ s1) : 8 + 2 * ((k - 2) ^ s2))] = ys[k];
+        }
+        __syncthreads();
+        uint4* dst = slices[stage - 1];
+        const bool keep = stage < 3;  // the last stage's result only goes to the output
+#pragma unroll
+        for (int i = 0; i < IPT; ++i) {  // vertical runs: tmp -> cur and the output
+          if (!vvalid[i]) continue;
+          const int base = vb[i];
+          uint4* og = dst + vout[i];
+          uint4 xs[8], ys[4];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) xs[k] = tmp[base + k * row_step];
+          run_max4(xs, ys);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (k < vvalid[i]) {
+              if (keep) cur[base + (k + 2) * row_step] = ys[k];
+              og[2 * k * w] = ys[k];
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+  }
+}
+
 bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 
@@ -643,6 +807,21 @@ ttn_status ttn_sppf_f16(const void* x, void* out, int64_t n, int64_t c1, int64_t
   }
   int64_t jobs = n * c1;
   const int64_t plane_vec = h * w * 2;
+  const size_t runs_smem = 2 * (size_t)(((h + 3) & ~3) + 4) * (((w + 3) & ~3) + 4) * 16 * 2;
+  const int64_t runs = h * ((w + 3) / 4) * 2 > w * ((h + 3) / 4) * 2 ? h * ((w + 3) / 4) * 2 : w * ((h + 3) / 4) * 2;
+  if (kernel == 5 && runs <= 2 * 256 && (int64_t)runs_smem <= max_dynamic_smem()) {
+    // the YOLO window: runs of four, fixed per-thread geometry
+    const void* fn = runs <= 256 ? (const void*)sppf_runs<1> : (const void*)sppf_runs<2>;
+    TTN_TRY(ensure_dynamic_smem(fn, (int)runs_smem));
+    unsigned grid = resident_grid(fn, 256, runs_smem, jobs, 1);
+    if (runs <= 256)
+      sppf_runs<1><<<grid, 256, runs_smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w,
+                                                FastDiv((uint32_t)w));
+    else
+      sppf_runs<2><<<grid, 256, runs_smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w,
+                                                FastDiv((uint32_t)w));
+    return launch_check(name);
+  }
   if (plane_vec <= 4 * 256) {  // fixed per-thread positions
     const int vpt = (int)((plane_vec + 255) / 256);
     const void* fn = vpt == 1 ? (const void*)sppf_planes_small<1>
