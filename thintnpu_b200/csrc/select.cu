@@ -257,7 +257,9 @@ __global__ void __launch_bounds__(256) class_max_planar_sigmoid(SelectView v, bo
         skey[j] = score_key(s2, nan_last);
         tie = skey[j] == score_key(s1, nan_last);
       }
-      if (live && (has_special || tie)) {
+      // A tie can only move the winner to a lower class index, so an anchor whose
+      // first largest logit is class 0 keeps it (e.g. a row of equal logits).
+      if (live && (has_special || (tie && clsj[j] != 0))) {
         redo |= 1u << j;
         skey[j] = 0;  // rescanned anchors always gather every class in the fused pair stage
       }
@@ -456,6 +458,106 @@ __device__ void bitonic_sort(unsigned long long* data, int count) {
   }
 }
 
+// Ascending sort of n = E * blockDim.x 32-bit values in shared memory `data`
+// (n a power of two; blockDim.x a power of two >= 32).  Thread t holds elements
+// t*E .. t*E+E-1 in registers through the bitonic network: strides below E stay
+// inside the thread, strides below 32*E are lane exchanges (shuffles), and only the
+// larger strides go through shared memory (two barriers each).  For E = 2 and
+// n = 512 that is 12 barriers instead of the 45 of a shared-memory network.
+template <int E>
+__device__ __forceinline__ void cmpx_in_thread(uint32_t (&v)[E], int s, int base, int span) {
+#pragma unroll
+  for (int ss = E / 2; ss >= 1; ss >>= 1) {
+    if (ss != s) continue;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      if (e & ss) continue;
+      const bool asc = ((base + e) & span) == 0;
+      const uint32_t lo = min(v[e], v[e | ss]), hi = max(v[e], v[e | ss]);
+      v[e] = asc ? lo : hi;
+      v[e | ss] = asc ? hi : lo;
+    }
+  }
+}
+
+template <int E>
+__device__ void block_sort_regs(uint32_t* data) {
+  const int t = threadIdx.x, lane = t & 31, base = t * E;
+  const int n = E * (int)blockDim.x;
+  uint32_t v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = data[base + e];
+  for (int span = 2; span <= n; span <<= 1) {
+    for (int s = span >> 1; s > 0; s >>= 1) {
+      if (s < E) {
+        cmpx_in_thread<E>(v, s, base, span);
+      } else if (s < 32 * E) {
+        const int m = s / E;  // partner lane = lane ^ m; the lower lane keeps the minimum when ascending
+        const bool low = (lane & m) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const uint32_t p = __shfl_xor_sync(0xffffffffu, v[e], m);
+          const bool keep_min = low == (((base + e) & span) == 0);
+          v[e] = keep_min ? min(v[e], p) : max(v[e], p);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) data[base + e] = v[e];
+        __syncthreads();
+        const bool low = (base & s) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const uint32_t p = data[(base + e) ^ s];
+          const bool keep_min = low == (((base + e) & span) == 0);
+          v[e] = keep_min ? min(v[e], p) : max(v[e], p);
+        }
+        __syncthreads();
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) data[base + e] = v[e];
+  __syncthreads();
+}
+
+// Ascending sort of `size` (a power of two >= 32) values in shared memory: the
+// register network when size is a multiple of the block with E = size / blockDim.x
+// up to MAXE (the caller's register budget), else a shared-memory bitonic network.
+template <int MAXE>
+__device__ void block_sort_u32(uint32_t* data, int size) {
+  const int e = size / (int)blockDim.x;
+  if (size >= (int)blockDim.x && e <= MAXE) {
+    if (e == 1) return block_sort_regs<1>(data);
+    if (MAXE >= 2 && e == 2) return block_sort_regs<(MAXE >= 2 ? 2 : 1)>(data);
+    if (MAXE >= 4 && e == 4) return block_sort_regs<(MAXE >= 4 ? 4 : 1)>(data);
+    if (MAXE >= 8 && e == 8) return block_sort_regs<(MAXE >= 8 ? 8 : 1)>(data);
+  }
+  for (int span = 2; span <= size; span <<= 1) {
+    for (int stride = span >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < size; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint32_t a = data[i], c = data[j];
+          if ((a > c) == ((i & span) == 0)) {
+            data[i] = c;
+            data[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Histogram increment with the warp's equal bins combined first (one shared-memory
+// atomic per distinct bin per warp step); `live` lanes take part, all lanes call.
+__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool live) {
+  const uint32_t mask = __ballot_sync(0xffffffffu, live);
+  if (!live) return;
+  const uint32_t peers = __match_any_sync(mask, bin);
+  if ((threadIdx.x & 31) == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+}
+
 struct TopkArgs {
   KeySource src;
   int64_t n;        // keys per image
@@ -597,17 +699,21 @@ constexpr int kStageKeys = 24576;  // keys staged in shared memory (48 KB)
 // (key << 12 | slot) composites.  comp and src are shared arrays of cap >= k
 // (a power of two >= 32, k <= 4096); out[i] = key << 32 | index for i < k.
 template <int WARPS, typename KeyAt>
-__device__ void cta_topk(int64_t n, int64_t k, int cap, KeyAt key_at, uint32_t* comp, uint32_t* src,
+__device__ void cta_topk(int n, int k, int cap, KeyAt key_at, uint32_t* comp, uint32_t* src,
                          unsigned long long* out) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sel_bucket, sel_below;
   __shared__ int warp_lt[WARPS], warp_eq[WARPS];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int trips = (n + (int)blockDim.x - 1) / (int)blockDim.x;  // warp-uniform loop counts
   // --- radix select
   for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
-    atomicAdd(&hist[key_at(i) >> 8], 1u);
+  for (int r = 0; r < trips; ++r) {
+    const int i = r * (int)blockDim.x + threadIdx.x;
+    const bool live = i < n;
+    hist_add(hist, live ? key_at(i) >> 8 : 0u, live);
+  }
   __syncthreads();
   if (warp == 0) find_bucket(hist, (uint32_t)k, 0u, &sel_bucket, &sel_below);
   __syncthreads();
@@ -615,22 +721,24 @@ __device__ void cta_topk(int64_t n, int64_t k, int cap, KeyAt key_at, uint32_t* 
   __syncthreads();
   for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    uint32_t key = key_at(i);
-    if ((key >> 8) == high) atomicAdd(&hist[key & 255u], 1u);
+  for (int r = 0; r < trips; ++r) {
+    const int i = r * (int)blockDim.x + threadIdx.x;
+    const uint32_t key = i < n ? key_at(i) : 0xffffffffu;
+    const bool live = (key >> 8) == high;
+    hist_add(hist, key & 255u, live);
   }
   __syncthreads();
   if (warp == 0) find_bucket(hist, (uint32_t)k, below_high, &sel_bucket, &sel_below);
   __syncthreads();
   const uint32_t threshold = (high << 8) | sel_bucket;
-  const int64_t need = k - (int64_t)sel_below;
+  const int need = k - (int)sel_below;
   // --- index-ordered collection
-  const int64_t span = ((n + WARPS - 1) / WARPS + 31) / 32 * 32;
-  const int64_t lo = warp * span, hi = lo + span < n ? lo + span : n;
+  const int span = ((n + WARPS - 1) / WARPS + 31) / 32 * 32;
+  const int lo = warp * span, hi = lo + span < n ? lo + span : n;
   int lt = 0, eq = 0;
-  for (int64_t base = lo; base < hi; base += 32) {
-    int64_t i = base + lane;
-    uint32_t key = i < hi ? key_at(i) : 0xffffffffu;
+  for (int base = lo; base < hi; base += 32) {
+    const int i = base + lane;
+    const uint32_t key = i < hi ? key_at(i) : 0xffffffffu;
     lt += __popc(__ballot_sync(0xffffffffu, key < threshold));
     eq += __popc(__ballot_sync(0xffffffffu, key == threshold));
   }
@@ -639,23 +747,23 @@ __device__ void cta_topk(int64_t n, int64_t k, int cap, KeyAt key_at, uint32_t* 
     warp_eq[warp] = eq;
   }
   __syncthreads();
-  int64_t eq_before = 0, taken_before = 0;
+  int eq_before = 0, taken_before = 0;
   for (int w = 0; w < warp; ++w) {
-    int64_t take_eq = need - eq_before;
+    int take_eq = need - eq_before;
     take_eq = take_eq < 0 ? 0 : (take_eq > warp_eq[w] ? warp_eq[w] : take_eq);
     taken_before += warp_lt[w] + take_eq;
     eq_before += warp_eq[w];
   }
   const uint32_t lane_lt = (1u << lane) - 1u;
-  for (int64_t base = lo; base < hi; base += 32) {
-    int64_t i = base + lane;
-    uint32_t key = i < hi ? key_at(i) : 0xffffffffu;
-    uint32_t eq_mask = __ballot_sync(0xffffffffu, key == threshold);
-    int64_t my_eq_rank = eq_before + __popc(eq_mask & lane_lt);
-    bool take = key < threshold || (key == threshold && my_eq_rank < need);
-    uint32_t take_mask = __ballot_sync(0xffffffffu, take);
+  for (int base = lo; base < hi; base += 32) {
+    const int i = base + lane;
+    const uint32_t key = i < hi ? key_at(i) : 0xffffffffu;
+    const uint32_t eq_mask = __ballot_sync(0xffffffffu, key == threshold);
+    const int my_eq_rank = eq_before + __popc(eq_mask & lane_lt);
+    const bool take = key < threshold || (key == threshold && my_eq_rank < need);
+    const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
     if (take) {
-      int pos = (int)(taken_before + __popc(take_mask & lane_lt));
+      const int pos = taken_before + __popc(take_mask & lane_lt);
       comp[pos] = (key << 12) | (uint32_t)pos;
       src[pos] = (uint32_t)i;
     }
@@ -664,25 +772,11 @@ __device__ void cta_topk(int64_t n, int64_t k, int cap, KeyAt key_at, uint32_t* 
   }
   __syncthreads();
   // --- stable sort by key (slot order = index order)
-  for (int i = (int)k + threadIdx.x; i < cap; i += blockDim.x) comp[i] = 0xffffffffu;
+  for (int i = k + threadIdx.x; i < cap; i += blockDim.x) comp[i] = 0xffffffffu;
   __syncthreads();
-  for (int span2 = 2; span2 <= cap; span2 <<= 1) {
-    for (int stride = span2 >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < cap; i += blockDim.x) {
-        int j = i ^ stride;
-        if (j > i) {
-          uint32_t a = comp[i], c = comp[j];
-          if ((a > c) == ((i & span2) == 0)) {
-            comp[i] = c;
-            comp[j] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
-    uint32_t c = comp[i];
+  block_sort_u32<4>(comp, cap);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const uint32_t c = comp[i];
     out[i] = ((unsigned long long)(c >> 12) << 32) | (unsigned long long)src[c & 0xfffu];
   }
 }
@@ -691,7 +785,8 @@ __device__ void cta_topk(int64_t n, int64_t k, int cap, KeyAt key_at, uint32_t* 
 template <bool kStaged>
 __global__ void __launch_bounds__(kSmallThreads) topk_small(TopkArgs args) {
   extern __shared__ uint32_t dyn[];  // [cap] composites, [cap] source indices, [n] staged keys
-  const int64_t b = blockIdx.x, n = args.n, k = args.k;
+  const int64_t b = blockIdx.x;
+  const int n = (int)args.n, k = (int)args.k;
   int cap = 32;
   while (cap < k) cap <<= 1;
   uint32_t* comp = dyn;
@@ -699,21 +794,24 @@ __global__ void __launch_bounds__(kSmallThreads) topk_small(TopkArgs args) {
   uint16_t* staged = reinterpret_cast<uint16_t*>(dyn + 2 * cap);
   unsigned long long* out = args.sorted + b * args.sorted_pitch;
   if (k <= 0) return;
+  const uint32_t* rec = args.src.records ? args.src.records + b * args.src.pitch : nullptr;
+  const uint16_t* bits = args.src.records ? nullptr : args.src.bits + b * args.src.pitch;
+  auto raw = [&](int i) -> uint16_t { return rec ? (uint16_t)(rec[i] & 0xffffu) : bits[i]; };
   if (kStaged) {  // one coalesced, 4-way unrolled pass computes every key once
-    int64_t i = threadIdx.x;
+    int i = threadIdx.x;
     for (; i + 3 * kSmallThreads < n; i += 4 * kSmallThreads) {
-      uint16_t h0 = args.src.get(b, i), h1 = args.src.get(b, i + kSmallThreads);
-      uint16_t h2 = args.src.get(b, i + 2 * kSmallThreads), h3 = args.src.get(b, i + 3 * kSmallThreads);
+      const uint16_t h0 = raw(i), h1 = raw(i + kSmallThreads), h2 = raw(i + 2 * kSmallThreads),
+                     h3 = raw(i + 3 * kSmallThreads);
       staged[i] = (uint16_t)score_key(h0, args.nan_last);
       staged[i + kSmallThreads] = (uint16_t)score_key(h1, args.nan_last);
       staged[i + 2 * kSmallThreads] = (uint16_t)score_key(h2, args.nan_last);
       staged[i + 3 * kSmallThreads] = (uint16_t)score_key(h3, args.nan_last);
     }
-    for (; i < n; i += kSmallThreads) staged[i] = (uint16_t)score_key(args.src.get(b, i), args.nan_last);
+    for (; i < n; i += kSmallThreads) staged[i] = (uint16_t)score_key(raw(i), args.nan_last);
     __syncthreads();
   }
-  auto key_at = [&](int64_t i) -> uint32_t {
-    return kStaged ? (uint32_t)staged[i] : score_key(args.src.get(b, i), args.nan_last);
+  auto key_at = [&](int i) -> uint32_t {
+    return kStaged ? (uint32_t)staged[i] : score_key(raw(i), args.nan_last);
   };
   cta_topk<kSmallWarps>(n, k, cap, key_at, comp, src, out);
 }
@@ -751,7 +849,7 @@ __global__ void __launch_bounds__(256) gather_pairs(SelectView v, bool sigmoid,
 // equal keys in flat-index order, as the stage-2 top-k orders them -- and the
 // first k packed.  More candidates (many ties at K1) take the exact top-k over
 // all k*nc pairs in the same CTA, keys read on the fly.
-constexpr int kPairThreads = 512;
+constexpr int kPairThreads = 256;
 constexpr int kPairCand = 4096;
 constexpr int64_t kPairFlatMax = 1 << 15;
 
@@ -812,11 +910,11 @@ __global__ void __launch_bounds__(kPairThreads) pairs_fused(SelectView v, bool n
   };
   if (n > kPairCand) {
     unsigned long long* sorted = reinterpret_cast<unsigned long long*>(pair_cand);
-    auto key_at = [&](int64_t i) -> uint32_t {
-      const int r = (int)(i / nc), c = (int)(i - (int64_t)r * nc);
+    auto key_at = [&](int i) -> uint32_t {
+      const int r = i / nc, c = i - r * nc;
       return score_key(score_bits(v, b, (int64_t)(s1[r] & 0xffffffffull), c, sigmoid), nan_last);
     };
-    cta_topk<kPairThreads / 32>((int64_t)k * nc, k, cap, key_at, topk_comp, topk_comp + cap, sorted);
+    cta_topk<kPairThreads / 32>(k * nc, k, cap, key_at, topk_comp, topk_comp + cap, sorted);
     __syncthreads();
     for (int j = tid; j < k; j += kPairThreads) pack(j, (int)(sorted[j] & 0xffffffffull));
     return;
@@ -825,21 +923,7 @@ __global__ void __launch_bounds__(kPairThreads) pairs_fused(SelectView v, bool n
   while (size < n) size <<= 1;
   for (int i = n + tid; i < size; i += kPairThreads) pair_cand[i] = 0xffffffffu;
   __syncthreads();
-  for (int span = 2; span <= size; span <<= 1) {
-    for (int stride = span >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < size; i += kPairThreads) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const uint32_t x = pair_cand[i], y = pair_cand[j];
-          if ((x > y) == ((i & span) == 0)) {
-            pair_cand[i] = y;
-            pair_cand[j] = x;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
+  block_sort_u32<8>(pair_cand, size);
   for (int j = tid; j < k; j += kPairThreads) pack(j, (int)(pair_cand[j] & 0x7fffu));
 }
 
