@@ -49,6 +49,16 @@ __device__ __forceinline__ uint16_t score_bits(const SelectView& v, int64_t b, i
   return sigmoid ? sigmoid_h_fast(raw) : raw;
 }
 
+// Per-image histograms of key high bytes kept in global memory: lanes adding to
+// the same slot are combined first (one atomic per distinct slot per warp step);
+// `live` lanes take part, all lanes of the warp call.
+__device__ __forceinline__ void hist_add_global(uint32_t* hist, uint32_t slot, bool live) {
+  const uint32_t mask = __ballot_sync(0xffffffffu, live);
+  if (!live) return;
+  const uint32_t peers = __match_any_sync(mask, slot);
+  if ((threadIdx.x & 31) == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&hist[slot], (uint32_t)__popc(peers));
+}
+
 // ------------------------------------------------------------ 1. class max
 
 // Thread per anchor (coalesced when anchors are the unit-stride dim).
@@ -150,17 +160,21 @@ __global__ void __launch_bounds__(256) class_max_planar8(SelectView v, bool nan_
 // sigmoid(second) equals sigmoid(best), in which case the warp rescans that
 // anchor's classes with the exact sigmoid, lanes over classes.
 __device__ __forceinline__ void rescan_anchor(const SelectView& v, int64_t b, int64_t a, bool nan_last,
-                                              uint32_t& out_bits, uint32_t& out_cls) {
+                                              uint32_t& out_bits, uint32_t& out_cls, uint32_t& out_second) {
   const int lane = threadIdx.x & 31;
   const uint16_t* p = v.base + b * v.sb + a * v.sa + 4 * v.sc;
-  uint32_t best = kInvalidKey, best_cls = 0xffffffffu, best_bits = 0;
+  // best (key, class, bits) and the smallest key among the other classes
+  uint32_t best = kInvalidKey, best_cls = 0xffffffffu, best_bits = 0, second = kInvalidKey;
   for (int64_t c = lane; c < v.classes; c += 32) {
     uint16_t bits = sigmoid_h_fast(p[c * v.sc]);
     uint32_t key = score_key(bits, nan_last);
     if (key < best) {
+      second = best;
       best = key;
       best_cls = (uint32_t)c;
       best_bits = bits;
+    } else {
+      second = min(second, key);
     }
   }
 #pragma unroll
@@ -168,14 +182,19 @@ __device__ __forceinline__ void rescan_anchor(const SelectView& v, int64_t b, in
     uint32_t ok = __shfl_xor_sync(0xffffffffu, best, o);
     uint32_t oc = __shfl_xor_sync(0xffffffffu, best_cls, o);
     uint32_t ob = __shfl_xor_sync(0xffffffffu, best_bits, o);
+    uint32_t os = __shfl_xor_sync(0xffffffffu, second, o);
     if (ok < best || (ok == best && oc < best_cls)) {
+      second = min(os, best);
       best = ok;
       best_cls = oc;
       best_bits = ob;
+    } else {
+      second = min(second, ok);
     }
   }
   out_bits = best_bits;
   out_cls = best_cls;
+  out_second = min(second, 0xffffu);
 }
 
 // Pass 1 works on the fp16 logits two anchors at a time (half2 lanes), since
@@ -191,7 +210,8 @@ __device__ __forceinline__ void rescan_anchor(const SelectView& v, int64_t b, in
 template <int APT>
 __global__ void __launch_bounds__(256) class_max_planar_sigmoid(SelectView v, bool nan_last,
                                                                 uint32_t* records, int64_t rec_pitch,
-                                                                uint16_t* trace_max, uint16_t* second_keys) {
+                                                                uint16_t* trace_max, uint16_t* second_keys,
+                                                                uint32_t* key_hist) {
   constexpr int W = APT / 2;      // half2 words per class row
   constexpr int ROWS = 32 / APT;  // class rows in flight
   using Vec = typename std::conditional<W == 4, uint4, typename std::conditional<W == 2, uint2, uint32_t>::type>::type;
@@ -259,10 +279,7 @@ __global__ void __launch_bounds__(256) class_max_planar_sigmoid(SelectView v, bo
       }
       // A tie can only move the winner to a lower class index, so an anchor whose
       // first largest logit is class 0 keeps it (e.g. a row of equal logits).
-      if (live && (has_special || (tie && clsj[j] != 0))) {
-        redo |= 1u << j;
-        skey[j] = 0;  // rescanned anchors always gather every class in the fused pair stage
-      }
+      if (live && (has_special || (tie && clsj[j] != 0))) redo |= 1u << j;
     }
     // exact rescans, one anchor at a time with the whole warp
     uint32_t pending = __ballot_sync(0xffffffffu, redo != 0);
@@ -273,18 +290,24 @@ __global__ void __launch_bounds__(256) class_max_planar_sigmoid(SelectView v, bo
       while (src_redo) {
         const int j = __ffs(src_redo) - 1;
         src_redo &= src_redo - 1;
-        uint32_t rb, rc;
-        rescan_anchor(v, sb, sa0 + j, nan_last, rb, rc);
+        uint32_t rb, rc, rs;
+        rescan_anchor(v, sb, sa0 + j, nan_last, rb, rc, rs);
         if (lane == src) {
 #pragma unroll
           for (int k = 0; k < APT; ++k)
             if (k == j) {
               out_bits[k] = rb;
               clsj[k] = rc;
+              skey[k] = rs;
             }
         }
       }
       pending &= pending - 1;
+    }
+    if (key_hist) {  // [b][256] counts of the anchors' best-key high bytes, for the stage-1 top-k
+#pragma unroll
+      for (int j = 0; j < APT; ++j)
+        hist_add_global(key_hist, (uint32_t)b * 256u + (score_key((uint16_t)out_bits[j], nan_last) >> 8), live);
     }
     if (live) {
       uint32_t out[APT];
@@ -518,6 +541,65 @@ __device__ void block_sort_regs(uint32_t* data) {
 #pragma unroll
   for (int e = 0; e < E; ++e) data[base + e] = v[e];
   __syncthreads();
+}
+
+// block_sort_regs for a block of THREADS threads known at compile time: the whole
+// network unrolled, so every stride and direction test is a constant.
+template <int E, int THREADS>
+__device__ void block_sort_fixed(uint32_t* data) {
+  constexpr int LOGN = __builtin_ctz(E * THREADS);
+  const int t = threadIdx.x, lane = t & 31, base = t * E;
+  uint32_t v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = data[base + e];
+#pragma unroll
+  for (int ls = 1; ls <= LOGN; ++ls) {
+    const int span = 1 << ls;
+#pragma unroll
+    for (int lt = ls - 1; lt >= 0; --lt) {
+      const int s = 1 << lt;
+      if (s < E) {
+        cmpx_in_thread<E>(v, s, base, span);
+      } else if (s < 32 * E) {
+        const int m = s / E;
+        const bool low = (lane & m) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const uint32_t p = __shfl_xor_sync(0xffffffffu, v[e], m);
+          const bool keep_min = low == (((base + e) & span) == 0);
+          v[e] = keep_min ? min(v[e], p) : max(v[e], p);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) data[base + e] = v[e];
+        __syncthreads();
+        const bool low = (base & s) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const uint32_t p = data[(base + e) ^ s];
+          const bool keep_min = low == (((base + e) & span) == 0);
+          v[e] = keep_min ? min(v[e], p) : max(v[e], p);
+        }
+        __syncthreads();
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) data[base + e] = v[e];
+  __syncthreads();
+}
+
+template <int MAXE>
+__device__ void block_sort_u32(uint32_t* data, int size);
+
+// block_sort_u32 for blocks of exactly THREADS threads, with the unrolled networks.
+template <int MAXE, int THREADS>
+__device__ void block_sort_u32_fixed(uint32_t* data, int size) {
+  if (size == THREADS) return block_sort_fixed<1, THREADS>(data);
+  if (MAXE >= 2 && size == 2 * THREADS) return block_sort_fixed<(MAXE >= 2 ? 2 : 1), THREADS>(data);
+  if (MAXE >= 4 && size == 4 * THREADS) return block_sort_fixed<(MAXE >= 4 ? 4 : 1), THREADS>(data);
+  if (MAXE >= 8 && size == 8 * THREADS) return block_sort_fixed<(MAXE >= 8 ? 8 : 1), THREADS>(data);
+  block_sort_u32<1>(data, size);  // shared-memory network (size below the block or above MAXE per thread)
 }
 
 // Ascending sort of `size` (a power of two >= 32) values in shared memory: the
@@ -816,6 +898,165 @@ __global__ void __launch_bounds__(kSmallThreads) topk_small(TopkArgs args) {
   cta_topk<kSmallWarps>(n, k, cap, key_at, comp, src, out);
 }
 
+// Stage-1 top-k from the class max's per-image histogram of key high bytes
+// (k <= 4096, anchors <= 65536): the bucket holding the k-th key comes from that
+// histogram, so one pass over the records keeps only the candidates (high byte at
+// or below that bucket) -- in index order, in a shared-memory segment per warp
+// span -- and builds the low-byte histogram of the bucket; the threshold, the
+// index-ordered collection and the sort then run on the candidates alone.  A CTA
+// whose candidates overflow a segment falls back to the full top-k.
+__host__ __device__ constexpr int hist_segment(int cap) { return cap / 4 > 512 ? cap / 4 : 512; }
+
+// The top k of one image's records with the class max's high-byte histogram
+// `key_hist` (256 counts).  `work` is shared memory of hist_topk_words(k) words;
+// out[i] = key << 32 | anchor for i < k, in key order, ties in anchor order.
+__host__ __device__ constexpr int topk_cap(int k) {
+  int cap = 32;
+  while (cap < k) cap <<= 1;
+  return cap;
+}
+__host__ __device__ constexpr int hist_topk_words(int k) {
+  return 2 * topk_cap(k) + kSmallWarps * hist_segment(topk_cap(k));
+}
+
+__device__ void hist_topk(const uint32_t* rec, int n, int k, bool nan_last, const uint32_t* key_hist,
+                          uint32_t* work, unsigned long long* out) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sel_bucket, sel_below;
+  __shared__ int warp_lt[kSmallWarps], warp_eq[kSmallWarps];
+  __shared__ int overflow;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cap = topk_cap(k);
+  uint32_t* comp = work;
+  uint32_t* src = work + cap;
+  const int seg_cap = hist_segment(cap);
+  uint32_t* seg = work + 2 * cap + warp * seg_cap;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = key_hist[i];
+  if (threadIdx.x == 0) overflow = 0;
+  __syncthreads();
+  if (warp == 0) find_bucket(hist, (uint32_t)k, 0u, &sel_bucket, &sel_below);
+  __syncthreads();
+  const uint32_t high = sel_bucket, below_high = sel_below;
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  // one pass over the records: this warp's span of whole uint4 groups (n % 4 == 0),
+  // four records per lane per load, candidates compacted in index order by a
+  // warp scan of the per-lane counts
+  const uint4* rec4 = reinterpret_cast<const uint4*>(rec);
+  const int n4 = n >> 2;
+  const int span4 = (n4 + kSmallWarps - 1) / kSmallWarps;
+  const int lo4 = warp * span4, hi4 = lo4 + span4 < n4 ? lo4 + span4 : n4;
+  const uint32_t lane_lt = (1u << lane) - 1u;
+  int count = 0;
+  constexpr int U = 4;  // uint4 loads in flight per lane
+  for (int base = lo4; base < hi4; base += 32 * U) {
+    uint4 q[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = base + u * 32 + lane;
+      q[u] = g < hi4 ? __ldg(rec4 + g) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = base + u * 32 + lane;
+      const uint32_t r4[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+      uint32_t key[4];
+      int mine = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        key[j] = score_key((uint16_t)(r4[j] & 0xffffu), nan_last);
+        mine += (g < hi4 && (key[j] >> 8) <= high) ? 1 : 0;
+      }
+      int incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      int pos = count + incl - mine;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (g < hi4 && (key[j] >> 8) <= high) {
+          if (pos < seg_cap) seg[pos] = (key[j] << 16) | (uint32_t)(4 * g + j);
+          ++pos;
+        }
+      }
+      count += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  if (lane == 0 && count > seg_cap) overflow = 1;
+  __syncthreads();
+  if (overflow) {  // candidates spill a segment (clustered scores): the full top-k, keys read again
+    auto key_at = [&](int i) -> uint32_t { return score_key((uint16_t)(rec[i] & 0xffffu), nan_last); };
+    cta_topk<kSmallWarps>(n, k, cap, key_at, comp, src, out);
+    return;
+  }
+  // low bytes of the keys in the selected high-byte bucket, from the candidates
+  for (int base = 0; base < count; base += 32) {
+    const int j = base + lane;
+    const uint32_t key = j < count ? seg[j] >> 16 : 0xffffffffu;
+    hist_add(hist, key & 255u, (key >> 8) == high);
+  }
+  __syncthreads();
+  if (warp == 0) find_bucket(hist, (uint32_t)k, below_high, &sel_bucket, &sel_below);
+  __syncthreads();
+  const uint32_t threshold = (high << 8) | sel_bucket;
+  const int need = k - (int)sel_below;
+  // index-ordered collection over the segments (warp order is index order)
+  int lt = 0, eq = 0;
+  for (int base = 0; base < count; base += 32) {
+    const int j = base + lane;
+    const uint32_t key = j < count ? seg[j] >> 16 : 0xffffffffu;
+    lt += __popc(__ballot_sync(0xffffffffu, key < threshold));
+    eq += __popc(__ballot_sync(0xffffffffu, key == threshold));
+  }
+  if (lane == 0) {
+    warp_lt[warp] = lt;
+    warp_eq[warp] = eq;
+  }
+  __syncthreads();
+  int eq_before = 0, taken_before = 0;
+  for (int w = 0; w < warp; ++w) {
+    int take_eq = need - eq_before;
+    take_eq = take_eq < 0 ? 0 : (take_eq > warp_eq[w] ? warp_eq[w] : take_eq);
+    taken_before += warp_lt[w] + take_eq;
+    eq_before += warp_eq[w];
+  }
+  for (int base = 0; base < count; base += 32) {
+    const int j = base + lane;
+    const uint32_t entry = j < count ? seg[j] : 0u;
+    const uint32_t key = j < count ? entry >> 16 : 0xffffffffu;
+    const uint32_t eq_mask = __ballot_sync(0xffffffffu, key == threshold);
+    const int my_eq_rank = eq_before + __popc(eq_mask & lane_lt);
+    const bool take = key < threshold || (key == threshold && my_eq_rank < need);
+    const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
+    if (take) {
+      const int pos = taken_before + __popc(take_mask & lane_lt);
+      comp[pos] = (key << 12) | (uint32_t)pos;
+      src[pos] = entry & 0xffffu;
+    }
+    taken_before += __popc(take_mask);
+    eq_before += __popc(eq_mask);
+  }
+  __syncthreads();
+  for (int i = k + threadIdx.x; i < cap; i += blockDim.x) comp[i] = 0xffffffffu;
+  __syncthreads();
+  block_sort_u32_fixed<4, kSmallThreads>(comp, cap);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const uint32_t c = comp[i];
+    out[i] = ((unsigned long long)(c >> 12) << 32) | (unsigned long long)src[c & 0xfffu];
+  }
+}
+
+__global__ void __launch_bounds__(kSmallThreads) topk_hist(TopkArgs args, const uint32_t* key_hist) {
+  extern __shared__ uint32_t dyn[];
+  const int64_t b = blockIdx.x;
+  if (args.k <= 0) return;
+  hist_topk(args.src.records + b * args.src.pitch, (int)args.n, (int)args.k, args.nan_last, key_hist + b * 256,
+            dyn, args.sorted + b * args.sorted_pitch);
+}
+
 // --------------------------------------------------------- 3. pair gather
 
 // pair_bits[b][r*nc + c] = score of class c at the stage-1 anchor of rank r.
@@ -842,7 +1083,8 @@ __global__ void __launch_bounds__(256) gather_pairs(SelectView v, bool sigmoid,
 // anchor r) all have keys <= K1, so every pair of the final top k has a key
 // <= K1 too; a non-best class of anchor r can qualify only if the best score
 // among its other classes has key <= K1 (the class-max pass records that key,
-// 0 for anchors it rescanned).  Candidates: (r, best class) for every other
+// from the second-largest logit, or from the exact rescan for the anchors it
+// rescans).  Candidates: (r, best class) for every other
 // anchor, and every class with key <= K1 of the anchors that may hold more
 // (read exactly, as gather_pairs does).  Up to kPairCand candidates, as 32-bit
 // composites (key << 15 | r*nc + c), are sorted ascending in shared memory --
@@ -927,6 +1169,135 @@ __global__ void __launch_bounds__(kPairThreads) pairs_fused(SelectView v, bool n
   for (int j = tid; j < k; j += kPairThreads) pack(j, (int)(pair_cand[j] & 0x7fffu));
 }
 
+// Stage 1, the class-aware pair stage and the pack for one image per CTA
+// (planar sigmoid scores, k <= 2048, no trace).  The stage-1 top-k (hist_topk)
+// stays in shared memory; right after it each of the k anchors' record, second
+// key and four box values are read in one batch, so the pack touches global
+// memory only for the rare non-best classes of anchors gathered in full.  The
+// candidate rule and ordering are those of pairs_fused.
+// Shared memory in words: stage-1 (2k), boxes (2k), records (k), then the
+// top-k work area, reused by the pair candidates.
+__host__ __device__ constexpr int finish_work_offset(int k) { return (5 * k + 1) & ~1; }
+__host__ __device__ constexpr int finish_words(int k) {
+  return finish_work_offset(k) + (hist_topk_words(k) > kPairCand + k + 2 * topk_cap(k)
+                                      ? hist_topk_words(k)
+                                      : kPairCand + k + 2 * topk_cap(k));
+}
+
+__global__ void __launch_bounds__(kSmallThreads) select_finish(SelectView v, bool nan_last, int k,
+                                                               const uint32_t* records,
+                                                               const uint16_t* second_keys,
+                                                               const uint32_t* key_hist, float* out) {
+  extern __shared__ __align__(16) unsigned long long finish_smem[];
+  __shared__ int count, n_full;
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const int nc = (int)v.classes;
+  uint32_t* words = reinterpret_cast<uint32_t*>(finish_smem);
+  unsigned long long* s1 = finish_smem;
+  uint2* boxes = reinterpret_cast<uint2*>(words + 2 * k);
+  uint32_t* recs = words + 4 * k;
+  uint32_t* work = words + finish_work_offset(k);
+  const uint32_t* rec_b = records + (int64_t)b * v.anchors;
+  const uint16_t* box_b = v.base + (int64_t)b * v.sb;  // planar: anchor stride 1
+  hist_topk(rec_b, (int)v.anchors, k, nan_last, key_hist + (int64_t)b * 256, work, s1);
+  if (tid == 0) count = n_full = 0;
+  __syncthreads();
+  const uint32_t k1 = (uint32_t)(s1[k - 1] >> 32);
+  uint32_t* pair_cand = work;
+  int* full = reinterpret_cast<int*>(work + kPairCand);
+  uint32_t* topk_comp = work + kPairCand + k;
+  const uint32_t lane_lt = (1u << lane) - 1u;
+  // appends to a shared list with one atomic per warp
+  auto append = [&](int* counter, bool take) -> int {
+    const uint32_t m = __ballot_sync(0xffffffffu, take);
+    int first = 0;
+    if (lane == 0 && m) first = atomicAdd(counter, __popc(m));
+    return __shfl_sync(0xffffffffu, first, 0) + __popc(m & lane_lt);
+  };
+  for (int base = 0; base < k; base += kSmallThreads) {  // CTA-uniform trips for the ballots
+    const int r = base + tid;
+    const bool live = r < k;
+    const unsigned long long e = live ? s1[r] : 0ull;
+    const int a = (int)(e & 0xffffffffull);
+    uint32_t rec = 0, second = 0xffffffffu, q[4] = {0u, 0u, 0u, 0u};
+    if (live) {
+      rec = rec_b[a];
+      second = second_keys[(int64_t)b * v.anchors + a];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q[j] = box_b[a + j * v.sc];
+      recs[r] = rec;
+      boxes[r] = make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
+    }
+    const bool best_only = live && second > k1;  // only the best class can rank
+    const int slot = append(&count, best_only);
+    if (best_only && slot < kPairCand)
+      pair_cand[slot] = ((uint32_t)(e >> 32) << 15) | (uint32_t)(r * nc + (int)(rec >> 16));
+    const int fslot = append(&n_full, live && !best_only);
+    if (live && !best_only) full[fslot] = r;
+  }
+  __syncthreads();
+  // every class of the anchors that may hold more than their best: (anchor, class)
+  // items over the whole CTA, four score loads in flight per thread
+  const int items = n_full * nc;
+  for (int base = 0; base < items; base += 4 * kSmallThreads) {
+    uint16_t raw[4];
+    int flat[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = base + u * kSmallThreads + tid;
+      flat[u] = -1;
+      raw[u] = 0;
+      if (t < items) {
+        const int f = t / nc, c = t - f * nc;
+        const int r = full[f];
+        raw[u] = box_b[(int64_t)(s1[r] & 0xffffffffull) + (int64_t)(c + 4) * v.sc];
+        flat[u] = r * nc + c;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t key = flat[u] >= 0 ? score_key(sigmoid_h_fast(raw[u]), nan_last) : 0xffffffffu;
+      const bool take = flat[u] >= 0 && key <= k1;
+      const int slot = append(&count, take);
+      if (take && slot < kPairCand) pair_cand[slot] = (key << 15) | (uint32_t)flat[u];
+    }
+  }
+  __syncthreads();
+  const int n = count;  // >= k: the k best-class pairs are always candidates
+  auto pack = [&](int j, int flat) {
+    const int r = flat / nc, c = flat - r * nc;
+    const uint32_t rec = recs[r];
+    const uint16_t bits = c == (int)(rec >> 16) ? (uint16_t)(rec & 0xffffu)
+                                                 : score_bits(v, b, (int64_t)(s1[r] & 0xffffffffull), c, true);
+    const uint2 bx = boxes[r];
+    const int64_t t = (int64_t)b * k + j;
+    uint32_t* row = reinterpret_cast<uint32_t*>(out + t * 6);
+    row[0] = float_bits_of_half((uint16_t)(bx.x & 0xffffu));
+    row[1] = float_bits_of_half((uint16_t)(bx.x >> 16));
+    row[2] = float_bits_of_half((uint16_t)(bx.y & 0xffffu));
+    row[3] = float_bits_of_half((uint16_t)(bx.y >> 16));
+    row[4] = float_bits_of_half(bits);
+    out[t * 6 + 5] = (float)c;
+  };
+  if (n > kPairCand) {  // many ties at K1: the exact top-k over all k*nc pairs, keys read on the fly
+    unsigned long long* sorted = reinterpret_cast<unsigned long long*>(pair_cand);
+    auto key_at = [&](int i) -> uint32_t {
+      const int r = i / nc, c = i - r * nc;
+      return score_key(score_bits(v, b, (int64_t)(s1[r] & 0xffffffffull), c, true), nan_last);
+    };
+    cta_topk<kSmallWarps>(k * nc, k, topk_cap(k), key_at, topk_comp, topk_comp + topk_cap(k), sorted);
+    __syncthreads();
+    for (int j = tid; j < k; j += kSmallThreads) pack(j, (int)(sorted[j] & 0xffffffffull));
+    return;
+  }
+  int size = 32;
+  while (size < n) size <<= 1;
+  for (int i = n + tid; i < size; i += kSmallThreads) pair_cand[i] = 0xffffffffu;
+  __syncthreads();
+  block_sort_u32_fixed<8, kSmallThreads>(pair_cand, size);
+  for (int j = tid; j < k; j += kSmallThreads) pack(j, (int)(pair_cand[j] & 0x7fffu));
+}
+
 // ------------------------------------------------------------------ 4. pack
 
 struct PackArgs {
@@ -984,7 +1355,7 @@ __global__ void __launch_bounds__(256) pack_rows(PackArgs p) {
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct Workspace {
-  size_t records, second, stage1, pairs, stage2, hist, scratch, total;
+  size_t records, second, key_hist, stage1, pairs, stage2, hist, scratch, total;
 };
 
 ttn_status launch_topk(const TopkArgs& args, int64_t batch, int64_t k, cudaStream_t s) {
@@ -1014,6 +1385,8 @@ Workspace layout(int64_t batch, int64_t anchors, int64_t classes, int64_t k, boo
   size_t off = align256((size_t)batch * anchors * 4);
   w.second = off;
   off += agnostic ? 0 : align256((size_t)batch * anchors * 2);
+  w.key_hist = off;
+  off += align256((size_t)batch * 256 * 4);
   w.stage1 = off;
   off += align256((size_t)batch * kp * 8);
   w.pairs = off;
@@ -1099,10 +1472,15 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
   const bool fused = planar && sigmoid && !agnostic && !traced && k >= 1 && k <= 2048 &&
                      k * v.classes <= kPairFlatMax && (int64_t)pair_smem <= max_dynamic_smem();
   uint16_t* second = fused ? (uint16_t*)(ws + w.second) : nullptr;
+  // the stage-1 top-k from a histogram the class max builds (planar sigmoid path)
+  const bool from_hist = planar && sigmoid && k >= 1 && k <= kSmemSort && v.anchors <= 65536;
+  uint32_t* key_hist = from_hist ? (uint32_t*)(ws + w.key_hist) : nullptr;
+  if (from_hist)
+    TTN_TRY(cuda_check(cudaMemsetAsync(key_hist, 0, (size_t)v.batch * 256 * 4, s), "ttn_select_f16 memset"));
   if (planar && sigmoid) {
     int64_t work = v.batch * (v.anchors / 4);
     class_max_planar_sigmoid<4><<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, records, v.anchors,
-                                                                       tr.class_max, second);
+                                                                       tr.class_max, second, key_hist);
   } else if (planar) {
     int64_t work = v.batch * (v.anchors / 8);
     class_max_planar8<<<grid_for(work, 256, 8), 256, 0, s>>>(v, nan_last, sigmoid, records,
@@ -1119,9 +1497,25 @@ ttn_status ttn_select_f16(const ttn_tensor* decoded, int64_t max_det, uint32_t f
   TTN_TRY(launch_check("ttn_select_f16 class_max"));
   if (!k) return TTN_OK;
 
+  // 2'-3'. class-aware without trace from the histogram: top-k, pairs and pack in one kernel
+  if (fused && from_hist && finish_words((int)k) * 4 <= max_dynamic_smem()) {
+    const int smem = finish_words((int)k) * 4;
+    TTN_TRY(ensure_dynamic_smem((const void*)select_finish, smem));
+    select_finish<<<(unsigned)v.batch, kSmallThreads, smem, s>>>(v, nan_last, (int)k, records, second, key_hist,
+                                                                 out);
+    return launch_check("ttn_select_f16 finish");
+  }
+
   // 2. stage-1 top-k over anchors
   TopkArgs t1{KeySource{records, nullptr, v.anchors}, v.anchors, k, nan_last, stage1, kp, hist, scratch};
-  TTN_TRY(launch_topk(t1, v.batch, k, s));
+  if (from_hist) {
+    const size_t smem = (size_t)hist_topk_words((int)k) * 4;
+    TTN_TRY(ensure_dynamic_smem((const void*)topk_hist, (int)smem));
+    topk_hist<<<(unsigned)v.batch, kSmallThreads, smem, s>>>(t1, key_hist);
+    TTN_TRY(launch_check("ttn_select_f16 topk"));
+  } else {
+    TTN_TRY(launch_topk(t1, v.batch, k, s));
+  }
 
   // 3'. class-aware without trace: candidate pairs, sort and pack in one kernel
   if (fused) {
