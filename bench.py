@@ -63,9 +63,10 @@ def parse():
     p.add_argument("--sweep", choices=("silu", "sigmoid", "c2f"),
                    help="print fp16 unary bandwidth by tensor size, or the C2f region fused vs op by op "
                         "(one GPU), and exit")
-    p.add_argument("--config", type=int, default=4, choices=(1, 2, 3, 4, 5, 6, 7, 8),
+    p.add_argument("--config", type=int, default=4, choices=(1, 2, 3, 4, 5, 6, 7, 8, 9),
                    help="BASELINE config; 4 (the op pass) is the headline workload; 6 = fused C2PSA attention; "
-                        "7 = YOLOv8s conv pass; 8 = YOLO11s depthwise convs")
+                        "7 = YOLOv8s conv pass; 8 = YOLO11s depthwise convs; 9 = the whole YOLOv8s forward "
+                        "(convs chained with the op pass)")
     return p.parse_args()
 
 

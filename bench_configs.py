@@ -368,7 +368,43 @@ class Config8:
             oops.depthwise(x, w, b, 3, 1, True)
 
 
-CONFIGS = {1: Config1, 2: Config2, 3: Config3, 5: Config5, 6: Config6, 7: Config7, 8: Config8}
+class Config9:
+    """The whole YOLOv8s-640 forward chained on the GPU (yolo.ModelPass): the 63 convs
+    with bias + SiLU fused in their epilogue, writing straight into the op pass's
+    buffers and concat slices, interleaved with the op pass in model order up to the
+    decoded [B, 84, 8400] head, one CUDA-graph replay per step.  Tensor-core bound."""
+    name = "config 9: YOLOv8s-640 whole forward, 63 fused convs chained with the op pass, NC1HWC0 fp16"
+    batch, cpu_batch = 32, 1
+    bound = "tensor"
+
+    def __init__(self):
+        from thintnpu_b200 import yolo
+        self.plan = yolo.yolov8s_plan(640)
+        self.flops_per_image = sum(sp.flops for sp in yolo.yolov8s_convs(640))
+        convs = Config7()
+        self.bytes_per_image = convs.bytes_per_image + sum(self.plan.bytes_per_image().values())
+        self.launches = 0
+
+    def setup(self, batch, device, seed):
+        from thintnpu_b200 import yolo
+        self.model = yolo.ModelPass(self.plan, yolo.model_weights(self.plan, device, seed),
+                                    yolo.synthetic_image(self.plan, batch, device, seed + 1))
+        self.launches = self.model.launches_per_pass()
+        self.model.capture(warmup=2)
+        return [self.model.image], [self.model.output]
+
+    def step(self):
+        self.model.graph.replay()
+
+    def cpu_step(self, batch):
+        from oracle import yolo as oyolo
+        from thintnpu_b200 import yolo
+        if not hasattr(self, "cpu_inputs"):
+            self.cpu_inputs = (yolo.model_weights(self.plan, "cpu", 9), yolo.synthetic_image(self.plan, batch, "cpu", 10))
+        oyolo.run_model(self.plan, *self.cpu_inputs)
+
+
+CONFIGS = {1: Config1, 2: Config2, 3: Config3, 5: Config5, 6: Config6, 7: Config7, 8: Config8, 9: Config9}
 
 
 def device_time(step, steps: int, warmup: int, device, barrier, max_over_ranks) -> float:

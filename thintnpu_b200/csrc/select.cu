@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(256) class_max_planar_sigmoid(SelectView v, bo
                                                                 uint16_t* trace_max, uint16_t* second_keys,
                                                                 uint32_t* key_hist) {
   constexpr int W = APT / 2;      // half2 words per class row
-  constexpr int ROWS = 32 / APT;  // class rows in flight
+  constexpr int ROWS = 64 / APT;  // class rows in flight
   using Vec = typename std::conditional<W == 4, uint4, typename std::conditional<W == 2, uint2, uint32_t>::type>::type;
   const int lane = threadIdx.x & 31;
   const int64_t groups = v.anchors / APT;

@@ -51,7 +51,12 @@ class Plan:
     nc: int
     shapes: Dict[str, Tuple[int, int, int]] = field(default_factory=dict)  # name -> (c1, h, w)
     conv_inputs: List[str] = field(default_factory=list)  # synthetic pass inputs, in model order
+    # per conv (same order): its input (None = the image) and (kernel, stride)
+    conv_sources: List[Optional[Ref]] = field(default_factory=list)
+    conv_kernels: List[Tuple[int, int]] = field(default_factory=list)
     steps: List[Step] = field(default_factory=list)
+    # the model order of convs and steps: ("conv", conv index) / ("step", step index)
+    order: List[Tuple[str, int]] = field(default_factory=list)
     levels: List[Tuple[int, int]] = field(default_factory=list)
     strides: List[float] = field(default_factory=list)
 
@@ -104,63 +109,71 @@ class _Builder:
         self.plan.shapes[name] = (c1, h, w)
         return name
 
-    def conv(self, channels: int, h: int, w: int, act: bool = True) -> Ref:
+    def step(self, step: Step) -> None:
+        self.plan.order.append(("step", len(self.plan.steps)))
+        self.plan.steps.append(step)
+
+    def conv(self, channels: int, h: int, w: int, act: bool = True, src: Optional[Ref] = None,
+             k: int = 1, s: int = 1) -> Ref:
+        """A conv with `channels` outputs at h x w from `src` (None: the image)."""
         c1 = (channels + C0 - 1) // C0
         raw = self._new("conv", c1, h, w)
+        self.plan.order.append(("conv", len(self.plan.conv_inputs)))
         self.plan.conv_inputs.append(raw)
+        self.plan.conv_sources.append(src)
+        self.plan.conv_kernels.append((k, s))
         if not act:
             return Ref(raw, 0, c1)
         out = self._new("act", c1, h, w)
-        self.plan.steps.append(Step("silu", (Ref(raw, 0, c1),), out))
+        self.step(Step("silu", (Ref(raw, 0, c1),), out))
         return Ref(out, 0, c1)
 
     def add(self, a: Ref, b: Ref) -> Ref:
         _, h, w = self.plan.shapes[a.name]
         out = self._new("add", a.count, h, w)
-        self.plan.steps.append(Step("add", (a, b), out))
+        self.step(Step("add", (a, b), out))
         return Ref(out, 0, a.count)
 
     def cat(self, refs: Sequence[Ref]) -> Ref:
         _, h, w = self.plan.shapes[refs[0].name]
         total = sum(r.count for r in refs)
         out = self._new("cat", total, h, w)
-        self.plan.steps.append(Step("cat", tuple(refs), out))
+        self.step(Step("cat", tuple(refs), out))
         return Ref(out, 0, total)
 
     def upsample(self, x: Ref) -> Ref:
         _, h, w = self.plan.shapes[x.name]
         out = self._new("up", x.count, 2 * h, 2 * w)
-        self.plan.steps.append(Step("upsample", (x,), out))
+        self.step(Step("upsample", (x,), out))
         return Ref(out, 0, x.count)
 
     def sppf_pools(self, x: Ref, k: int = 5) -> Ref:
         _, h, w = self.plan.shapes[x.name]
         out = self._new("sppf", 4 * x.count, h, w)
-        self.plan.steps.append(Step("sppf", (x,), out, (k,)))
+        self.step(Step("sppf", (x,), out, (k,)))
         return Ref(out, 0, 4 * x.count)
 
     # --- modules
-    def c2f(self, x_hw: Tuple[int, int], c2: int, n: int, shortcut: bool) -> Ref:
+    def c2f(self, x_hw: Tuple[int, int], c2: int, n: int, shortcut: bool, x: Optional[Ref] = None) -> Ref:
         h, w = x_hw
         c = c2 // 2
-        y = self.conv(2 * c, h, w)                       # cv1
+        y = self.conv(2 * c, h, w, src=x)                # cv1
         half = y.count // 2
         parts = [Ref(y.name, y.start, half), Ref(y.name, y.start + half, half)]
         last = parts[-1]
         for _ in range(n):                               # Bottleneck(c, c, shortcut, e=1.0)
-            t = self.conv(c, h, w)
-            t = self.conv(c, h, w)
+            t = self.conv(c, h, w, src=last, k=3)
+            t = self.conv(c, h, w, src=t, k=3)
             last = self.add(last, t) if shortcut else t
             parts.append(last)
         cat = self.cat(parts)
-        del cat
-        return self.conv(c2, h, w)                       # cv2
+        return self.conv(c2, h, w, src=cat)              # cv2
 
-    def sppf(self, hw: Tuple[int, int], c2: int) -> Ref:
+    def sppf(self, hw: Tuple[int, int], c2: int, x: Optional[Ref] = None) -> Ref:
         h, w = hw
-        a = self.conv(c2 // 2, h, w)                     # cv1
-        self.sppf_pools(a, 5)
-        return self.conv(c2, h, w)                       # cv2
+        a = self.conv(c2 // 2, h, w, src=x)              # cv1
+        pools = self.sppf_pools(a, 5)
+        return self.conv(c2, h, w, src=pools)            # cv2
 
 
 def yolov8s_plan(imgsz: int = 640, nc: int = 80) -> Plan:
@@ -169,47 +182,45 @@ def yolov8s_plan(imgsz: int = 640, nc: int = 80) -> Plan:
         raise ValueError("imgsz must be a multiple of 32")
     b = _Builder(imgsz, nc)
     s = imgsz
-    b.conv(32, s // 2, s // 2)                                   # 0 P1/2
-    b.conv(64, s // 4, s // 4)                                   # 1 P2/4
-    b.c2f((s // 4, s // 4), 64, 1, True)                         # 2
-    b.conv(128, s // 8, s // 8)                                  # 3 P3/8
-    p3 = b.c2f((s // 8, s // 8), 128, 2, True)                   # 4
-    b.conv(256, s // 16, s // 16)                                # 5 P4/16
-    p4 = b.c2f((s // 16, s // 16), 256, 2, True)                 # 6
-    b.conv(512, s // 32, s // 32)                                # 7 P5/32
-    b.c2f((s // 32, s // 32), 512, 1, True)                      # 8
-    p5 = b.sppf((s // 32, s // 32), 512)                         # 9
+    x = b.conv(32, s // 2, s // 2, k=3, s=2)                     # 0 P1/2
+    x = b.conv(64, s // 4, s // 4, src=x, k=3, s=2)              # 1 P2/4
+    x = b.c2f((s // 4, s // 4), 64, 1, True, x)                  # 2
+    x = b.conv(128, s // 8, s // 8, src=x, k=3, s=2)             # 3 P3/8
+    p3 = b.c2f((s // 8, s // 8), 128, 2, True, x)                # 4
+    x = b.conv(256, s // 16, s // 16, src=p3, k=3, s=2)          # 5 P4/16
+    p4 = b.c2f((s // 16, s // 16), 256, 2, True, x)              # 6
+    x = b.conv(512, s // 32, s // 32, src=p4, k=3, s=2)          # 7 P5/32
+    x = b.c2f((s // 32, s // 32), 512, 1, True, x)               # 8
+    p5 = b.sppf((s // 32, s // 32), 512, x)                      # 9
     up = b.upsample(p5)                                          # 10
     cat = b.cat([up, p4])                                        # 11
-    h12 = b.c2f((s // 16, s // 16), 256, 1, False)               # 12
-    del cat
+    h12 = b.c2f((s // 16, s // 16), 256, 1, False, cat)          # 12
     up = b.upsample(h12)                                         # 13
-    b.cat([up, p3])                                              # 14
-    o3 = b.c2f((s // 8, s // 8), 128, 1, False)                  # 15 (P3 out)
-    d = b.conv(128, s // 16, s // 16)                            # 16
-    b.cat([d, h12])                                              # 17
-    o4 = b.c2f((s // 16, s // 16), 256, 1, False)                # 18 (P4 out)
-    d = b.conv(256, s // 32, s // 32)                            # 19
-    b.cat([d, p5])                                               # 20
-    o5 = b.c2f((s // 32, s // 32), 512, 1, False)                # 21 (P5 out)
-    del o3, o4, o5
+    cat = b.cat([up, p3])                                        # 14
+    o3 = b.c2f((s // 8, s // 8), 128, 1, False, cat)             # 15 (P3 out)
+    d = b.conv(128, s // 16, s // 16, src=o3, k=3, s=2)          # 16
+    cat = b.cat([d, h12])                                        # 17
+    o4 = b.c2f((s // 16, s // 16), 256, 1, False, cat)           # 18 (P4 out)
+    d = b.conv(256, s // 32, s // 32, src=o4, k=3, s=2)          # 19
+    cat = b.cat([d, p5])                                         # 20
+    o5 = b.c2f((s // 32, s // 32), 512, 1, False, cat)           # 21 (P5 out)
     # 22 Detect(nc, ch=(128, 256, 512)): c2 = max(16, 128//4, 64) = 64, c3 = max(128, min(nc, 100))
     c3 = max(128, min(nc, 100))
     anchor = 0
-    for stride in (8, 16, 32):
+    for stride, feat in ((8, o3), (16, o4), (32, o5)):
         h = w = s // stride
-        b.conv(64, h, w)
-        b.conv(64, h, w)
-        box = b.conv(64, h, w, act=False)
-        b.conv(c3, h, w)
-        b.conv(c3, h, w)
-        cls = b.conv(nc, h, w, act=False)
-        b.plan.steps.append(Step("restore", (box,), None, (0, 64, anchor)))
-        b.plan.steps.append(Step("restore", (cls,), None, (64, nc, anchor)))
+        t = b.conv(64, h, w, src=feat, k=3)
+        t = b.conv(64, h, w, src=t, k=3)
+        box = b.conv(64, h, w, act=False, src=t)
+        t = b.conv(c3, h, w, src=feat, k=3)
+        t = b.conv(c3, h, w, src=t, k=3)
+        cls = b.conv(nc, h, w, act=False, src=t)
+        b.step(Step("restore", (box,), None, (0, 64, anchor)))
+        b.step(Step("restore", (cls,), None, (64, nc, anchor)))
         b.plan.levels.append((h, w))
         b.plan.strides.append(float(stride))
         anchor += h * w
-    b.plan.steps.append(Step("decode", (), None, (True,)))
+    b.step(Step("decode", (), None, (True,)))
     return b.plan
 
 
@@ -431,6 +442,122 @@ class OpPass:
         """Kernels one pass launches: one per step, two for the decode (the box
         reduction and the class-row sigmoid, on forked branches)."""
         return sum(2 if step.op == "decode" else 1 for step in self.steps)
+
+
+def model_weights(plan: Plan, device, seed: int = 9):
+    """Seeded weights for every conv of the plan, one generator per conv (seed + index):
+    OIHW fp16 ~ N(0, 2 / fan-in) and bias fp16 ~ N(0, 0.1), drawn in FP32 on the CPU,
+    then moved to ``device``."""
+    out = []
+    for index, name in enumerate(plan.conv_inputs):
+        src = plan.conv_sources[index]
+        cin = 3 if src is None else src.count * C0
+        cout = plan.shapes[name][0] * C0
+        k, _ = plan.conv_kernels[index]
+        g = torch.Generator().manual_seed(seed + index)
+        w = (torch.randn(cout, cin, k, k, generator=g) * (2.0 / (cin * k * k)) ** 0.5).half()
+        b = (torch.randn(cout, generator=g) * 0.1).half()
+        out.append((w.to(device), b.to(device)))
+    return out
+
+
+def synthetic_image(plan: Plan, batch: int, device, seed: int = 3) -> torch.Tensor:
+    """Seeded image batch in NC1HWC0 [B, 1, S, S, 16] fp16: 3 channels ~ U(0, 1), the
+    other 13 zero (the stem's input channels padded to one block)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.zeros((batch, 1, plan.imgsz, plan.imgsz, C0), dtype=torch.float16)
+    x[..., :3] = torch.rand((batch, 1, plan.imgsz, plan.imgsz, 3), generator=g).half()
+    return x.to(device)
+
+
+class ModelPass(OpPass):
+    """The whole YOLOv8s forward on one device: the 63 convolutions (tcgen05 implicit
+    GEMM, bias and SiLU fused in the epilogue as the reference's conv does) chained with
+    the op pass in model order, capturable as one CUDA graph (the reference's whole-model
+    FrozenGraph around its blocked model, blocked_graph.py:4-23, whole_blocked.py:159-327).
+
+    Each activated conv writes its post-SiLU output straight into the op pass's
+    activation buffer -- with ``concat_in_place`` that is a C1 slice of the concat it
+    feeds -- so the pass's separate SiLU steps are dropped; the Detect box and class
+    convs (no activation) write the buffers the restore steps read.  ``weights`` is one
+    (OIHW fp16, bias fp16) pair per conv in model order (``model_weights``); ``image``
+    is the NC1HWC0 input [B, 1, S, S, 16] (``synthetic_image``).  Class count and every
+    conv width must be multiples of 16."""
+
+    def __init__(self, plan: Plan, weights, image: torch.Tensor, concat_in_place: bool = True):
+        ops._require(len(weights) == len(plan.conv_inputs), "ModelPass: one (weight, bias) pair per conv")
+        ops._require(plan.nc % C0 == 0, "ModelPass: the class count must be a multiple of 16")
+        ops._require(image.dtype == torch.float16 and tuple(image.shape[1:]) == (1, plan.imgsz, plan.imgsz, C0),
+                     f"ModelPass: image must be fp16 [B, 1, {plan.imgsz}, {plan.imgsz}, 16]")
+        self.plan = plan
+        self.image = image
+        self.batch = image.size(0)
+        self.device = image.device
+        self.act_of = {st.inputs[0].name: st.output for st in plan.steps if st.op == "silu"}
+        self.placed, self.elided = concat_placements(plan) if concat_in_place else ({}, set())
+
+        def alloc(name):
+            c1, h, w = plan.shapes[name]
+            return torch.empty((self.batch, c1, h, w, C0), dtype=torch.float16, device=self.device)
+
+        self.buffers: Dict[str, torch.Tensor] = {}
+        for name in self.elided:
+            self.buffers[name] = alloc(name)
+        for name, (cat, pos) in self.placed.items():
+            self.buffers[name] = self.buffers[cat][:, pos:pos + plan.shapes[name][0]]
+        for step in plan.steps:
+            if step.output is not None and step.output not in self.buffers:
+                self.buffers[step.output] = alloc(step.output)
+        self.convs = []
+        for index, name in enumerate(plan.conv_inputs):
+            out = self.act_of.get(name, name)
+            if out not in self.buffers:
+                self.buffers[out] = alloc(out)
+            w, b = weights[index]
+            k, stride = plan.conv_kernels[index]
+            self.convs.append((plan.conv_sources[index], ops.conv2d_pack_weights(w.contiguous()), b.contiguous(),
+                               int(w.size(0)), k, stride, name in self.act_of, out))
+        self.schedule = []
+        for kind, index in plan.order:
+            if kind == "conv":
+                self.schedule.append(("conv", index))
+            else:
+                step = plan.steps[index]
+                if step.op != "silu" and not (step.op == "cat" and step.output in self.elided):
+                    self.schedule.append(("step", step))
+        self.steps = [item for kind, item in self.schedule if kind == "step"]
+        self.head = torch.empty((self.batch, 64 + plan.nc, plan.anchors), dtype=torch.float16,
+                                device=self.device)
+        self.output = torch.empty((self.batch, 4 + plan.nc, plan.anchors), dtype=torch.float16,
+                                  device=self.device)
+        self.graph = None
+
+    def conv_input(self, index: int) -> torch.Tensor:
+        src = self.convs[index][0]
+        return self.image if src is None else self.view(src)
+
+    def run_conv(self, index: int) -> None:
+        _, packed, bias, cout, k, stride, silu, out = self.convs[index]
+        ops.conv2d(self.conv_input(index), packed, bias, cout, k, stride, silu=silu, out=self.buffers[out])
+
+    def run(self) -> torch.Tensor:
+        for kind, item in self.schedule:
+            if kind == "conv":
+                self.run_conv(item)
+            else:
+                self.run_step(item)
+        return self.output
+
+    def launches_per_pass(self) -> int:
+        return len(self.convs) + super().launches_per_pass()
+
+    def flops_per_image(self) -> int:
+        total = 0
+        for index, (src, _, _, cout, k, stride, _, out) in enumerate(self.convs):
+            cin = 3 if src is None else src.count * C0
+            _, oh, ow = self.plan.shapes[self.plan.conv_inputs[index]]
+            total += 2 * cin * cout * k * k * oh * ow
+        return total
 
 
 class C2fRegion:
