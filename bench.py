@@ -52,7 +52,8 @@ def parse():
     p.add_argument("--batch", type=int, default=256, help="images per GPU per step")
     p.add_argument("--imgsz", type=int, default=640)
     p.add_argument("--impl", choices=("ttn", "reference"), default="ttn")
-    p.add_argument("--cpu-threads", type=int, default=0, help="--impl reference: host threads (0 = all)")
+    p.add_argument("--cpu-threads", type=int, default=0,
+                   help="host threads of the CPU legs (--impl reference and cpu_baseline; 0 = all)")
     p.add_argument("--cpu-seconds", type=float, default=0.0,
                    help="--impl reference: keep sampling until this much CPU time has been timed")
     p.add_argument("--e2e-steps", type=int, default=10)

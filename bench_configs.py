@@ -534,7 +534,7 @@ def run_config(args):
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) != 0:
             return
-        threads = os.cpu_count() or 1
+        threads = getattr(args, "cpu_threads", 0) or os.cpu_count() or 1
         torch.set_num_threads(threads)
         cfg.cpu_step(cfg.cpu_batch)  # builds the inputs
         rate = cpu_rate(lambda: cfg.cpu_step(cfg.cpu_batch), cfg.cpu_batch, warmup=args.warmup,
@@ -598,7 +598,7 @@ def run_config(args):
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in inputs),
                     "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in outputs)}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
+        threads = getattr(args, "cpu_threads", 0) or os.cpu_count() or 1
         torch.set_num_threads(threads)
         cfg.cpu_step(cfg.cpu_batch)
         rate = cpu_rate(lambda: cfg.cpu_step(cfg.cpu_batch), cfg.cpu_batch)
