@@ -236,7 +236,6 @@ def run_pass(args):
 
     plan = yolo.yolov8s_plan(args.imgsz)
     per_image = plan.bytes_per_image()
-    bytes_per_image = sum(per_image.values()) - per_image.get("cat", 0)  # zero-copy plan: no concat copies
 
     def barrier():
         torch.cuda.synchronize(device)
@@ -249,8 +248,9 @@ def run_pass(args):
     # --- inputs resident in HBM; rank r owns images shard_range(world*B, world, r)
     images_mine = shard.shard_range(world * args.batch, world, rank)
     inputs = yolo.synthetic_inputs(plan, len(images_mine), device, seed=4 + images_mine.start)
-    op_pass = yolo.OpPass(plan, inputs, concat_in_place=True)
+    op_pass = yolo.OpPass(plan, inputs, concat_in_place=True, fuse_silu_add=True)
     op_pass.capture(warmup=2)
+    bytes_per_image = op_pass.bytes_per_image()  # no concat copies; no round trip of the fused SiLUs
     stream = torch.cuda.current_stream(device)
 
     # --- per-op instrumented pass (events on the launching stream) for the roofline
@@ -265,7 +265,7 @@ def run_pass(args):
             events.append((step, s, e))
         torch.cuda.synchronize(device)
     for step, s, e in events:
-        k = kinds.setdefault(step.op, {"ms": 0.0, "bytes": 0, "launches": 0})
+        k = kinds.setdefault(op_pass.kind(step), {"ms": 0.0, "bytes": 0, "launches": 0})
         k["ms"] += s.elapsed_time(e)
         k["bytes"] += plan.step_bytes(step) * args.batch
         k["launches"] += 1
@@ -321,6 +321,19 @@ def run_pass(args):
         plain.graph = None
         del plain
         torch.cuda.empty_cache()
+        unfused = yolo.OpPass(plan, inputs, concat_in_place=True)
+        unfused.capture(warmup=2)
+        ums = bench_configs.device_time(unfused.replay, args.steps, args.warmup, device, barrier, max_over_ranks)
+        ubytes = unfused.bytes_per_image()
+        variants["zero_copy_unfused"] = {
+            "value": images / (ums / 1000.0), "unit": "images/s", "ms_per_step": ums / args.steps,
+            "gpu_launches": unfused.launches_per_pass() * args.steps, "algorithmic_bytes_per_image": ubytes,
+            "achieved_hbm_gbs_pass": ubytes * args.batch * args.steps / (ums / 1000.0) / 1e9,
+            "note": "the zero-copy pass with the six bottleneck SiLUs run as their own kernels "
+                    "(outputs bit-identical)"}
+        unfused.graph = None
+        del unfused
+        torch.cuda.empty_cache()
         for key, cfg, total, seed in (("config3_b64", bench_configs.Config3(), 64, 30),
                                       ("config5_n512", bench_configs.Config5(), 512, 50)):
             variants[key] = bench_configs.measure_config(cfg, total, args.steps, args.warmup, device, rank, world,
@@ -344,12 +357,13 @@ def run_pass(args):
                    "parallelism": f"image-sharded x{world}, no data-path collective (gloo control plane)",
                    "l2": "inputs larger than L2 (no flush needed)",
                    "algorithmic_bytes_per_image": bytes_per_image, "replay": "one CUDA graph per step",
-                   "concat": "zero-copy: every concat buffer filled in place by its producers (no copy kernels)"},
+                   "concat": "zero-copy: every concat buffer filled in place by its producers (no copy kernels)",
+                   "fusion": "the six bottleneck SiLUs run inside their residual adds (ttn_add_silu_f16)"},
         "achieved_hbm_gbs_pass": bytes_per_image * args.batch * args.steps / (elapsed_ms / 1000.0) / 1e9,
-        "roofline": {"kernel": "silu (ttn_silu, 57 launches per pass)", "bound": "hbm",
+        "roofline": {"kernel": f"silu (ttn_silu, {silu['launches']} launches per pass)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-                     "traffic": silu_traffic_per_launch(plan, args.batch),
+                     "traffic": silu_traffic_per_launch(plan, op_pass.steps, args.batch),
                      "how": "algorithmic bytes (read+write, 4 B/element) of all SiLU launches of one "
                             "pass / their summed CUDA-event durations"},
         "kernels": {k: {"ms_per_pass": v["ms"], "launches": v["launches"],
@@ -372,14 +386,14 @@ def run_pass(args):
         dist.destroy_process_group()
 
 
-def silu_traffic_per_launch(plan, batch):
-    """DRAM bytes of the average SiLU launch of the pass, scaled from the
-    committed ncu capture's bytes per element (profiles/silu_f16.json)."""
+def silu_traffic_per_launch(plan, steps, batch):
+    """DRAM bytes of the average SiLU launch of the pass (`steps`, the ones it runs),
+    scaled from the committed ncu capture's bytes per element (profiles/silu_f16.json)."""
     path = ROOT / "profiles" / "silu_f16.json"
     if not path.exists():
         return None
     per_element = float(json.loads(path.read_text())["dram_bytes_per_element"])
-    silu_steps = [s for s in plan.steps if s.op == "silu"]
+    silu_steps = [s for s in steps if s.op == "silu"]
     elements = sum(plan.elements(s.inputs[0].name) for s in silu_steps)
     return per_element * elements * batch / len(silu_steps)
 
@@ -413,7 +427,7 @@ def run_e2e(args, plan, op_pass, inputs, device, world, barrier, max_over_ranks)
         if filled == pool_elems:
             break
     second = {n: torch.empty_like(t) for n, t in inputs.items()}
-    passes = [op_pass, yolo.OpPass(plan, second, concat_in_place=True)]
+    passes = [op_pass, yolo.OpPass(plan, second, concat_in_place=True, fuse_silu_add=True)]
     passes[1].capture(warmup=1)
     results = [torch.empty(p.output.shape, dtype=torch.float16, pin_memory=True) for p in passes]
     compute = torch.cuda.current_stream(device)

@@ -105,6 +105,16 @@ ttn_status ttn_sigmoid(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stre
 ttn_status ttn_binary(int op, float alpha, const ttn_tensor* x, const ttn_tensor* y,
                       const ttn_tensor* out, ttn_stream stream);
 
+/* out = a + SiLU(raw) over equal-sized fp16 views that are rows of 16-byte aligned
+ * contiguous vectors (e.g. NC1HWC0 images, channel-block slices): SiLU of raw
+ * rounded to fp16, then the add in FP32 with one rounding -- bit-identical to
+ * ttn_silu followed by ttn_binary(TTN_ADD).  The C2f bottleneck's activation and
+ * residual add (silu_ ops.cpp:498-512 on the conv output, then
+ * y.append(y[-1] + value) blocked_c2f.py:20-24) without the activation's round
+ * trip through HBM.  TTN_UNSUPPORTED for other layouts. */
+ttn_status ttn_add_silu_f16(const ttn_tensor* a, const ttn_tensor* raw, const ttn_tensor* out,
+                            ttn_stream stream);
+
 /* out = x (op) scalar, the scalar rounded to FP32 first (CPU eager "tensor op
  * python number").  Replaces the fp16 scale multiply whole_blocked.py:101-102. */
 ttn_status ttn_binary_scalar(int op, double scalar, const ttn_tensor* x,

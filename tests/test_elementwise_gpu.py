@@ -152,6 +152,37 @@ def test_silu_inplace_on_strided_parent_and_c2f_chain(device):
         assert_bits_equal(z, torch.cat((rp, rq + rq), 1), "c2f chain")
 
 
+def test_add_silu_every_input_bit_exact(device):
+    """a + SiLU(raw): raw over all 65,536 fp16 patterns (twice, against two random a),
+    bit-identical to CPU eager SiLU then the fp16 add wherever that sum is a number,
+    and to ttn's own silu then add where it is NaN (NaN or -inf raw: the device add
+    returns its canonical NaN, as ttn_binary does); dense, then NC1HWC0 channel slices
+    of wider buffers (batch-strided rows), then a layout that takes the silu-then-add
+    fallback (rows of 12 elements)."""
+    import thintnpu_b200 as ttn
+    g = torch.Generator().manual_seed(3)
+    raw = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.float16).repeat(2)
+    a = (torch.randn(raw.numel(), generator=g) * 4).half()
+    want = a + oops.silu(raw)
+    got = ttn.ops.add_silu(a.to(device), raw.to(device)).cpu()
+    number = ~torch.isnan(want)
+    assert_bits_equal(got[number], want[number], "dense")
+    two_step = ttn.add(a.to(device), ttn.silu(raw.to(device))).cpu()
+    assert torch.isnan(got[~number]).all()
+    assert_bits_equal(got[~number], two_step[~number], "dense NaN")
+    wide_a = (torch.randn(3, 6, 20, 20, 16, generator=g) * 2).half()
+    wide_raw = (torch.randn(3, 4, 20, 20, 16, generator=g) * 3).half()
+    out = torch.zeros(3, 8, 20, 20, 16, dtype=torch.float16, device=device)
+    da, draw = wide_a.to(device), wide_raw.to(device)
+    ttn.ops.add_silu(da[:, 1:3], draw[:, 2:4], out=out[:, 4:6])
+    assert_bits_equal(out[:, 4:6], wide_a[:, 1:3] + oops.silu(wide_raw[:, 2:4]), "channel slices")
+    assert torch.count_nonzero(out[:, :4]) == 0 and torch.count_nonzero(out[:, 6:]) == 0
+    odd_a = (torch.randn(5, 12, generator=g)).half()
+    odd_raw = (torch.randn(5, 16, generator=g) * 3).half()[:, :12]
+    got = ttn.ops.add_silu(odd_a.to(device), odd_raw.to(device))
+    assert_bits_equal(got, odd_a + oops.silu(odd_raw), "fallback layout")
+
+
 def test_config1_bias_silu_residual(device):
     import thintnpu_b200 as ttn
     g = torch.Generator().manual_seed(1)

@@ -76,3 +76,34 @@ def test_concat_in_place_equals_op_by_op(device, batch):
     fused.replay()
     torch.cuda.synchronize()
     assert_bits_equal(fused.output, plain.output, "decoded after replay")
+
+
+@pytest.mark.parametrize("concat_in_place", [False, True])
+def test_silu_add_fusion_equals_op_by_op(device, concat_in_place):
+    """The six bottleneck SiLUs run inside their residual adds: every tensor the
+    fused pass still makes is bit-identical, six fewer launches, 6 x 4 B per element
+    of those activations fewer algorithmic bytes; the CPU-eager pass agrees at B=2."""
+    from thintnpu_b200 import yolo
+    plan = yolo.yolov8s_plan(640)
+    inputs = yolo.synthetic_inputs(plan, 2, "cpu", seed=12)
+    dev = {k: v.to(device) for k, v in inputs.items()}
+    plain = yolo.OpPass(plan, dev, concat_in_place=concat_in_place)
+    fused = yolo.OpPass(plan, dev, concat_in_place=concat_in_place, fuse_silu_add=True)
+    assert len(fused.fused) == 6 and fused.launches_per_pass() == plain.launches_per_pass() - 6
+    skipped = {silu.output for _, silu in fused.fused.values()}
+    saved = sum(plan.step_bytes(silu) for _, silu in fused.fused.values())
+    assert plain.bytes_per_image() - fused.bytes_per_image() == saved
+    plain.run()
+    fused.run()
+    want, buffers, head = oyolo.run_pass(plan, inputs, keep=True)
+    for step in plan.steps:
+        if step.output is not None and step.output not in skipped:
+            assert_bits_equal(fused.buffers[step.output], plain.buffers[step.output], step.output)
+            assert_bits_equal(fused.buffers[step.output], buffers[step.output], f"{step.op} {step.output} (CPU)")
+    assert_bits_equal(fused.output, plain.output, "decoded")
+    assert_bits_equal(fused.head, head, "head (CPU)")
+    fused.capture()
+    fused.replay()
+    torch.cuda.synchronize()
+    assert_bits_equal(fused.output, plain.output, "decoded after replay")
+

@@ -8,7 +8,7 @@ is no CPU or PyTorch fallback.
 """
 from . import _lib
 from . import ops  # noqa: E402
-from .ops import (add, attention, bias_silu_residual, cat, contiguous, conv2d, conv2d_pack_weights,
+from .ops import (add, add_silu, attention, bias_silu_residual, cat, contiguous, conv2d, conv2d_pack_weights,
                   copy_, depthwise, depthwise_pack_weights, detection_select,  # noqa: E402,F401
                   dfl_decode, div, maxpool2d, maxpool_blocked, mul, pack, sigmoid, silu, silu_,
                   softmax, sppf, sub, unpack, upsample_blocked, upsample_nearest2d)

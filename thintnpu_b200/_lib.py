@@ -20,13 +20,14 @@ CONV_SILU, CONV_NCHW = 1, 2
 
 STATUS = {0: "TTN_OK", 1: "TTN_INVALID_ARG", 2: "TTN_UNSUPPORTED", 3: "TTN_CUDA_ERROR",
           4: "TTN_TIMEOUT", 5: "TTN_DEVICE_FAULT_FLAG"}
+UNSUPPORTED = 2
 
 # Every symbol include/ttn.h declares (checked by the CPU test suite).
 EXPORTS = (
     "ttn_version", "ttn_status_string", "ttn_last_error",
     "ttn_graph_create", "ttn_graph_begin", "ttn_graph_end", "ttn_graph_replay",
     "ttn_graph_close", "ttn_graph_destroy",
-    "ttn_silu", "ttn_sigmoid", "ttn_binary", "ttn_binary_scalar",
+    "ttn_silu", "ttn_sigmoid", "ttn_binary", "ttn_binary_scalar", "ttn_add_silu_f16",
     "ttn_bias_silu_residual_nc1hwc0_f16",
     "ttn_copy", "ttn_cat", "ttn_nc1hwc0_to_nchw_f16", "ttn_nchw_to_nc1hwc0_f16",
     "ttn_upsample2x", "ttn_upsample2x_nc1hwc0_f16", "ttn_maxpool", "ttn_sppf_f16",
@@ -80,6 +81,7 @@ _SIGNATURES = {
     "ttn_silu": (ctypes.c_int, [_TP, _TP, _P]),
     "ttn_sigmoid": (ctypes.c_int, [_TP, _TP, _P]),
     "ttn_binary": (ctypes.c_int, [ctypes.c_int, ctypes.c_float, _TP, _TP, _TP, _P]),
+    "ttn_add_silu_f16": (ctypes.c_int, [_TP, _TP, _TP, _P]),
     "ttn_binary_scalar": (ctypes.c_int, [ctypes.c_int, ctypes.c_double, _TP, _TP, _P]),
     "ttn_bias_silu_residual_nc1hwc0_f16": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "ttn_copy": (ctypes.c_int, [_TP, _TP, _P]),

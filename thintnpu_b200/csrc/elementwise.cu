@@ -320,6 +320,73 @@ ttn_status launch_lut(int kind, const uint16_t* x, uint16_t* y, const LutRows& r
   return launch_check(name);
 }
 
+// y = a + SiLU(raw), the residual add of a bottleneck whose second operand is a
+// conv output that nothing else reads: the SiLU table kernel with a second input.
+// Per element SiLU(raw) comes from the table (the exact fp16 value), then the add
+// runs as the binary kernels do, in FP32 with one rounding to fp16 -- bit-identical
+// to SiLU followed by the add.  raw and a stream through a per-thread ring of
+// kAddSlots slot pairs (2 x 16 bytes each), beside the 128 KB table.  Rows: n1 rows
+// of vpr vectors, element strides rs (raw), as (a) and ys (y) between rows.
+constexpr int kAddSlots = 4;
+constexpr int kAddSmem = kLutBytes + kAddSlots * kLutThreads * 32;
+
+struct AddRows {
+  int64_t rs, as, ys;
+  FastDiv vpr;
+};
+
+__device__ __forceinline__ uint32_t add_word(uint32_t a, uint32_t b) {
+  const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&a));
+  const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&b));
+  const __half2 h = __floats2half2_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(kLutThreads, 1) add_silu_lut(const uint16_t* table, const uint16_t* raw,
+                                                               const uint16_t* a, uint16_t* y, AddRows rows,
+                                                               uint32_t total) {
+  extern __shared__ __align__(16) uint8_t lut_smem[];
+  uint16_t* lut = reinterpret_cast<uint16_t*>(lut_smem);
+  uint4* ring_r = reinterpret_cast<uint4*>(lut_smem + kLutBytes) + threadIdx.x;
+  uint4* ring_a = ring_r + kAddSlots * kLutThreads;
+  const uint32_t stride = gridDim.x * kLutThreads;
+  const uint32_t first = blockIdx.x * kLutThreads + threadIdx.x;
+  auto fetch = [&](int slot, uint32_t g) {
+    const uint32_t row = rows.vpr.div(g), col = g - row * rows.vpr.d;
+    cp_async16(ring_r + slot * kLutThreads, raw + (int64_t)row * rows.rs + (int64_t)col * 8);
+    cp_async16(ring_a + slot * kLutThreads, a + (int64_t)row * rows.as + (int64_t)col * 8);
+  };
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(table);
+    uint4* dst = reinterpret_cast<uint4*>(lut);
+    for (int t = threadIdx.x; t < kLutBytes / 16; t += kLutThreads) cp_async16(dst + t, src + t);
+    cp_async_commit();
+  }
+#pragma unroll
+  for (int k = 0; k < kAddSlots - 1; ++k) {
+    const uint32_t g = first + k * stride;
+    if (g < total) fetch(k, g);
+    cp_async_commit();
+  }
+  cp_async_wait<kAddSlots - 1>();  // the table group has landed (for this thread's part)
+  __syncthreads();                 // ... and for every thread's part
+  int slot = 0;
+  for (uint32_t g = first; g < total; g += stride) {
+    const uint32_t ahead = g + (kAddSlots - 1) * stride;
+    const int refill = slot == 0 ? kAddSlots - 1 : slot - 1;  // the slot used last iteration
+    if (ahead < total) fetch(refill, ahead);
+    cp_async_commit();
+    cp_async_wait<kAddSlots - 1>();  // the group that filled `slot`
+    const uint4 v = lut_vec(lut, ring_r[slot * kLutThreads]);
+    const uint4 u = ring_a[slot * kLutThreads];
+    const uint32_t row = rows.vpr.div(g), col = g - row * rows.vpr.d;
+    *reinterpret_cast<uint4*>(y + (int64_t)row * rows.ys + (int64_t)col * 8) =
+        make_uint4(add_word(u.x, v.x), add_word(u.y, v.y), add_word(u.z, v.z), add_word(u.w, v.w));
+    slot = slot == kAddSlots - 1 ? 0 : slot + 1;
+  }
+  cp_async_wait<0>();
+}
+
 template <int K>
 ttn_status rows2(const uint16_t* x, int64_t xs1, int64_t xs2, uint16_t* y, int64_t ys1, int64_t ys2,
                  int64_t n1, int64_t n2, int64_t ncols, cudaStream_t s) {
@@ -708,6 +775,40 @@ ttn_status ttn_silu(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream)
 
 ttn_status ttn_sigmoid(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream) {
   return unary<kSigmoid>(x, y, stream, "ttn_sigmoid");
+}
+
+ttn_status ttn_add_silu_f16(const ttn_tensor* a, const ttn_tensor* raw, const ttn_tensor* out,
+                            ttn_stream stream) {
+  const char* name = "ttn_add_silu_f16";
+  TTN_TRY(validate(a, name));
+  TTN_TRY(validate(raw, name));
+  TTN_TRY(validate(out, name));
+  if (!same_sizes(a, raw) || !same_sizes(a, out)) return fail(TTN_INVALID_ARG, "%s: operand sizes differ", name);
+  if (a->dtype != TTN_F16 || raw->dtype != TTN_F16 || out->dtype != TTN_F16)
+    return fail(TTN_INVALID_ARG, "%s: fp16 operands only", name);
+  const ttn_tensor* views[3] = {raw, a, out};
+  Coalesced c = coalesce(views, 3);
+  if (!c.numel) return TTN_OK;
+  // rows of contiguous 16-byte vectors: at most two coalesced dims, unit inner stride
+  const bool rows_ok = c.ndim <= 2 && c.stride[0][0] == 1 && c.stride[1][0] == 1 && c.stride[2][0] == 1 &&
+                       c.size[0] % 8 == 0 && aligned16(raw->data) && aligned16(a->data) && aligned16(out->data) &&
+                       (c.ndim == 1 || (c.stride[0][1] % 8 == 0 && c.stride[1][1] % 8 == 0 && c.stride[2][1] % 8 == 0));
+  if (!rows_ok)
+    return fail(TTN_UNSUPPORTED, "%s: operands must be rows of 16-byte aligned contiguous vectors", name);
+  const int64_t vpr = c.size[0] / 8, n1 = c.ndim == 2 ? c.size[1] : 1, total = n1 * vpr;
+  if (total >= ((int64_t)1 << 31) || vpr >= ((int64_t)1 << 32))
+    return fail(TTN_UNSUPPORTED, "%s: more than 2^31 vectors", name);
+  AddRows rows{c.ndim == 2 ? c.stride[0][1] : 0, c.ndim == 2 ? c.stride[1][1] : 0,
+               c.ndim == 2 ? c.stride[2][1] : 0, FastDiv((uint32_t)vpr)};
+  cudaStream_t s = (cudaStream_t)stream;
+  const uint16_t* table = nullptr;
+  TTN_TRY(unary_table(kSilu, s, &table));
+  TTN_TRY(ensure_dynamic_smem((const void*)add_silu_lut, kAddSmem));
+  const int64_t want = (total + 4 * kLutThreads - 1) / (4 * kLutThreads);
+  const unsigned grid = (unsigned)(want < sm_count() ? (want < 1 ? 1 : want) : sm_count());
+  add_silu_lut<<<grid, kLutThreads, kAddSmem, s>>>(table, (const uint16_t*)raw->data, (const uint16_t*)a->data,
+                                                   (uint16_t*)out->data, rows, (uint32_t)total);
+  return launch_check(name);
 }
 
 ttn_status ttn_binary(int op, float alpha, const ttn_tensor* x, const ttn_tensor* y,

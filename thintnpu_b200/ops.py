@@ -118,6 +118,25 @@ def binary(op: str, x, y, alpha: float = 1.0, out: Optional[torch.Tensor] = None
     return z
 
 
+def add_silu(a: torch.Tensor, raw: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """a + SiLU(raw) in one pass (fp16, equal shapes): the C2f bottleneck's activation and
+    residual add (ops.cpp:498-512, blocked_c2f.py:20-24), bit-identical to ``silu`` then
+    ``add``.  Views that are not rows of aligned contiguous vectors take those two kernels."""
+    _cuda(a, "add_silu")
+    _cuda(raw, "add_silu")
+    _require(a.dtype == raw.dtype == torch.float16 and a.shape == raw.shape and a.device == raw.device,
+             "add_silu requires fp16 operands of one shape on one device")
+    z = torch.empty_like(a, memory_format=torch.contiguous_format) if out is None else out
+    _require(z.shape == a.shape and z.dtype == torch.float16, "add_silu: out must match a")
+    if not z.numel():
+        return z
+    status = _lib.lib().ttn_add_silu_f16(_ref(desc(a)), _ref(desc(raw)), _ref(desc(z)), stream())
+    if status == _lib.UNSUPPORTED:
+        return binary("add", a, silu(raw), out=z)
+    _lib.check("ttn_add_silu_f16", status)
+    return z
+
+
 def add(x, y, alpha: float = 1.0) -> torch.Tensor:
     return binary("add", x, y, alpha)
 

@@ -346,6 +346,28 @@ def concat_placements(plan: Plan):
     return placed, elided
 
 
+def silu_add_fusions(plan: Plan) -> Dict[str, Tuple[Ref, Step]]:
+    """Residual adds one of whose operands is the whole output of a SiLU step that no
+    other step reads: {add output: (the other operand, that SiLU step)}.  In YOLOv8s
+    these are the bottlenecks' second conv activations (six adds)."""
+    readers: Dict[str, int] = {}
+    for st in plan.steps:
+        for ref in st.inputs:
+            readers[ref.name] = readers.get(ref.name, 0) + 1
+    silus = {st.output: st for st in plan.steps if st.op == "silu"}
+    out = {}
+    for st in plan.steps:
+        if st.op != "add":
+            continue
+        for mine, other in ((st.inputs[1], st.inputs[0]), (st.inputs[0], st.inputs[1])):
+            silu = silus.get(mine.name)
+            if (silu is not None and readers[mine.name] == 1 and mine.start == 0
+                    and mine.count == plan.shapes[mine.name][0]):
+                out[st.output] = (other, silu)
+                break
+    return out
+
+
 class OpPass:
     """Executes a Plan on one CUDA device with preallocated buffers.
 
@@ -355,15 +377,21 @@ class OpPass:
     ``output`` is the decoded [B, 4+nc, anchors] fp16 tensor.
 
     ``concat_in_place`` turns on the zero-copy concat plan (concat_placements):
-    the same tensors result, every concat buffer filled by its producers."""
+    the same tensors result, every concat buffer filled by its producers.
+    ``fuse_silu_add`` runs each residual add whose operand is a SiLU output read by
+    nothing else as one ``add_silu`` launch on the conv output (silu_add_fusions):
+    the add's result is the same, and that SiLU output is never materialised."""
 
-    def __init__(self, plan: Plan, inputs: Dict[str, torch.Tensor], concat_in_place: bool = False):
+    def __init__(self, plan: Plan, inputs: Dict[str, torch.Tensor], concat_in_place: bool = False,
+                 fuse_silu_add: bool = False):
         self.plan = plan
         first = inputs[plan.conv_inputs[0]]
         self.batch = first.size(0)
         self.device = first.device
         self.buffers: Dict[str, torch.Tensor] = dict(inputs)
         self.placed, self.elided = concat_placements(plan) if concat_in_place else ({}, set())
+        self.fused = silu_add_fusions(plan) if fuse_silu_add else {}
+        skipped = {raw_silu.output for _, raw_silu in self.fused.values()}
 
         def alloc(name):
             c1, h, w = plan.shapes[name]
@@ -375,9 +403,10 @@ class OpPass:
             c1 = plan.shapes[name][0]
             self.buffers[name] = self.buffers[cat][:, pos:pos + c1]
         for step in plan.steps:
-            if step.output is not None and step.output not in self.buffers:
+            if step.output is not None and step.output not in self.buffers and step.output not in skipped:
                 self.buffers[step.output] = alloc(step.output)
-        self.steps = [st for st in plan.steps if not (st.op == "cat" and st.output in self.elided)]
+        self.steps = [st for st in plan.steps
+                      if not (st.op == "cat" and st.output in self.elided) and st.output not in skipped]
         self.head = torch.empty((self.batch, 64 + plan.nc, plan.anchors), dtype=torch.float16,
                                 device=self.device)
         self.output = torch.empty((self.batch, 4 + plan.nc, plan.anchors), dtype=torch.float16,
@@ -394,6 +423,9 @@ class OpPass:
         p = self.plan
         if step.op == "silu":
             ops.silu(self.view(step.inputs[0]), out=self.buffers[step.output])
+        elif step.op == "add" and step.output in self.fused:
+            other, silu = self.fused[step.output]
+            ops.add_silu(self.view(other), self.view(silu.inputs[0]), out=self.buffers[step.output])
         elif step.op == "add":
             ops.binary("add", self.view(step.inputs[0]), self.view(step.inputs[1]),
                        out=self.buffers[step.output])
@@ -442,6 +474,14 @@ class OpPass:
         """Kernels one pass launches: one per step, two for the decode (the box
         reduction and the class-row sigmoid, on forked branches)."""
         return sum(2 if step.op == "decode" else 1 for step in self.steps)
+
+    def bytes_per_image(self) -> int:
+        """Algorithmic bytes of the steps this pass runs (a fused add moves what the
+        add alone does; skipped SiLUs and elided concats move nothing)."""
+        return sum(self.plan.step_bytes(step) for step in self.steps)
+
+    def kind(self, step: Step) -> str:
+        return "add_silu" if step.op == "add" and step.output in self.fused else step.op
 
 
 def model_weights(plan: Plan, device, seed: int = 9):
@@ -495,6 +535,7 @@ class ModelPass(OpPass):
         self.device = image.device
         self.act_of = {st.inputs[0].name: st.output for st in plan.steps if st.op == "silu"}
         self.placed, self.elided = concat_placements(plan) if concat_in_place else ({}, set())
+        self.fused = {}  # the convs apply the SiLU themselves
 
         def alloc(name):
             c1, h, w = plan.shapes[name]
