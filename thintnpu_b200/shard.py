@@ -106,4 +106,4 @@ class Heartbeat:
                 return
             if time.monotonic() > deadline:
                 raise PeerFailure(f"ranks {behind} did not reach step {step} within {wait_s} s")
-            time.sleep(0.01)
+            time.sleep(0.001)
