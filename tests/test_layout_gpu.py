@@ -187,9 +187,12 @@ def test_sppf(device, n, c1, hw):
 
 
 @pytest.mark.parametrize("n,c1,h,w", [(2, 3, 13, 7), (1, 2, 5, 22), (1, 1, 1, 9), (2, 1, 3, 1), (1, 2, 21, 18),
-                                      (3, 5, 4, 4), (1, 1, 30, 31)])
+                                      (3, 5, 4, 4), (1, 1, 30, 31), (2, 3, 20, 7), (1, 2, 16, 32), (1, 1, 10, 1),
+                                      (2, 2, 20, 31), (1, 2, 10, 10), (3, 1, 16, 2)])
 def test_sppf_rectangular_planes(device, n, c1, h, w):
-    """Rows and columns that are not multiples of the kernel's four-output runs."""
+    """Rows and columns that are not multiples of the kernel's four-output runs, and
+    planes of 10, 16 or 20 rows and at most 32 columns (the warp-per-plane kernel,
+    its exact path taken by the plane holding NaN and -0)."""
     import thintnpu_b200 as ttn
     g = torch.Generator().manual_seed(h * 100 + w)
     x = torch.randn(n, c1, h, w, 16, generator=g).half()
