@@ -58,45 +58,64 @@ __global__ void __launch_bounds__(128) blocked_to_nchw(const uint16_t* x, int64_
 }
 
 // Register-transpose variant for hw % 4 == 0 and 8-byte aligned channel rows:
-// one thread per (plane, 4-pixel group) loads 4 pixels x 16 lanes (128 B,
-// contiguous per thread, consecutive threads contiguous) and writes 16 channel
-// rows of 4 pixels (8 B each; consecutive threads fill consecutive 8 B of a
-// row).  The 4x16 fp16 transpose is 32 byte permutes, no shared memory.
+// one thread per (plane, 4-pixel group) takes 4 pixels x 16 lanes (128 B) and
+// writes 16 channel rows of 4 pixels (8 B each; consecutive threads fill
+// consecutive 8 B of a row).  The warp loads its 32 groups together through a
+// shared-memory tile (one 512-byte coalesced load per instruction instead of 32
+// separate 128-byte runs); the 4x16 fp16 transpose is 32 byte permutes.
 __global__ void __launch_bounds__(256) blocked_to_nchw_regs(const uint4* x, int64_t n, int64_t c1,
                                                             int64_t hw, int64_t channels, uint16_t* y,
                                                             int64_t ybs, int64_t ycs) {
+  // A warp's 32 (plane, 4-pixel) items are one contiguous 4 KB of x (planes are
+  // adjacent), loaded with consecutive lanes on consecutive 16-byte vectors into a
+  // per-warp tile; vector j sits at j ^ ((j >> 3) & 7), so both the loads' stores
+  // (8 lanes on 8 consecutive vectors) and each lane's read-back of its own 8
+  // vectors (8 lanes 8 vectors apart) cover all 8 bank groups.
+  __shared__ uint4 tile[8][256];
+  uint4* mine = tile[threadIdx.x >> 5];
+  const int lane = threadIdx.x & 31;
   const int64_t groups = hw / 4;
   const int64_t total = n * c1 * groups;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
-    const int64_t plane = t / groups, g = t - plane * groups;
-    const int64_t b = plane / c1, cb = plane - b * c1;
-    const uint4* src = x + (plane * hw + g * 4) * 2;  // 2 uint4 (16 channels) per pixel
-    uint32_t in[4][8];                                 // [pixel][channel pair]
+  for (int64_t t0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); t0 < total; t0 += stride) {
+    const int64_t vecs = (total - t0) * 8 < 256 ? (total - t0) * 8 : 256;
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const uint4 lo = src[p * 2], hi = src[p * 2 + 1];
-      in[p][0] = lo.x;
-      in[p][1] = lo.y;
-      in[p][2] = lo.z;
-      in[p][3] = lo.w;
-      in[p][4] = hi.x;
-      in[p][5] = hi.y;
-      in[p][6] = hi.z;
-      in[p][7] = hi.w;
+    for (int k = 0; k < 8; ++k) {
+      const int j = k * 32 + lane;
+      if (j < vecs) mine[j ^ ((j >> 3) & 7)] = x[t0 * 8 + j];
     }
-    const int valid = (int)(channels - cb * 16 < 16 ? channels - cb * 16 : 16);
-    uint16_t* dst = y + b * ybs + (cb * 16) * ycs + g * 4;
+    __syncwarp();
+    const int64_t t = t0 + lane;
+    if (t < total) {
+      const int64_t plane = t / groups, g = t - plane * groups;
+      const int64_t b = plane / c1, cb = plane - b * c1;
+      uint32_t in[4][8];  // [pixel][channel pair]
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      if (c < valid) {
-        const uint32_t sel = (c & 1) ? 0x7632u : 0x5410u;  // high or low lane of each word
-        uint2 o;
-        o.x = __byte_perm(in[0][c >> 1], in[1][c >> 1], sel);
-        o.y = __byte_perm(in[2][c >> 1], in[3][c >> 1], sel);
-        *reinterpret_cast<uint2*>(dst + c * ycs) = o;
+      for (int p = 0; p < 4; ++p) {
+        const uint4 lo = mine[(8 * lane + 2 * p) ^ (lane & 7)], hi = mine[(8 * lane + 2 * p + 1) ^ (lane & 7)];
+        in[p][0] = lo.x;
+        in[p][1] = lo.y;
+        in[p][2] = lo.z;
+        in[p][3] = lo.w;
+        in[p][4] = hi.x;
+        in[p][5] = hi.y;
+        in[p][6] = hi.z;
+        in[p][7] = hi.w;
+      }
+      const int valid = (int)(channels - cb * 16 < 16 ? channels - cb * 16 : 16);
+      uint16_t* dst = y + b * ybs + (cb * 16) * ycs + g * 4;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        if (c < valid) {
+          const uint32_t sel = (c & 1) ? 0x7632u : 0x5410u;  // high or low lane of each word
+          uint2 o;
+          o.x = __byte_perm(in[0][c >> 1], in[1][c >> 1], sel);
+          o.y = __byte_perm(in[2][c >> 1], in[3][c >> 1], sel);
+          *reinterpret_cast<uint2*>(dst + c * ycs) = o;
+        }
       }
     }
+    __syncwarp();  // the tile is refilled next round
   }
 }
 
