@@ -184,6 +184,27 @@ __global__ void __launch_bounds__(256) upsample_blocked(const uint4* x, uint4* y
   }
 }
 
+// upsample_blocked for launches below 2^31 vectors: the vector's (image, plane,
+// row, column, half) from 32-bit multiply-high divisions instead of 64-bit ones.
+__global__ void __launch_bounds__(256) upsample_blocked32(const uint4* x, uint4* y, uint32_t nvec,
+                                                          FastDiv per_image, FastDiv hdiv, FastDiv wdiv,
+                                                          int64_t x_bs, int64_t y_bs) {
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const int64_t w = wdiv.d, h = hdiv.d;
+  for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    const uint32_t b = per_image.div(v), local = v - b * per_image.d;
+    const uint4 q = x[b * x_bs + local];
+    const uint32_t p = local >> 1, j = local & 1;
+    const uint32_t rest = wdiv.div(p), col = p - rest * wdiv.d;
+    const uint32_t plane = hdiv.div(rest), row = rest - plane * hdiv.d;
+    const int64_t base = b * y_bs + (((int64_t)plane * 2 * h + 2 * row) * 2 * w + 2 * col) * 2 + j;
+    y[base] = q;
+    y[base + 2] = q;
+    y[base + 4 * w] = q;
+    y[base + 4 * w + 2] = q;
+  }
+}
+
 // NCHW with w % 4 == 0: read 4 input columns (8 bytes), write 8 output columns
 // (16 bytes) to both output rows.
 __global__ void __launch_bounds__(256) upsample_nchw_vec(const uint2* x, uint4* y, int64_t planes,
@@ -720,8 +741,13 @@ ttn_status ttn_upsample2x(int layout, int dtype, const void* x, void* y, int64_t
     if (dtype != TTN_F16) return fail(TTN_UNSUPPORTED, "%s: NC1HWC0 supports float16", name);
     if (!aligned16(x) || !aligned16(y)) return fail(TTN_INVALID_ARG, "%s: 16-byte alignment", name);
     int64_t nvec = n * c * h * w * 2;
-    upsample_blocked<<<grid_for(nvec, 256), 256, 0, s>>>((const uint4*)x, (uint4*)y, n, c, h, w,
-                                                         c * h * w * 2, c * h * w * 8);
+    if (nvec < ((int64_t)1 << 31))
+      upsample_blocked32<<<grid_for(nvec, 256), 256, 0, s>>>(
+          (const uint4*)x, (uint4*)y, (uint32_t)nvec, FastDiv((uint32_t)(c * h * w * 2)), FastDiv((uint32_t)h),
+          FastDiv((uint32_t)w), c * h * w * 2, c * h * w * 8);
+    else
+      upsample_blocked<<<grid_for(nvec, 256), 256, 0, s>>>((const uint4*)x, (uint4*)y, n, c, h, w,
+                                                           c * h * w * 2, c * h * w * 8);
     return launch_check(name);
   }
   if (dtype == TTN_F16 && w % 4 == 0 && aligned16(y) && ((uintptr_t)x & 7u) == 0) {
@@ -750,6 +776,12 @@ ttn_status ttn_upsample2x_nc1hwc0_f16(const void* x, int64_t x_batch_stride, voi
   if (x_batch_stride < c1 * h * w * 16 || y_batch_stride < c1 * h * w * 64)
     return fail(TTN_INVALID_ARG, "%s: batch stride smaller than one image", name);
   int64_t nvec = n * c1 * h * w * 2;
+  if (nvec < ((int64_t)1 << 31)) {
+    upsample_blocked32<<<grid_for(nvec, 256), 256, 0, (cudaStream_t)stream>>>(
+        (const uint4*)x, (uint4*)y, (uint32_t)nvec, FastDiv((uint32_t)(c1 * h * w * 2)), FastDiv((uint32_t)h),
+        FastDiv((uint32_t)w), x_batch_stride / 8, y_batch_stride / 8);
+    return launch_check(name);
+  }
   upsample_blocked<<<grid_for(nvec, 256), 256, 0, (cudaStream_t)stream>>>(
       (const uint4*)x, (uint4*)y, n, c1, h, w, x_batch_stride / 8, y_batch_stride / 8);
   return launch_check(name);
