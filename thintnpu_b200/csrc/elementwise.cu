@@ -189,6 +189,8 @@ __global__ void __launch_bounds__(kThreads) unary_f16_dense(const uint16_t* x, u
   int tile = blockIdx.x * (kThreads / 32) + warp;
   if (lane == 0) q_count[warp] = 0;
   __syncwarp();
+  pdl_trigger();
+  pdl_wait();
   int count = 0;
   uint4 next[kVec];
   auto fetch = [&](int t) {
@@ -284,6 +286,8 @@ __global__ void __launch_bounds__(kLutThreads, 1) unary_f16_lut(const uint16_t* 
     for (int t = threadIdx.x; t < kLutBytes / 16; t += kLutThreads) cp_async16(dst + t, src + t);
     cp_async_commit();
   }
+  pdl_trigger();  // the table is built once per device, never written by a predecessor
+  pdl_wait();
 #pragma unroll
   for (int k = 0; k < kLutSlots - 1; ++k) {
     const uint32_t g = first + k * stride;
@@ -316,7 +320,9 @@ ttn_status launch_lut(int kind, const uint16_t* x, uint16_t* y, const LutRows& r
   TTN_TRY(ensure_dynamic_smem((const void*)unary_f16_lut<kRows>, kLutSmem));
   const int64_t want = (total + 4 * kLutThreads - 1) / (4 * kLutThreads);
   const unsigned grid = (unsigned)(want < sm_count() ? (want < 1 ? 1 : want) : sm_count());
-  unary_f16_lut<kRows><<<grid, kLutThreads, kLutSmem, s>>>(table, x, y, rows, (uint32_t)total, xt, yt, tail);
+  TTN_TRY(cuda_check(launch_pdl(unary_f16_lut<kRows>, grid, kLutThreads, kLutSmem, s, table, x, y, rows,
+                                (uint32_t)total, xt, yt, tail),
+                     name));
   return launch_check(name);
 }
 
@@ -362,6 +368,8 @@ __global__ void __launch_bounds__(kLutThreads, 1) add_silu_lut(const uint16_t* t
     for (int t = threadIdx.x; t < kLutBytes / 16; t += kLutThreads) cp_async16(dst + t, src + t);
     cp_async_commit();
   }
+  pdl_trigger();
+  pdl_wait();
 #pragma unroll
   for (int k = 0; k < kAddSlots - 1; ++k) {
     const uint32_t g = first + k * stride;
@@ -700,10 +708,11 @@ ttn_status unary(const ttn_tensor* x, const ttn_tensor* y, ttn_stream stream, co
       } else {
         unsigned grid = resident_grid(unary_f16_dense<K>, kThreads, 0, nvec ? nvec : 1,
                                       (int64_t)kThreads * kVec);
-        unary_f16_dense<K><<<grid, kThreads, 0, s>>>(
-            (const uint16_t*)x->data + v0 * 8, (uint16_t*)y->data + v0 * 8, (int)nvec,
-            (const uint16_t*)x->data + total_vec * 8, (uint16_t*)y->data + total_vec * 8,
-            last ? tail : 0);
+        TTN_TRY(cuda_check(launch_pdl(unary_f16_dense<K>, dim3(grid), dim3(kThreads), 0, s,
+                                      (const uint16_t*)x->data + v0 * 8, (uint16_t*)y->data + v0 * 8, (int)nvec,
+                                      (const uint16_t*)x->data + total_vec * 8,
+                                      (uint16_t*)y->data + total_vec * 8, last ? tail : 0),
+                           name));
       }
       TTN_TRY(launch_check(name));
       if (last) break;
@@ -806,8 +815,9 @@ ttn_status ttn_add_silu_f16(const ttn_tensor* a, const ttn_tensor* raw, const tt
   TTN_TRY(ensure_dynamic_smem((const void*)add_silu_lut, kAddSmem));
   const int64_t want = (total + 4 * kLutThreads - 1) / (4 * kLutThreads);
   const unsigned grid = (unsigned)(want < sm_count() ? (want < 1 ? 1 : want) : sm_count());
-  add_silu_lut<<<grid, kLutThreads, kAddSmem, s>>>(table, (const uint16_t*)raw->data, (const uint16_t*)a->data,
-                                                   (uint16_t*)out->data, rows, (uint32_t)total);
+  TTN_TRY(cuda_check(launch_pdl(add_silu_lut, grid, kLutThreads, kAddSmem, s, table, (const uint16_t*)raw->data,
+                                (const uint16_t*)a->data, (uint16_t*)out->data, rows, (uint32_t)total),
+                     name));
   return launch_check(name);
 }
 

@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(256) blocked_to_nchw_regs(const uint4* x, int6
   __shared__ uint4 tile[8][256];
   uint4* mine = tile[threadIdx.x >> 5];
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   const int64_t groups = hw / 4;
   const int64_t total = n * c1 * groups;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -191,6 +193,8 @@ __global__ void __launch_bounds__(256) upsample_blocked32(const uint4* x, uint4*
                                                           int64_t x_bs, int64_t y_bs) {
   const uint32_t stride = gridDim.x * blockDim.x;
   const int64_t w = wdiv.d, h = hdiv.d;
+  pdl_trigger();
+  pdl_wait();
   for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
     const uint32_t b = per_image.div(v), local = v - b * per_image.d;
     const uint4 q = x[b * x_bs + local];
@@ -614,6 +618,8 @@ __global__ void __launch_bounds__(256, 4) sppf_runs(const uint16_t* x, uint16_t*
   const int row_step = 2 * pw;
   const uint4 ninf = make_uint4(0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u);
   for (int v = threadIdx.x; v < 2 * padded_vec; v += blockDim.x) cur[v] = ninf;
+  pdl_trigger();
+  pdl_wait();
   __syncthreads();
 #pragma unroll 1
   for (int64_t job = blockIdx.x; job < n * c1; job += gridDim.x) {
@@ -699,9 +705,11 @@ ttn_status ttn_nc1hwc0_to_nchw_f16(const void* x, int64_t n, int64_t c1, int64_t
   bool vec = aligned16(y) && y_batch_stride % 8 == 0 && y_channel_stride % 8 == 0;
   if (((uintptr_t)y & 7u) == 0 && y_batch_stride % 4 == 0 && y_channel_stride % 4 == 0 && hw % 4 == 0) {
     int64_t threads = n * c1 * (hw / 4);
-    blocked_to_nchw_regs<<<grid_for(threads, 256, 8), 256, 0, (cudaStream_t)stream>>>(
-        (const uint4*)x, n, c1, hw, (c1 * 16 < channels ? c1 * 16 : channels), (uint16_t*)y,
-        y_batch_stride, y_channel_stride);
+    TTN_TRY(cuda_check(launch_pdl(blocked_to_nchw_regs, dim3(grid_for(threads, 256, 8)), dim3(256), 0,
+                                  (cudaStream_t)stream, (const uint4*)x, n, c1, hw,
+                                  (c1 * 16 < channels ? c1 * 16 : channels), (uint16_t*)y, y_batch_stride,
+                                  y_channel_stride),
+                       name));
     return launch_check(name);
   }
   int64_t jobs = n * c1 * ((hw + kPix - 1) / kPix);
@@ -777,9 +785,11 @@ ttn_status ttn_upsample2x_nc1hwc0_f16(const void* x, int64_t x_batch_stride, voi
     return fail(TTN_INVALID_ARG, "%s: batch stride smaller than one image", name);
   int64_t nvec = n * c1 * h * w * 2;
   if (nvec < ((int64_t)1 << 31)) {
-    upsample_blocked32<<<grid_for(nvec, 256), 256, 0, (cudaStream_t)stream>>>(
-        (const uint4*)x, (uint4*)y, (uint32_t)nvec, FastDiv((uint32_t)(c1 * h * w * 2)), FastDiv((uint32_t)h),
-        FastDiv((uint32_t)w), x_batch_stride / 8, y_batch_stride / 8);
+    TTN_TRY(cuda_check(launch_pdl(upsample_blocked32, dim3(grid_for(nvec, 256)), dim3(256), 0, (cudaStream_t)stream,
+                                  (const uint4*)x, (uint4*)y, (uint32_t)nvec, FastDiv((uint32_t)(c1 * h * w * 2)),
+                                  FastDiv((uint32_t)h), FastDiv((uint32_t)w), x_batch_stride / 8,
+                                  y_batch_stride / 8),
+                       name));
     return launch_check(name);
   }
   upsample_blocked<<<grid_for(nvec, 256), 256, 0, (cudaStream_t)stream>>>(
@@ -866,11 +876,13 @@ ttn_status ttn_sppf_f16(const void* x, void* out, int64_t n, int64_t c1, int64_t
     TTN_TRY(ensure_dynamic_smem(fn, (int)runs_smem));
     unsigned grid = resident_grid(fn, 256, runs_smem, jobs, 1);
     if (runs <= 256)
-      sppf_runs<1><<<grid, 256, runs_smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w,
-                                                FastDiv((uint32_t)w));
+      TTN_TRY(cuda_check(launch_pdl(sppf_runs<1>, dim3(grid), dim3(256), runs_smem, s, (const uint16_t*)x,
+                                    (uint16_t*)out, n, c1, (int)h, (int)w, FastDiv((uint32_t)w)),
+                         name));
     else
-      sppf_runs<2><<<grid, 256, runs_smem, s>>>((const uint16_t*)x, (uint16_t*)out, n, c1, (int)h, (int)w,
-                                                FastDiv((uint32_t)w));
+      TTN_TRY(cuda_check(launch_pdl(sppf_runs<2>, dim3(grid), dim3(256), runs_smem, s, (const uint16_t*)x,
+                                    (uint16_t*)out, n, c1, (int)h, (int)w, FastDiv((uint32_t)w)),
+                         name));
     return launch_check(name);
   }
   if (plane_vec <= 4 * 256) {  // fixed per-thread positions
