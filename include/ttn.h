@@ -74,6 +74,24 @@ const char* ttn_status_string(ttn_status status);
 /* Message of the last failing call on this thread ("" if none). */
 const char* ttn_last_error(void);
 
+/* Device memory for callers without their own allocator, the C-side twin of the
+ * backend allocator (reference backend.cpp:140-151: aclrtMalloc of the size rounded
+ * up to whole 32-byte blocks, aclrtFree): cudaMalloc of the rounded size (at least
+ * 256-byte aligned), cudaFree.  0 bytes gives a null pointer; ttn_free(NULL) is a
+ * no-op.  Not for use while a stream of the calling thread is being captured. */
+ttn_status ttn_malloc(void** ptr, size_t bytes);
+ttn_status ttn_free(void* ptr);
+
+/* Page-locked host memory (aclrtMallocHost -> cudaMallocHost), the kind the
+ * host-buffer path copies from at full link speed; same rounding. */
+ttn_status ttn_malloc_host(void** ptr, size_t bytes);
+ttn_status ttn_free_host(void* ptr);
+
+/* One asynchronous copy on `stream` (aclrtMemcpyAsync -> cudaMemcpyAsync);
+ * kind: 0 host to device, 1 device to host, 2 device to device. */
+typedef enum ttn_copy_kind { TTN_HOST_TO_DEVICE = 0, TTN_DEVICE_TO_HOST = 1, TTN_DEVICE_TO_DEVICE = 2 } ttn_copy_kind;
+ttn_status ttn_memcpy_async(void* dst, const void* src, size_t bytes, int kind, ttn_stream stream);
+
 /* Stream capture on caller-owned memory, the C-side twin of
  * thin_backend::RuntimeGraph (reference backend.cpp:62-113):
  * aclmdlRICaptureBegin(THREAD_LOCAL) -> cudaStreamBeginCapture(ThreadLocal),

@@ -225,3 +225,36 @@ def test_bias_silu_residual_via_torch_ops(device):
     b = (torch.randn(64, generator=g) * 0.1).half()
     got = torch.ops.thin_native_flow.bias_silu_residual(x.to(device), b.to(device), r.to(device))
     assert ulp_diff(got, oops.bias_silu_residual(x, b, r)).max() <= 2
+
+
+def test_memory_entry_points_round_trip(device):
+    """ttn_malloc / ttn_malloc_host / ttn_memcpy_async / ttn_free*: host -> device ->
+    device -> host through the C ABI returns the bytes; 0 bytes gives a null pointer;
+    freeing null is a no-op; an unknown copy kind is refused."""
+    import ctypes
+    from thintnpu_b200 import _lib
+    lib = _lib.lib()
+    n = 1000003  # not a multiple of the 32-byte block
+    ptrs = [ctypes.c_void_p() for _ in range(4)]
+    host_in, dev_a, dev_b, host_out = ptrs
+    _lib.check("ttn_malloc_host", lib.ttn_malloc_host(ctypes.byref(host_in), n))
+    _lib.check("ttn_malloc_host", lib.ttn_malloc_host(ctypes.byref(host_out), n))
+    _lib.check("ttn_malloc", lib.ttn_malloc(ctypes.byref(dev_a), n))
+    _lib.check("ttn_malloc", lib.ttn_malloc(ctypes.byref(dev_b), n))
+    assert all(p.value for p in ptrs) and dev_a.value % 256 == 0
+    pattern = bytes((i * 7 + 3) & 0xFF for i in range(n))
+    ctypes.memmove(host_in.value, pattern, n)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _lib.check("ttn_memcpy_async", lib.ttn_memcpy_async(dev_a, host_in, n, 0, stream))
+    _lib.check("ttn_memcpy_async", lib.ttn_memcpy_async(dev_b, dev_a, n, 2, stream))
+    _lib.check("ttn_memcpy_async", lib.ttn_memcpy_async(host_out, dev_b, n, 1, stream))
+    torch.cuda.synchronize(device)
+    assert ctypes.string_at(host_out.value, n) == pattern
+    assert lib.ttn_memcpy_async(dev_b, dev_a, n, 7, stream) == 1  # TTN_INVALID_ARG
+    zero = ctypes.c_void_p(123)
+    _lib.check("ttn_malloc", lib.ttn_malloc(ctypes.byref(zero), 0))
+    assert zero.value is None
+    assert lib.ttn_free(None) == 0 and lib.ttn_free_host(None) == 0
+    for p, free in ((dev_a, lib.ttn_free), (dev_b, lib.ttn_free), (host_in, lib.ttn_free_host),
+                    (host_out, lib.ttn_free_host)):
+        _lib.check("ttn_free", free(p))

@@ -25,6 +25,7 @@ UNSUPPORTED = 2
 # Every symbol include/ttn.h declares (checked by the CPU test suite).
 EXPORTS = (
     "ttn_version", "ttn_status_string", "ttn_last_error",
+    "ttn_malloc", "ttn_free", "ttn_malloc_host", "ttn_free_host", "ttn_memcpy_async",
     "ttn_graph_create", "ttn_graph_begin", "ttn_graph_end", "ttn_graph_replay",
     "ttn_graph_close", "ttn_graph_destroy",
     "ttn_silu", "ttn_sigmoid", "ttn_binary", "ttn_binary_scalar", "ttn_add_silu_f16",
@@ -72,6 +73,11 @@ _SIGNATURES = {
     "ttn_version": (ctypes.c_int, []),
     "ttn_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ttn_last_error": (ctypes.c_char_p, []),
+    "ttn_malloc": (ctypes.c_int, [ctypes.POINTER(_P), ctypes.c_size_t]),
+    "ttn_free": (ctypes.c_int, [_P]),
+    "ttn_malloc_host": (ctypes.c_int, [ctypes.POINTER(_P), ctypes.c_size_t]),
+    "ttn_free_host": (ctypes.c_int, [_P]),
+    "ttn_memcpy_async": (ctypes.c_int, [_P, _P, ctypes.c_size_t, ctypes.c_int, _P]),
     "ttn_graph_create": (ctypes.c_int, [ctypes.POINTER(_P)]),
     "ttn_graph_begin": (ctypes.c_int, [_P, _P]),
     "ttn_graph_end": (ctypes.c_int, [_P]),

@@ -225,6 +225,37 @@ const char* ttn_status_string(ttn_status status) {
 
 const char* ttn_last_error(void) { return g_error; }
 
+static size_t round_blocks(size_t bytes) { return (bytes + 31) / 32 * 32; }
+
+ttn_status ttn_malloc(void** ptr, size_t bytes) {
+  if (!ptr) return fail(TTN_INVALID_ARG, "ttn_malloc: null output");
+  *ptr = nullptr;
+  if (!bytes) return TTN_OK;
+  if (bytes > SIZE_MAX - 31) return fail(TTN_INVALID_ARG, "ttn_malloc: size overflows");
+  return cuda_check(cudaMalloc(ptr, round_blocks(bytes)), "ttn_malloc");
+}
+
+ttn_status ttn_free(void* ptr) { return ptr ? cuda_check(cudaFree(ptr), "ttn_free") : TTN_OK; }
+
+ttn_status ttn_malloc_host(void** ptr, size_t bytes) {
+  if (!ptr) return fail(TTN_INVALID_ARG, "ttn_malloc_host: null output");
+  *ptr = nullptr;
+  if (!bytes) return TTN_OK;
+  if (bytes > SIZE_MAX - 31) return fail(TTN_INVALID_ARG, "ttn_malloc_host: size overflows");
+  return cuda_check(cudaMallocHost(ptr, round_blocks(bytes)), "ttn_malloc_host");
+}
+
+ttn_status ttn_free_host(void* ptr) { return ptr ? cuda_check(cudaFreeHost(ptr), "ttn_free_host") : TTN_OK; }
+
+ttn_status ttn_memcpy_async(void* dst, const void* src, size_t bytes, int kind, ttn_stream stream) {
+  static const cudaMemcpyKind kinds[3] = {cudaMemcpyHostToDevice, cudaMemcpyDeviceToHost,
+                                          cudaMemcpyDeviceToDevice};
+  if (kind < 0 || kind > 2) return fail(TTN_INVALID_ARG, "ttn_memcpy_async: unknown kind %d", kind);
+  if (!bytes) return TTN_OK;
+  if (!dst || !src) return fail(TTN_INVALID_ARG, "ttn_memcpy_async: null pointer");
+  return cuda_check(cudaMemcpyAsync(dst, src, bytes, kinds[kind], (cudaStream_t)stream), "ttn_memcpy_async");
+}
+
 ttn_status ttn_graph_create(ttn_graph** graph) {
   if (!graph) return fail(TTN_INVALID_ARG, "ttn_graph_create: null output");
   *graph = new (std::nothrow) ttn_graph();
