@@ -66,6 +66,15 @@ def test_conv_matches_cpu(device, b, ci, co, h, w, k, stride):
     _run(device, b, ci, co, h, w, k, stride)
 
 
+@pytest.mark.parametrize("b,ci,co,h,w", [(2, 3, 32, 64, 64), (1, 3, 16, 33, 47), (1, 16, 64, 40, 40), (1, 1, 48, 20, 21),
+                                         (2, 5, 32, 17, 18), (1, 3, 32, 160, 160)])
+def test_stem_conv_matches_cpu(device, b, ci, co, h, w):
+    """One input channel block, 3x3 stride 2 (the YOLO stem): the CUDA-core kernel,
+    which reads only the channels the weights use; odd sizes, 1 to 16 real channels."""
+    _run(device, b, ci, co, h, w, 3, 2)
+    _run(device, b, ci, co, h, w, 3, 2, silu=False, bias=False, seed=5)
+
+
 def test_conv_without_bias_or_silu(device):
     _run(device, 2, 64, 64, 20, 20, 3, 1, silu=False, bias=False, seed=3)
     _run(device, 1, 32, 64, 40, 40, 1, 1, silu=False, bias=True, seed=4)

@@ -394,4 +394,38 @@ __device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsig
   return d;
 }
 
+// SiLU of two FP32 values as a packed fp16 pair, rounded exactly as
+// fp16(silu_f32(x)) is, or flagged.  Fast core: a_i = 1 + 2^(-x_i log2 e)
+// (ex2.approx), one rcp.approx for both lanes: q = 1/(a0 a1), r0 = x0 (a1 q),
+// r1 = x1 (a0 q) (a1 q's own error in a1 cancels).  Relative error of r: rounding
+// the exponent argument t = -x log2 e (fp32 constant 2^-26.2 off, product rounding
+// 2^-24) costs ln2 |t| 1.22 2^-24 = |x| 2^-23.71; ex2.approx 2^-22, rcp.approx
+// 2^-23 and four roundings 2^-24: in all under |x| 2^-23.71 + 2^-20.68.  silu_f32
+// (expf within 2 ulps, then 1 + e and the IEEE divide) is within 2^-21.42 of the
+// true value, and forming the bracket ends costs 2^-24.  So with
+//   eps(x) = 2^-19.75 + |x| 2^-23.5   (> 1.1 x the sum of those terms)
+// silu_f32's result lies in [r (1 - eps), r (1 + eps)], and when both ends round
+// to the same fp16 value it rounds to that value as well (rounding is monotonic).
+// The pair is returned as u, the rounded upper ends, with `d` = the rounded lower
+// ends: a lane whose halves of u and d differ takes silu_f32 itself.  When a0 a1 is
+// not below 2^126 (a NaN, -inf, or a product too large for rcp), d = ~u flags both.
+constexpr float kEps0 = 1.1341162462485954e-06f;  // 2^-19.75
+constexpr float kEps1 = 8.429369557916289e-08f;   // 2^-23.5
+__device__ __forceinline__ uint32_t silu_pair_fast(unsigned long long xx, uint32_t& d) {
+  const unsigned long long t = f2_mul(xx, f2_pack(-1.44269504088896341f, -1.44269504088896341f));
+  const float2 tt = f2_unpack(t);
+  const unsigned long long a = f2_add(f2_pack(ex2_approx(tt.x), ex2_approx(tt.y)), f2_pack(1.0f, 1.0f));
+  const float2 aa = f2_unpack(a);
+  const float p = aa.x * aa.y, q = rcp_approx(p);
+  const unsigned long long r = f2_mul(xx, f2_mul(f2_pack(aa.y, aa.x), f2_pack(q, q)));
+  const unsigned long long ax = xx & 0x7fffffff7fffffffull;  // |x0|, |x1|
+  const unsigned long long eps = f2_fma(ax, f2_pack(kEps1, kEps1), f2_pack(kEps0, kEps0));
+  const unsigned long long neps = f2_fma(ax, f2_pack(-kEps1, -kEps1), f2_pack(-kEps0, -kEps0));
+  const float2 up = f2_unpack(f2_fma(r, eps, r)), dn = f2_unpack(f2_fma(r, neps, r));
+  const __half2 hu = __floats2half2_rn(up.x, up.y), hd = __floats2half2_rn(dn.x, dn.y);
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&hu);
+  d = (p < 8.50705917302346159e+37f) ? *reinterpret_cast<const uint32_t*>(&hd) : ~u;  // 2^126
+  return u;
+}
+
 }  // namespace ttn

@@ -317,6 +317,149 @@ int gcd_int(int x, int y) {
   return x;
 }
 
+// The stem convolution -- one input channel block, 3x3, stride 2 (YOLO's first
+// layer: 3 real channels padded to 16) -- on the CUDA cores.  On the tensor cores
+// every tap re-reads its input through 32-byte TMA rows; here each output pixel
+// reads its nine input rows once (neighbours share them in L1) and only the input
+// channels the weights use: the block finds the highest channel with a nonzero
+// weight (input channels past the real count are zero by contract) and takes the
+// body compiled for that many channels (1-4, 8 or 16), so the channel loops are
+// static.  Thread = PIX adjacent output pixels x the 16 output channels of its
+// block's channel group (grid y); the group's weights sit in shared memory as FP32
+// pairs of output channels, so each (channel, tap) is one broadcast load and one
+// f32x2 FMA per pixel and channel pair.  Epilogue: +
+// bias, then fp16(silu_f32) as the tensor-core kernel rounds it, from the bracketed
+// ex2/rcp core (silu_pair_fast) with silu_f32 itself for the lanes it flags; NC1HWC0
+// output, 32 bytes per channel block.
+constexpr int kStemThreads = 128;
+
+struct StemArgs {
+  const uint16_t* x;
+  int64_t x_bs;
+  int h, w, oh, ow, batch, silu;
+  uint16_t* out;
+  int64_t out_bs;
+};
+
+template <int CO, int PIX, int CE>
+__device__ void stem_pixels(const StemArgs& a, const unsigned long long* wsm, const float* bsm) {
+  constexpr int PAIRS = CO / 2;  // CO: the output channels of this block's group
+  const int groups_w = (a.ow + PIX - 1) / PIX;
+  const int64_t total = (int64_t)a.batch * a.oh * groups_w;
+  for (int64_t t = (int64_t)blockIdx.x * kStemThreads + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * kStemThreads) {
+    const int64_t b = t / ((int64_t)a.oh * groups_w);
+    const int r = (int)(t - b * a.oh * groups_w), oy = r / groups_w, ox0 = (r - oy * groups_w) * PIX;
+    const uint16_t* img = a.x + b * a.x_bs;
+    unsigned long long acc[PIX][PAIRS];
+#pragma unroll
+    for (int p = 0; p < PIX; ++p)
+#pragma unroll
+      for (int q = 0; q < PAIRS; ++q) acc[p][q] = 0ull;
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+      const int iy = 2 * oy - 1 + tap / 3;
+      uint32_t words[PIX][(CE + 1) / 2];  // the used channels' fp16 pairs
+#pragma unroll
+      for (int p = 0; p < PIX; ++p) {
+        const int ix = 2 * (ox0 + p) - 1 + tap % 3;
+        const bool in = iy >= 0 && iy < a.h && ix >= 0 && ix < a.w && ox0 + p < a.ow;
+        const uint16_t* src = img + ((int64_t)iy * a.w + ix) * 16;
+        if constexpr (CE <= 4) {
+          const uint2 v = in ? __ldg(reinterpret_cast<const uint2*>(src)) : make_uint2(0u, 0u);
+          words[p][0] = v.x;
+          if constexpr (CE > 2) words[p][1] = v.y;
+        } else {
+#pragma unroll
+          for (int hv = 0; hv < CE / 8; ++hv) {
+            const uint4 v = in ? __ldg(reinterpret_cast<const uint4*>(src) + hv) : make_uint4(0u, 0u, 0u, 0u);
+            words[p][4 * hv] = v.x, words[p][4 * hv + 1] = v.y, words[p][4 * hv + 2] = v.z, words[p][4 * hv + 3] = v.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < CE; ++c) {
+        const unsigned long long* wc = wsm + (c * 9 + tap) * PAIRS;
+        unsigned long long xv[PIX];
+#pragma unroll
+        for (int p = 0; p < PIX; ++p) {
+          const float v = __half2float(__ushort_as_half((uint16_t)(words[p][c >> 1] >> (16 * (c & 1)))));
+          xv[p] = f2_pack(v, v);
+        }
+#pragma unroll
+        for (int q = 0; q < PAIRS; ++q) {
+          const unsigned long long wq = wc[q];
+#pragma unroll
+          for (int p = 0; p < PIX; ++p) acc[p][q] = f2_fma(xv[p], wq, acc[p][q]);
+        }
+      }
+    }
+    uint16_t* dst = a.out + b * a.out_bs + (int64_t)blockIdx.y * a.oh * a.ow * 16;
+#pragma unroll
+    for (int p = 0; p < PIX; ++p) {
+      if (ox0 + p >= a.ow) continue;
+#pragma unroll
+      for (int blk = 0; blk < CO / 16; ++blk) {
+        uint32_t o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const unsigned long long sum =
+              f2_add(acc[p][blk * 8 + e], f2_pack(bsm[blk * 16 + 2 * e], bsm[blk * 16 + 2 * e + 1]));
+          if (!a.silu) {
+            const float2 v = f2_unpack(sum);
+            o[e] = h2_bits(__floats2half2_rn(v.x, v.y));
+            continue;
+          }
+          uint32_t lower;
+          o[e] = silu_pair_fast(sum, lower);  // fp16(silu_f32) unless flagged
+          const uint32_t open = o[e] ^ lower;
+          if (open) {
+            const float2 v = f2_unpack(sum);
+            if (open & 0xffffu) o[e] = (o[e] & 0xffff0000u) | __half_as_ushort(__float2half_rn(silu_f32(v.x)));
+            if (open >> 16) o[e] = (o[e] & 0xffffu) | ((uint32_t)__half_as_ushort(__float2half_rn(silu_f32(v.y))) << 16);
+          }
+        }
+        uint4* q = reinterpret_cast<uint4*>(dst + (((int64_t)blk * a.oh + oy) * a.ow + ox0 + p) * 16);
+        q[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        q[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+    }
+  }
+}
+
+template <int CO, int PIX>
+__global__ void __launch_bounds__(kStemThreads) conv_stem(StemArgs a, const uint16_t* packed, int co64,
+                                                          const uint16_t* bias) {
+  constexpr int PAIRS = CO / 2;
+  const int group = blockIdx.y * CO;  // this block's first output channel
+  __shared__ unsigned long long wsm[16 * 9 * PAIRS];  // [channel][tap][output pair] packed f32x2
+  __shared__ float bsm[CO];
+  __shared__ int used;
+  const int tid = threadIdx.x;
+  if (tid == 0) used = 0;
+  __syncthreads();
+  int mine = 0;
+  for (int i = tid; i < 16 * 9 * PAIRS; i += kStemThreads) {
+    const int q = i % PAIRS, rest = i / PAIRS, tap = rest % 9, c = rest / 9;
+    const float w0 = __half2float(__ushort_as_half(packed[((int64_t)tap * co64 + group + 2 * q) * 16 + c]));
+    const float w1 = __half2float(__ushort_as_half(packed[((int64_t)tap * co64 + group + 2 * q + 1) * 16 + c]));
+    wsm[i] = f2_pack(w0, w1);
+    if (w0 != 0.0f || w1 != 0.0f) mine = c + 1;
+  }
+  if (mine) atomicMax(&used, mine);
+  for (int i = tid; i < CO; i += kStemThreads) bsm[i] = bias ? __half2float(__ushort_as_half(bias[group + i])) : 0.0f;
+  __syncthreads();
+  switch (used) {  // block-uniform
+    case 0:
+    case 1: stem_pixels<CO, PIX, 1>(a, wsm, bsm); break;
+    case 2: stem_pixels<CO, PIX, 2>(a, wsm, bsm); break;
+    case 3: stem_pixels<CO, PIX, 3>(a, wsm, bsm); break;
+    case 4: stem_pixels<CO, PIX, 4>(a, wsm, bsm); break;
+    case 5: case 6: case 7: case 8: stem_pixels<CO, PIX, 8>(a, wsm, bsm); break;
+    default: stem_pixels<CO, PIX, 16>(a, wsm, bsm); break;
+  }
+}
+
 }  // namespace
 }  // namespace ttn
 
@@ -350,6 +493,15 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
     return fail(TTN_INVALID_ARG, "%s: output images overlap", name);
   if (c1 > 65535 || h > 65535 || w > 65535 || co > 65536 || batch > INT32_MAX)
     return fail(TTN_UNSUPPORTED, "%s: shape beyond the supported range", name);
+  if (c1 == 1 && kernel == 3 && stride == 2 && !nchw && !residual && co <= 64) {  // the stem
+    const dim3 grid(grid_for(batch * oh * ((ow + 1) / 2), kStemThreads, 16), (unsigned)(co / 16));
+    const StemArgs a{(const uint16_t*)x, batch > 1 ? x_batch_stride : 0, (int)h, (int)w, (int)oh, (int)ow,
+                     (int)batch, (flags & TTN_CONV_SILU) ? 1 : 0, (uint16_t*)out, batch > 1 ? out_batch_stride : 0};
+    conv_stem<16, 2><<<grid, kStemThreads, 0, (cudaStream_t)stream>>>(a, (const uint16_t*)packed_weights,
+                                                                       (int)((co + 63) / 64 * 64),
+                                                                       (const uint16_t*)bias);
+    return launch_check(name);
+  }
   if (residual) {
     if (nchw) return fail(TTN_UNSUPPORTED, "%s: the residual needs NC1HWC0 output", name);
     if (((uintptr_t)residual & 15u) || residual_batch_stride % 8)
