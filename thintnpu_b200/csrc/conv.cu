@@ -70,7 +70,8 @@ struct ConvArgs {
   int groups;            // steps per tap: ceil(c1 / blocks)
   int64_t tiles;         // batch * tiles_h * tiles_w * co_tiles
   int silu, nchw;
-  int stages;            // ring depth
+  int bias_vec;          // the bias is 16-byte aligned: 32 channels in four vector loads
+  int stages;           // ring depth
   int sub;               // pixel sub-tiles per tile (2 when tile_n <= 128: they share each weight stage)
   int halo;              // 3x3 stride 1: one halo box per channel block, the taps as shifted descriptors
   int steps;             // ring stages per tile
@@ -80,6 +81,66 @@ struct ConvArgs {
 struct ConvMaps {
   CUtensorMap x, w;
 };
+
+// Bias and activation of 32 accumulator columns (output channels co0 .. co0 + 31 of one
+// pixel), packed in fp16 pairs: fp16(silu_f32(acc + bias)) or fp16(acc + bias), the bias
+// added in FP32 where the channel exists.  With a 16-byte aligned bias and all 32
+// channels present the bias comes in four 16-byte loads.  The SiLU is silu_pair_fast;
+// lanes it flags take silu_f32 itself, so each output is exactly fp16(silu_f32(s)).
+__device__ __forceinline__ void conv_epilogue32(const uint32_t (&r)[32], const uint16_t* bias, int co0, int co,
+                                                bool bias_vec, bool silu, uint32_t (&packed)[16]) {
+  unsigned long long v[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) v[e] = f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+  if (bias) {
+    if (bias_vec && co0 + 32 <= co) {
+      const uint4* bp = reinterpret_cast<const uint4*>(bias + co0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = __ldg(bp + q);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 b = __half22float2(bits_h2(words[i]));
+          v[4 * q + i] = f2_add(v[4 * q + i], f2_pack(b.x, b.y));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        float2 s = f2_unpack(v[e]);
+        if (co0 + 2 * e < co) s.x = __fadd_rn(s.x, __half2float(__ushort_as_half(bias[co0 + 2 * e])));
+        if (co0 + 2 * e + 1 < co) s.y = __fadd_rn(s.y, __half2float(__ushort_as_half(bias[co0 + 2 * e + 1])));
+        v[e] = f2_pack(s.x, s.y);
+      }
+    }
+  }
+  if (silu) {
+    uint32_t lower[16], open = 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      packed[e] = silu_pair_fast(v[e], lower[e]);
+      open |= packed[e] ^ lower[e];
+    }
+    if (open) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const uint32_t diff = packed[e] ^ lower[e];
+        if (diff) {
+          const float2 s = f2_unpack(v[e]);
+          if (diff & 0xffffu) packed[e] = (packed[e] & 0xffff0000u) | hbits(__float2half_rn(silu_f32(s.x)));
+          if (diff >> 16) packed[e] = (packed[e] & 0x0000ffffu) | ((uint32_t)hbits(__float2half_rn(silu_f32(s.y))) << 16);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float2 s = f2_unpack(v[e]);
+      packed[e] = h2_bits(__floats2half2_rn(s.x, s.y));
+    }
+  }
+}
 
 
 template <bool kResidual>
@@ -242,14 +303,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
         const int co0 = n0 + (a.sub == 2 ? 0 : col0) + c;
         if (!pixel || co0 >= a.co) continue;
         uint32_t packed[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float s0 = __uint_as_float(r[e]), s1 = __uint_as_float(r[e + 1]);
-          if (a.bias && co0 + e < a.co) s0 = __fadd_rn(s0, __half2float(__ushort_as_half(a.bias[co0 + e])));
-          if (a.bias && co0 + e + 1 < a.co) s1 = __fadd_rn(s1, __half2float(__ushort_as_half(a.bias[co0 + e + 1])));
-          if (a.silu) s0 = silu_f32(s0), s1 = silu_f32(s1);
-          packed[e / 2] = h2_bits(__floats2half2_rn(s0, s1));
-        }
+        conv_epilogue32(r, a.bias, co0, a.co, a.bias_vec, a.silu, packed);
         if (a.nchw) {
           const int64_t plane = (int64_t)a.oh * a.ow;
           uint16_t* o = out + (int64_t)co0 * plane + (int64_t)oh * a.ow + ow;
@@ -548,6 +602,7 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
   a.tiles = batch * a.tiles_h * a.tiles_w * a.co_tiles;
   a.silu = (flags & TTN_CONV_SILU) ? 1 : 0;
   a.nchw = nchw ? 1 : 0;
+  a.bias_vec = bias && ((uintptr_t)bias & 15u) == 0 ? 1 : 0;
   a.withhold = g_withhold_next_conv.exchange(false) ? 1 : 0;
 
   ConvMaps maps;
