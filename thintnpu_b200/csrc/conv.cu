@@ -26,10 +26,11 @@
 //  * warp 1, lane 0: MMA issuer into one of two TMEM accumulators (2 x 256
 //    columns), committing each stage back to its empty barrier and each finished
 //    tile to the accumulator's full barrier.
-//  * warps 2-9: epilogue.  Warp w reads TMEM lanes 32(w%4).. (its 32 pixels) and
-//    half of the tile's columns, adds the bias, applies the SiLU, rounds once and
+//  * warps 2-17: epilogue.  Warp w reads TMEM lanes 32(w%4).. (its 32 pixels) and
+//    every fourth 16-column chunk, adds the bias, applies the SiLU, rounds once and
 //    stores 32-byte NC1HWC0 rows (or NCHW elements); then frees the accumulator,
-//    so tile t's stores overlap tile t+1's products.
+//    so tile t's stores overlap tile t+1's products.  Sixteen warps (four per lane
+//    quarter) keep enough work in flight to hide the latency of the SiLU chain.
 // Every wait is bounded (200 ms of wall time); a role that gives up records the
 // reason in a device word (ttn_conv2d_fault_f16: 1 = copy, 2 = stage, 4 =
 // accumulator), stops, and the CTA drains its copies and frees its TMEM.
@@ -46,7 +47,7 @@ constexpr int kConvM = 128;          // output pixels per tile (UMMA M, TMEM lan
 constexpr int kConvMaxN = 256;       // output channels per tile (UMMA N, TMEM columns per accumulator)
 constexpr int kConvMaxStages = 8;    // shared-memory ring depth: as many stages as fit, up to 8
 constexpr int kConvBlocksPerStep = 4;  // 16-channel blocks (K=16 each) per ring stage
-constexpr int kConvEpiWarps = 8;
+constexpr int kConvEpiWarps = 16;
 constexpr int kHaloW = 16;  // halo box width (pixels) for 8-pixel-wide 3x3 tiles: 512-byte rows keep
                             // every 8-row operand group on a 256-byte swizzle atom
 constexpr int kConvThreads = 64 + 32 * kConvEpiWarps;
@@ -82,21 +83,23 @@ struct ConvMaps {
   CUtensorMap x, w;
 };
 
-// Bias and activation of 32 accumulator columns (output channels co0 .. co0 + 31 of one
-// pixel), packed in fp16 pairs: fp16(silu_f32(acc + bias)) or fp16(acc + bias), the bias
-// added in FP32 where the channel exists.  With a 16-byte aligned bias and all 32
-// channels present the bias comes in four 16-byte loads.  The SiLU is silu_pair_fast;
+// Bias and activation of N accumulator columns (output channels co0 .. co0 + N - 1 of
+// one pixel), packed in fp16 pairs: fp16(silu_f32(acc + bias)) or fp16(acc + bias), the
+// bias added in FP32 where the channel exists.  With a 16-byte aligned bias and all N
+// channels present the bias comes in N / 8 16-byte loads.  The SiLU is silu_pair_fast;
 // lanes it flags take silu_f32 itself, so each output is exactly fp16(silu_f32(s)).
-__device__ __forceinline__ void conv_epilogue32(const uint32_t (&r)[32], const uint16_t* bias, int co0, int co,
-                                                bool bias_vec, bool silu, uint32_t (&packed)[16]) {
-  unsigned long long v[16];
+template <int N>
+__device__ __forceinline__ void conv_epilogue(const uint32_t (&r)[N], const uint16_t* bias, int co0, int co,
+                                              bool bias_vec, bool silu, uint32_t (&packed)[N / 2]) {
+  constexpr int P = N / 2;
+  unsigned long long v[P];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) v[e] = f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+  for (int e = 0; e < P; ++e) v[e] = f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
   if (bias) {
-    if (bias_vec && co0 + 32 <= co) {
+    if (bias_vec && co0 + N <= co) {
       const uint4* bp = reinterpret_cast<const uint4*>(bias + co0);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < N / 8; ++q) {
         const uint4 w = __ldg(bp + q);
         const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -107,7 +110,7 @@ __device__ __forceinline__ void conv_epilogue32(const uint32_t (&r)[32], const u
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
+      for (int e = 0; e < P; ++e) {
         float2 s = f2_unpack(v[e]);
         if (co0 + 2 * e < co) s.x = __fadd_rn(s.x, __half2float(__ushort_as_half(bias[co0 + 2 * e])));
         if (co0 + 2 * e + 1 < co) s.y = __fadd_rn(s.y, __half2float(__ushort_as_half(bias[co0 + 2 * e + 1])));
@@ -116,15 +119,15 @@ __device__ __forceinline__ void conv_epilogue32(const uint32_t (&r)[32], const u
     }
   }
   if (silu) {
-    uint32_t lower[16], open = 0;
+    uint32_t lower[P], open = 0;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
+    for (int e = 0; e < P; ++e) {
       packed[e] = silu_pair_fast(v[e], lower[e]);
       open |= packed[e] ^ lower[e];
     }
     if (open) {
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
+      for (int e = 0; e < P; ++e) {
         const uint32_t diff = packed[e] ^ lower[e];
         if (diff) {
           const float2 s = f2_unpack(v[e]);
@@ -135,7 +138,7 @@ __device__ __forceinline__ void conv_epilogue32(const uint32_t (&r)[32], const u
     }
   } else {
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
+    for (int e = 0; e < P; ++e) {
       const float2 s = f2_unpack(v[e]);
       packed[e] = h2_bits(__floats2half2_rn(s.x, s.y));
     }
@@ -162,14 +165,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
   const int count = a.tiles > (int64_t)blockIdx.x ? (int)((a.tiles - blockIdx.x + stride - 1) / stride) : 0;
   const int steps = a.steps;
   // tile j of this CTA -> image, output-pixel origin, first output channel
-  auto tile_coords = [&](int j, int& img, int& oh0, int& ow0, int& n0) {
-    int64_t t = blockIdx.x + (int64_t)j * stride;
-    n0 = (int)(t % a.co_tiles) * a.tile_n;
-    t /= a.co_tiles;
-    ow0 = (int)(t % a.tiles_w) * a.wt;
-    t /= a.tiles_w;
-    oh0 = (int)(t % a.tiles_h) * a.ht * a.sub;
-    img = (int)(t / a.tiles_h);
+  auto tile_coords = [&](int j, int& img, int& oh0, int& ow0, int& n0) {  // 32-bit: tiles < 2^31
+    uint32_t t = blockIdx.x + (uint32_t)j * gridDim.x;
+    n0 = (int)(t % (uint32_t)a.co_tiles) * a.tile_n;
+    t /= (uint32_t)a.co_tiles;
+    ow0 = (int)(t % (uint32_t)a.tiles_w) * a.wt;
+    t /= (uint32_t)a.tiles_w;
+    oh0 = (int)(t % (uint32_t)a.tiles_h) * a.ht * a.sub;
+    img = (int)(t / (uint32_t)a.tiles_h);
   };
 
   if (tid == 0) {
@@ -277,13 +280,15 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
       if (ok) umma_commit(acc_full(acc));
     }
   } else if (warp >= 2) {  // epilogue
-    const int quarter = warp & 3, half = (warp - 2) >> 2, m = quarter * 32 + lane;
+    // Warp w reads TMEM lanes 32 (w % 4) .. (its 32 pixels of each sub-tile) and every
+    // fourth 16-column chunk of the accumulator, starting at chunk (w - 2) / 4.  The
+    // chunk count, sub * tile_n / 16, is 4, 8, 12 or 16: the four warps of a lane
+    // quarter take the same number.
+    constexpr int kGroups = kConvEpiWarps / 4;
+    const int quarter = warp & 3, group = (warp - 2) >> 2, m = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const int th = m / a.wt, tw = m % a.wt;
-    // sub = 1: this warp's columns [half * cols, half * cols + cols) of the one sub-tile;
-    // sub = 2: all columns of sub-tile `half`
-    const int cols = a.sub == 2 ? a.tile_n : a.tile_n / 2, col0 = a.sub == 2 ? half * a.tile_n : half * cols;
-    const int row0 = a.sub == 2 ? half * a.ht : 0;
+    const int chunks = a.sub * a.tile_n / 16;
     for (int j = 0; j < count; ++j) {
       const int acc = j & 1;
       if (!mbar_wait(acc_full(acc), (j >> 1) & 1)) {
@@ -293,43 +298,39 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
       tc_fence_after();
       int img, oh0, ow0, n0;
       tile_coords(j, img, oh0, ow0, n0);
-      const int oh = oh0 + row0 + th, ow = ow0 + tw;
-      const bool pixel = oh < a.oh && ow < a.ow;
+      const int ow = ow0 + tw;
       uint16_t* out = a.out + img * a.out_bs;
-      for (int c = 0; c < cols; c += 32) {
-        uint32_t r[32];
+      for (int c = group; c < chunks; c += kGroups) {
+        const int u = c * 16 >= a.tile_n ? 1 : 0;  // sub-tile: the next ht output rows
+        const int co0 = n0 + c * 16 - u * a.tile_n, oh = oh0 + u * a.ht + th;
+        uint32_t r[16];
         __syncwarp();  // the tensor-memory load is warp-collective: reconverge after the stores
-        tmem_ld32(lane_addr + acc * kConvMaxN + col0 + c, r);
-        const int co0 = n0 + (a.sub == 2 ? 0 : col0) + c;
-        if (!pixel || co0 >= a.co) continue;
-        uint32_t packed[16];
-        conv_epilogue32(r, a.bias, co0, a.co, a.bias_vec, a.silu, packed);
+        tmem_ld16(lane_addr + acc * kConvMaxN + c * 16, r);
+        if (oh >= a.oh || ow >= a.ow || co0 >= a.co) continue;
+        uint32_t packed[8];
+        conv_epilogue<16>(r, a.bias, co0, a.co, a.bias_vec, a.silu, packed);
         if (a.nchw) {
           const int64_t plane = (int64_t)a.oh * a.ow;
           uint16_t* o = out + (int64_t)co0 * plane + (int64_t)oh * a.ow + ow;
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
+          for (int e = 0; e < 16; ++e)
             if (co0 + e < a.co) o[e * plane] = (uint16_t)(packed[e / 2] >> (16 * (e & 1)));
-        } else {  // co is a multiple of 16: both 16-channel blocks are whole
+        } else {  // co is a multiple of 16: the chunk is one whole 16-channel block
+          const int64_t at = (((int64_t)(co0 / 16) * a.oh + oh) * a.ow + ow) << 4;
+          if (kResidual) {  // the reference's separate fp16 add: fp16(float(res) + float(y))
+            const uint4* rp = reinterpret_cast<const uint4*>(a.res + img * a.res_bs + at);
+            const uint4 q0 = rp[0], q1 = rp[1];
+            const uint32_t rv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-          for (int blk = 0; blk < 2; ++blk) {
-            if (co0 + 16 * blk >= a.co) break;
-            const int64_t at = (((int64_t)(co0 / 16 + blk) * a.oh + oh) * a.ow + ow) << 4;
-            if (kResidual) {  // the reference's separate fp16 add: fp16(float(res) + float(y))
-              const uint4* rp = reinterpret_cast<const uint4*>(a.res + img * a.res_bs + at);
-              const uint4 q0 = rp[0], q1 = rp[1];
-              const uint32_t rv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float2 y2 = __half22float2(bits_h2(packed[8 * blk + e]));
-                const float2 r2 = __half22float2(bits_h2(rv[e]));
-                packed[8 * blk + e] = h2_bits(__floats2half2_rn(__fadd_rn(r2.x, y2.x), __fadd_rn(r2.y, y2.y)));
-              }
+            for (int e = 0; e < 8; ++e) {
+              const float2 y2 = __half22float2(bits_h2(packed[e]));
+              const float2 r2 = __half22float2(bits_h2(rv[e]));
+              packed[e] = h2_bits(__floats2half2_rn(__fadd_rn(r2.x, y2.x), __fadd_rn(r2.y, y2.y)));
             }
-            uint4* o = reinterpret_cast<uint4*>(out + at);
-            o[0] = make_uint4(packed[8 * blk], packed[8 * blk + 1], packed[8 * blk + 2], packed[8 * blk + 3]);
-            o[1] = make_uint4(packed[8 * blk + 4], packed[8 * blk + 5], packed[8 * blk + 6], packed[8 * blk + 7]);
           }
+          uint4* o = reinterpret_cast<uint4*>(out + at);
+          o[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          o[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
         }
       }
       tc_fence_before();
@@ -600,6 +601,7 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
   a.b_off = (a.a_bytes + 1023u) & ~1023u;
   a.stage_bytes = (a.b_off + a.b_bytes + 1023u) & ~1023u;
   a.tiles = batch * a.tiles_h * a.tiles_w * a.co_tiles;
+  if (a.tiles >= ((int64_t)1 << 31)) return fail(TTN_UNSUPPORTED, "%s: more than 2^31 output tiles", name);
   a.silu = (flags & TTN_CONV_SILU) ? 1 : 0;
   a.nchw = nchw ? 1 : 0;
   a.bias_vec = bias && ((uintptr_t)bias & 15u) == 0 ? 1 : 0;
