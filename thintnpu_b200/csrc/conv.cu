@@ -71,7 +71,8 @@ struct ConvArgs {
   int groups;            // steps per tap: ceil(c1 / blocks)
   int64_t tiles;         // batch * tiles_h * tiles_w * co_tiles
   int silu, nchw;
-  int bias_vec;          // the bias is 16-byte aligned: 32 channels in four vector loads
+  int bias_vec;          // the bias is 32-byte aligned: 16 channels in one 32-byte load
+  int row32;             // output (and residual) rows are 32-byte aligned: one 32-byte access per pixel row
   int stages;           // ring depth
   int sub;               // pixel sub-tiles per tile (2 when tile_n <= 128: they share each weight stage)
   int halo;              // 3x3 stride 1: one halo box per channel block, the taps as shifted descriptors
@@ -83,30 +84,39 @@ struct ConvMaps {
   CUtensorMap x, w;
 };
 
+// 32-byte global accesses (one 256-bit load or store per lane); the address must be
+// 32-byte aligned.
+__device__ __forceinline__ void ld_global_v8(const uint16_t* p, uint32_t (&w)[8]) {
+  asm volatile("ld.global.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void st_global_v8(uint16_t* p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 // Bias and activation of N accumulator columns (output channels co0 .. co0 + N - 1 of
 // one pixel), packed in fp16 pairs: fp16(silu_f32(acc + bias)) or fp16(acc + bias), the
-// bias added in FP32 where the channel exists.  With a 16-byte aligned bias and all N
-// channels present the bias comes in N / 8 16-byte loads.  The SiLU is silu_pair_fast;
+// bias added in FP32 where the channel exists: from `bias_words` (the N values, loaded by
+// the caller ahead of the tensor-memory load) when `bias_vec`, else element by element.
+// The SiLU is silu_pair_fast;
 // lanes it flags take silu_f32 itself, so each output is exactly fp16(silu_f32(s)).
 template <int N>
-__device__ __forceinline__ void conv_epilogue(const uint32_t (&r)[N], const uint16_t* bias, int co0, int co,
-                                              bool bias_vec, bool silu, uint32_t (&packed)[N / 2]) {
+__device__ __forceinline__ void conv_epilogue(const uint32_t (&r)[N], bool bias_vec, const uint32_t (&bias_words)[N / 2],
+                                              const uint16_t* bias, int co0, int co, bool silu,
+                                              uint32_t (&packed)[N / 2]) {
   constexpr int P = N / 2;
   unsigned long long v[P];
 #pragma unroll
   for (int e = 0; e < P; ++e) v[e] = f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
   if (bias) {
-    if (bias_vec && co0 + N <= co) {
-      const uint4* bp = reinterpret_cast<const uint4*>(bias + co0);
+    if (bias_vec) {  // bias_words: the N fp16 bias values, loaded by the caller
 #pragma unroll
-      for (int q = 0; q < N / 8; ++q) {
-        const uint4 w = __ldg(bp + q);
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 b = __half22float2(bits_h2(words[i]));
-          v[4 * q + i] = f2_add(v[4 * q + i], f2_pack(b.x, b.y));
-        }
+      for (int e = 0; e < P; ++e) {
+        const float2 b = __half22float2(bits_h2(bias_words[e]));
+        v[e] = f2_add(v[e], f2_pack(b.x, b.y));
       }
     } else {
 #pragma unroll
@@ -303,12 +313,17 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
       for (int c = group; c < chunks; c += kGroups) {
         const int u = c * 16 >= a.tile_n ? 1 : 0;  // sub-tile: the next ht output rows
         const int co0 = n0 + c * 16 - u * a.tile_n, oh = oh0 + u * a.ht + th;
+        // the chunk's bias first (one address for the whole warp), so its latency overlaps the
+        // tensor-memory load's: the load's wait orders every later memory access behind it
+        const bool bias_vec = a.bias && a.bias_vec && co0 + 16 <= a.co;
+        uint32_t bias_words[8];
+        if (bias_vec) ld_global_v8(a.bias + co0, bias_words);
         uint32_t r[16];
         __syncwarp();  // the tensor-memory load is warp-collective: reconverge after the stores
         tmem_ld16(lane_addr + acc * kConvMaxN + c * 16, r);
         if (oh >= a.oh || ow >= a.ow || co0 >= a.co) continue;
         uint32_t packed[8];
-        conv_epilogue<16>(r, a.bias, co0, a.co, a.bias_vec, a.silu, packed);
+        conv_epilogue<16>(r, bias_vec, bias_words, a.bias, co0, a.co, a.silu, packed);
         if (a.nchw) {
           const int64_t plane = (int64_t)a.oh * a.ow;
           uint16_t* o = out + (int64_t)co0 * plane + (int64_t)oh * a.ow + ow;
@@ -318,9 +333,15 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
         } else {  // co is a multiple of 16: the chunk is one whole 16-channel block
           const int64_t at = (((int64_t)(co0 / 16) * a.oh + oh) * a.ow + ow) << 4;
           if (kResidual) {  // the reference's separate fp16 add: fp16(float(res) + float(y))
-            const uint4* rp = reinterpret_cast<const uint4*>(a.res + img * a.res_bs + at);
-            const uint4 q0 = rp[0], q1 = rp[1];
-            const uint32_t rv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            const uint16_t* rp = a.res + img * a.res_bs + at;
+            uint32_t rv[8];
+            if (a.row32) {
+              ld_global_v8(rp, rv);
+            } else {
+              const uint4 q0 = reinterpret_cast<const uint4*>(rp)[0], q1 = reinterpret_cast<const uint4*>(rp)[1];
+              rv[0] = q0.x, rv[1] = q0.y, rv[2] = q0.z, rv[3] = q0.w, rv[4] = q1.x, rv[5] = q1.y, rv[6] = q1.z,
+              rv[7] = q1.w;
+            }
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const float2 y2 = __half22float2(bits_h2(packed[e]));
@@ -328,9 +349,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
               packed[e] = h2_bits(__floats2half2_rn(__fadd_rn(r2.x, y2.x), __fadd_rn(r2.y, y2.y)));
             }
           }
-          uint4* o = reinterpret_cast<uint4*>(out + at);
-          o[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-          o[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+          if (a.row32) {
+            st_global_v8(out + at, packed);  // the pixel's whole 32-byte row: full sectors
+          } else {
+            uint4* o = reinterpret_cast<uint4*>(out + at);
+            o[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            o[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+          }
         }
       }
       tc_fence_before();
@@ -604,7 +629,9 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
   if (a.tiles >= ((int64_t)1 << 31)) return fail(TTN_UNSUPPORTED, "%s: more than 2^31 output tiles", name);
   a.silu = (flags & TTN_CONV_SILU) ? 1 : 0;
   a.nchw = nchw ? 1 : 0;
-  a.bias_vec = bias && ((uintptr_t)bias & 15u) == 0 ? 1 : 0;
+  a.bias_vec = bias && ((uintptr_t)bias & 31u) == 0 ? 1 : 0;
+  a.row32 = ((uintptr_t)out & 31u) == 0 && (batch == 1 || out_batch_stride % 16 == 0) &&
+            (!residual || (((uintptr_t)residual & 31u) == 0 && (batch == 1 || residual_batch_stride % 16 == 0)));
   a.withhold = g_withhold_next_conv.exchange(false) ? 1 : 0;
 
   ConvMaps maps;
