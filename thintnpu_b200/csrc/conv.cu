@@ -65,7 +65,9 @@ struct ConvArgs {
   int64_t out_bs;        // elements between images of the output
   int64_t res_bs;        // elements between images of the residual
   int c1, oh, ow, co, kernel, stride, pad;
-  int wt, ht;            // output tile: wt x ht pixels, wt * ht = 128
+  int wt, ht;            // output sub-tile: wt x ht pixels, wt * ht = 128
+  int tile_w, tile_h;    // output pixels per tile along w and h (both sub-tiles)
+  int sub_dw, sub_dh;    // offset of sub-tile 1 from sub-tile 0 (0 and ht, or wt and 0)
   int tiles_w, tiles_h, co_tiles, tile_n;
   int blocks;            // channel blocks per step: min(4, c1)
   int groups;            // steps per tap: ceil(c1 / blocks)
@@ -179,9 +181,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
     uint32_t t = blockIdx.x + (uint32_t)j * gridDim.x;
     n0 = (int)(t % (uint32_t)a.co_tiles) * a.tile_n;
     t /= (uint32_t)a.co_tiles;
-    ow0 = (int)(t % (uint32_t)a.tiles_w) * a.wt;
+    ow0 = (int)(t % (uint32_t)a.tiles_w) * a.tile_w;
     t /= (uint32_t)a.tiles_w;
-    oh0 = (int)(t % (uint32_t)a.tiles_h) * a.ht * a.sub;
+    oh0 = (int)(t % (uint32_t)a.tiles_h) * a.tile_h;
     img = (int)(t / (uint32_t)a.tiles_h);
   };
 
@@ -226,8 +228,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
           const int tap = step / a.groups, cb = (step % a.groups) * a.blocks;
           const int kh = tap / a.kernel, kw = tap % a.kernel;
           for (int u = 0; u < a.sub; ++u)
-            tma_load5(sa + u * a_box, &maps.x, 0, ow0 * a.stride + kw - a.pad,
-                      (oh0 + u * a.ht) * a.stride + kh - a.pad, cb, img, full_bar(s));
+            tma_load5(sa + u * a_box, &maps.x, 0, (ow0 + u * a.sub_dw) * a.stride + kw - a.pad,
+                      (oh0 + u * a.sub_dh) * a.stride + kh - a.pad, cb, img, full_bar(s));
           tma_load4(sb, &maps.w, 0, n0, tap, cb, full_bar(s));
         }
         ++fills[s];
@@ -308,11 +310,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
       tc_fence_after();
       int img, oh0, ow0, n0;
       tile_coords(j, img, oh0, ow0, n0);
-      const int ow = ow0 + tw;
       uint16_t* out = a.out + img * a.out_bs;
       for (int c = group; c < chunks; c += kGroups) {
-        const int u = c * 16 >= a.tile_n ? 1 : 0;  // sub-tile: the next ht output rows
-        const int co0 = n0 + c * 16 - u * a.tile_n, oh = oh0 + u * a.ht + th;
+        const int u = c * 16 >= a.tile_n ? 1 : 0;  // sub-tile 1: sub_dh rows down or sub_dw pixels on
+        const int co0 = n0 + c * 16 - u * a.tile_n, oh = oh0 + u * a.sub_dh + th, ow = ow0 + u * a.sub_dw + tw;
         // the chunk's bias first (one address for the whole warp), so its latency overlaps the
         // tensor-memory load's: the load's wait orders every later memory access behind it
         const bool bias_vec = a.bias && a.bias_vec && co0 + 16 <= a.co;
@@ -590,27 +591,40 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return fail(TTN_CUDA_ERROR, "%s: cuTensorMapEncodeTiled is not available", name);
 
+  // A 1x1 conv (stride 1) has no spatial neighbourhood: each image is one row of h * w
+  // pixels, so a tile is 128 consecutive pixels (its sub-tile the next 128) whatever the
+  // image's shape, and pads at most the image's last tile.
+  const bool flat = kernel == 1;
+  if (flat && h * w > INT32_MAX) return fail(TTN_UNSUPPORTED, "%s: more than 2^31 pixels per image", name);
+  const int64_t gh = flat ? 1 : h, gw = flat ? h * w : w, goh = flat ? 1 : oh, gow = flat ? oh * ow : ow;
+
   ConvArgs a;
   a.bias = (const uint16_t*)bias;
   a.res = (const uint16_t*)residual;
   a.out = (uint16_t*)out;
   a.out_bs = out_batch_stride;
   a.res_bs = batch > 1 ? residual_batch_stride : 0;
-  a.c1 = (int)c1, a.oh = (int)oh, a.ow = (int)ow, a.co = (int)co;
+  a.c1 = (int)c1, a.oh = (int)goh, a.ow = (int)gow, a.co = (int)co;
   a.kernel = kernel, a.stride = stride, a.pad = pad;
   // halo tiles are 8 pixels wide; where the plain path gets 16-pixel-wide tiles sharing their weight
   // stages (ow a multiple of 16 below 128, e.g. 80) it measured faster on a B200, elsewhere slower
   a.halo = kernel == 3 && stride == 1 && !(ow % 16 == 0 && ow < 128);
-  a.wt = a.halo ? 8 : gcd_int((int)ow, kConvM);  // halo: one 8-pixel row per 8-row operand group
+  a.wt = a.halo ? 8 : flat ? kConvM : gcd_int((int)ow, kConvM);  // halo: one 8-pixel row per 8-row operand group
   a.ht = kConvM / a.wt;
-  a.tiles_w = (int)((ow + a.wt - 1) / a.wt);
   const int64_t co_pad = (co + 63) / 64 * 64;
   a.tile_n = (int)(co_pad < kConvMaxN ? co_pad : kConvMaxN);
-  {  // two sub-tiles share the weight stages when they fit the accumulators and pad no extra rows
-    const int64_t rows1 = (oh + a.ht - 1) / a.ht * a.ht, rows2 = (oh + 2 * a.ht - 1) / (2 * a.ht) * (2 * a.ht);
-    a.sub = a.tile_n <= kConvMaxN / 2 && rows2 <= rows1 ? 2 : 1;
+  {  // two sub-tiles share the weight stages when they fit the accumulators and pad no extra pixels:
+     // the next ht rows, or (flat) the next 128 pixels
+    const int64_t len = flat ? gow : goh, step = flat ? a.wt : a.ht;
+    const int64_t pad1 = (len + step - 1) / step * step, pad2 = (len + 2 * step - 1) / (2 * step) * (2 * step);
+    a.sub = a.tile_n <= kConvMaxN / 2 && pad2 <= pad1 ? 2 : 1;
   }
-  a.tiles_h = (int)((oh + a.sub * a.ht - 1) / (a.sub * a.ht));
+  a.sub_dw = flat ? a.wt : 0;
+  a.sub_dh = flat ? 0 : a.ht;
+  a.tile_w = flat ? a.sub * a.wt : a.wt;
+  a.tile_h = flat ? a.ht : a.sub * a.ht;
+  a.tiles_w = (int)((gow + a.tile_w - 1) / a.tile_w);
+  a.tiles_h = (int)((goh + a.tile_h - 1) / a.tile_h);
   a.co_tiles = (int)((co_pad + a.tile_n - 1) / a.tile_n);
   a.blocks = a.halo ? 1 : (int)(c1 < kConvBlocksPerStep ? c1 : kConvBlocksPerStep);
   a.groups = (int)((c1 + a.blocks - 1) / a.blocks);
@@ -636,8 +650,8 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
 
   ConvMaps maps;
   {  // input: (16 channels, w, h, c1, image), boxes of 16 x (wt, ht) pixels at the conv stride x blocks
-    const cuuint64_t dims[5] = {16, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)c1, (cuuint64_t)batch};
-    const cuuint64_t str[4] = {32, (cuuint64_t)w * 32, (cuuint64_t)(h * w * 32),
+    const cuuint64_t dims[5] = {16, (cuuint64_t)gw, (cuuint64_t)gh, (cuuint64_t)c1, (cuuint64_t)batch};
+    const cuuint64_t str[4] = {32, (cuuint64_t)gw * 32, (cuuint64_t)(gh * gw * 32),
                                batch > 1 ? (cuuint64_t)x_batch_stride * 2 : 16};  // bytes: dims 1..4
     const cuuint32_t box[5] = {16, (cuuint32_t)(a.halo ? kHaloW : a.wt * stride),
                                (cuuint32_t)(a.halo ? a.sub * a.ht + 2 : a.ht * stride), (cuuint32_t)a.blocks, 1};
