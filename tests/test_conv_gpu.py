@@ -61,7 +61,7 @@ def _run(device, b, ci, co, h, w, k, stride, silu=True, bias=True, nchw=False, s
     (2, 64, 128, 40, 40, 1, 1), (1, 32, 32, 80, 80, 1, 1), (3, 128, 256, 20, 20, 1, 1), (1, 128, 512, 20, 20, 1, 1),
     (2, 64, 64, 40, 40, 3, 1), (1, 16, 32, 20, 20, 3, 1), (2, 32, 64, 80, 80, 3, 2), (1, 256, 256, 20, 20, 3, 2),
     (1, 32, 48, 13, 13, 3, 1), (1, 32, 64, 13, 13, 3, 2), (1, 3, 32, 64, 64, 6, 2), (2, 80, 96, 24, 24, 3, 1),
-    (1, 64, 64, 32, 32, 3, 1), (2, 32, 64, 80, 80, 3, 1)])  # 3x3 stride 1 without the halo tiles (width % 16 == 0)
+    (1, 64, 64, 32, 32, 3, 1), (2, 32, 64, 80, 80, 3, 1)])  # halo tiles whose second sub-tile pads rows (80 -> 96)
 def test_conv_matches_cpu(device, b, ci, co, h, w, k, stride):
     _run(device, b, ci, co, h, w, k, stride)
 

@@ -606,18 +606,19 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
   a.res_bs = batch > 1 ? residual_batch_stride : 0;
   a.c1 = (int)c1, a.oh = (int)goh, a.ow = (int)gow, a.co = (int)co;
   a.kernel = kernel, a.stride = stride, a.pad = pad;
-  // halo tiles are 8 pixels wide; where the plain path gets 16-pixel-wide tiles sharing their weight
-  // stages (ow a multiple of 16 below 128, e.g. 80) it measured faster on a B200, elsewhere slower
-  a.halo = kernel == 3 && stride == 1 && !(ow % 16 == 0 && ow < 128);
+  // every 3x3 stride-1 conv takes the 8-pixel-wide halo tiles, two sub-tiles (16 rows each) sharing
+  // the weights where tile_n <= 128 even when that pads the last tile's rows (80 rows -> 96): on a B200
+  // that beat the plain 16 x 16 tiles at 80x80 (128 -> 128: 118 -> 83 us), which reload the input per tap
+  a.halo = kernel == 3 && stride == 1;
   a.wt = a.halo ? 8 : flat ? kConvM : gcd_int((int)ow, kConvM);  // halo: one 8-pixel row per 8-row operand group
   a.ht = kConvM / a.wt;
   const int64_t co_pad = (co + 63) / 64 * 64;
   a.tile_n = (int)(co_pad < kConvMaxN ? co_pad : kConvMaxN);
-  {  // two sub-tiles share the weight stages when they fit the accumulators and pad no extra pixels:
-     // the next ht rows, or (flat) the next 128 pixels
+  {  // two sub-tiles (the next ht rows, or flat the next 128 pixels) share the weight stages when
+     // they fit the accumulators and, except for halo tiles, pad no extra pixels
     const int64_t len = flat ? gow : goh, step = flat ? a.wt : a.ht;
     const int64_t pad1 = (len + step - 1) / step * step, pad2 = (len + 2 * step - 1) / (2 * step) * (2 * step);
-    a.sub = a.tile_n <= kConvMaxN / 2 && pad2 <= pad1 ? 2 : 1;
+    a.sub = a.tile_n <= kConvMaxN / 2 && (pad2 <= pad1 || a.halo) ? 2 : 1;
   }
   a.sub_dw = flat ? a.wt : 0;
   a.sub_dh = flat ? 0 : a.ht;
