@@ -575,6 +575,16 @@ __device__ __noinline__ void sppf_plane_exact(uint4* cur, uint4* tmp, int pw, in
   }
 }
 
+// Row pitch, in pixels, of sppf_runs' padded planes: the 4-aligned width, the 2-pixel
+// borders, and one or two unused columns so consecutive rows start on different
+// 16-byte bank groups (a pitch of a multiple of 8 vectors put the horizontal runs of
+// neighbouring rows on the same banks: a quarter of the passes' shared-memory
+// wavefronts were conflict replays at 20 x 20; one column more leaves 7%).
+__host__ __device__ __forceinline__ int sppf_pitch(int w) {
+  const int w4 = (w + 3) & ~3;
+  return w4 + 4 + (((w4 >> 2) & 1) ? 1 : 2);
+}
+
 // Each thread takes at most IPT runs per pass; every plane has the same
 // geometry, so the runs' shared-memory bases and swizzle terms are computed once
 // per kernel.
@@ -583,7 +593,7 @@ __global__ void __launch_bounds__(256, 4) sppf_runs(const uint16_t* x, uint16_t*
                                                  int w, FastDiv wdiv) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int w4 = (w + 3) & ~3, h4 = (h + 3) & ~3;
-  const int pw = w4 + 4, ph = h4 + 4;  // padded plane, in pixels
+  const int pw = sppf_pitch(w), ph = h4 + 4;  // padded plane, in pixels (columns past w4 + 3 unused)
   const int padded_vec = ph * pw * 2;
   uint4* cur = reinterpret_cast<uint4*>(smem_raw);  // the plane being pooled
   uint4* tmp = cur + padded_vec;                     // the horizontal-pass scratch
@@ -868,7 +878,7 @@ ttn_status ttn_sppf_f16(const void* x, void* out, int64_t n, int64_t c1, int64_t
   }
   int64_t jobs = n * c1;
   const int64_t plane_vec = h * w * 2;
-  const size_t runs_smem = 2 * (size_t)(((h + 3) & ~3) + 4) * (((w + 3) & ~3) + 4) * 16 * 2;
+  const size_t runs_smem = 2 * (size_t)(((h + 3) & ~3) + 4) * sppf_pitch((int)w) * 16 * 2;
   const int64_t runs = h * ((w + 3) / 4) * 2 > w * ((h + 3) / 4) * 2 ? h * ((w + 3) / 4) * 2 : w * ((h + 3) / 4) * 2;
   if (kernel == 5 && runs <= 2 * 256 && (int64_t)runs_smem <= max_dynamic_smem()) {
     // the YOLO window: runs of four, fixed per-thread geometry
