@@ -61,9 +61,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-variants", action="store_true")
-    p.add_argument("--sweep", choices=("silu", "sigmoid", "c2f"),
-                   help="print fp16 unary bandwidth by tensor size, or the C2f region fused vs op by op "
-                        "(one GPU), and exit")
+    p.add_argument("--sweep", choices=("silu", "sigmoid", "c2f", "conv"),
+                   help="print fp16 unary bandwidth by tensor size, the C2f region fused vs op by op, or "
+                        "each config-7 conv shape timed alone (one GPU), and exit")
     p.add_argument("--config", type=int, default=4, choices=(1, 2, 3, 4, 5, 6, 7, 8, 9),
                    help="BASELINE config; 4 (the op pass) is the headline workload; 6 = fused C2PSA attention; "
                         "7 = YOLOv8s conv pass; 8 = YOLO11s depthwise convs; 9 = the whole YOLOv8s forward "
@@ -207,6 +207,8 @@ def main():
         import bench_configs
         if args.sweep == "c2f":
             print(json.dumps({"sweep": "c2f", "unit": "us", **bench_configs.c2f_sweep()}))
+        elif args.sweep == "conv":
+            print(json.dumps({"sweep": "conv", "unit": "us", **bench_configs.conv_sweep()}))
         else:
             print(json.dumps({"sweep": args.sweep, "unit": "us / GB/s", **bench_configs.unary_sweep(args.sweep)}))
         return

@@ -513,6 +513,55 @@ def c2f_sweep(batch: int = 32, reps: int = 20) -> dict:
     return out
 
 
+
+def conv_sweep(batch: int = 32, reps: int = 20) -> dict:
+    """Each distinct (cin, cout, kernel, stride, input size) of config 7's 63 YOLOv8s
+    convolutions at 640 (the stem excepted: it takes ``conv_stem``), timed alone with
+    the bias + SiLU epilogue and with the bias only, seeded random NC1HWC0 input and
+    weights; median of ``reps`` CUDA-event timings after 3 warm-ups, with the bytes
+    moved once (input + output) and the FLOPs."""
+    from thintnpu_b200 import yolo
+    thintnpu_b200.load()
+    device = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator().manual_seed(2)
+    shapes = []
+    for sp in yolo.yolov8s_convs(640):
+        key = (sp.cin, sp.cout, sp.k, sp.s, sp.h)
+        if sp.cin >= 16 and key not in shapes:
+            shapes.append(key)
+
+    def median_us(fn):
+        for _ in range(3):
+            fn()
+        times = []
+        for _ in range(reps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize(device)
+            times.append(s.elapsed_time(e))
+        return sorted(times)[len(times) // 2] * 1000
+
+    rows = []
+    for cin, cout, k, stride, h in shapes:
+        x = torch.randn(batch, cin // 16, h, h, 16, generator=g).half().to(device)
+        w = (torch.randn(cout, cin, k, k, generator=g) * (2.0 / (cin * k * k)) ** 0.5).half().to(device)
+        b = (torch.randn(cout, generator=g) * 0.1).half().to(device)
+        packed = ops.conv2d_pack_weights(w)
+        out = ops.conv2d(x, packed, b, cout, k, stride)
+        oh = out.shape[2]
+        silu = median_us(lambda: ops.conv2d(x, packed, b, cout, k, stride, silu=True, out=out))
+        plain = median_us(lambda: ops.conv2d(x, packed, b, cout, k, stride, silu=False, out=out))
+        moved = (x.numel() + out.numel()) * 2
+        flops = 2 * batch * oh * oh * cout * cin * k * k
+        rows.append({"shape": f"{cin}->{cout} k{k} s{stride} {h}x{h}", "silu_us": round(silu, 1),
+                     "bias_only_us": round(plain, 1), "gbs": round(moved / silu / 1e3), "tflops": round(flops / silu / 1e6)})
+    torch.cuda.synchronize(device)
+    if ops.conv2d_fault():
+        raise RuntimeError("conv_sweep: a convolution wait ran out")
+    return {"batch": batch, "layers": rows}
+
 def _control_plane(world: int, device):
     """Barrier and max-over-ranks on a gloo group (host tensors; no NCCL)."""
     import torch.distributed as dist
