@@ -61,6 +61,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-variants", action="store_true")
+    p.add_argument("--graph-steps", action="store_true",
+                   help="configs other than 4: time the K steps as one captured CUDA graph (kernels "
+                        "shorter than the host's per-call work then run back to back)")
     p.add_argument("--sweep", choices=("silu", "sigmoid", "c2f", "conv"),
                    help="print fp16 unary bandwidth by tensor size, the C2f region fused vs op by op, or "
                         "each config-7 conv shape timed alone (one GPU), and exit")
