@@ -182,20 +182,23 @@ __global__ void __launch_bounds__(256) softmax_warp_rows_h8(const uint16_t* x, u
 }
 
 // Contiguous fp16 rows (row pitch == reduce, 16-byte aligned, reduce % 8 == 0,
-// reduce <= 1024): each warp double-buffers its rows in shared memory with
-// cp.async 16-byte copies, so the next row streams in while the current one is
-// reduced; completion is tracked by cp.async.wait_group (no software spin).
+// reduce <= 1024): each warp streams its rows through a ring of SLOTS row buffers
+// in shared memory with cp.async 16-byte copies, so SLOTS - 1 rows are in flight
+// while the current one is reduced; completion is tracked by cp.async.wait_group
+// (no software spin).  Rows of up to 512 fp16 take four slots (three rows of
+// 1 KB or less in flight per warp keep enough bytes moving at small batches),
+// longer rows two.
 constexpr int kRowsWarps = 8;
 constexpr int kRowMaxVec = 128;  // 1024 fp16 per row
 
-template <int PER>
+template <int PER, int SLOTS>
 __global__ void __launch_bounds__(kRowsWarps * 32) softmax_rows_pipelined(const uint16_t* x, uint16_t* y,
                                                                           int64_t rows, int reduce,
                                                                           float scale, bool scaled) {
-  extern __shared__ __align__(16) uint4 rowbuf[];  // [warps][2][nvec]
+  extern __shared__ __align__(16) uint4 rowbuf[];  // [warps][SLOTS][nvec]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = reduce >> 3;
-  uint4* buf = rowbuf + (size_t)warp * 2 * nvec;
+  uint4* buf = rowbuf + (size_t)warp * SLOTS * nvec;
   const int64_t warps = (int64_t)gridDim.x * kRowsWarps;
   int64_t row = (int64_t)blockIdx.x * kRowsWarps + warp;
   auto prefetch = [&](int64_t r, int slot) {
@@ -205,12 +208,13 @@ __global__ void __launch_bounds__(kRowsWarps * 32) softmax_rows_pipelined(const 
     }
     cp_async_commit();
   };
-  prefetch(row, 0);
+#pragma unroll
+  for (int k = 0; k < SLOTS - 1; ++k) prefetch(row + k * warps, k);
   for (int i = 0; row < rows; row += warps, ++i) {
-    prefetch(row + warps, (i + 1) & 1);
-    cp_async_wait<1>();
+    prefetch(row + (SLOTS - 1) * warps, (i + SLOTS - 1) % SLOTS);  // the slot row i - 1 used
+    cp_async_wait<SLOTS - 1>();
     __syncwarp();
-    const uint4* xv = buf + (i & 1) * nvec;
+    const uint4* xv = buf + (i % SLOTS) * nvec;
     float v[PER][8];
     float m = -INFINITY;
 #pragma unroll
@@ -264,7 +268,7 @@ __global__ void __launch_bounds__(kRowsWarps * 32) softmax_rows_pipelined(const 
         yv[e] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
-    __syncwarp();  // this slot is refilled two rows later
+    __syncwarp();  // this slot is refilled at the next row
   }
   cp_async_wait<0>();
 }
@@ -632,23 +636,24 @@ ttn_status launch_softmax(const ttn_tensor* x, const ttn_tensor* y, int dim, flo
       bool packed = vec && rs.ndim <= 1 && (rs.ndim == 0 || (rs.sx[0] == reduce && rs.sy[0] == reduce));
       if (packed && rows >= 1024) {  // contiguous rows: cp.async double buffering
         int nvec = (int)(reduce / 8);
-        size_t smem = (size_t)kRowsWarps * 2 * nvec * 16;
         int per = nvec <= 32 ? 1 : nvec <= 64 ? 2 : 4;
-        const void* fn = per == 1 ? (const void*)softmax_rows_pipelined<1>
-                       : per == 2 ? (const void*)softmax_rows_pipelined<2>
-                                  : (const void*)softmax_rows_pipelined<4>;
+        const int slots = per <= 2 ? 4 : 2;
+        size_t smem = (size_t)kRowsWarps * slots * nvec * 16;
+        const void* fn = per == 1 ? (const void*)softmax_rows_pipelined<1, 4>
+                       : per == 2 ? (const void*)softmax_rows_pipelined<2, 4>
+                                  : (const void*)softmax_rows_pipelined<4, 2>;
         TTN_TRY(ensure_dynamic_smem(fn, (int)smem));
         unsigned grid = (unsigned)(sm_count() * resident_blocks(fn, kRowsWarps * 32, smem));
         int64_t need = (rows + kRowsWarps - 1) / kRowsWarps;
         if ((int64_t)grid > need) grid = (unsigned)need;
         if (per == 1)
-          softmax_rows_pipelined<1><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
+          softmax_rows_pipelined<1, 4><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
                                                                        rows, (int)reduce, scale, scaled);
         else if (per == 2)
-          softmax_rows_pipelined<2><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
+          softmax_rows_pipelined<2, 4><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
                                                                        rows, (int)reduce, scale, scaled);
         else
-          softmax_rows_pipelined<4><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
+          softmax_rows_pipelined<4, 2><<<grid, kRowsWarps * 32, smem, s>>>((const uint16_t*)xp, (uint16_t*)yp,
                                                                        rows, (int)reduce, scale, scaled);
         return launch_check("ttn_softmax");
       }
