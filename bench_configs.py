@@ -543,8 +543,9 @@ def conv_sweep(batch: int = 32, reps: int = 20) -> dict:
     """Each distinct (cin, cout, kernel, stride, input size) of config 7's 63 YOLOv8s
     convolutions at 640 (the stem excepted: it takes ``conv_stem``), timed alone with
     the bias + SiLU epilogue and with the bias only, seeded random NC1HWC0 input and
-    weights; median of ``reps`` CUDA-event timings after 3 warm-ups, with the bytes
-    moved once (input + output) and the FLOPs."""
+    weights: ``reps`` back-to-back calls between two CUDA events after 3 warm-ups
+    (so the host's per-call work overlaps the kernels), with the bytes moved once
+    (input + output) and the FLOPs."""
     from thintnpu_b200 import yolo
     thintnpu_b200.load()
     device = torch.device("cuda", torch.cuda.current_device())
@@ -555,18 +556,17 @@ def conv_sweep(batch: int = 32, reps: int = 20) -> dict:
         if sp.cin >= 16 and key not in shapes:
             shapes.append(key)
 
-    def median_us(fn):
+    def mean_us(fn):  # over `reps` back-to-back calls
         for _ in range(3):
             fn()
-        times = []
+        torch.cuda.synchronize(device)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
         for _ in range(reps):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
             fn()
-            e.record()
-            torch.cuda.synchronize(device)
-            times.append(s.elapsed_time(e))
-        return sorted(times)[len(times) // 2] * 1000
+        e.record()
+        torch.cuda.synchronize(device)
+        return s.elapsed_time(e) / reps * 1000
 
     rows = []
     for cin, cout, k, stride, h in shapes:
@@ -576,8 +576,8 @@ def conv_sweep(batch: int = 32, reps: int = 20) -> dict:
         packed = ops.conv2d_pack_weights(w)
         out = ops.conv2d(x, packed, b, cout, k, stride)
         oh = out.shape[2]
-        silu = median_us(lambda: ops.conv2d(x, packed, b, cout, k, stride, silu=True, out=out))
-        plain = median_us(lambda: ops.conv2d(x, packed, b, cout, k, stride, silu=False, out=out))
+        silu = mean_us(lambda: ops.conv2d(x, packed, b, cout, k, stride, silu=True, out=out))
+        plain = mean_us(lambda: ops.conv2d(x, packed, b, cout, k, stride, silu=False, out=out))
         moved = (x.numel() + out.numel()) * 2
         flops = 2 * batch * oh * oh * cout * cin * k * k
         rows.append({"shape": f"{cin}->{cout} k{k} s{stride} {h}x{h}", "silu_us": round(silu, 1),
