@@ -543,9 +543,10 @@ def conv_sweep(batch: int = 32, reps: int = 20) -> dict:
     """Each distinct (cin, cout, kernel, stride, input size) of config 7's 63 YOLOv8s
     convolutions at 640 (the stem excepted: it takes ``conv_stem``), timed alone with
     the bias + SiLU epilogue and with the bias only, seeded random NC1HWC0 input and
-    weights: ``reps`` back-to-back calls between two CUDA events after 3 warm-ups
-    (so the host's per-call work overlaps the kernels), with the bytes moved once
-    (input + output) and the FLOPs."""
+    weights: ``reps`` calls captured into one CUDA graph after 3 warm-ups, its replay
+    between two CUDA events (as the layers run in the model's graph: the host's
+    per-call work, ~23 µs, would otherwise set the time of the small layers), with
+    the bytes moved once (input + output) and the FLOPs."""
     from thintnpu_b200 import yolo
     thintnpu_b200.load()
     device = torch.device("cuda", torch.cuda.current_device())
@@ -556,14 +557,19 @@ def conv_sweep(batch: int = 32, reps: int = 20) -> dict:
         if sp.cin >= 16 and key not in shapes:
             shapes.append(key)
 
-    def mean_us(fn):  # over `reps` back-to-back calls
+    def mean_us(fn):  # over `reps` calls replayed from one graph
         for _ in range(3):
             fn()
         torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize(device)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for _ in range(reps):
-            fn()
+        graph.replay()
         e.record()
         torch.cuda.synchronize(device)
         return s.elapsed_time(e) / reps * 1000
