@@ -508,6 +508,19 @@ __device__ void stem_pixels(const StemArgs& a, const unsigned long long* wsm, co
   }
 }
 
+// True (block-wide; every thread must call it) when any of the co output channels
+// has a nonzero weight on an input channel past the third: the stem then needs the
+// CUDA-core kernel, otherwise the tensor-core one (K = 27) takes it.  Both kernels
+// decide from this same predicate, so exactly one of them does the work.
+__device__ __forceinline__ bool stem_wide(const uint16_t* packed, int co64, int co) {
+  int mine = 0;
+  for (int i = threadIdx.x; i < 13 * 9 * co; i += blockDim.x) {
+    const int c = 3 + i % 13, rest = i / 13, tap = rest % 9, n = rest / 9;
+    if (__half2float(__ushort_as_half(packed[((int64_t)tap * co64 + n) * 16 + c])) != 0.0f) mine = 1;
+  }
+  return __syncthreads_or(mine) != 0;
+}
+
 template <int CO, int PIX>
 __global__ void __launch_bounds__(kStemThreads) conv_stem(StemArgs a, const uint16_t* packed, int co64,
                                                           const uint16_t* bias) {
@@ -517,6 +530,7 @@ __global__ void __launch_bounds__(kStemThreads) conv_stem(StemArgs a, const uint
   __shared__ float bsm[CO];
   __shared__ int used;
   const int tid = threadIdx.x;
+  if (!stem_wide(packed, co64, (int)gridDim.y * CO)) return;  // conv_stem_tc takes it
   if (tid == 0) used = 0;
   __syncthreads();
   int mine = 0;
@@ -538,6 +552,129 @@ __global__ void __launch_bounds__(kStemThreads) conv_stem(StemArgs a, const uint
     case 4: stem_pixels<CO, PIX, 4>(a, wsm, bsm); break;
     case 5: case 6: case 7: case 8: stem_pixels<CO, PIX, 8>(a, wsm, bsm); break;
     default: stem_pixels<CO, PIX, 16>(a, wsm, bsm); break;
+  }
+}
+
+// The stem on the tensor cores when its weights use input channels 0-2 only (the
+// YOLO image): the reduction is 27 long (k = tap * 3 + channel, zero-padded to 32)
+// instead of nine 16-channel taps.  A tile is 128 consecutive output pixels of one
+// image.  Each thread gathers its pixel's 27 inputs (nine 8-byte loads, zeros past
+// the border) into a 128 x 32 K-major operand in shared memory (two 32-byte rows per
+// pixel, the 32-byte swizzle the descriptors name); the weights are a 32 x co operand
+// built once per CTA.  One thread issues the two K = 16 products (M = 128, N = co)
+// into tensor memory and commits them to an mbarrier; each warp then reads its 32
+// pixels' accumulators in 16-column chunks and runs conv_tc's epilogue (bias,
+// bracketed SiLU, one rounding, 32-byte NC1HWC0 rows).  Persistent CTAs, several per
+// SM, so one CTA's gather overlaps another's epilogue.  The wait on the products is
+// bounded; a CTA whose wait runs out sets bit 4 of the fault word and stops.
+constexpr int kStemTcThreads = 128;
+constexpr int kStemTcBlocks = 6;  // CTAs per SM (85 registers; TMEM 6 x 64 columns at most)
+
+__global__ void __launch_bounds__(kStemTcThreads, kStemTcBlocks) conv_stem_tc(StemArgs a, const uint16_t* packed, int co64,
+                                                                  int co, const uint16_t* bias, int bias_vec,
+                                                                  int row32) {
+  __shared__ __align__(1024) unsigned char a_tile[2 * kConvM * 32];  // [K block][pixel][32 bytes]
+  __shared__ __align__(1024) unsigned char b_tile[2 * 64 * 32];      // [K block][output channel][32 bytes]
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t tmem_slot;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (stem_wide(packed, co64, co)) return;  // conv_stem takes it
+  const uint32_t sa = (uint32_t)__cvta_generic_to_shared(a_tile), sb = (uint32_t)__cvta_generic_to_shared(b_tile);
+  const uint32_t bar_addr = (uint32_t)__cvta_generic_to_shared(&bar);
+  const uint32_t cols = co <= 32 ? 32 : 64;
+  // row r of a K-major operand, 16-byte half h: the 32-byte swizzle moves the half of rows 4-7
+  // of every 8-row group
+  auto swz = [](int r, int h) { return (uint32_t)(r * 32 + ((h ^ ((r >> 2) & 1)) << 4)); };
+  for (int i = tid; i < co * 32; i += kStemTcThreads) {  // weights: row n, k = tap * 3 + channel
+    const int n = i >> 5, k = i & 31, kb = k >> 4, kk = k & 15;
+    const uint16_t v = k < 27 ? packed[((int64_t)(k / 3) * co64 + n) * 16 + k % 3] : (uint16_t)0;
+    *reinterpret_cast<uint16_t*>(b_tile + kb * co * 32 + swz(n, kk >> 3) + (kk & 7) * 2) = v;
+  }
+  if (tid == 0) {
+    mbar_init(bar_addr, 1);
+    mbar_init_fence();
+  }
+  if (warp == 0) tmem_alloc((uint32_t)__cvta_generic_to_shared(&tmem_slot), cols);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot, lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t idesc = umma_idesc(kConvM, co, false, false);
+  const uint64_t adesc = smem_desc(sa, 16, 256, kSwizzle32B), bdesc = smem_desc(sb, 16, 256, kSwizzle32B);
+  const int plane = a.oh * a.ow, tiles_img = (plane + kConvM - 1) / kConvM;
+  const int64_t total = (int64_t)a.batch * tiles_img;
+  uint32_t phase = 0;
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    const int64_t img = t / tiles_img;
+    const int p = (int)(t - img * tiles_img) * kConvM + tid;
+    const bool valid = p < plane;
+    const int oy = valid ? p / a.ow : 0, ox = valid ? p - oy * a.ow : 0;
+    {  // gather: this pixel's 27 inputs as one 64-byte K row (two swizzled 32-byte rows)
+      const uint16_t* src = a.x + img * a.x_bs;
+      uint16_t hv[32];
+#pragma unroll
+      for (int tap = 0; tap < 9; ++tap) {
+        const int iy = 2 * oy - 1 + tap / 3, ix = 2 * ox - 1 + tap % 3;
+        const bool in = valid && iy >= 0 && iy < a.h && ix >= 0 && ix < a.w;
+        const uint2 v = in ? __ldg(reinterpret_cast<const uint2*>(src + ((int64_t)iy * a.w + ix) * 16))
+                           : make_uint2(0u, 0u);
+        hv[3 * tap] = (uint16_t)v.x, hv[3 * tap + 1] = (uint16_t)(v.x >> 16), hv[3 * tap + 2] = (uint16_t)v.y;
+      }
+#pragma unroll
+      for (int k = 27; k < 32; ++k) hv[k] = 0;
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int k0 = kb * 16 + h * 8;
+          uint4 q;
+          q.x = hv[k0] | ((uint32_t)hv[k0 + 1] << 16), q.y = hv[k0 + 2] | ((uint32_t)hv[k0 + 3] << 16);
+          q.z = hv[k0 + 4] | ((uint32_t)hv[k0 + 5] << 16), q.w = hv[k0 + 6] | ((uint32_t)hv[k0 + 7] << 16);
+          *reinterpret_cast<uint4*>(a_tile + kb * kConvM * 32 + swz(tid, h)) = q;
+        }
+    }
+    fence_proxy_async_smem();  // the generic stores above, before the products read them
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      umma_ss(tmem, adesc, bdesc, idesc, false);
+      umma_ss(tmem, adesc + ((kConvM * 32) >> 4), bdesc + ((uint32_t)(co * 32) >> 4), idesc, true);
+      umma_commit(bar_addr);
+    }
+    if (!__syncthreads_and(mbar_wait(bar_addr, phase))) {
+      atomicOr(&g_conv_fault, 4u);
+      break;
+    }
+    phase ^= 1;
+    tc_fence_after();
+    uint16_t* out = a.out + img * a.out_bs;
+    for (int c0 = 0; c0 < co; c0 += 16) {
+      const bool bv = bias && bias_vec;
+      uint32_t bias_words[8];
+      if (bv) ld_global_v8(bias + c0, bias_words);
+      uint32_t r[16];
+      __syncwarp();
+      tmem_ld16(lane_addr + c0, r);
+      if (!valid) continue;
+      uint32_t packed_out[8];
+      conv_epilogue<16>(r, bv, bias_words, bias, c0, co, a.silu, packed_out);
+      uint16_t* o = out + (((int64_t)(c0 / 16) * a.oh + oy) * a.ow + ox) * 16;
+      if (row32) {
+        st_global_v8(o, packed_out);
+      } else {
+        reinterpret_cast<uint4*>(o)[0] = make_uint4(packed_out[0], packed_out[1], packed_out[2], packed_out[3]);
+        reinterpret_cast<uint4*>(o)[1] = make_uint4(packed_out[4], packed_out[5], packed_out[6], packed_out[7]);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // the accumulators and the operand tile are free for the next tile
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, cols);
   }
 }
 
@@ -578,6 +715,17 @@ ttn_status conv_launch(const char* name, const void* x, int64_t batch, int64_t c
     const dim3 grid(grid_for(batch * oh * ((ow + 1) / 2), kStemThreads, 16), (unsigned)(co / 16));
     const StemArgs a{(const uint16_t*)x, batch > 1 ? x_batch_stride : 0, (int)h, (int)w, (int)oh, (int)ow,
                      (int)batch, (flags & TTN_CONV_SILU) ? 1 : 0, (uint16_t*)out, batch > 1 ? out_batch_stride : 0};
+    // both launch; from the weights each block decides whether its kernel applies (at most
+    // three input channels used: the tensor cores; more: the CUDA cores)
+    const int64_t tiles = batch * ((oh * ow + kConvM - 1) / kConvM);
+    const int64_t slots = (int64_t)sm_count() * kStemTcBlocks;
+    const unsigned grid_tc = (unsigned)(tiles < slots ? tiles : slots);
+    const int bias_vec = bias && ((uintptr_t)bias & 31u) == 0 ? 1 : 0;
+    const int row32 = ((uintptr_t)out & 31u) == 0 && (batch == 1 || out_batch_stride % 16 == 0) ? 1 : 0;
+    conv_stem_tc<<<grid_tc, kStemTcThreads, 0, (cudaStream_t)stream>>>(
+        a, (const uint16_t*)packed_weights, (int)((co + 63) / 64 * 64), (int)co, (const uint16_t*)bias, bias_vec,
+        row32);
+    TTN_TRY(launch_check(name));
     conv_stem<16, 2><<<grid, kStemThreads, 0, (cudaStream_t)stream>>>(a, (const uint16_t*)packed_weights,
                                                                        (int)((co + 63) / 64 * 64),
                                                                        (const uint16_t*)bias);
