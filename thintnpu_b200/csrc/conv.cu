@@ -399,10 +399,12 @@ int gcd_int(int x, int y) {
 }
 
 // The stem convolution -- one input channel block, 3x3, stride 2 (YOLO's first
-// layer: 3 real channels padded to 16) -- on the CUDA cores.  On the tensor cores
-// every tap re-reads its input through 32-byte TMA rows; here each output pixel
-// reads its nine input rows once (neighbours share them in L1) and only the input
-// channels the weights use: the block finds the highest channel with a nonzero
+// layer: 3 real channels padded to 16).  Weights that use at most three input
+// channels go to conv_stem_tc (below: a 27-long reduction on the tensor cores);
+// wider ones run here on the CUDA cores (conv_tc would re-read every tap through
+// 32-byte TMA rows).  Each output pixel reads its nine input rows once (neighbours
+// share them in L1) and only the input channels the weights use: the block finds
+// the highest channel with a nonzero
 // weight (input channels past the real count are zero by contract) and takes the
 // body compiled for that many channels (1-4, 8 or 16), so the channel loops are
 // static.  Thread = PIX adjacent output pixels x the 16 output channels of its
