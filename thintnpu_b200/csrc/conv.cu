@@ -514,13 +514,17 @@ __device__ void stem_pixels(const StemArgs& a, const unsigned long long* wsm, co
 // has a nonzero weight on an input channel past the third: the stem then needs the
 // CUDA-core kernel, otherwise the tensor-core one (K = 27) takes it.  Both kernels
 // decide from this same predicate, so exactly one of them does the work.
+// Each (tap, output channel) weight row is 32 bytes (16 input channels), read as two
+// 16-byte loads; a value is nonzero exactly when its bits without the sign are.
 __device__ __forceinline__ bool stem_wide(const uint16_t* packed, int co64, int co) {
-  int mine = 0;
-  for (int i = threadIdx.x; i < 13 * 9 * co; i += blockDim.x) {
-    const int c = 3 + i % 13, rest = i / 13, tap = rest % 9, n = rest / 9;
-    if (__half2float(__ushort_as_half(packed[((int64_t)tap * co64 + n) * 16 + c])) != 0.0f) mine = 1;
+  uint32_t mine = 0;
+  for (int i = threadIdx.x; i < 9 * co; i += blockDim.x) {
+    const int tap = i / co, n = i - tap * co;
+    const uint4* row = reinterpret_cast<const uint4*>(packed + ((int64_t)tap * co64 + n) * 16);
+    const uint4 q0 = __ldg(row), q1 = __ldg(row + 1);
+    mine |= (q0.y & 0x7fff0000u) | ((q0.z | q0.w | q1.x | q1.y | q1.z | q1.w) & 0x7fff7fffu);  // channels 3-15
   }
-  return __syncthreads_or(mine) != 0;
+  return __syncthreads_or(mine != 0) != 0;
 }
 
 template <int CO, int PIX>
