@@ -67,10 +67,13 @@ def test_conv_matches_cpu(device, b, ci, co, h, w, k, stride):
 
 
 @pytest.mark.parametrize("b,ci,co,h,w", [(2, 3, 32, 64, 64), (1, 3, 16, 33, 47), (1, 16, 64, 40, 40), (1, 1, 48, 20, 21),
-                                         (2, 5, 32, 17, 18), (1, 3, 32, 160, 160)])
+                                         (2, 5, 32, 17, 18), (1, 3, 32, 160, 160), (1, 2, 64, 31, 29),
+                                         (3, 3, 48, 9, 9)])
 def test_stem_conv_matches_cpu(device, b, ci, co, h, w):
-    """One input channel block, 3x3 stride 2 (the YOLO stem): the CUDA-core kernel,
-    which reads only the channels the weights use; odd sizes, 1 to 16 real channels."""
+    """One input channel block, 3x3 stride 2 (the YOLO stem): up to 3 real channels the
+    tensor-core kernel (27-long reduction), more the CUDA-core kernel, which reads
+    only the channels the weights use; odd sizes, 1 to 16 real channels, 16-64
+    outputs."""
     _run(device, b, ci, co, h, w, 3, 2)
     _run(device, b, ci, co, h, w, 3, 2, silu=False, bias=False, seed=5)
 
@@ -276,3 +279,25 @@ def test_bounded_wait_runs_out_and_is_reported(device):
     torch.cuda.synchronize()
     assert ttn.ops.conv2d_fault() == 0
     _check(oops.from_blocked(out.cpu()), x, wt, bs, 1, True)
+
+
+def test_stem_conv_into_a_channel_slice(device):
+    """The stem writing into channel blocks 1-2 of a wider buffer (batch stride past the
+    dense image; 32-byte aligned rows) and into rows that are only 16-byte aligned:
+    both bit-identical to the dense output, the blocks around them untouched."""
+    import thintnpu_b200 as ttn
+    x, wt, bs = _case(2, 3, 32, 48, 48, 3, 11)
+    xd = oops.pack_padded(x).to(device)
+    packed = ttn.conv2d_pack_weights(wt.to(device))
+    dense = ttn.conv2d(xd, packed, bs.to(device), 32, 3, 2)
+    wide = torch.full((2, 4, 24, 24, 16), 7.0, dtype=torch.float16, device=device)
+    ttn.conv2d(xd, packed, bs.to(device), 32, 3, 2, out=wide[:, 1:3])
+    flat = torch.full((2 * 4 * 24 * 24 * 16 + 8,), 7.0, dtype=torch.float16, device=device)
+    shifted = flat[8:].view(2, 4, 24, 24, 16)  # 16 bytes past a 32-byte boundary
+    ttn.conv2d(xd, packed, bs.to(device), 32, 3, 2, out=shifted[:, :2])
+    torch.cuda.synchronize()
+    assert ttn.ops.conv2d_fault() == 0
+    assert torch.equal(wide[:, 1:3].view(torch.int16), dense.view(torch.int16))
+    assert torch.equal(shifted[:, :2].view(torch.int16), dense.view(torch.int16))
+    assert bool((wide[:, 0] == 7).all()) and bool((wide[:, 3] == 7).all())
+    assert bool((shifted[:, 2:] == 7).all())
