@@ -285,7 +285,7 @@ class Config7:
     def __init__(self):
         from thintnpu_b200 import yolo
         self.specs = yolo.yolov8s_convs(640)
-        self.launches = len(self.specs)
+        self.launches = sum(sp.launches for sp in self.specs)
         self.flops_per_image = sum(sp.flops for sp in self.specs)
         self.bytes_per_image = sum(2 * 16 * ((sp.cin + 15) // 16) * sp.h * sp.w + 2 * sp.cout * sp.out_hw[0] *
                                    sp.out_hw[1] for sp in self.specs)

@@ -55,3 +55,13 @@ def test_cpu_chain_equals_its_op_pass():
     assert torch.equal(out.view(torch.int16), again.view(torch.int16))
     assert torch.equal(head.view(torch.int16), head2.view(torch.int16))
     assert torch.isfinite(out.float()).all()
+
+
+def test_conv_launch_count():
+    """The stem-shaped conv (one input channel block, 3x3 stride 2, <= 64 outputs)
+    launches the tensor-core and the CUDA-core stem kernels; every other conv one."""
+    specs = yolo.yolov8s_convs(640)
+    assert [sp.launches for sp in specs].count(2) == 1 and specs[0].launches == 2
+    assert sum(sp.launches for sp in specs) == 64
+    assert yolo.conv_launches(16, 64, 3, 2) == 2 and yolo.conv_launches(32, 64, 3, 2) == 1
+    assert yolo.conv_launches(3, 80, 3, 2) == 1 and yolo.conv_launches(3, 32, 1, 1) == 1

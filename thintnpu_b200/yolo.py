@@ -246,6 +246,17 @@ class ConvSpec:
         oh, ow = self.out_hw
         return 2 * self.cin * self.cout * self.k * self.k * oh * ow
 
+    @property
+    def launches(self) -> int:
+        return conv_launches(self.cin, self.cout, self.k, self.s)
+
+
+def conv_launches(cin: int, cout: int, k: int, stride: int) -> int:
+    """Kernels one ``ops.conv2d`` call launches (NC1HWC0 output, no residual): two for
+    a stem-shaped conv (one 16-channel input block, 3x3 stride 2, at most 64 outputs:
+    the tensor-core and CUDA-core stem kernels, one of which returns at once), else one."""
+    return 2 if cin <= C0 and k == 3 and stride == 2 and cout <= 64 else 1
+
 
 def yolov8s_convs(imgsz: int = 640, nc: int = 80) -> List[ConvSpec]:
     """The 63 convolutions of YOLOv8s at imgsz x imgsz in model order (the same
@@ -590,7 +601,10 @@ class ModelPass(OpPass):
         return self.output
 
     def launches_per_pass(self) -> int:
-        return len(self.convs) + super().launches_per_pass()
+        convs = 0
+        for src, _, _, cout, k, stride, _, _ in self.convs:
+            convs += conv_launches(3 if src is None else src.count * C0, cout, k, stride)
+        return convs + super().launches_per_pass()
 
     def flops_per_image(self) -> int:
         total = 0
