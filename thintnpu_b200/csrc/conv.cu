@@ -105,7 +105,22 @@ __device__ __forceinline__ void st_global_v8(uint16_t* p, const uint32_t (&w)[8]
 // the caller ahead of the tensor-memory load) when `bias_vec`, else element by element.
 // The SiLU is silu_pair_fast;
 // lanes it flags take silu_f32 itself, so each output is exactly fp16(silu_f32(s)).
-template <int N>
+// fp16(x sigmoid(x)) for two FP32 values from silu_pair_fast's ex2/rcp core, rounded
+// once without its bracket: within ~2^-19 (relative) of silu_f32, so an output can be
+// the neighbouring fp16 value where silu_f32's result sits that close to a rounding
+// midpoint.  `big` is set where a0 a1 >= 2^126 (a NaN, -inf, or inputs so negative
+// that the shared reciprocal underflows): those lanes take silu_f32.
+__device__ __forceinline__ uint32_t silu_pair_plain(unsigned long long xx, bool& big) {
+  const unsigned long long t = f2_mul(xx, f2_pack(-1.44269504088896341f, -1.44269504088896341f));
+  const float2 tt = f2_unpack(t);
+  const float2 aa = f2_unpack(f2_add(f2_pack(ex2_approx(tt.x), ex2_approx(tt.y)), f2_pack(1.0f, 1.0f)));
+  const float p = aa.x * aa.y, q = rcp_approx(p);
+  const float2 r = f2_unpack(f2_mul(xx, f2_mul(f2_pack(aa.y, aa.x), f2_pack(q, q))));
+  big = !(p < 8.50705917302346159e+37f);  // 2^126
+  return h2_bits(__floats2half2_rn(r.x, r.y));
+}
+
+template <int N, bool kBracket = true>
 __device__ __forceinline__ void conv_epilogue(const uint32_t (&r)[N], bool bias_vec, const uint32_t (&bias_words)[N / 2],
                                               const uint16_t* bias, int co0, int co, bool silu,
                                               uint32_t (&packed)[N / 2]) {
@@ -130,7 +145,22 @@ __device__ __forceinline__ void conv_epilogue(const uint32_t (&r)[N], bool bias_
       }
     }
   }
-  if (silu) {
+  if (silu && !kBracket) {
+    bool big[P], any = false;
+#pragma unroll
+    for (int e = 0; e < P; ++e) {
+      packed[e] = silu_pair_plain(v[e], big[e]);
+      any |= big[e];
+    }
+    if (any) {
+#pragma unroll
+      for (int e = 0; e < P; ++e)
+        if (big[e]) {
+          const float2 s = f2_unpack(v[e]);
+          packed[e] = h2_bits(__floats2half2_rn(silu_f32(s.x), silu_f32(s.y)));
+        }
+    }
+  } else if (silu) {
     uint32_t lower[P], open = 0;
 #pragma unroll
     for (int e = 0; e < P; ++e) {
@@ -324,7 +354,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc(ConvArgs a, const __g
         tmem_ld16(lane_addr + acc * kConvMaxN + c * 16, r);
         if (oh >= a.oh || ow >= a.ow || co0 >= a.co) continue;
         uint32_t packed[8];
-        conv_epilogue<16>(r, bias_vec, bias_words, a.bias, co0, a.co, a.silu, packed);
+        conv_epilogue<16, false>(r, bias_vec, bias_words, a.bias, co0, a.co, a.silu, packed);
         if (a.nchw) {
           const int64_t plane = (int64_t)a.oh * a.ow;
           uint16_t* o = out + (int64_t)co0 * plane + (int64_t)oh * a.ow + ow;
@@ -664,7 +694,7 @@ __global__ void __launch_bounds__(kStemTcThreads, kStemTcBlocks) conv_stem_tc(St
       tmem_ld16(lane_addr + c0, r);
       if (!valid) continue;
       uint32_t packed_out[8];
-      conv_epilogue<16>(r, bv, bias_words, bias, c0, co, a.silu, packed_out);
+      conv_epilogue<16, false>(r, bv, bias_words, bias, c0, co, a.silu, packed_out);
       uint16_t* o = out + (((int64_t)(c0 / 16) * a.oh + oy) * a.ow + ox) * 16;
       if (row32) {
         st_global_v8(o, packed_out);
