@@ -1,7 +1,7 @@
 """Regenerate tests/golden/ from the reference's own CPU selection restatement.
 
-Runs only where the reference checkout is present (default /root/reference,
-override with REFERENCE_ROOT).  It imports verify_selection_flow.py from the
+Runs only where the reference checkout is present (its location comes from
+REFERENCE_ROOT, with the build container's checkout as the default).  It imports verify_selection_flow.py from the
 reference, walks its 47 fixtures with their layouts (fixtures() :168-199,
 backing_and_view() :202-213), evaluates its ``reference()`` (:27-47) and
 stores inputs and all 8 trace outputs as raw bits, plus the reference's
