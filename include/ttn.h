@@ -243,8 +243,13 @@ ttn_status ttn_attention_f16(const void* q, const void* k, const void* v, void* 
 ttn_status ttn_attention_fault_f16(uint32_t* fault);
 
 /* Dense 2-D convolution with the reference's fused epilogue, on the tensor cores
- * (tcgen05 implicit GEMM, FP32 accumulation): out = fp16(silu(conv(x, w) + bias))
- * with TTN_CONV_SILU (silu(s) = s / (1 + exp(-s)) in FP32), else fp16(conv + bias).
+ * (tcgen05 implicit GEMM, FP32 accumulation; a stem-shaped call -- c1 == 1, 3x3
+ * stride 2, co <= 64 -- whose weights use input channels past the third runs on the
+ * CUDA cores): out = fp16(silu(conv(x, w) + bias)) with TTN_CONV_SILU, else
+ * fp16(conv + bias), one rounding.  silu(s) = s / (1 + exp(-s)) evaluated in FP32
+ * from exp2 and reciprocal approximations, within ~2^-19 (relative) of the IEEE
+ * evaluation, so an output can be the neighbouring fp16 value where that value lies
+ * so close to a rounding midpoint (as the FP32 summation order already allows).
  * x: NC1HWC0 fp16 [batch, c1, h, w, 16] (image i at x + i*x_batch_stride; input
  * channels past the real count must be zero, as the reference's pack_input pads).
  * packed_weights: the reference's prepared layout [c1][kernel^2][co64][16] with
